@@ -1,0 +1,1244 @@
+// Verify-round sampling kernels for B200 (sm_100a).
+//
+// Reference path replaced: specdec/sampling.py:34-95 (to_probs, residual_probs,
+// gather_prob, sample_from_probs) and the accept / residual / bonus block of
+// specdec/engine.py:282-303.
+//
+// Design
+// ------
+// * bf16 / fp16 logits at any vocabulary size: one CTA per logits vector builds
+//   an EXACT count histogram over the 65,536 possible 16-bit values in shared
+//   memory (two 16-bit counters per 32-bit word, one shared-memory atomic per
+//   element).  Every element of a bin has the same logit, hence the same
+//   probability, so the softmax normaliser, the top-k threshold and the top-p
+//   nucleus (including how many members of the boundary tie class are kept)
+//   are computed per distinct value, with float64 sums, and never need a sort.
+//   Tie order inside the boundary class is ascending vocabulary index; the
+//   index of the last kept member (idx_cut) is found by one ordered scan.
+// * fp32 / any dtype with V <= SMALLV_MAX: one CTA per vector computes every
+//   probability, sorts (p desc, index asc) with a bitonic sort in shared memory
+//   and materialises the final probabilities in the workspace.
+// * greedy (T <= 0): only the target argmax is needed; the draft logits are
+//   never read.
+// * the finish kernel runs per (row, vocabulary chunk): it decides the accepted
+//   prefix from the per-vector probe probabilities p_i(x_i), q_i(x_i), sums the
+//   residual (or bonus) mass of its chunk, and the last chunk of a row to
+//   finish performs the inverse-CDF draw.  No CTA ever waits on another.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "sd_common.cuh"
+
+namespace sd {
+
+constexpr int HT = 512;                 // threads of the histogram stats kernel
+constexpr int HIST_WORDS = 32768;       // 65536 16-bit counters
+constexpr int NGROUP = 8192;            // key groups of 8 keys
+constexpr int NCORR_MAX = 96;           // counter-wrap corrections per vector
+constexpr int SMALLV_MAX = 2048;        // small-vocabulary exact path
+constexpr int ST = 512;                 // threads of the small-V kernel
+constexpr int FT = 512;                 // threads of the finish / probs kernels
+constexpr int NCH_MAX = 64;             // vocabulary chunks per row in finish
+
+constexpr uint32_t NO_CUT = 0x7FFFFFFFu;
+
+struct VecStats {
+  float m;          // max of fl(x / T)
+  float inv_s;      // fl(1 / S)
+  float zf;         // max(fl(Z), 1e-12): kept mass after top-k / top-p
+  float probe_p;    // final probability of the probe token (0 if no probe)
+  uint32_t kth;     // top-k: keep fkey(x) >= kth
+  uint32_t vstar;   // top-p boundary class (fkey); keys > vstar kept
+  int32_t idx_cut;  // members of the vstar class with index <= idx_cut kept
+  int32_t argmax;   // greedy: first index of the maximum
+  int32_t flags;    // bit0: histogram overflow path taken; bit1: correction table full
+  int32_t n_keep;   // kept members of the boundary class (diagnostics)
+  int32_t pad[2];
+};
+static_assert(sizeof(VecStats) == 48, "VecStats layout");
+
+// Two logits tensors addressed as one list of vectors, row-major:
+// vector v -> row b = v / (npos0 + npos1), then set 0 positions, then set 1.
+struct VecSet {
+  const void* base[2];
+  int64_t bs[2], ps[2];
+  int npos[2];
+  const int64_t* probe;      // probe token ids [rows, probe_bs]
+  int64_t probe_bs;
+  int probe_npos[2];         // positions < probe_npos[s] have a probe
+  int nrows;
+};
+
+__device__ __forceinline__ void vec_locate(const VecSet& vs, int v, int* set, int* row, int* pos) {
+  const int per = vs.npos[0] + vs.npos[1];
+  const int b = v / per, l = v - b * per;
+  *row = b;
+  if (l < vs.npos[0]) { *set = 0; *pos = l; } else { *set = 1; *pos = l - vs.npos[0]; }
+}
+
+__device__ __forceinline__ const void* vec_ptr(const VecSet& vs, int set, int row, int pos, int dtype) {
+  const int esz = dtype == SD_DTYPE_F32 ? 4 : 2;
+  const char* p = reinterpret_cast<const char*>(vs.base[set]);
+  return p + (row * vs.bs[set] + pos * vs.ps[set]) * esz;
+}
+
+__device__ __forceinline__ int64_t vec_probe(const VecSet& vs, int set, int row, int pos) {
+  if (vs.probe == nullptr || pos >= vs.probe_npos[set]) return -1;
+  return vs.probe[row * vs.probe_bs + pos];
+}
+
+// ---------------------------------------------------------------------------
+// histogram stats kernel (bf16 / fp16)
+// ---------------------------------------------------------------------------
+struct HistSmem {
+  uint32_t hist[HIST_WORDS];           // 128 KB
+  uint16_t list[NGROUP];               // populated key groups, descending key order
+  uint32_t segc[HT];                   // count per 128-key segment (segment t)
+  uint16_t occ[HT];                    // populated-group mask per segment
+  uint32_t corr_raw[NCORR_MAX];
+  int32_t corr_add[NCORR_MAX];
+  double dred[40];
+  uint32_t ured[40];
+  int ncorr;
+  int corr_full;
+  uint32_t keyk16;     // top-k threshold key (16-bit), 0 if inactive
+  uint32_t vstar16;    // boundary key (16-bit) or 0xFFFFFFFF if none
+  int n_keep;
+  int vcount;          // count of the boundary class
+  double z;            // kept mass
+  int32_t idx_cut;
+  int found_cut;
+};
+
+__device__ __forceinline__ uint32_t hist_field(const HistSmem& s, uint32_t raw) {
+  return (s.hist[raw >> 1] >> ((raw & 1u) << 4)) & 0xFFFFu;
+}
+
+__device__ __forceinline__ uint32_t hist_count(const HistSmem& s, uint32_t raw) {
+  uint32_t c = hist_field(s, raw);
+  const int n = s.ncorr;
+  for (int i = 0; i < n; ++i)
+    if (s.corr_raw[i] == raw) c += s.corr_add[i];
+  return c;
+}
+
+__device__ __forceinline__ void corr_log(HistSmem& s, uint32_t raw, int add) {
+  int i = atomicAdd(&s.ncorr, 1);
+  if (i < NCORR_MAX) { s.corr_raw[i] = raw; s.corr_add[i] = add; }
+  else s.corr_full = 1;
+}
+
+template <bool CHECKED>
+__device__ __forceinline__ void hist_add(HistSmem& s, uint32_t raw) {
+  const uint32_t inc = 1u << ((raw & 1u) << 4);
+  if (!CHECKED) {
+    atomicAdd(&s.hist[raw >> 1], inc);
+  } else {
+    const uint32_t old = atomicAdd(&s.hist[raw >> 1], inc);
+    if ((raw & 1u) == 0u) {
+      if ((old & 0xFFFFu) == 0xFFFFu) {        // low counter wrapped, carried into high
+        corr_log(s, raw, 65536);
+        corr_log(s, raw + 1, -1);
+        if ((old >> 16) == 0xFFFFu) corr_log(s, raw + 1, 65536);
+      }
+    } else if ((old >> 16) == 0xFFFFu) {      // high counter wrapped out of the word
+      corr_log(s, raw, 65536);
+    }
+  }
+}
+
+template <bool CHECKED>
+__device__ void hist_build(HistSmem& s, const uint16_t* p, int V) {
+  const int t = threadIdx.x;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  int head = (int)(((16u - (uint32_t)(a & 15u)) & 15u) >> 1);
+  if (head > V) head = V;
+  const int nb = (V - head) >> 3;
+  const int tail0 = head + (nb << 3);
+  const uint4* body = reinterpret_cast<const uint4*>(p + head);
+  constexpr int U = 8;
+  int u = t;
+  for (; u + (U - 1) * HT < nb; u += U * HT) {
+    uint4 w[U];
+#pragma unroll
+    for (int i = 0; i < U; ++i) w[i] = __ldg(body + u + i * HT);
+#pragma unroll
+    for (int i = 0; i < U; ++i) {
+      hist_add<CHECKED>(s, w[i].x & 0xFFFFu); hist_add<CHECKED>(s, w[i].x >> 16);
+      hist_add<CHECKED>(s, w[i].y & 0xFFFFu); hist_add<CHECKED>(s, w[i].y >> 16);
+      hist_add<CHECKED>(s, w[i].z & 0xFFFFu); hist_add<CHECKED>(s, w[i].z >> 16);
+      hist_add<CHECKED>(s, w[i].w & 0xFFFFu); hist_add<CHECKED>(s, w[i].w >> 16);
+    }
+  }
+  for (; u < nb; u += HT) {
+    const uint4 w = __ldg(body + u);
+    hist_add<CHECKED>(s, w.x & 0xFFFFu); hist_add<CHECKED>(s, w.x >> 16);
+    hist_add<CHECKED>(s, w.y & 0xFFFFu); hist_add<CHECKED>(s, w.y >> 16);
+    hist_add<CHECKED>(s, w.z & 0xFFFFu); hist_add<CHECKED>(s, w.z >> 16);
+    hist_add<CHECKED>(s, w.w & 0xFFFFu); hist_add<CHECKED>(s, w.w >> 16);
+  }
+  // ragged head / tail elements
+  const int nrag = head + (V - tail0);
+  for (int i = t; i < nrag; i += HT) {
+    const int j = i < head ? i : tail0 + (i - head);
+    hist_add<CHECKED>(s, __ldg(reinterpret_cast<const unsigned short*>(p) + j));
+  }
+}
+
+__device__ void hist_clear(HistSmem& s) {
+  uint4* h = reinterpret_cast<uint4*>(s.hist);
+  for (int i = threadIdx.x; i < HIST_WORDS / 4; i += HT) h[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) { s.ncorr = 0; s.corr_full = 0; }
+}
+
+// Pass A: thread t owns segment t = key groups [16t, 16t+16) = keys [128t, 128t+128).
+// Returns the total count (fields only) and writes segc / occ; block-reduces max key.
+__device__ void hist_pass_a(HistSmem& s, uint32_t* total_out, uint32_t* maxkey_out) {
+  const int t = threadIdx.x;
+  uint32_t cnt = 0, occ = 0, kmax = 0;
+  bool any = false;
+#pragma unroll 4
+  for (int jj = 0; jj < 16; ++jj) {
+    const int j = (jj + t) & 15;                 // bank-conflict-free order
+    const uint32_t G = 16u * t + j;
+    uint32_t wo;
+    const bool pos = G >= 4096u;
+    wo = pos ? 4u * (G - 4096u) : 0x7FFCu - 4u * G;
+    const uint4 w = *reinterpret_cast<const uint4*>(&s.hist[wo]);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    uint32_t gsum = 0;
+    int hi_idx = -1, lo_idx = 8;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t f0 = ws[q] & 0xFFFFu, f1 = ws[q] >> 16;
+      gsum += f0 + f1;
+      if (f0) { hi_idx = max(hi_idx, 2 * q); lo_idx = min(lo_idx, 2 * q); }
+      if (f1) { hi_idx = max(hi_idx, 2 * q + 1); lo_idx = min(lo_idx, 2 * q + 1); }
+    }
+    cnt += gsum;
+    if (gsum) {
+      occ |= 1u << j;
+      // highest key of the group: positive -> highest raw; negative -> lowest raw
+      const uint32_t raw = 2u * wo + (pos ? (uint32_t)hi_idx : (uint32_t)lo_idx);
+      const uint32_t key = key16(raw);
+      kmax = any ? max(kmax, key) : key;
+      any = true;
+    }
+  }
+  s.segc[t] = cnt;
+  s.occ[t] = (uint16_t)occ;
+  const uint32_t tot = block_sum<uint32_t>(cnt, s.ured);
+  const uint32_t km = block_max<uint32_t>(any ? kmax : 0u, s.ured, 0u);
+  *total_out = tot;
+  *maxkey_out = km;
+}
+
+struct HistParams {
+  VecSet vs;
+  int dtype, V, nvec;
+  float T, top_p;
+  int top_k;
+  VecStats* stats;
+};
+
+__global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  HistSmem& s = *reinterpret_cast<HistSmem*>(smem_raw);
+  const int t = threadIdx.x;
+  const int V = P.V;
+  const bool topk_on = P.top_k > 0 && P.top_k < V;
+  const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
+  const float tp32 = P.top_p;
+
+  hist_clear(s);
+  __syncthreads();
+
+  for (int v = blockIdx.x; v < P.nvec; v += gridDim.x) {
+    int set, row, pos;
+    vec_locate(P.vs, v, &set, &row, &pos);
+    const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
+    const int64_t probe = vec_probe(P.vs, set, row, pos);
+
+    hist_build<false>(s, x, V);
+    __syncthreads();
+    uint32_t total, maxkey;
+    // -0 joins +0 (one tie class per value)
+    if (t == 0) {
+      const uint32_t fneg0 = hist_field(s, 0x8000u);
+      if (fneg0) { s.hist[0x4000] &= 0xFFFF0000u; corr_log(s, 0u, (int)fneg0); }
+    }
+    __syncthreads();
+    hist_pass_a(s, &total, &maxkey);
+    int flags = 0;
+    {
+      uint32_t csum = 0;
+      for (int i = 0; i < s.ncorr && i < NCORR_MAX; ++i) csum += (uint32_t)s.corr_add[i];
+      if (total + csum != (uint32_t)V) {
+        // a 16-bit counter wrapped: rebuild with wrap logging (rare: >65535 equal values)
+        __syncthreads();
+        hist_clear(s);
+        __syncthreads();
+        hist_build<true>(s, x, V);
+        __syncthreads();
+        if (t == 0) {
+          const uint32_t fneg0 = hist_field(s, 0x8000u);
+          if (fneg0) { s.hist[0x4000] &= 0xFFFF0000u; corr_log(s, 0u, (int)fneg0); }
+        }
+        __syncthreads();
+        hist_pass_a(s, &total, &maxkey);
+        flags |= 1;
+      }
+    }
+    __syncthreads();
+    // fold corrections into segment counts / occupancy (all lanes see the same ncorr)
+    if (t == 0) {
+      const int n = min(s.ncorr, NCORR_MAX);
+      for (int i = 0; i < n; ++i) {
+        const uint32_t key = key16(s.corr_raw[i]);
+        const uint32_t G = key >> 3;
+        s.segc[G >> 4] += (uint32_t)s.corr_add[i];
+        s.occ[G >> 4] |= (uint16_t)(1u << (G & 15u));
+        if (s.corr_add[i] > 0 && key > maxkey) maxkey = key;
+      }
+      s.ured[34] = maxkey;
+      if (s.corr_full) flags |= 2;
+    }
+    __syncthreads();
+    maxkey = s.ured[34];
+    const float m = scaled_logit(bits16_to_float(raw16(maxkey), P.dtype), P.T);
+
+    // list of populated groups in descending key order: thread t handles segment 511-t
+    {
+      const int seg = HT - 1 - t;
+      const uint32_t o = s.occ[seg];
+      uint32_t tot;
+      uint32_t off = block_excl_scan<uint32_t>(__popc(o), s.ured, &tot);
+      for (int j = 15; j >= 0; --j)
+        if (o & (1u << j)) s.list[off++] = (uint16_t)(16 * seg + j);
+      __syncthreads();
+      if (t == 0) s.ured[35] = tot;
+      __syncthreads();
+    }
+    const int nlist = (int)s.ured[35];
+    const int per = (nlist + HT - 1) / HT;
+    const int l0 = min(nlist, t * per), l1 = min(nlist, l0 + per);
+
+    // top-k threshold (by counts, descending keys)
+    uint32_t keyk = 0;
+    if (topk_on) {
+      uint32_t c = 0;
+      for (int l = l0; l < l1; ++l) {
+        const uint32_t G = s.list[l];
+        for (int q = 7; q >= 0; --q) c += hist_count(s, raw16(8 * G + q));
+      }
+      uint32_t tot;
+      const uint32_t pre = block_excl_scan<uint32_t>(c, s.ured, &tot);
+      if (t == 0) s.keyk16 = 0;
+      __syncthreads();
+      if (pre < (uint32_t)P.top_k && pre + c >= (uint32_t)P.top_k) {
+        uint32_t run = pre;
+        for (int l = l0; l < l1 && run < (uint32_t)P.top_k; ++l) {
+          const uint32_t G = s.list[l];
+          for (int q = 7; q >= 0; --q) {
+            const uint32_t key = 8 * G + q;
+            run += hist_count(s, raw16(key));
+            if (run >= (uint32_t)P.top_k) { s.keyk16 = key; break; }
+          }
+        }
+      }
+      __syncthreads();
+      keyk = s.keyk16;
+    }
+
+    // softmax normaliser S over every element
+    double es = 0.0;
+    for (int l = l0; l < l1; ++l) {
+      const uint32_t G = s.list[l];
+      for (int q = 7; q >= 0; --q) {
+        const uint32_t raw = raw16(8 * G + q);
+        const uint32_t c = hist_count(s, raw);
+        if (c) es += (double)c * (double)softmax_num(bits16_to_float(raw, P.dtype), P.T, m);
+      }
+    }
+    const double S = block_sum<double>(es, s.dred);
+    const float inv_s = __double2float_rn(1.0 / S);
+
+    // kept mass (keys >= keyk) per thread, in p units
+    double pm = 0.0;
+    for (int l = l0; l < l1; ++l) {
+      const uint32_t G = s.list[l];
+      for (int q = 7; q >= 0; --q) {
+        const uint32_t key = 8 * G + q;
+        if (key < keyk) continue;
+        const uint32_t raw = raw16(key);
+        const uint32_t c = hist_count(s, raw);
+        if (c) pm += (double)c * (double)prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
+      }
+    }
+    double z;
+    if (!topp_on) {
+      z = block_sum<double>(pm, s.dred);
+      if (t == 0) { s.vstar16 = 0xFFFFFFFFu; s.n_keep = 0; }
+    } else {
+      double ptot;
+      const double pre = block_excl_scan<double>(pm, s.dred, &ptot);
+      if (t == 0) { s.vstar16 = 0xFFFFFFFFu; s.ured[36] = 0; }
+      __syncthreads();
+      // walk: every thread whose range may hold the first class whose last member
+      // is dropped reports that class; the highest such key is the boundary.
+      if (l0 < l1 && pre + pm >= (double)tp32 - 1e-9) {
+        double C = pre;
+        bool done = false;
+        for (int l = l0; l < l1 && !done; ++l) {
+          const uint32_t G = s.list[l];
+          for (int q = 7; q >= 0; --q) {
+            const uint32_t key = 8 * G + q;
+            if (key < keyk) { done = true; break; }
+            const uint32_t raw = raw16(key);
+            const uint32_t c = hist_count(s, raw);
+            if (!c) continue;
+            const float p = prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
+            const float cl = __fsub_rn(__double2float_rn(C + (double)c * (double)p), p);
+            if (!(cl < tp32)) { atomicMax(&s.ured[36], key + 1u); done = true; break; }
+            C += (double)c * (double)p;
+          }
+        }
+      }
+      __syncthreads();
+      const uint32_t vk1 = s.ured[36];
+      // owner of the boundary class computes how many of its members are kept
+      if (vk1 != 0u && l0 < l1) {
+        const uint32_t vkey = vk1 - 1u;
+        const uint32_t Gv = vkey >> 3;
+        bool mine = false;
+        for (int l = l0; l < l1; ++l) mine |= (s.list[l] == Gv);
+        if (mine) {
+          double C = pre;
+          for (int l = l0; l < l1; ++l) {
+            const uint32_t G = s.list[l];
+            for (int q = 7; q >= 0; --q) {
+              const uint32_t key = 8 * G + q;
+              const uint32_t raw = raw16(key);
+              const uint32_t c = key >= keyk ? hist_count(s, raw) : 0u;
+              if (!c) continue;
+              const float p = prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
+              if (key == vkey) {
+                // largest n in [0, c] with keep(j) for all j < n (keep is monotone)
+                int lo = 0, hi = (int)c;   // keep(lo-1) true, answer in [lo, hi]
+                while (lo < hi) {
+                  const int mid = (lo + hi) >> 1;   // test keep(mid)
+                  const float cl = __fsub_rn(
+                      __double2float_rn(C + (double)(mid + 1) * (double)p), p);
+                  if (cl < tp32) lo = mid + 1; else hi = mid;
+                }
+                int nk = lo;
+                if (nk == 0 && key == maxkey) nk = 1;   // the first sorted entry is always kept
+                s.vstar16 = vkey;
+                s.n_keep = nk;
+                s.vcount = (int)c;
+                s.z = C + (double)nk * (double)p;
+              }
+              C += (double)c * (double)p;
+            }
+          }
+        }
+      }
+      __syncthreads();
+      z = (s.vstar16 == 0xFFFFFFFFu) ? ptot : s.z;
+    }
+    __syncthreads();
+    const uint32_t vstar16 = s.vstar16;
+    const float zf = fmaxf(__double2float_rn(z), 1e-12f);
+
+    // idx_cut: index of the n_keep-th member (ascending index) of the boundary class
+    int32_t idx_cut = (int32_t)NO_CUT;
+    if (vstar16 != 0xFFFFFFFFu) {
+      const int nk = s.n_keep;
+      if (nk == 0) idx_cut = -1;
+      else if (nk < s.vcount) {
+        const uint32_t r0 = raw16(vstar16);
+        const bool zero_cls = (r0 == 0u);
+        const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
+        if (t == 0) s.found_cut = 0;
+        __syncthreads();
+        uint32_t run = 0;
+        constexpr int PT = 32;                     // elements per thread per tile
+        for (int base = 0; base < V; base += HT * PT) {
+          const int j0 = base + t * PT;
+          uint32_t c = 0;
+          for (int e = 0; e < PT; ++e) {
+            const int j = j0 + e;
+            if (j < V) {
+              const uint32_t r = __ldg(xs + j);
+              c += (r == r0) || (zero_cls && r == 0x8000u);
+            }
+          }
+          uint32_t tot;
+          const uint32_t pre = block_excl_scan<uint32_t>(c, s.ured, &tot);
+          if (run + pre < (uint32_t)nk && run + pre + c >= (uint32_t)nk) {
+            uint32_t rr = run + pre;
+            for (int e = 0; e < PT; ++e) {
+              const int j = j0 + e;
+              if (j < V) {
+                const uint32_t r = __ldg(xs + j);
+                if ((r == r0) || (zero_cls && r == 0x8000u)) {
+                  if (++rr == (uint32_t)nk) { s.idx_cut = j; s.found_cut = 1; break; }
+                }
+              }
+            }
+          }
+          run += tot;
+          __syncthreads();
+          if (s.found_cut) break;
+        }
+        idx_cut = s.idx_cut;
+      }
+    }
+
+    if (t == 0) {
+      VecStats st;
+      st.m = m;
+      st.inv_s = inv_s;
+      st.zf = zf;
+      st.kth = topk_on ? fkey(bits16_to_float(raw16(keyk), P.dtype)) : 0u;
+      st.vstar = vstar16 == 0xFFFFFFFFu ? 0u : fkey(bits16_to_float(raw16(vstar16), P.dtype));
+      st.idx_cut = vstar16 == 0xFFFFFFFFu ? (int32_t)NO_CUT : idx_cut;
+      st.argmax = -1;
+      st.flags = flags;
+      st.n_keep = vstar16 == 0xFFFFFFFFu ? -1 : s.n_keep;
+      st.pad[0] = st.pad[1] = 0;
+      float pp = 0.f;
+      if (probe >= 0 && probe < V) {
+        const float xv = bits16_to_float(__ldg(reinterpret_cast<const unsigned short*>(x) + probe), P.dtype);
+        const uint32_t kx = fkey(xv);
+        const bool kept = kx >= st.kth &&
+                          (kx > st.vstar || (kx == st.vstar && probe <= (int64_t)st.idx_cut));
+        if (kept) pp = __fdiv_rn(prob_of(xv, P.T, m, inv_s), zf);
+      }
+      st.probe_p = pp;
+      P.stats[v] = st;
+    }
+    __syncthreads();
+    hist_clear(s);
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// small-vocabulary exact kernel: materialises the final probabilities
+// ---------------------------------------------------------------------------
+struct SmallParams {
+  VecSet vs;
+  int dtype, V, nvec;
+  float T, top_p;
+  int top_k;
+  VecStats* stats;
+  float* mat;          // [nvec, V]
+};
+
+__global__ void __launch_bounds__(ST) small_stats_kernel(SmallParams P) {
+  __shared__ float pv[SMALLV_MAX];
+  __shared__ unsigned long long sk[SMALLV_MAX];
+  __shared__ double dred[40];
+  __shared__ float fred[40];
+  const int v = blockIdx.x, t = threadIdx.x, V = P.V;
+  int set, row, pos;
+  vec_locate(P.vs, v, &set, &row, &pos);
+  const void* x = vec_ptr(P.vs, set, row, pos, P.dtype);
+  const int64_t probe = vec_probe(P.vs, set, row, pos);
+  float* out = P.mat + (int64_t)v * V;
+
+  float lmax = -INFINITY;
+  for (int j = t; j < V; j += ST) {
+    const float d = scaled_logit(load_logit(x, P.dtype, j), P.T);
+    pv[j] = d;
+    lmax = fmaxf(lmax, d);
+  }
+  const float m = block_max<float>(lmax, fred, -INFINITY);
+  double es = 0.0;
+  for (int j = t; j < V; j += ST) {
+    const float e = expf(__fsub_rn(pv[j], m));
+    pv[j] = e;
+    es += (double)e;
+  }
+  const double S = block_sum<double>(es, dred);
+  const float inv_s = __double2float_rn(1.0 / S);
+  int N = 1;
+  while (N < V) N <<= 1;
+  for (int j = t; j < N; j += ST) {
+    if (j < V) {
+      const float p = __fmul_rn(pv[j], inv_s);
+      pv[j] = p;
+      sk[j] = ((unsigned long long)fkey(p) << 32) | (0xFFFFFFFFu - (uint32_t)j);
+    } else {
+      sk[j] = 0ull;
+    }
+  }
+  __syncthreads();
+  const bool topk_on = P.top_k > 0 && P.top_k < V;
+  const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
+  if (topk_on || topp_on) {
+    // bitonic sort, descending
+    for (int k2 = 2; k2 <= N; k2 <<= 1) {
+      for (int j2 = k2 >> 1; j2 > 0; j2 >>= 1) {
+        for (int i = t; i < N; i += ST) {
+          const int ixj = i ^ j2;
+          if (ixj > i) {
+            const unsigned long long a = sk[i], b = sk[ixj];
+            const bool desc = (i & k2) == 0;
+            if (desc ? (a < b) : (a > b)) { sk[i] = b; sk[ixj] = a; }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    // sorted entries: p = pv[idx]; top-k: keep p >= p of entry top_k-1
+    float kth = 0.f;
+    if (topk_on) kth = pv[0xFFFFFFFFu - (uint32_t)(sk[P.top_k - 1] & 0xFFFFFFFFu)];
+    __syncthreads();
+    if (topk_on) {
+      for (int j = t; j < V; j += ST)
+        if (pv[j] < kth) pv[j] = 0.f;
+      __syncthreads();
+    }
+    if (topp_on) {
+      // float64 running sum in sorted order, processed in tiles of ST
+      const float tp32 = P.top_p;
+      double carry = 0.0;
+      for (int base = 0; base < V; base += ST) {
+        const int i = base + t;
+        uint32_t idx = 0;
+        float p = 0.f;
+        if (i < V) { idx = 0xFFFFFFFFu - (uint32_t)(sk[i] & 0xFFFFFFFFu); p = pv[idx]; }
+        double tot;
+        const double pre = block_excl_scan<double>((double)p, dred, &tot);
+        bool keep = true;
+        if (i < V) {
+          const float cum = __double2float_rn(carry + pre + (double)p);
+          keep = __fsub_rn(cum, p) < tp32 || i == 0;
+        }
+        __syncthreads();
+        if (i < V && !keep) pv[idx] = -pv[idx] - 1.0f;   // mark dropped, keep value
+        carry += tot;
+        __syncthreads();
+      }
+      for (int j = t; j < V; j += ST)
+        if (pv[j] < 0.f) pv[j] = 0.f;
+      __syncthreads();
+    }
+  }
+  double zs = 0.0;
+  for (int j = t; j < V; j += ST) zs += (double)pv[j];
+  const double Z = block_sum<double>(zs, dred);
+  const float zf = fmaxf(__double2float_rn(Z), 1e-12f);
+  for (int j = t; j < V; j += ST) out[j] = __fdiv_rn(pv[j], zf);
+  __syncthreads();
+  if (t == 0) {
+    VecStats st;
+    st.m = m; st.inv_s = inv_s; st.zf = zf;
+    st.kth = 0; st.vstar = 0; st.idx_cut = (int32_t)NO_CUT; st.argmax = -1;
+    st.flags = 0; st.n_keep = -1; st.pad[0] = st.pad[1] = 0;
+    st.probe_p = (probe >= 0 && probe < V) ? out[probe] : 0.f;
+    P.stats[v] = st;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// greedy: argmax per target vector, then the accept / emit decision per row
+// ---------------------------------------------------------------------------
+struct ArgmaxParams {
+  VecSet vs;           // set 0 only
+  int dtype, V, nvec, nch, chunk;
+  unsigned long long* partial;   // [nvec, nch]
+  int* vec_counter;              // [nvec]
+  int* row_counter;              // [rows]
+  VecStats* stats;
+  // row decision (verify mode: k >= 1; draft mode: k == 0)
+  int k;
+  const int64_t* xs; int64_t xs_bs;
+  const float* u_acc; int64_t u_bs;
+  const uint8_t* alive;
+  int64_t* n_acc; int64_t* y; float* px; float* qx;
+};
+
+__global__ void __launch_bounds__(FT) argmax_kernel(ArgmaxParams P) {
+  __shared__ unsigned long long ured[40];
+  __shared__ int last;
+  const int c = blockIdx.x % P.nch, v = blockIdx.x / P.nch, t = threadIdx.x;
+  int set, row, pos;
+  vec_locate(P.vs, v, &set, &row, &pos);
+  const void* x = vec_ptr(P.vs, set, row, pos, P.dtype);
+  const int j0 = c * P.chunk, j1 = min(P.V, j0 + P.chunk);
+  unsigned long long best = 0ull;
+  for (int j = j0 + t; j < j1; j += FT) {
+    const unsigned long long key = ((unsigned long long)fkey(load_logit(x, P.dtype, j)) << 32) |
+                                   (0xFFFFFFFFu - (uint32_t)j);
+    best = key > best ? key : best;
+  }
+  best = block_max<unsigned long long>(best, ured, 0ull);
+  if (t == 0) {
+    P.partial[(int64_t)v * P.nch + c] = best;
+    __threadfence();
+    last = atomicAdd(&P.vec_counter[v], 1) == P.nch - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (t == 0) {
+    unsigned long long b = 0ull;
+    for (int i = 0; i < P.nch; ++i) {
+      const unsigned long long w = *((volatile unsigned long long*)&P.partial[(int64_t)v * P.nch + i]);
+      b = w > b ? w : b;
+    }
+    const int am = (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFu));
+    P.vec_counter[v] = 0;
+    VecStats st;
+    st.m = 0.f; st.inv_s = 1.f; st.zf = 1.f; st.probe_p = 0.f;
+    st.kth = 0; st.vstar = 0; st.idx_cut = (int32_t)NO_CUT; st.argmax = am;
+    st.flags = 0; st.n_keep = -1; st.pad[0] = st.pad[1] = 0;
+    P.stats[v] = st;
+    __threadfence();
+    const int per = P.vs.npos[0];
+    if (P.k >= 0 && atomicAdd(&P.row_counter[row], 1) == per - 1) {
+      __threadfence();
+      P.row_counter[row] = 0;
+      const volatile VecStats* vst = P.stats + (int64_t)row * per;
+      if (P.k == 0) {
+        P.y[row] = vst[0].argmax;
+        if (P.qx) P.qx[row] = 1.0f;
+      } else {
+        // p_i(x_i) is 1 iff x_i is the target argmax; the ratio is then >= 1
+        // whatever q is, so the test is u < 1 (engine.py:290-292 with one-hot p).
+        int n = 0;
+        bool alive = P.alive ? P.alive[row] != 0 : true;
+        for (int i = 0; i < P.k; ++i) {
+          const int64_t xi = P.xs[row * P.xs_bs + i];
+          const float pxi = (xi == (int64_t)vst[i].argmax) ? 1.f : 0.f;
+          if (P.px) P.px[row * P.k + i] = pxi;
+          if (P.qx) P.qx[row * P.k + i] = nanf("");
+          const float thr = pxi > 0.f ? 1.f : 0.f;
+          if (alive && n == i && P.u_acc[row * P.u_bs + i] < thr) ++n; else alive = false;
+        }
+        P.n_acc[row] = n;
+        P.y[row] = vst[n].argmax;     // residual and bonus are both one-hot at argmax p_n
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// finish: accept decision, residual / bonus mass per chunk, inverse-CDF draw
+// ---------------------------------------------------------------------------
+struct FinishParams {
+  VecSet vs;           // set 0: target [rows, k+1]; set 1: draft [rows, k]
+  int dtype, V, k, nch, chunk;
+  float T;
+  const VecStats* stats;
+  const float* mat;    // materialised probabilities [nvec, V] or nullptr
+  const float* u_acc; int64_t u_bs;
+  const float* u_res;
+  const uint8_t* alive;
+  int64_t* n_acc; int64_t* y; float* px; float* qx; float* y_prob;
+  double* partial;     // [rows, nch, 2]
+  int* counter;        // [rows]
+};
+
+struct SelVec {
+  const void* x;       // logits (hist mode)
+  const float* mat;    // materialised probabilities (small mode)
+  VecStats st;
+};
+
+__device__ __forceinline__ float final_prob(const SelVec& s, int dtype, float T, int j) {
+  if (s.mat) return s.mat[j];
+  const float xv = load_logit(s.x, dtype, j);
+  const uint32_t kx = fkey(xv);
+  const bool kept = kx >= s.st.kth &&
+                    (kx > s.st.vstar || (kx == s.st.vstar && j <= s.st.idx_cut));
+  if (!kept) return 0.f;
+  return __fdiv_rn(prob_of(xv, T, s.st.m, s.st.inv_s), s.st.zf);
+}
+
+// mass of element j of the distribution the row draws from
+__device__ __forceinline__ float draw_mass(const SelVec& p, const SelVec& q, bool resid, bool use_p,
+                                           int dtype, float T, int j) {
+  const float pj = final_prob(p, dtype, T, j);
+  if (!resid || use_p || pj == 0.f) return pj;
+  const float qj = final_prob(q, dtype, T, j);
+  return fmaxf(__fsub_rn(pj, qj), 0.f);
+}
+
+__global__ void __launch_bounds__(FT) finish_kernel(FinishParams P) {
+  __shared__ double dred[40];
+  __shared__ int s_n, s_last;
+  __shared__ int64_t s_y;
+  const int c = blockIdx.x % P.nch, b = blockIdx.x / P.nch, t = threadIdx.x;
+  const int npos = P.vs.npos[0] + P.vs.npos[1];
+  const int vrow = b * npos;
+  if (t == 0) {
+    int n = 0;
+    bool alive = P.alive ? P.alive[b] != 0 : true;
+    for (int i = 0; i < P.k; ++i) {
+      const float pxi = P.stats[vrow + i].probe_p;
+      const float qxi = P.stats[vrow + P.vs.npos[0] + i].probe_p;
+      const float thr = fminf(__fdiv_rn(pxi, fmaxf(qxi, 1e-10f)), 1.0f);
+      if (c == 0) {
+        if (P.px) P.px[b * P.k + i] = pxi;
+        if (P.qx) P.qx[b * P.k + i] = qxi;
+      }
+      if (alive && n == i && P.u_acc[b * P.u_bs + i] < thr) ++n; else alive = false;
+    }
+    s_n = n;
+  }
+  __syncthreads();
+  const int n = s_n;
+  const bool resid = n < P.k;
+  const int ppos = resid ? n : P.k;            // pick = min(n, k-1) when resid
+  SelVec ps, qs;
+  ps.st = P.stats[vrow + ppos];
+  ps.x = vec_ptr(P.vs, 0, b, ppos, P.dtype);
+  ps.mat = P.mat ? P.mat + (int64_t)(vrow + ppos) * P.V : nullptr;
+  if (resid) {
+    qs.st = P.stats[vrow + P.vs.npos[0] + n];
+    qs.x = vec_ptr(P.vs, 1, b, n, P.dtype);
+    qs.mat = P.mat ? P.mat + (int64_t)(vrow + P.vs.npos[0] + n) * P.V : nullptr;
+  } else {
+    qs = ps;
+  }
+  const int j0 = c * P.chunk, j1 = min(P.V, j0 + P.chunk);
+  double sr = 0.0, sp = 0.0;
+  for (int j = j0 + t; j < j1; j += FT) {
+    const float pj = final_prob(ps, P.dtype, P.T, j);
+    sp += (double)pj;
+    if (resid && pj != 0.f) sr += (double)fmaxf(__fsub_rn(pj, final_prob(qs, P.dtype, P.T, j)), 0.f);
+  }
+  sr = block_sum<double>(sr, dred);
+  sp = block_sum<double>(sp, dred);
+  if (t == 0) {
+    double* part = P.partial + ((int64_t)b * P.nch + c) * 2;
+    part[0] = sr;
+    part[1] = sp;
+    __threadfence();
+    s_last = atomicAdd(&P.counter[b], 1) == P.nch - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // ---- last CTA of the row: totals in chunk order, locate the chunk, scan it
+  __shared__ double s_pre, s_tot;
+  __shared__ int s_cstar, s_usep;
+  if (t == 0) {
+    const volatile double* part = P.partial + (int64_t)b * P.nch * 2;
+    double R = 0.0, Pm = 0.0;
+    for (int i = 0; i < P.nch; ++i) { R += part[2 * i]; Pm += part[2 * i + 1]; }
+    const bool use_p = !resid || (__double2float_rn(R) <= 1e-9f);   // sampling.py:86-89
+    const double tot = use_p ? Pm : R;
+    const double target = (double)P.u_res[b] * tot;
+    double pre = 0.0, prelast = 0.0;
+    int cstar = -1, lastnz = 0;
+    for (int i = 0; i < P.nch; ++i) {
+      const double w = use_p ? part[2 * i + 1] : part[2 * i];
+      if (w > 0.0) { lastnz = i; prelast = pre; }
+      if (cstar < 0 && pre + w > target) { cstar = i; s_pre = pre; }
+      pre += w;
+    }
+    if (cstar < 0) { cstar = lastnz; s_pre = prelast; }
+    s_cstar = cstar;
+    s_usep = use_p;
+    s_tot = tot;
+    P.counter[b] = 0;
+  }
+  __syncthreads();
+  const bool use_p = s_usep;
+  const double tgt = (double)P.u_res[b] * s_tot;
+  const int cs = s_cstar;
+  const int k0 = cs * P.chunk, k1 = min(P.V, k0 + P.chunk);
+  const int len = k1 - k0;
+  const int sub = (len + FT - 1) / FT;
+  const int a0 = k0 + min(len, t * sub), a1 = k0 + min(len, (t + 1) * sub);
+  double ls = 0.0;
+  for (int j = a0; j < a1; ++j) ls += (double)draw_mass(ps, qs, resid, use_p, P.dtype, P.T, j);
+  double ctot;
+  const double pre = s_pre + block_excl_scan<double>(ls, dred, &ctot);
+  if (t == 0) s_y = -1;
+  __syncthreads();
+  if (a0 < a1 && pre <= tgt && pre + ls > tgt) {
+    double run = pre;
+    for (int j = a0; j < a1; ++j) {
+      run += (double)draw_mass(ps, qs, resid, use_p, P.dtype, P.T, j);
+      if (run > tgt) { s_y = j; break; }
+    }
+  }
+  __syncthreads();
+  if (t == 0 && s_y < 0) {
+    // rounding put the crossing past this chunk: last element with mass
+    for (int j = k1 - 1; j >= k0; --j)
+      if (draw_mass(ps, qs, resid, use_p, P.dtype, P.T, j) > 0.f) { s_y = j; break; }
+    if (s_y < 0) s_y = k0;
+  }
+  __syncthreads();
+  if (t == 0) {
+    if (P.n_acc) P.n_acc[b] = n;
+    P.y[b] = s_y;
+    if (P.y_prob) P.y_prob[b] = final_prob(ps, P.dtype, P.T, (int)s_y);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// probs writer (to_probs API)
+// ---------------------------------------------------------------------------
+struct ProbsParams {
+  VecSet vs;
+  int dtype, V, nch, chunk, greedy;
+  float T;
+  const VecStats* stats;
+  const float* mat;
+  float* out; int64_t out_stride;
+};
+
+__global__ void __launch_bounds__(FT) probs_kernel(ProbsParams P) {
+  const int c = blockIdx.x % P.nch, v = blockIdx.x / P.nch, t = threadIdx.x;
+  int set, row, pos;
+  vec_locate(P.vs, v, &set, &row, &pos);
+  SelVec s;
+  s.st = P.stats[v];
+  s.x = vec_ptr(P.vs, set, row, pos, P.dtype);
+  s.mat = P.mat ? P.mat + (int64_t)v * P.V : nullptr;
+  float* o = P.out + (int64_t)v * P.out_stride;
+  const int j0 = c * P.chunk, j1 = min(P.V, j0 + P.chunk);
+  for (int j = j0 + t; j < j1; j += FT)
+    o[j] = P.greedy ? (j == s.st.argmax ? 1.f : 0.f) : final_prob(s, P.dtype, P.T, j);
+}
+
+// ---------------------------------------------------------------------------
+// fp32-probability utilities: residual_probs, sample_from_probs, gather_prob
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(FT) residual_kernel(const float* p, const float* q, int V, float* out) {
+  __shared__ double dred[40];
+  const int r = blockIdx.x, t = threadIdx.x;
+  const float* pr = p + (int64_t)r * V;
+  const float* qr = q + (int64_t)r * V;
+  float* o = out + (int64_t)r * V;
+  double s = 0.0, sp = 0.0;
+  for (int j = t; j < V; j += FT) {
+    s += (double)fmaxf(__fsub_rn(pr[j], qr[j]), 0.f);
+    sp += (double)pr[j];
+  }
+  s = block_sum<double>(s, dred);
+  sp = block_sum<double>(sp, dred);
+  const bool deg = __double2float_rn(s) <= 1e-9f;
+  const float tot = fmaxf(__double2float_rn(deg ? sp : s), 1e-12f);
+  for (int j = t; j < V; j += FT) {
+    const float rj = deg ? pr[j] : fmaxf(__fsub_rn(pr[j], qr[j]), 0.f);
+    o[j] = __fdiv_rn(rj, tot);
+  }
+}
+
+__global__ void __launch_bounds__(FT) sample_probs_kernel(const float* probs, int V, const float* u,
+                                                          int64_t* out) {
+  __shared__ double dred[40];
+  __shared__ int64_t s_y;
+  const int r = blockIdx.x, t = threadIdx.x;
+  const float* pr = probs + (int64_t)r * V;
+  const int sub = (V + FT - 1) / FT;
+  const int a0 = min(V, t * sub), a1 = min(V, (t + 1) * sub);
+  double ls = 0.0;
+  for (int j = a0; j < a1; ++j) ls += (double)pr[j];
+  double tot;
+  const double pre = block_excl_scan<double>(ls, dred, &tot);
+  const double tgt = (double)u[r] * tot;
+  if (t == 0) s_y = -1;
+  __syncthreads();
+  if (a0 < a1 && pre <= tgt && pre + ls > tgt) {
+    double run = pre;
+    for (int j = a0; j < a1; ++j) {
+      run += (double)pr[j];
+      if (run > tgt) { s_y = j; break; }
+    }
+  }
+  __syncthreads();
+  if (t == 0) {
+    if (s_y < 0) {
+      for (int j = V - 1; j >= 0; --j)
+        if (pr[j] > 0.f) { s_y = j; break; }
+      if (s_y < 0) s_y = V - 1;
+    }
+    out[r] = s_y;
+  }
+}
+
+__global__ void gather_kernel(const float* probs, int n, int V, const int64_t* ids, float* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const int64_t j = ids[i];
+    out[i] = (j >= 0 && j < V) ? probs[(int64_t)i * V + j] : nanf("");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static int g_num_sms[64];
+static bool g_attr_set[64];
+
+static int device_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!g_num_sms[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_num_sms[dev] = n > 0 ? n : 148;
+  }
+  if (!g_attr_set[dev]) {
+    cudaFuncSetAttribute(hist_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(HistSmem));
+    g_attr_set[dev] = true;
+  }
+  return g_num_sms[dev];
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct WsLayout {
+  size_t stats, partial, counter, vcounter, rcounter, apartial, mat, total;
+};
+
+static int nch_for(int V) {
+  int n = (V + 4095) / 4096;
+  return n < 1 ? 1 : (n > NCH_MAX ? NCH_MAX : n);
+}
+
+static WsLayout ws_layout(int n_rows, int n_vec, int V, bool small) {
+  WsLayout L;
+  size_t off = 0;
+  L.stats = off; off = align256(off + (size_t)n_vec * sizeof(VecStats));
+  L.partial = off; off = align256(off + (size_t)n_rows * NCH_MAX * 2 * sizeof(double));
+  L.counter = off; off = align256(off + (size_t)n_rows * sizeof(int));
+  L.vcounter = off; off = align256(off + (size_t)n_vec * sizeof(int));
+  L.rcounter = off; off = align256(off + (size_t)n_rows * sizeof(int));
+  L.apartial = off; off = align256(off + (size_t)n_vec * NCH_MAX * sizeof(unsigned long long));
+  L.mat = off; off = align256(off + (small ? (size_t)n_vec * V * sizeof(float) : 0));
+  L.total = off;
+  return L;
+}
+
+static bool use_small(int V, int dtype) { return V <= SMALLV_MAX || dtype == SD_DTYPE_F32; }
+
+static int check_launch() {
+  return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+}
+
+// Stats for every vector of `vs` (non-greedy).
+static int run_stats(const VecSet& vs, int nvec, int dtype, int V, float T, float top_p, int top_k,
+                     const WsLayout& L, char* ws, cudaStream_t st) {
+  VecStats* stats = reinterpret_cast<VecStats*>(ws + L.stats);
+  if (use_small(V, dtype)) {
+    if (V > SMALLV_MAX) return SD_ENOTSUP;
+    SmallParams P;
+    P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec; P.T = T; P.top_p = top_p;
+    P.top_k = top_k; P.stats = stats; P.mat = reinterpret_cast<float*>(ws + L.mat);
+    small_stats_kernel<<<nvec, ST, 0, st>>>(P);
+    return check_launch();
+  }
+  HistParams P;
+  P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec; P.T = T; P.top_p = top_p;
+  P.top_k = top_k; P.stats = stats;
+  const int nsm = device_sms();
+  const int grid = nvec < nsm ? nvec : nsm;
+  hist_stats_kernel<<<grid, HT, sizeof(HistSmem), st>>>(P);
+  return check_launch();
+}
+
+static int validate_common(int dtype, int V, float T) {
+  if (dtype != SD_DTYPE_F32 && dtype != SD_DTYPE_F16 && dtype != SD_DTYPE_BF16) return SD_EINVAL;
+  if (V <= 0 || V > (1 << 21)) return SD_EINVAL;
+  if (!(T == T)) return SD_EINVAL;
+  return SD_OK;
+}
+
+}  // namespace sd
+
+using namespace sd;
+
+extern "C" {
+
+int sd_version(void) { return 1; }
+
+size_t sd_sampling_workspace_bytes(int n_rows, int n_vec, int V, int dtype) {
+  return ws_layout(n_rows, n_vec, V, use_small(V, dtype)).total;
+}
+
+int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
+                     const void* drf, int64_t drf_bs, int64_t drf_ps, int dtype,
+                     const int64_t* xs, int64_t xs_bs, const float* u_acc, int64_t u_bs,
+                     const float* u_res, const uint8_t* alive,
+                     int B, int k, int V, float temperature, float top_p, int top_k,
+                     int64_t* n_acc, int64_t* y, float* px, float* qx,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = validate_common(dtype, V, temperature);
+  if (rc) return rc;
+  if (B <= 0 || k < 1 || k > 64 || !tgt || !xs || !u_acc || !u_res || !n_acc || !y || !workspace)
+    return SD_EINVAL;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool greedy = !(temperature > 0.0f);
+  char* ws = reinterpret_cast<char*>(workspace);
+  if (greedy) {
+    const int nvec = B * (k + 1);
+    WsLayout L = ws_layout(B, nvec, V, false);
+    if (workspace_bytes < L.total) return SD_ENOSPC;
+    VecSet vs = {};
+    vs.base[0] = tgt; vs.bs[0] = tgt_bs; vs.ps[0] = tgt_ps; vs.npos[0] = k + 1;
+    vs.npos[1] = 0; vs.nrows = B;
+    ArgmaxParams P;
+    P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec;
+    P.nch = nch_for(V); P.chunk = (V + P.nch - 1) / P.nch;
+    P.partial = reinterpret_cast<unsigned long long*>(ws + L.apartial);
+    P.vec_counter = reinterpret_cast<int*>(ws + L.vcounter);
+    P.row_counter = reinterpret_cast<int*>(ws + L.rcounter);
+    P.stats = reinterpret_cast<VecStats*>(ws + L.stats);
+    P.k = k; P.xs = xs; P.xs_bs = xs_bs; P.u_acc = u_acc; P.u_bs = u_bs; P.alive = alive;
+    P.n_acc = n_acc; P.y = y; P.px = px; P.qx = qx;
+    argmax_kernel<<<P.nch * nvec, FT, 0, st>>>(P);
+    return check_launch();
+  }
+  if (!drf) return SD_EINVAL;
+  const int nvec = B * (2 * k + 1);
+  const bool small = use_small(V, dtype);
+  WsLayout L = ws_layout(B, nvec, V, small);
+  if (workspace_bytes < L.total) return SD_ENOSPC;
+  VecSet vs = {};
+  vs.base[0] = tgt; vs.bs[0] = tgt_bs; vs.ps[0] = tgt_ps; vs.npos[0] = k + 1;
+  vs.base[1] = drf; vs.bs[1] = drf_bs; vs.ps[1] = drf_ps; vs.npos[1] = k;
+  vs.probe = xs; vs.probe_bs = xs_bs; vs.probe_npos[0] = k; vs.probe_npos[1] = k;
+  vs.nrows = B;
+  rc = run_stats(vs, nvec, dtype, V, temperature, top_p, top_k, L, ws, st);
+  if (rc) return rc;
+  FinishParams F;
+  F.vs = vs; F.dtype = dtype; F.V = V; F.k = k;
+  F.nch = nch_for(V); F.chunk = (V + F.nch - 1) / F.nch;
+  F.T = temperature;
+  F.stats = reinterpret_cast<const VecStats*>(ws + L.stats);
+  F.mat = small ? reinterpret_cast<const float*>(ws + L.mat) : nullptr;
+  F.u_acc = u_acc; F.u_bs = u_bs; F.u_res = u_res; F.alive = alive;
+  F.n_acc = n_acc; F.y = y; F.px = px; F.qx = qx; F.y_prob = nullptr;
+  F.partial = reinterpret_cast<double*>(ws + L.partial);
+  F.counter = reinterpret_cast<int*>(ws + L.counter);
+  finish_kernel<<<F.nch * B, FT, 0, st>>>(F);
+  return check_launch();
+}
+
+int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, int V,
+                    const float* u, float temperature, float top_p, int top_k,
+                    int64_t* x, float* qx, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  int rc = validate_common(dtype, V, temperature);
+  if (rc) return rc;
+  if (B <= 0 || !logits || !u || !x || !workspace) return SD_EINVAL;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = reinterpret_cast<char*>(workspace);
+  VecSet vs = {};
+  vs.base[0] = logits; vs.bs[0] = row_stride; vs.ps[0] = 0; vs.npos[0] = 1; vs.npos[1] = 0;
+  vs.nrows = B;
+  if (!(temperature > 0.0f)) {
+    WsLayout L = ws_layout(B, B, V, false);
+    if (workspace_bytes < L.total) return SD_ENOSPC;
+    ArgmaxParams P;
+    P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = B;
+    P.nch = nch_for(V); P.chunk = (V + P.nch - 1) / P.nch;
+    P.partial = reinterpret_cast<unsigned long long*>(ws + L.apartial);
+    P.vec_counter = reinterpret_cast<int*>(ws + L.vcounter);
+    P.row_counter = reinterpret_cast<int*>(ws + L.rcounter);
+    P.stats = reinterpret_cast<VecStats*>(ws + L.stats);
+    P.k = 0; P.xs = nullptr; P.xs_bs = 0; P.u_acc = nullptr; P.u_bs = 0; P.alive = nullptr;
+    P.n_acc = nullptr; P.y = x; P.px = nullptr; P.qx = qx;
+    argmax_kernel<<<P.nch * B, FT, 0, st>>>(P);
+    return check_launch();
+  }
+  const bool small = use_small(V, dtype);
+  WsLayout L = ws_layout(B, B, V, small);
+  if (workspace_bytes < L.total) return SD_ENOSPC;
+  rc = run_stats(vs, B, dtype, V, temperature, top_p, top_k, L, ws, st);
+  if (rc) return rc;
+  FinishParams F;
+  F.vs = vs; F.dtype = dtype; F.V = V; F.k = 0;
+  F.nch = nch_for(V); F.chunk = (V + F.nch - 1) / F.nch;
+  F.T = temperature;
+  F.stats = reinterpret_cast<const VecStats*>(ws + L.stats);
+  F.mat = small ? reinterpret_cast<const float*>(ws + L.mat) : nullptr;
+  F.u_acc = nullptr; F.u_bs = 0; F.u_res = u; F.alive = nullptr;
+  F.n_acc = nullptr; F.y = x; F.px = nullptr; F.qx = nullptr; F.y_prob = qx;
+  F.partial = reinterpret_cast<double*>(ws + L.partial);
+  F.counter = reinterpret_cast<int*>(ws + L.counter);
+  finish_kernel<<<F.nch * B, FT, 0, st>>>(F);
+  return check_launch();
+}
+
+int sd_to_probs(const void* logits, int64_t row_stride, int dtype, int n_rows, int V,
+                float temperature, float top_p, int top_k, float* out, int64_t out_stride,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = validate_common(dtype, V, temperature);
+  if (rc) return rc;
+  if (n_rows < 0 || !logits || !out || !workspace) return SD_EINVAL;
+  if (n_rows == 0) return SD_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = reinterpret_cast<char*>(workspace);
+  VecSet vs = {};
+  vs.base[0] = logits; vs.bs[0] = row_stride; vs.ps[0] = 0; vs.npos[0] = 1; vs.npos[1] = 0;
+  vs.nrows = n_rows;
+  const bool greedy = !(temperature > 0.0f);
+  const bool small = !greedy && use_small(V, dtype);
+  WsLayout L = ws_layout(n_rows, n_rows, V, small);
+  if (workspace_bytes < L.total) return SD_ENOSPC;
+  ProbsParams P;
+  P.vs = vs; P.dtype = dtype; P.V = V; P.nch = nch_for(V); P.chunk = (V + P.nch - 1) / P.nch;
+  P.greedy = greedy; P.T = temperature;
+  P.stats = reinterpret_cast<const VecStats*>(ws + L.stats);
+  P.mat = small ? reinterpret_cast<const float*>(ws + L.mat) : nullptr;
+  P.out = out; P.out_stride = out_stride;
+  if (greedy) {
+    ArgmaxParams A;
+    A.vs = vs; A.dtype = dtype; A.V = V; A.nvec = n_rows;
+    A.nch = P.nch; A.chunk = P.chunk;
+    A.partial = reinterpret_cast<unsigned long long*>(ws + L.apartial);
+    A.vec_counter = reinterpret_cast<int*>(ws + L.vcounter);
+    A.row_counter = reinterpret_cast<int*>(ws + L.rcounter);
+    A.stats = reinterpret_cast<VecStats*>(ws + L.stats);
+    A.k = -1;   // stats only: per-row decision skipped (npos 1 row counter reaches 0 -> k<0)
+    A.xs = nullptr; A.xs_bs = 0; A.u_acc = nullptr; A.u_bs = 0; A.alive = nullptr;
+    A.n_acc = nullptr; A.y = nullptr; A.px = nullptr; A.qx = nullptr;
+    argmax_kernel<<<A.nch * n_rows, FT, 0, st>>>(A);
+    if ((rc = check_launch())) return rc;
+  } else {
+    rc = run_stats(vs, n_rows, dtype, V, temperature, top_p, top_k, L, ws, st);
+    if (rc) return rc;
+  }
+  probs_kernel<<<P.nch * n_rows, FT, 0, st>>>(P);
+  return check_launch();
+}
+
+int sd_residual_probs(const float* p, const float* q, int n_rows, int V, float* out, void* stream) {
+  if (n_rows < 0 || V <= 0 || !p || !q || !out) return SD_EINVAL;
+  if (n_rows == 0) return SD_OK;
+  residual_kernel<<<n_rows, FT, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p, q, V, out);
+  return check_launch();
+}
+
+int sd_sample_from_probs(const float* probs, int n_rows, int V, const float* u, int64_t* out,
+                         void* stream) {
+  if (n_rows < 0 || V <= 0 || !probs || !u || !out) return SD_EINVAL;
+  if (n_rows == 0) return SD_OK;
+  sample_probs_kernel<<<n_rows, FT, 0, reinterpret_cast<cudaStream_t>(stream)>>>(probs, V, u, out);
+  return check_launch();
+}
+
+int sd_gather_prob(const float* probs, int n_rows, int V, const int64_t* ids, float* out,
+                   void* stream) {
+  if (n_rows < 0 || V <= 0 || !probs || !ids || !out) return SD_EINVAL;
+  if (n_rows == 0) return SD_OK;
+  gather_kernel<<<(n_rows + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      probs, n_rows, V, ids, out);
+  return check_launch();
+}
+
+}  // extern "C"

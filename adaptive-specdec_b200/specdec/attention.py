@@ -1,0 +1,91 @@
+"""Verify attention over the ragged cache, and its transformers hook.
+
+``verify_attention`` is the Python face of sd_verify_attn: grouped-query
+attention where query j of row b reads cache slots s <= lengths[b] + j (and
+s < valid[b] in a right-padded prefill).  It replaces the reference's HF SDPA
+over ``_RaggedLayer.update``'s max-width view plus the additive mask
+(specdec/kvcache.py:61-74 and :138-162, called at specdec/engine.py:274): each
+row reads only its own live keys.
+
+``register()`` installs it as the transformers attention implementation
+"specdec_b200" (with a mask function that builds no mask); a model loaded with
+``attn_implementation="specdec_b200"`` and run against a
+``RaggedCache(..., attn_impl="specdec_b200")`` then attends through the kernel.
+"""
+import torch
+
+from specdec import _lib as L
+
+IMPL = "specdec_b200"
+_ATTN_DTYPES = {torch.bfloat16: 2, torch.float32: 0}
+
+
+class _WS:
+    def __init__(self):
+        self.t = {}
+
+    def get(self, n, device):
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        cur = self.t.get(key)
+        if cur is None or cur.numel() < n:
+            cur = torch.empty(max(int(n), 1 << 20), dtype=torch.uint8, device=device)
+            self.t[key] = cur
+        return cur
+
+
+_ws = _WS()
+
+
+def verify_attention(q, k_cache, v_cache, lengths, valid=None, scale=None, out=None):
+    """q [B, Hq, qlen, D], caches [B, Hkv, C, D] -> out [B, qlen, Hq, D].
+
+    ``lengths`` [B] int64 on the device are the lengths before this forward's
+    advance (the new keys were already appended at lengths[b] + j).
+    """
+    L.require_cuda(q, k_cache, v_cache, lengths)
+    if q.dtype not in _ATTN_DTYPES or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise L.SpecdecError(f"verify_attention supports bf16 / fp32, got {q.dtype}")
+    B, Hq, qlen, D = q.shape
+    _, Hkv, C, _ = k_cache.shape
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    kc = k_cache if k_cache.is_contiguous() else k_cache.contiguous()
+    vc = v_cache if v_cache.is_contiguous() else v_cache.contiguous()
+    if out is None:
+        out = torch.empty(B, qlen, Hq, D, dtype=q.dtype, device=q.device)
+    sc = float(scale) if scale is not None else D ** -0.5
+    lens = lengths.to(torch.long).contiguous()
+    val = None if valid is None else valid.to(q.device, torch.long).contiguous()
+    lib = L.lib()
+    with torch.cuda.device(q.device):
+        nws = lib.sd_verify_attn_workspace_bytes(B, Hq, Hkv, D, C, qlen)
+        ws = _ws.get(nws, q.device)
+        L.check(lib.sd_verify_attn(L.ptr(q), q.stride(0), q.stride(1), q.stride(2), L.ptr(kc),
+                                   L.ptr(vc), L.ptr(lens), L.ptr(val), B, Hq, Hkv, D, C, qlen, sc,
+                                   L.ptr(out), out.stride(0), out.stride(1), out.stride(2),
+                                   _ATTN_DTYPES[q.dtype], L.ptr(ws), ws.numel(),
+                                   L.stream_ptr(q.device)), "verify_attn")
+    return out
+
+
+def hf_attention(module, query, key, value, attention_mask, dropout=0.0, scaling=None, **kwargs):
+    """transformers AttentionInterface function for RaggedCache buffers."""
+    cache = getattr(key, "_sd_cache", None)
+    if cache is None:
+        raise L.SpecdecError("attn_implementation='specdec_b200' needs a RaggedCache created with "
+                             "attn_impl='specdec_b200'")
+    out = verify_attention(query, key, value, cache.lengths, valid=cache.valid, scale=scaling)
+    return out, None
+
+
+def _no_mask(*args, **kwargs):
+    return None
+
+
+def register():
+    """Register the kernel as attention implementation "specdec_b200"."""
+    from transformers import AttentionInterface
+    from transformers.masking_utils import AttentionMaskInterface
+    AttentionInterface.register(IMPL, hf_attention)
+    AttentionMaskInterface.register(IMPL, _no_mask)
+    return IMPL

@@ -1,0 +1,385 @@
+"""Benchmark of the fused verify round (config 2) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--mode sample|greedy]
+
+A step is one verify call over one batch: B=64 rows, k=4 draft tokens,
+V=151936, bf16 target [64,5,V] and draft [64,4,V] logits, T=0.7, top-p 0.9
+(mode greedy: T=0, target only).  Rows are sharded across ranks with no
+collective (weak scaling: every rank verifies its own 64-row batch); `value`
+is rows/s summed over ranks, timed on the device with CUDA events as the max
+over ranks.  Two input sets (350 MB, > the 126 MB L2) alternate so no step
+reads logits left in L2 by the previous one.  Steps are replayed from CUDA
+graphs of up to 100 calls.
+
+`e2e` is the same metric through the public API from pinned host buffers:
+every step copies that step's logits host->device, runs verify_sample and
+reads n_acc / y back.  `cpu_baseline` times the CPU oracle (a restatement of
+the reference path, single thread) on 64 rows of the same workload.
+`--impl reference` times that CPU path on the host cores alone.
+"""
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+for _p in (str(ROOT / "adaptive-specdec_b200"), str(ROOT)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+B, K_DRAFT, VOCAB = 64, 4, 151936
+T_SAMPLE, TOP_P = 0.7, 0.9
+NBUF = 2
+GRAPH_CALLS = 100
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default="sample", choices=["sample", "greedy"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def metric_name(mode):
+    if mode == "greedy":
+        return "verify rows/s (B=64,k=4,V=151936 bf16, greedy)"
+    return "verify rows/s (B=64,k=4,V=151936 bf16, T=0.7 top-p 0.9)"
+
+
+def workload_config(mode, n):
+    return {"workload": f"config 2 fused verify round, {'greedy' if mode == 'greedy' else 'T=0.7 top-p 0.9'}",
+            "rows_per_gpu": B, "k": K_DRAFT, "vocab": VOCAB, "logits": "bf16",
+            "parallelism": f"row-sharded x{n}, no collective",
+            "l2": "2 input sets of 175 MB alternate (> 126 MB L2)"}
+
+
+# ---------------------------------------------------------------------------
+# CPU path (oracle restatement of the reference), used by both arms
+# ---------------------------------------------------------------------------
+def _cpu_inputs(rows, seed):
+    import numpy as np
+    import torch
+    from specdec import workloads as W
+    g = torch.Generator().manual_seed(seed)
+    tgt = W.zipf_logits(rows * (K_DRAFT + 1), VOCAB, g).reshape(rows, K_DRAFT + 1, VOCAB)
+    drf = tgt[:, :K_DRAFT] + torch.randn(rows, K_DRAFT, VOCAB, generator=g) * W.DRAFT_SIGMA
+    tgt = tgt.bfloat16().float().numpy()
+    drf = drf.bfloat16().float().numpy()
+    rng = np.random.default_rng(seed)
+    xs = tgt[:, :K_DRAFT].argmax(-1)
+    xs = np.where(rng.random((rows, K_DRAFT)) < 0.5, xs, rng.integers(0, VOCAB, (rows, K_DRAFT)))
+    ua = rng.random((rows, K_DRAFT), dtype=np.float32)
+    ur = rng.random(rows, dtype=np.float32)
+    return tgt, drf, xs, ua, ur
+
+
+def _cpu_rows(args):
+    tgt, drf, xs, ua, ur, T, tp = args
+    from oracle import sampling_oracle as O
+    return O.verify(tgt, drf, xs, ua, ur, T, tp, 0)
+
+
+def _cpu_vec(args):
+    x, T, tp = args
+    from oracle import sampling_oracle as O
+    return O.to_probs_row(x, T, tp, 0)
+
+
+def cpu_baseline(mode, rows=64):
+    """Oracle on `rows` rows, one thread; returns (rows/s, seconds)."""
+    T, tp = (0.0, 1.0) if mode == "greedy" else (T_SAMPLE, TOP_P)
+    tgt, drf, xs, ua, ur = _cpu_inputs(rows, seed=11)
+    t0 = time.perf_counter()
+    _cpu_rows((tgt, drf, xs, ua, ur, T, tp))
+    dt = time.perf_counter() - t0
+    return rows / dt, dt
+
+
+def reference_arm(a):
+    """--impl reference: the CPU path on all host cores.
+
+    One step verifies one config-2 row: its 9 to_probs vectors (5 target,
+    4 draft; 5 in greedy mode) run in parallel in a spawn process pool, the
+    accept test and the draw follow in the parent.  That bounds every step to
+    tens of milliseconds, so any --steps finishes within minutes.
+    """
+    import multiprocessing as mp
+    import numpy as np
+    from oracle import sampling_oracle as O
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    greedy = a.mode == "greedy"
+    T, tp = (0.0, 1.0) if greedy else (T_SAMPLE, TOP_P)
+    nrow = 4
+    tgt, drf, xs, ua, ur = _cpu_inputs(nrow, seed=11)
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        def step(i):
+            r = i % nrow
+            vecs = [tgt[r, j] for j in range(K_DRAFT + 1)]
+            if not greedy:
+                vecs += [drf[r, j] for j in range(K_DRAFT)]
+            probs = pool.map(_cpu_vec, [(v, T, tp) for v in vecs])
+            P = np.stack(probs[:K_DRAFT + 1])[None]
+            Q = np.stack(probs[K_DRAFT + 1:])[None] if not greedy else P[:, :K_DRAFT]
+            O.verify_from_probs(P, Q, xs[r:r + 1], ua[r:r + 1], ur[r:r + 1])
+        for i in range(max(1, a.warmup)):
+            step(i)
+        t0 = time.perf_counter()
+        for i in range(a.steps):
+            step(i)
+        dt = time.perf_counter() - t0
+    rows_s = a.steps / dt
+    print(json.dumps({
+        "impl": "reference", "metric": metric_name(a.mode), "value": rows_s, "unit": "rows/s",
+        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * dt / a.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded config-2 logits)",
+        "config": dict(workload_config(a.mode, 1), rows_per_step=1),
+        "cpu_baseline": {"value": rows_s, "unit": "rows/s", "cores": cores, "kind": "port",
+                         "sample": "one config-2 row per step, its to_probs vectors spread over "
+                                   f"{cores} processes (the reference path restated in "
+                                   "oracle/sampling_oracle.py)"},
+        "e2e": {"value": rows_s, "unit": "rows/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}))
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML polling thread)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x20: "sync_boost", 0x40: "sw_thermal_slowdown",
+               0x80: "hw_thermal_slowdown", 0x100: "hw_power_brake_slowdown",
+               0x200: "display_clock_setting"}
+
+    def __init__(self, index):
+        self.samples, self.reasons = [], 0
+        self._stop = threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            try:
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(
+                    "GPU-" + str(torch.cuda.get_device_properties(index).uuid))
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                fn = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                self.reasons |= fn(self.h)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.nv is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return reference_arm(a)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cpu_rate = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu_rate = cpu_baseline(a.mode)       # before any CUDA work
+    import torch
+    import torch.distributed as dist
+    from specdec import sampling as S
+    from specdec import workloads as W
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    greedy = a.mode == "greedy"
+    T, tp = (0.0, 1.0) if greedy else (T_SAMPLE, TOP_P)
+
+    bufs = []
+    for i in range(NBUF):
+        tgt, drf = W.cfg2_logits(B, K_DRAFT, VOCAB, seed=100 * rank + i, device=dev)
+        xs, _ = S.draft_sample(drf.reshape(-1, VOCAB), torch.rand(B * K_DRAFT, device=dev), T, tp)
+        ua, ur = W.uniforms(B, K_DRAFT, seed=100 * rank + i, device=dev)
+        out = (torch.empty(B, dtype=torch.long, device=dev), torch.empty(B, dtype=torch.long,
+                                                                        device=dev))
+        bufs.append((tgt, drf, xs.view(B, K_DRAFT), ua, ur, out))
+
+    def call(i):
+        tgt, drf, xs, ua, ur, out = bufs[i % NBUF]
+        n, y = S.verify_sample(tgt, drf, xs, ua, ur, T, tp)
+        out[0].copy_(n)
+        out[1].copy_(y)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for i in range(max(3, a.warmup)):
+            call(i)
+    torch.cuda.synchronize(dev)
+    graphs = {}
+
+    def graph_of(n):
+        if n not in graphs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for i in range(n):
+                    call(i)
+            graphs[n] = g
+        return graphs[n]
+
+    plan = [GRAPH_CALLS] * (a.steps // GRAPH_CALLS)
+    if a.steps % GRAPH_CALLS:
+        plan.append(a.steps % GRAPH_CALLS)
+    for n in set(plan):
+        graph_of(n).replay()      # warm the graphs too
+    torch.cuda.synchronize(dev)
+
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        ev0.record(s)
+        for n in plan:
+            graph_of(n).replay()
+        ev1.record(s)
+        torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        dist.barrier()
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / a.steps
+    value = world * B * a.steps / (ms / 1e3)
+    calls_s = 1e3 / ms_step
+    bytes_call = W.bytes_per_verify(B, K_DRAFT, VOCAB, greedy=greedy)
+    gbs = bytes_call * calls_s / 1e9
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    peak = peaks.get("hbm_gbs")
+    peak_src = "measured" if peak else "fallback"
+    peak = peak or 6650.0
+
+    # end to end through the public API from pinned host buffers
+    host = []
+    for i in range(NBUF):
+        tgt, drf, xs, ua, ur, _ = bufs[i]
+        host.append(tuple(t.cpu().pin_memory() for t in (tgt, drf, xs, ua, ur)))
+    dev_in = [tuple(torch.empty_like(t, device=dev) for t in host[0]) for _ in range(NBUF)]
+    res = [(torch.empty(B, dtype=torch.long).pin_memory(),
+            torch.empty(B, dtype=torch.long).pin_memory()) for _ in range(NBUF)]
+    n_e2e = max(3, min(a.steps, 100))
+
+    def e2e_step(i):
+        d = dev_in[i % NBUF]
+        for dst, src in zip(d, host[i % NBUF]):
+            dst.copy_(src, non_blocking=True)
+        n, y = S.verify_sample(d[0], None if greedy else d[1], d[2], d[3], d[4], T, tp)
+        res[i % NBUF][0].copy_(n, non_blocking=True)
+        res[i % NBUF][1].copy_(y, non_blocking=True)
+
+    with torch.cuda.stream(s):
+        for i in range(3):
+            e2e_step(i)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for i in range(n_e2e):
+            e2e_step(i)
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(t.numel() * t.element_size() for t in host[0][:1] + host[0][2:])
+    if not greedy:
+        h2d += host[0][1].numel() * host[0][1].element_size()
+    traffic = None
+    prof = ROOT / "profiles" / ("verify_greedy_traffic.json" if greedy else "verify_sample_traffic.json")
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get("bytes_per_call")
+    launches_per_step = 1 if greedy else 2
+    line = {
+        "metric": metric_name(a.mode), "value": value, "unit": "rows/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded config-2 logits, see specdec/workloads.py)",
+        "config": workload_config(a.mode, world),
+        "hbm_gbs": gbs,
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "traffic": traffic,
+                     "peak_source": peak_src,
+                     "scope": "the whole verify call (all its kernels); algorithmic bytes "
+                              f"{bytes_call} per call = every logits element read once"},
+        "e2e": {"value": world * B * n_e2e / (e2e_ms / 1e3), "unit": "rows/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 2 * B * 8, "steps": n_e2e},
+        "gpu_launches": launches_per_step * a.steps,
+        "clocks": clk.summary(),
+    }
+    if cpu_rate is not None:
+        line["cpu_baseline"] = {"value": cpu_rate[0], "unit": "rows/s", "cores": 1, "kind": "port",
+                                "sample": f"64 rows of config 2 through oracle/sampling_oracle.py "
+                                          f"({cpu_rate[1]:.1f} s, numpy, one thread)"}
+    if rank == 0:
+        print(json.dumps(line))
+    for g in graphs.values():
+        del g
+    graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

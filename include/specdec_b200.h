@@ -1,0 +1,167 @@
+/*
+ * specdec_b200 -- C ABI of the B200-native verify-round kernels.
+ *
+ * Conventions (all entry points):
+ *   - plain device pointers and sizes; the caller owns every buffer, including
+ *     the workspace, and the library allocates nothing;
+ *   - all work is enqueued on `stream` (a cudaStream_t passed as void*), no
+ *     host synchronisation;
+ *   - return 0 on success or a negative errno-style code (SD_E*) for bad
+ *     shapes, unsupported configurations, a too-small workspace or a failed
+ *     launch;
+ *   - token ids are int64 (torch.long, as the reference uses);
+ *   - logits rows are contiguous along the vocabulary; other dimensions are
+ *     addressed by element strides.
+ *
+ * Uniforms are passed in as arrays so that every draw is a deterministic
+ * function of its inputs: the draw from a distribution r over the vocabulary
+ * is the smallest index j whose running float64 sum of r exceeds u * sum(r).
+ */
+#ifndef SPECDEC_B200_H_
+#define SPECDEC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SD_OK 0
+#define SD_EINVAL (-22)    /* bad shape / argument */
+#define SD_ENOTSUP (-95)   /* configuration not supported by these kernels */
+#define SD_ENOSPC (-28)    /* workspace too small */
+#define SD_ERANGE (-34)    /* length would leave [0, capacity] */
+#define SD_ELAUNCH (-5)    /* CUDA launch error */
+
+#define SD_DTYPE_F32 0
+#define SD_DTYPE_F16 1
+#define SD_DTYPE_BF16 2
+
+/* Library version and build information, for the loaders' sanity checks. */
+int sd_version(void);
+
+/* Workspace bytes needed by sd_verify_sample / sd_draft_sample / sd_to_probs
+ * for n_vec logits vectors of width V split over n_rows rows.  The first use
+ * of a workspace must see it zeroed; the kernels leave it reusable. */
+size_t sd_sampling_workspace_bytes(int n_rows, int n_vec, int V, int dtype);
+
+/*
+ * Fused verify round: to_probs on every target/draft vector, the accept test
+ * u < min(1, p(x)/max(q(x),1e-10)) with prefix-alive semantics, and the
+ * residual draw from norm((p-q)+) at the first rejection, or the bonus draw
+ * from p_k when every draft token was accepted.
+ *
+ * Replaces reference specdec/engine.py:282-303 (the k+1 to_probs calls, the
+ * accept loop and the two sample_from_probs calls) and, inside it,
+ * specdec/sampling.py:34-95 (to_probs, residual_probs, gather_prob).
+ *
+ *   tgt    [B, k+1, V] logits, element strides (tgt_bs, tgt_ps, 1)
+ *   drf    [B, k,   V] logits, element strides (drf_bs, drf_ps, 1); unused
+ *          (may be NULL) when temperature <= 0 (greedy reads the target only)
+ *   xs     [B, k] int64 draft tokens, row stride xs_bs
+ *   u_acc  [B, k] float uniforms for the accept tests, row stride u_bs
+ *   u_res  [B] float uniform for the residual / bonus draw
+ *   alive  [B] uint8 or NULL (NULL = all rows alive; the reference's ~done)
+ *   n_acc  [B] int64 out: accepted draft tokens per row
+ *   y      [B] int64 out: the emitted token (residual or bonus draw)
+ *   px, qx [B, k] float out or NULL: p_i(x_i) and q_i(x_i)
+ */
+int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
+                     const void* drf, int64_t drf_bs, int64_t drf_ps, int dtype,
+                     const int64_t* xs, int64_t xs_bs, const float* u_acc, int64_t u_bs,
+                     const float* u_res, const uint8_t* alive,
+                     int B, int k, int V, float temperature, float top_p, int top_k,
+                     int64_t* n_acc, int64_t* y, float* px, float* qx,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * One draft step: x[b] ~ to_probs(logits[b]) drawn by inverse CDF with u[b],
+ * and qx[b] = q(x[b]).  Replaces reference specdec/engine.py:250-251 and 256
+ * (to_probs, sample_from_probs, gather_prob for the confidence product).
+ *   logits [B, V], row stride row_stride; x [B] int64; qx [B] float or NULL.
+ */
+int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, int V,
+                    const float* u, float temperature, float top_p, int top_k,
+                    int64_t* x, float* qx, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/*
+ * to_probs: logits [n_rows, V] (row stride row_stride) -> fp32 probabilities
+ * [n_rows, V] (row stride out_stride).  Replaces specdec/sampling.py:34-67.
+ */
+int sd_to_probs(const void* logits, int64_t row_stride, int dtype, int n_rows, int V,
+                float temperature, float top_p, int top_k, float* out, int64_t out_stride,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/* residual_probs: norm((p-q)+) row-wise, p falling back when the positive
+ * part sums to <= 1e-9.  Replaces specdec/sampling.py:77-90.  fp32 [n, V]. */
+int sd_residual_probs(const float* p, const float* q, int n_rows, int V, float* out,
+                      void* stream);
+
+/* sample_from_probs with given uniforms: out[i] = inverse-CDF draw of row i.
+ * Replaces specdec/sampling.py:70-74 (torch.multinomial). */
+int sd_sample_from_probs(const float* probs, int n_rows, int V, const float* u,
+                         int64_t* out, void* stream);
+
+/* gather_prob: out[i] = probs[i, ids[i]].  Replaces specdec/sampling.py:93-95. */
+int sd_gather_prob(const float* probs, int n_rows, int V, const int64_t* ids, float* out,
+                   void* stream);
+
+/* ---- ragged KV cache (reference specdec/kvcache.py) --------------------- */
+
+/*
+ * lengths[b] += delta[b] (delta NULL: += q for every row).  Any row leaving
+ * [0, capacity] is left unchanged and sets *err (device int) to 1.
+ * Replaces RaggedCache.advance / rollback / set_lengths bookkeeping
+ * (specdec/kvcache.py:165-190) with device-resident lengths: O(1), no data
+ * movement, no host sync.  `sign` is +1 (advance) or -1 (rollback).
+ */
+int sd_kv_lengths_update(int64_t* lengths, const int64_t* delta, int64_t q, int sign,
+                         int B, int64_t capacity, int* err, void* stream);
+
+/*
+ * Commit a verify round: lengths[b] -= k - n_acc[b] (drops the rejected tail).
+ * Replaces the rollback at specdec/engine.py:309-312 without the host copy.
+ */
+int sd_kv_commit(int64_t* lengths, const int64_t* n_acc, int k, int B, int* err,
+                 void* stream);
+
+/*
+ * Append q new tokens per row at each row's own offset:
+ *   cache[b, h, lengths[b] + j, :] = new[b, h, j, :]   for j < q
+ * for the K and V caches of one layer ([B, H, C, D] contiguous) from
+ * new_k / new_v ([B, H, q, D] with element strides (nbs, nhs, nqs, 1)).
+ * Replaces the scatter in _RaggedLayer.update (specdec/kvcache.py:61-74).
+ * Rows whose write would pass `capacity` are skipped and set *err.
+ */
+int sd_kv_append(void* kcache, void* vcache, const void* new_k, const void* new_v,
+                 int64_t nbs, int64_t nhs, int64_t nqs, const int64_t* lengths,
+                 int B, int H, int C, int D, int q, int dtype, int* err, void* stream);
+
+/*
+ * Verify attention over the ragged cache (after the append of this forward):
+ * query j of row b (position lengths[b] + j) attends to cache slots
+ * s <= lengths[b] + j, i.e. the reference mask s <= len[b] + j
+ * (specdec/kvcache.py:138-162) with SDPA (HF Qwen3 attention at
+ * specdec/engine.py:274), grouped-query: query head h reads kv head
+ * h / (Hq/Hkv).  `lengths` are the lengths BEFORE this forward's advance.
+ *   q   [B, Hq, qlen, D] (strides qbs, qhs, qqs, 1)
+ *   k/v [B, Hkv, C, D] contiguous
+ *   out [B, qlen, Hq, D] (strides obs, oqs, ohs, 1)
+ *   valid [B] int64 or NULL: optional cap s < valid[b] (right-padded prefill)
+ *   dtype SD_DTYPE_BF16 (the Qwen3 path) or SD_DTYPE_F32; fp32 accumulation.
+ */
+int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs,
+                   const void* kcache, const void* vcache, const int64_t* lengths,
+                   const int64_t* valid, int B, int Hq, int Hkv, int D, int C, int qlen,
+                   float scale, void* out, int64_t obs, int64_t oqs, int64_t ohs, int dtype,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+size_t sd_verify_attn_workspace_bytes(int B, int Hq, int Hkv, int D, int C, int qlen);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECDEC_B200_H_ */

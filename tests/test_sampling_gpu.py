@@ -1,0 +1,262 @@
+"""GPU parity of the verify-round sampling kernels against the CPU oracle.
+
+Bar (from the task's parity contract):
+* accept counts and emitted tokens bit-exact, except rows whose decision sits
+  within 1e-6 of a boundary: |u - min(1, p/q)| < 1e-6 at a tested position, an
+  inverse-CDF crossing within 1e-6 * total of u * total, or a top-p edge
+  |fl32(cum - p) - top_p| < 1e-6 on a vector the row used;
+* probabilities within 1e-5 relative (the contract asks 1e-3);
+* the statistical rejection-rule test (TV <= 0.02, here 0.01) on the kernels.
+
+Inputs are seeded; the oracle is oracle/sampling_oracle.py, itself pinned to
+the reference by tests/test_oracle_golden.py.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import sampling_oracle as O
+from specdec import sampling as S
+from specdec import workloads as W
+from tests.golden import GOLDEN
+
+pytestmark = pytest.mark.gpu
+EPS = 1e-6
+PREL = 1e-5
+DEV = "cuda"
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _ok(d):
+    return (d["acc_margin"] > EPS) & (d["cdf_margin"] > EPS) & (d["topp_margin"] > EPS)
+
+
+def _check_verify(tgt, drf, xs, ua, ur, T, tp, tk, max_exempt=0.1, tag=""):
+    """Kernel vs oracle on the same (already device-resident) inputs."""
+    n_k, y_k, px_k, qx_k = S.verify_sample(tgt, drf, xs, ua, ur, T, tp, tk, return_probs=True)
+    n_o, y_o, d = O.verify(_np(tgt), _np(drf), xs.cpu().numpy(), _np(ua), _np(ur), T, tp, tk,
+                           return_details=True)
+    ok = _ok(d)
+    assert ok.mean() >= 1.0 - max_exempt, f"{tag}: too many boundary rows {(~ok).sum()}"
+    n_k, y_k = n_k.cpu().numpy(), y_k.cpu().numpy()
+    bad = np.nonzero(ok & ((n_k != n_o) | (y_k != y_o)))[0]
+    assert bad.size == 0, (f"{tag}: rows {bad[:8]} differ: kernel n/y "
+                           f"{n_k[bad[:8]]}/{y_k[bad[:8]]} oracle {n_o[bad[:8]]}/{y_o[bad[:8]]}")
+    if T is not None and T > 0:
+        px_k, qx_k = px_k.cpu().numpy(), qx_k.cpu().numpy()
+        sel = ok[:, None] & np.ones_like(px_k, dtype=bool)
+        np.testing.assert_allclose(px_k[sel], d["px"][sel], rtol=2e-6, atol=1e-30, err_msg=tag)
+        np.testing.assert_allclose(qx_k[sel], d["qx"][sel], rtol=2e-6, atol=1e-30, err_msg=tag)
+    return n_k, y_k, ok
+
+
+# ---------------------------------------------------------------------------
+# golden cases (pinned to the reference)
+# ---------------------------------------------------------------------------
+_VZ = np.load(GOLDEN / "verify.npz")
+
+
+@pytest.mark.parametrize("case", [str(n) for n in _VZ["names"]])
+def test_verify_golden(case):
+    g = {k: _VZ[f"{case}__{k}"] for k in ("tgt", "drf", "xs", "u_acc", "u_res", "n_acc", "y",
+                                          "params")}
+    T, tp, tk = (float(g["params"][0]), float(g["params"][1]), int(g["params"][2]))
+    dt = torch.bfloat16 if "bf16" in case or "greedy" in case else torch.float32
+    tgt = torch.from_numpy(g["tgt"]).to(DEV, dt)
+    drf = torch.from_numpy(g["drf"]).to(DEV, dt)
+    xs = torch.from_numpy(g["xs"]).to(DEV)
+    ua = torch.from_numpy(g["u_acc"]).to(DEV)
+    ur = torch.from_numpy(g["u_res"]).to(DEV)
+    n_k, y_k, ok = _check_verify(tgt, drf, xs, ua, ur, T, tp, tk, max_exempt=0.25, tag=case)
+    # and directly against the reference's own outputs
+    np.testing.assert_array_equal(n_k[ok], g["n_acc"][ok])
+    np.testing.assert_array_equal(y_k[ok], g["y"][ok])
+
+
+_TZ = np.load(GOLDEN / "to_probs.npz")
+
+
+@pytest.mark.parametrize("case", [str(n) for n in _TZ["names"]])
+def test_to_probs_golden(case):
+    x = _TZ[case + "__x"]
+    T, tp, tk = _TZ[case + "__params"]
+    dt = torch.bfloat16 if "bf16" in case or "greedy" in case else torch.float32
+    got = _np(S.to_probs(torch.from_numpy(x).to(DEV, dt), float(T), float(tp), int(tk)))
+    infos = []
+    want = O.to_probs(x, float(T), float(tp), int(tk), infos=infos)
+    ref = _TZ[case + "__stable"]
+    for r in range(x.shape[0]):
+        if infos[r].topp_margin < EPS:
+            continue
+        np.testing.assert_array_equal(got[r] > 0, want[r] > 0, err_msg=f"{case} row {r}")
+        np.testing.assert_allclose(got[r], want[r], rtol=PREL, atol=0, err_msg=f"{case} row {r}")
+        np.testing.assert_allclose(got[r], ref[r], rtol=PREL, atol=1e-12, err_msg=f"{case} ref")
+
+
+# ---------------------------------------------------------------------------
+# config 2 at full size (B=64, k=4, V=151936 bf16) and the greedy case
+# ---------------------------------------------------------------------------
+@pytest.fixture(scope="module")
+def cfg2():
+    tgt, drf = W.cfg2_logits(seed=0)
+    ua, ur = W.uniforms(64, 4, seed=0)
+    xs, _ = S.draft_sample(drf.reshape(-1, drf.shape[-1]), torch.rand(
+        256, generator=torch.Generator(device=DEV).manual_seed(3), device=DEV), 0.7, 0.9)
+    return tgt, drf, xs.reshape(64, 4), ua, ur
+
+
+def test_cfg2_sampling_parity(cfg2):
+    tgt, drf, xs, ua, ur = cfg2
+    n_k, y_k, ok = _check_verify(tgt, drf, xs, ua, ur, 0.7, 0.9, 0, max_exempt=0.05, tag="cfg2")
+    assert len(set(n_k.tolist())) >= 3, "instance should exercise several accept lengths"
+
+
+def test_cfg2_greedy_parity(cfg2):
+    tgt, drf, xs, ua, ur = cfg2
+    am = tgt.float().argmax(-1)                    # [64, 5]
+    xs_g = torch.where(torch.rand(64, 4, device=DEV) < 0.7, am[:, :4], xs)
+    _check_verify(tgt, drf, xs_g, ua, ur, 0.0, 1.0, 0, max_exempt=0.0, tag="greedy")
+
+
+def test_cfg2_topk_and_topp(cfg2):
+    tgt, drf, xs, ua, ur = cfg2
+    _check_verify(tgt[:16], drf[:16], xs[:16], ua[:16], ur[:16], 1.0, 0.8, 40, tag="topk40+topp")
+
+
+def test_cfg2_to_probs_full_rows(cfg2):
+    tgt = cfg2[0]
+    x = tgt[:3].reshape(-1, tgt.shape[-1])[:8]
+    got = _np(S.to_probs(x, 0.7, 0.9))
+    infos = []
+    want = O.to_probs(_np(x), 0.7, 0.9, infos=infos)
+    for r in range(x.shape[0]):
+        if infos[r].topp_margin < EPS:
+            continue
+        np.testing.assert_array_equal(got[r] > 0, want[r] > 0)
+        np.testing.assert_allclose(got[r], want[r], rtol=PREL, atol=0)
+
+
+# ---------------------------------------------------------------------------
+# histogram-path edge cases
+# ---------------------------------------------------------------------------
+def _to_probs_case(x, T, tp, tk, dt=torch.bfloat16):
+    xd = x.to(DEV, dt)
+    got = _np(S.to_probs(xd, T, tp, tk))
+    infos = []
+    want = O.to_probs(_np(xd), T, tp, tk, infos=infos)
+    for r in range(x.shape[0]):
+        if infos[r].topp_margin < EPS:
+            continue
+        np.testing.assert_array_equal(got[r] > 0, want[r] > 0, err_msg=f"row {r}")
+        np.testing.assert_allclose(got[r], want[r], rtol=PREL, atol=0, err_msg=f"row {r}")
+
+
+def test_odd_vocab_unaligned_rows():
+    g = torch.Generator().manual_seed(1)
+    x = W.zipf_logits(6, 5003, g)                     # rows start off 16-byte boundaries
+    _to_probs_case(x, 0.8, 0.9, 0)
+    _to_probs_case(x, 1.0, 1.0, 17)
+
+
+def test_counter_overflow_many_equal_values():
+    """>65535 equal logits (e.g. masked vocabulary) take the wrap-logging path."""
+    g = torch.Generator().manual_seed(2)
+    V = 150000
+    x = torch.full((3, V), -30.0)
+    x[:, :2000] = torch.randn(3, 2000, generator=g) * 2
+    x[1, 5000:] = -0.0
+    x[1, 2000:5000] = 0.0
+    _to_probs_case(x, 1.0, 0.95, 0)
+    _to_probs_case(x, 0.7, 0.5, 100)
+
+
+def test_signed_zero_is_one_tie_class():
+    V = 8192
+    x = torch.zeros(2, V)
+    x[:, ::2] = -0.0
+    x[0, 7] = 3.0
+    _to_probs_case(x, 1.0, 0.5, 0)
+
+
+def test_fp16_logits():
+    g = torch.Generator().manual_seed(4)
+    x = W.zipf_logits(4, 32000, g)
+    _to_probs_case(x, 0.7, 0.9, 0, dt=torch.float16)
+
+
+def test_boundary_tie_class_index_order():
+    """Many equal values at the nucleus edge: kept members are the lowest indices."""
+    V = 10000
+    x = torch.full((1, V), 1.0)
+    x[0, 100] = 8.0
+    _to_probs_case(x, 1.0, 0.5, 0)
+    p = _np(S.to_probs(x.to(DEV, torch.bfloat16), 1.0, 0.5))[0]
+    kept = np.nonzero(p[np.arange(V) != 100] > 0)[0]
+    assert kept.size > 0 and kept.max() == kept.size - 1 + (kept.max() >= 100)
+
+
+# ---------------------------------------------------------------------------
+# draft step and the fp32-probability utilities
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("T,tp,tk,V", [(0.7, 0.9, 0, 151936), (1.0, 1.0, 0, 32), (0.0, 1.0, 0, 4096),
+                                       (1.2, 0.95, 50, 32000)])
+def test_draft_sample_parity(T, tp, tk, V):
+    g = torch.Generator().manual_seed(5)
+    x = W.zipf_logits(16, V, g).to(DEV, torch.bfloat16 if V > 32 else torch.float32)
+    u = torch.rand(16, generator=g).to(DEV)
+    xk, qk = S.draft_sample(x, u, T, tp, tk)
+    xo, qo, d = O.draft_sample(_np(x), _np(u), T, tp, tk, return_details=True)
+    ok = (d["cdf_margin"] > EPS) & (d["topp_margin"] > EPS)
+    assert ok.mean() > 0.8
+    np.testing.assert_array_equal(xk.cpu().numpy()[ok], xo[ok])
+    np.testing.assert_allclose(qk.cpu().numpy()[ok], qo[ok], rtol=2e-6)
+
+
+def test_prob_utilities():
+    z = np.load(GOLDEN / "residual.npz")
+    p = torch.from_numpy(z["p"]).to(DEV)
+    q = torch.from_numpy(z["q"]).to(DEV)
+    np.testing.assert_allclose(_np(S.residual_probs(p, q)), z["r"], rtol=1e-6, atol=1e-9)
+    ids = torch.from_numpy(z["ids"]).to(DEV)
+    np.testing.assert_array_equal(_np(S.gather_prob(p, ids)), z["gathered"])
+    u = torch.rand(p.shape[0], generator=torch.Generator().manual_seed(0)).to(DEV)
+    np.testing.assert_array_equal(S.sample_from_probs(p, u=u).cpu().numpy(),
+                                  O.sample_inverse_cdf(z["p"], _np(u)))
+
+
+def test_cpu_tensors_are_rejected():
+    with pytest.raises(RuntimeError):
+        S.to_probs(torch.randn(2, 8), 1.0)
+
+
+# ---------------------------------------------------------------------------
+# gate G1 part A on the kernels: the rule reproduces p; broken rules do not
+# ---------------------------------------------------------------------------
+def _tv(a, b):
+    return 0.5 * float(np.abs(a - b).sum())
+
+
+def test_rejection_rule_is_lossless():
+    V, N = 16, 200_000
+    g = torch.Generator().manual_seed(0)
+    lp = torch.randn(1, V, generator=g) * 1.5
+    lq = torch.randn(1, V, generator=g) * 1.5
+    for (tp, lq_use) in ((1.0, lq), (0.9, lp + torch.randn(1, V, generator=g) * 0.8)):
+        p = O.to_probs(lp.numpy(), 1.0, tp)[0]
+        tgt = torch.cat([lp, lp]).unsqueeze(0).expand(N, 2, V).contiguous().to(DEV)
+        drf = lq_use.unsqueeze(0).expand(N, 1, V).contiguous().to(DEV)
+        gd = torch.Generator(device=DEV).manual_seed(7)
+        x, _ = S.draft_sample(drf[:, 0], torch.rand(N, generator=gd, device=DEV), 1.0, tp)
+        ua = torch.rand(N, 1, generator=gd, device=DEV)
+        ur = torch.rand(N, generator=gd, device=DEV)
+        n, y = S.verify_sample(tgt, drf, x.view(N, 1), ua, ur, 1.0, tp)
+        first = torch.where(n == 1, x, y).cpu().numpy()
+        emp = np.bincount(first, minlength=V) / N
+        assert _tv(emp, p) < 0.01, f"top_p={tp}: TV={_tv(emp, p):.4f}"
+        # negative control: skipping the accept test emits x ~ q
+        bad = np.bincount(x.cpu().numpy(), minlength=V) / N
+        if tp == 1.0:
+            assert _tv(bad, p) > 0.02
