@@ -116,7 +116,7 @@ __device__ __forceinline__ uint32_t hist_field(const HistSmem& s, uint32_t raw) 
 
 __device__ __forceinline__ uint32_t hist_count(const HistSmem& s, uint32_t raw) {
   uint32_t c = hist_field(s, raw);
-  const int n = s.ncorr;
+  const int n = min(s.ncorr, NCORR_MAX);
   for (int i = 0; i < n; ++i)
     if (s.corr_raw[i] == raw) c += s.corr_add[i];
   return c;
