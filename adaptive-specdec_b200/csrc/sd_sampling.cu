@@ -128,6 +128,19 @@ __device__ __forceinline__ void corr_log(HistSmem& s, uint32_t raw, int add) {
   else s.corr_full = 1;
 }
 
+// -0 (raw 0x8000) joins +0 (raw 0x0000): its counter and any wrap corrections
+// logged against it move to +0, so equal values form one tie class.
+__device__ void merge_signed_zero(HistSmem& s) {
+  const uint32_t fneg0 = hist_field(s, 0x8000u);
+  if (fneg0) {
+    s.hist[0x4000] &= 0xFFFF0000u;
+    corr_log(s, 0u, (int)fneg0);
+  }
+  const int n = min(s.ncorr, NCORR_MAX);
+  for (int i = 0; i < n; ++i)
+    if (s.corr_raw[i] == 0x8000u) s.corr_raw[i] = 0u;
+}
+
 template <bool CHECKED>
 __device__ __forceinline__ void hist_add(HistSmem& s, uint32_t raw) {
   const uint32_t inc = 1u << ((raw & 1u) << 4);
@@ -239,6 +252,8 @@ struct HistParams {
   float T, top_p;
   int top_k;
   VecStats* stats;
+  int* zero_ctr;       // completion counters of the kernel that follows; zeroed here
+  int n_ctr;
 };
 
 __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
@@ -250,6 +265,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
   const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
   const float tp32 = P.top_p;
 
+  for (int i = blockIdx.x * HT + t; i < P.n_ctr; i += gridDim.x * HT) P.zero_ctr[i] = 0;
   hist_clear(s);
   __syncthreads();
 
@@ -263,10 +279,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
     __syncthreads();
     uint32_t total, maxkey;
     // -0 joins +0 (one tie class per value)
-    if (t == 0) {
-      const uint32_t fneg0 = hist_field(s, 0x8000u);
-      if (fneg0) { s.hist[0x4000] &= 0xFFFF0000u; corr_log(s, 0u, (int)fneg0); }
-    }
+    if (t == 0) merge_signed_zero(s);
     __syncthreads();
     hist_pass_a(s, &total, &maxkey);
     int flags = 0;
@@ -280,10 +293,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
         __syncthreads();
         hist_build<true>(s, x, V);
         __syncthreads();
-        if (t == 0) {
-          const uint32_t fneg0 = hist_field(s, 0x8000u);
-          if (fneg0) { s.hist[0x4000] &= 0xFFFF0000u; corr_log(s, 0u, (int)fneg0); }
-        }
+        if (t == 0) merge_signed_zero(s);
         __syncthreads();
         hist_pass_a(s, &total, &maxkey);
         flags |= 1;
@@ -534,6 +544,8 @@ struct SmallParams {
   int top_k;
   VecStats* stats;
   float* mat;          // [nvec, V]
+  int* zero_ctr;
+  int n_ctr;
 };
 
 __global__ void __launch_bounds__(ST) small_stats_kernel(SmallParams P) {
@@ -542,6 +554,7 @@ __global__ void __launch_bounds__(ST) small_stats_kernel(SmallParams P) {
   __shared__ double dred[40];
   __shared__ float fred[40];
   const int v = blockIdx.x, t = threadIdx.x, V = P.V;
+  for (int i = v * ST + t; i < P.n_ctr; i += gridDim.x * ST) P.zero_ctr[i] = 0;
   int set, row, pos;
   vec_locate(P.vs, v, &set, &row, &pos);
   const void* x = vec_ptr(P.vs, set, row, pos, P.dtype);
@@ -1038,16 +1051,26 @@ static int run_stats(const VecSet& vs, int nvec, int dtype, int V, float T, floa
     SmallParams P;
     P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec; P.T = T; P.top_p = top_p;
     P.top_k = top_k; P.stats = stats; P.mat = reinterpret_cast<float*>(ws + L.mat);
+    P.zero_ctr = reinterpret_cast<int*>(ws + L.counter); P.n_ctr = vs.nrows;
     small_stats_kernel<<<nvec, ST, 0, st>>>(P);
     return check_launch();
   }
   HistParams P;
   P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec; P.T = T; P.top_p = top_p;
   P.top_k = top_k; P.stats = stats;
+  P.zero_ctr = reinterpret_cast<int*>(ws + L.counter); P.n_ctr = vs.nrows;
   const int nsm = device_sms();
   const int grid = nvec < nsm ? nvec : nsm;
   hist_stats_kernel<<<grid, HT, sizeof(HistSmem), st>>>(P);
   return check_launch();
+}
+
+// Completion counters live at shape-dependent offsets, so every call zeroes
+// the ones it uses before its first kernel increments them.
+static int zero_argmax_counters(const WsLayout& L, int nvec, int nrows, char* ws, cudaStream_t st) {
+  if (cudaMemsetAsync(ws + L.vcounter, 0, (size_t)nvec * sizeof(int), st) != cudaSuccess) return 1;
+  if (cudaMemsetAsync(ws + L.rcounter, 0, (size_t)nrows * sizeof(int), st) != cudaSuccess) return 1;
+  return 0;
 }
 
 static int validate_common(int dtype, int V, float T) {
@@ -1099,6 +1122,7 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
     P.stats = reinterpret_cast<VecStats*>(ws + L.stats);
     P.k = k; P.xs = xs; P.xs_bs = xs_bs; P.u_acc = u_acc; P.u_bs = u_bs; P.alive = alive;
     P.n_acc = n_acc; P.y = y; P.px = px; P.qx = qx;
+    if (zero_argmax_counters(L, nvec, B, ws, st)) return SD_ELAUNCH;
     argmax_kernel<<<P.nch * nvec, FT, 0, st>>>(P);
     return check_launch();
   }
@@ -1152,6 +1176,7 @@ int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, in
     P.stats = reinterpret_cast<VecStats*>(ws + L.stats);
     P.k = 0; P.xs = nullptr; P.xs_bs = 0; P.u_acc = nullptr; P.u_bs = 0; P.alive = nullptr;
     P.n_acc = nullptr; P.y = x; P.px = nullptr; P.qx = qx;
+    if (zero_argmax_counters(L, B, B, ws, st)) return SD_ELAUNCH;
     argmax_kernel<<<P.nch * B, FT, 0, st>>>(P);
     return check_launch();
   }
@@ -1207,6 +1232,7 @@ int sd_to_probs(const void* logits, int64_t row_stride, int dtype, int n_rows, i
     A.k = -1;   // stats only: per-row decision skipped (npos 1 row counter reaches 0 -> k<0)
     A.xs = nullptr; A.xs_bs = 0; A.u_acc = nullptr; A.u_bs = 0; A.alive = nullptr;
     A.n_acc = nullptr; A.y = nullptr; A.px = nullptr; A.qx = nullptr;
+    if (zero_argmax_counters(L, n_rows, n_rows, ws, st)) return SD_ELAUNCH;
     argmax_kernel<<<A.nch * n_rows, FT, 0, st>>>(A);
     if ((rc = check_launch())) return rc;
   } else {

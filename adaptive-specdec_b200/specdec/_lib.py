@@ -101,10 +101,11 @@ def dtype_code(dt):
 
 
 class _Workspaces:
-    """Per (device, stream) zero-initialised scratch, grown on demand.
+    """Per (device, stream) scratch, grown on demand.
 
-    The kernels leave their counters at zero when they finish, so a workspace
-    is reusable by later calls on the same stream without clearing.
+    Each call zeroes the completion counters it uses, so a workspace is
+    reusable by any later call on the same stream; one per stream keeps calls
+    on different streams from overlapping in the same scratch.
     """
 
     def __init__(self):

@@ -71,10 +71,19 @@ def verify_attention(q, k_cache, v_cache, lengths, valid=None, scale=None, out=N
 def hf_attention(module, query, key, value, attention_mask, dropout=0.0, scaling=None, **kwargs):
     """transformers AttentionInterface function for RaggedCache buffers."""
     cache = getattr(key, "_sd_cache", None)
-    if cache is None:
-        raise L.SpecdecError("attn_implementation='specdec_b200' needs a RaggedCache created with "
-                             "attn_impl='specdec_b200'")
-    out = verify_attention(query, key, value, cache.lengths, valid=cache.valid, scale=scaling)
+    if cache is not None:
+        out = verify_attention(query, key, value, cache.lengths, valid=cache.valid, scale=scaling)
+        return out, None
+    # a forward without a RaggedCache: causal self-attention over the given
+    # K/V, i.e. the same kernel with every row starting at length 0
+    if attention_mask is not None and attention_mask.dim() == 4 and not bool(
+            (attention_mask == 0).all()):
+        raise L.SpecdecError("specdec_b200 attention without a RaggedCache supports plain "
+                             "causal masks only")
+    if key.shape[2] != query.shape[2]:
+        raise L.SpecdecError("specdec_b200 attention without a RaggedCache needs q_len == kv_len")
+    lens = torch.zeros(query.shape[0], dtype=torch.long, device=query.device)
+    out = verify_attention(query, key.contiguous(), value.contiguous(), lens, scale=scaling)
     return out, None
 
 

@@ -42,8 +42,10 @@ extern "C" {
 int sd_version(void);
 
 /* Workspace bytes needed by sd_verify_sample / sd_draft_sample / sd_to_probs
- * for n_vec logits vectors of width V split over n_rows rows.  The first use
- * of a workspace must see it zeroed; the kernels leave it reusable. */
+ * for n_vec logits vectors of width V split over n_rows rows.  A workspace
+ * needs no initialisation (each call zeroes the counters it uses) and may be
+ * reused by later calls on the same stream; calls that overlap on the GPU
+ * need separate workspaces. */
 size_t sd_sampling_workspace_bytes(int n_rows, int n_vec, int V, int dtype);
 
 /*

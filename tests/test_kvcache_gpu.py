@@ -60,8 +60,13 @@ def test_commit_and_device_errors():
     with pytest.raises(RuntimeError):
         c.check_errors()
     assert c.lengths.tolist() == [11, 25, 33, 44]
+    c.advance(30)                                              # beyond capacity: refused
     with pytest.raises(RuntimeError):
-        c.advance(30)                                          # beyond capacity
+        c.check_errors()
+    assert c.lengths.tolist() == [11, 25, 33, 44]
+    c.set_lengths([60, 0, 0, 0])
+    with pytest.raises(RuntimeError):
+        c.advance(5)                                           # host-known: raises at once
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
