@@ -31,7 +31,6 @@
 
 namespace sd {
 
-constexpr int HT = 512;                 // threads of the histogram stats kernel
 constexpr int HIST_WORDS = 32768;       // 65536 16-bit counters
 constexpr int NGROUP = 8192;            // key groups of 8 keys
 constexpr int NCORR_MAX = 96;           // counter-wrap corrections per vector
@@ -88,17 +87,39 @@ __device__ __forceinline__ int64_t vec_probe(const VecSet& vs, int set, int row,
 }
 
 // ---------------------------------------------------------------------------
-// histogram stats kernel (bf16 / fp16)
+// histogram stats kernel (bf16 / fp16): persistent, TMA ring, producer warp
 // ---------------------------------------------------------------------------
+// Per vector the consumer warps see every element once (from a shared-memory
+// ring filled by cp.async.bulk).  Elements within A_top base-2 units of the
+// running maximum ("top" elements) are counted exactly in a 65,536-bin
+// histogram of their 16-bit patterns; everything lower ("bulk") can never
+// reach the top-p boundary nor the top-k threshold checked below, and only
+// its softmax mass is needed: it is summed with ex2.approx relative to the
+// thread's running maximum (its share of S is <= V * 2^-A_top, so the
+// approximation moves S by < 4e-8 relative).  The exact per-class quantities
+// (S of the top classes, top-k key, top-p boundary class and how many of its
+// members are kept) are then computed per distinct value.  Any case the
+// window cannot decide (a top-k threshold below the window, a boundary not
+// found, a 16-bit counter wrap) rebuilds that vector's histogram with every
+// element counted, reading it again from global memory.
+constexpr int NCW = 16;                  // consumer warps
+constexpr int CT = NCW * 32;             // consumer threads
+constexpr int HT = CT + 32;              // + one producer warp
+constexpr int SLOT = 16384;              // bytes per ring slot
+constexpr int NSLOT = 4;
+constexpr long long WAIT_CYCLES = 1LL << 32;   // ~2 s at 2 GHz: bound on every wait
+
 struct HistSmem {
-  uint32_t hist[HIST_WORDS];           // 128 KB
+  uint32_t hist[HIST_WORDS];           // 128 KB: two 16-bit counters per word
+  alignas(128) unsigned char ring[NSLOT][SLOT];
   uint16_t list[NGROUP];               // populated key groups, descending key order
-  uint32_t segc[HT];                   // count per 128-key segment (segment t)
-  uint16_t occ[HT];                    // populated-group mask per segment
+  uint16_t occ[CT];                    // populated-group mask per 128-key segment
   uint32_t corr_raw[NCORR_MAX];
   int32_t corr_add[NCORR_MAX];
   double dred[40];
   uint32_t ured[40];
+  alignas(8) unsigned long long full[NSLOT];
+  alignas(8) unsigned long long empty[NSLOT];
   int ncorr;
   int corr_full;
   uint32_t keyk16;     // top-k threshold key (16-bit), 0 if inactive
@@ -108,6 +129,108 @@ struct HistSmem {
   double z;            // kept mass
   int32_t idx_cut;
   int found_cut;
+  int abort_flag;
+  int need_full;
+};
+
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
+template <typename T>
+__device__ __forceinline__ T c_sum(T v, T* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  v = warp_sum(v);
+  cbar();
+  if (lane == 0) red[wid] = v;
+  cbar();
+  T t = lane < NCW ? red[lane] : T(0);
+  return warp_sum(t);
+}
+
+template <typename T>
+__device__ __forceinline__ T c_max(T v, T* red, T lowest) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  v = warp_max(v);
+  cbar();
+  if (lane == 0) red[wid] = v;
+  cbar();
+  T t = lane < NCW ? red[lane] : lowest;
+  return warp_max(t);
+}
+
+template <typename T>
+__device__ __forceinline__ T c_excl_scan(T v, T* red, T* total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  T inc = warp_incl_scan(v);
+  cbar();
+  if (lane == 31) red[wid] = inc;
+  cbar();
+  if (wid == 0) {
+    T w = lane < NCW ? red[lane] : T(0);
+    T wi = warp_incl_scan(w);
+    if (lane < NCW) red[lane] = wi - w;
+    if (lane == NCW - 1) red[32] = wi;
+  }
+  cbar();
+  *total = red[32];
+  return red[wid] + inc - v;
+}
+
+// ---- mbarrier / bulk-copy primitives --------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+               :: "r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+// Bounded wait for the phase of parity `parity` to complete.  Returns false
+// (and raises the CTA's abort flag) after WAIT_CYCLES or when another thread
+// already aborted.
+__device__ __forceinline__ bool mbar_wait(unsigned long long* b, uint32_t parity, int* abort_flag) {
+  const uint32_t a = smem_u32(b);
+  const long long t0 = clock64();
+  for (;;) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}" : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+    if (ok) return true;
+    if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
+    if (clock64() - t0 > WAIT_CYCLES) {
+      *reinterpret_cast<volatile int*>(abort_flag) = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         unsigned long long* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Vector geometry shared by producer and consumers: ragged head elements up to
+// the first 16-byte boundary, a body of whole 16-byte units split into ring
+// chunks, ragged tail elements.
+struct VecGeom {
+  int head, nunits, tail0, nchunk;
+  __device__ VecGeom(const void* p, int V) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    head = (int)(((16u - (uint32_t)(a & 15u)) & 15u) >> 1);
+    if (head > V) head = V;
+    nunits = (V - head) >> 3;
+    tail0 = head + (nunits << 3);
+    nchunk = (nunits * 16 + SLOT - 1) / SLOT;
+  }
 };
 
 __device__ __forceinline__ uint32_t hist_field(const HistSmem& s, uint32_t raw) {
@@ -160,52 +283,56 @@ __device__ __forceinline__ void hist_add(HistSmem& s, uint32_t raw) {
   }
 }
 
-template <bool CHECKED>
-__device__ void hist_build(HistSmem& s, const uint16_t* p, int V) {
-  const int t = threadIdx.x;
-  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-  int head = (int)(((16u - (uint32_t)(a & 15u)) & 15u) >> 1);
-  if (head > V) head = V;
-  const int nb = (V - head) >> 3;
-  const int tail0 = head + (nb << 3);
-  const uint4* body = reinterpret_cast<const uint4*>(p + head);
-  constexpr int U = 8;
-  int u = t;
-  for (; u + (U - 1) * HT < nb; u += U * HT) {
-    uint4 w[U];
+// Exact build of every element from global memory (the fallback path).
+__device__ void hist_build_all(HistSmem& s, const uint16_t* p, int V) {
+  for (int j = threadIdx.x; j < V; j += CT) hist_add<true>(s, __ldg(p + j));
+}
+
+// Per-thread streaming state of one vector.
+struct Stream {
+  float m;        // running max (logit units)
+  float mc;       // m * c2
+  float thr;      // m - wtop
+  double bulk;    // sum of 2^((x - m) c2) over bulk elements, relative to m
+  uint32_t ntop;  // elements counted in the histogram
+};
+
+__device__ __forceinline__ void stream_group(HistSmem& s, Stream& st, const uint32_t* w, int n,
+                                             int dtype, float c2, float wtop) {
+  float x[8];
+  uint32_t r[8];
 #pragma unroll
-    for (int i = 0; i < U; ++i) w[i] = __ldg(body + u + i * HT);
+  for (int q = 0; q < 4; ++q) {
+    r[2 * q] = w[q] & 0xFFFFu;
+    r[2 * q + 1] = w[q] >> 16;
+  }
 #pragma unroll
-    for (int i = 0; i < U; ++i) {
-      hist_add<CHECKED>(s, w[i].x & 0xFFFFu); hist_add<CHECKED>(s, w[i].x >> 16);
-      hist_add<CHECKED>(s, w[i].y & 0xFFFFu); hist_add<CHECKED>(s, w[i].y >> 16);
-      hist_add<CHECKED>(s, w[i].z & 0xFFFFu); hist_add<CHECKED>(s, w[i].z >> 16);
-      hist_add<CHECKED>(s, w[i].w & 0xFFFFu); hist_add<CHECKED>(s, w[i].w >> 16);
+  for (int e = 0; e < 8; ++e) x[e] = (e < n) ? bits16_to_float(r[e], dtype) : -INFINITY;
+  float gm = x[0];
+#pragma unroll
+  for (int e = 1; e < 8; ++e) gm = fmaxf(gm, x[e]);
+  if (gm > st.m) {
+    if (st.bulk != 0.0) st.bulk *= (double)ex2_approx((st.m - gm) * c2);
+    st.m = gm;
+    st.mc = gm * c2;
+    st.thr = gm - wtop;
+  }
+  float gs = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    if (e < n) {
+      if (x[e] >= st.thr) {
+        hist_add<false>(s, r[e]);
+        ++st.ntop;
+      } else {
+        gs += ex2_approx(fmaf(x[e], c2, -st.mc));
+      }
     }
   }
-  for (; u < nb; u += HT) {
-    const uint4 w = __ldg(body + u);
-    hist_add<CHECKED>(s, w.x & 0xFFFFu); hist_add<CHECKED>(s, w.x >> 16);
-    hist_add<CHECKED>(s, w.y & 0xFFFFu); hist_add<CHECKED>(s, w.y >> 16);
-    hist_add<CHECKED>(s, w.z & 0xFFFFu); hist_add<CHECKED>(s, w.z >> 16);
-    hist_add<CHECKED>(s, w.w & 0xFFFFu); hist_add<CHECKED>(s, w.w >> 16);
-  }
-  // ragged head / tail elements
-  const int nrag = head + (V - tail0);
-  for (int i = t; i < nrag; i += HT) {
-    const int j = i < head ? i : tail0 + (i - head);
-    hist_add<CHECKED>(s, __ldg(reinterpret_cast<const unsigned short*>(p) + j));
-  }
+  st.bulk += (double)gs;
 }
 
-__device__ void hist_clear(HistSmem& s) {
-  uint4* h = reinterpret_cast<uint4*>(s.hist);
-  for (int i = threadIdx.x; i < HIST_WORDS / 4; i += HT) h[i] = make_uint4(0, 0, 0, 0);
-  if (threadIdx.x == 0) { s.ncorr = 0; s.corr_full = 0; }
-}
-
-// Pass A: thread t owns segment t = key groups [16t, 16t+16) = keys [128t, 128t+128).
-// Returns the total count (fields only) and writes segc / occ; block-reduces max key.
+// Pass A: consumer thread t owns segment t = key groups [16t, 16t+16).
 __device__ void hist_pass_a(HistSmem& s, uint32_t* total_out, uint32_t* maxkey_out) {
   const int t = threadIdx.x;
   uint32_t cnt = 0, occ = 0, kmax = 0;
@@ -214,9 +341,8 @@ __device__ void hist_pass_a(HistSmem& s, uint32_t* total_out, uint32_t* maxkey_o
   for (int jj = 0; jj < 16; ++jj) {
     const int j = (jj + t) & 15;                 // bank-conflict-free order
     const uint32_t G = 16u * t + j;
-    uint32_t wo;
     const bool pos = G >= 4096u;
-    wo = pos ? 4u * (G - 4096u) : 0x7FFCu - 4u * G;
+    const uint32_t wo = pos ? 4u * (G - 4096u) : 0x7FFCu - 4u * G;
     const uint4 w = *reinterpret_cast<const uint4*>(&s.hist[wo]);
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
     uint32_t gsum = 0;
@@ -231,19 +357,15 @@ __device__ void hist_pass_a(HistSmem& s, uint32_t* total_out, uint32_t* maxkey_o
     cnt += gsum;
     if (gsum) {
       occ |= 1u << j;
-      // highest key of the group: positive -> highest raw; negative -> lowest raw
       const uint32_t raw = 2u * wo + (pos ? (uint32_t)hi_idx : (uint32_t)lo_idx);
       const uint32_t key = key16(raw);
       kmax = any ? max(kmax, key) : key;
       any = true;
     }
   }
-  s.segc[t] = cnt;
   s.occ[t] = (uint16_t)occ;
-  const uint32_t tot = block_sum<uint32_t>(cnt, s.ured);
-  const uint32_t km = block_max<uint32_t>(any ? kmax : 0u, s.ured, 0u);
-  *total_out = tot;
-  *maxkey_out = km;
+  *total_out = c_sum<uint32_t>(cnt, s.ured);
+  *maxkey_out = c_max<uint32_t>(any ? kmax : 0u, s.ured, 0u);
 }
 
 struct HistParams {
@@ -254,283 +376,405 @@ struct HistParams {
   VecStats* stats;
   int* zero_ctr;       // completion counters of the kernel that follows; zeroed here
   int n_ctr;
+  int* status;         // device status word: bit0 = a bounded wait timed out
 };
 
-__global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  HistSmem& s = *reinterpret_cast<HistSmem*>(smem_raw);
+// Everything after the histogram of one vector is built: exact per-class
+// quantities, the probe, and the stats record.  Returns true when the vector
+// must be rebuilt with every element counted.
+__device__ bool finalize_vector(HistSmem& s, const HistParams& P, const Stream& st, int v,
+                                const uint16_t* x, int64_t probe, float c2, float wtop,
+                                bool windowed, int flags) {
   const int t = threadIdx.x;
   const int V = P.V;
   const bool topk_on = P.top_k > 0 && P.top_k < V;
   const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
   const float tp32 = P.top_p;
 
+  if (t == 0) merge_signed_zero(s);
+  cbar();
+  uint32_t total, maxkey;
+  hist_pass_a(s, &total, &maxkey);
+  const uint32_t ntop = c_sum<uint32_t>(st.ntop, s.ured);
+  uint32_t csum = 0;
+  for (int i = 0; i < min(s.ncorr, NCORR_MAX); ++i) csum += (uint32_t)s.corr_add[i];
+  if (total + csum != ntop || s.corr_full) {
+    if (windowed) return true;          // a 16-bit counter wrapped: rebuild with wrap logging
+    flags |= 2;                         // rebuild itself overflowed its table: counts inexact
+  }
+  cbar();
+  if (t == 0) {
+    const int n = min(s.ncorr, NCORR_MAX);
+    for (int i = 0; i < n; ++i) {
+      const uint32_t key = key16(s.corr_raw[i]);
+      const uint32_t G = key >> 3;
+      s.occ[G >> 4] |= (uint16_t)(1u << (G & 15u));
+      if (s.corr_add[i] > 0 && key > maxkey) maxkey = key;
+    }
+    s.ured[34] = maxkey;
+  }
+  cbar();
+  maxkey = s.ured[34];
+  const float M = bits16_to_float(raw16(maxkey), P.dtype);
+  const float m = scaled_logit(M, P.T);
+  // classes with value >= M - wtop hold every occurrence; lower classes may
+  // have members in the bulk sum
+  const float wlow = windowed ? M - wtop : -INFINITY;
+
+  // bulk mass relative to M (exp of the running-max offsets)
+  double sb = 0.0;
+  if (windowed && st.bulk > 0.0 && st.m > -INFINITY)
+    sb = st.bulk * (double)exp2f((st.m - M) * c2);
+  const double S_bulk = c_sum<double>(sb, s.dred);
+
+  // populated groups in descending key order: thread t handles segment CT-1-t
+  {
+    const int seg = CT - 1 - t;
+    const uint32_t o = s.occ[seg];
+    uint32_t tot;
+    uint32_t off = c_excl_scan<uint32_t>(__popc(o), s.ured, &tot);
+    for (int j = 15; j >= 0; --j)
+      if (o & (1u << j)) s.list[off++] = (uint16_t)(16 * seg + j);
+    cbar();
+    if (t == 0) s.ured[35] = tot;
+    cbar();
+  }
+  const int nlist = (int)s.ured[35];
+  const int per = (nlist + CT - 1) / CT;
+  const int l0 = min(nlist, t * per), l1 = min(nlist, l0 + per);
+
+  // top-k threshold (by counts, descending keys)
+  uint32_t keyk = 0;
+  if (topk_on) {
+    uint32_t c = 0;
+    for (int l = l0; l < l1; ++l) {
+      const uint32_t G = s.list[l];
+      for (int q = 7; q >= 0; --q) c += hist_count(s, raw16(8 * G + q));
+    }
+    uint32_t tot;
+    const uint32_t pre = c_excl_scan<uint32_t>(c, s.ured, &tot);
+    if (t == 0) s.keyk16 = 0xFFFFFFFFu;
+    cbar();
+    if (pre < (uint32_t)P.top_k && pre + c >= (uint32_t)P.top_k) {
+      uint32_t run = pre;
+      for (int l = l0; l < l1 && run < (uint32_t)P.top_k; ++l) {
+        const uint32_t G = s.list[l];
+        for (int q = 7; q >= 0; --q) {
+          const uint32_t key = 8 * G + q;
+          run += hist_count(s, raw16(key));
+          if (run >= (uint32_t)P.top_k) { s.keyk16 = key; break; }
+        }
+      }
+    }
+    cbar();
+    keyk = s.keyk16;
+    // the k-th value must be a complete class of the window
+    if (keyk == 0xFFFFFFFFu || bits16_to_float(raw16(keyk), P.dtype) < wlow) return true;
+  }
+
+  // softmax normaliser S: exact over the histogram, plus the bulk
+  double es = 0.0;
+  for (int l = l0; l < l1; ++l) {
+    const uint32_t G = s.list[l];
+    for (int q = 7; q >= 0; --q) {
+      const uint32_t raw = raw16(8 * G + q);
+      const uint32_t c = hist_count(s, raw);
+      if (c) es += (double)c * (double)softmax_num(bits16_to_float(raw, P.dtype), P.T, m);
+    }
+  }
+  const double S = c_sum<double>(es, s.dred) + S_bulk;
+  const float inv_s = __double2float_rn(1.0 / S);
+
+  // kept mass (keys >= keyk) per thread, in p units
+  double pm = 0.0;
+  for (int l = l0; l < l1; ++l) {
+    const uint32_t G = s.list[l];
+    for (int q = 7; q >= 0; --q) {
+      const uint32_t key = 8 * G + q;
+      if (key < keyk) continue;
+      const uint32_t raw = raw16(key);
+      const uint32_t c = hist_count(s, raw);
+      if (c) pm += (double)c * (double)prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
+    }
+  }
+  double z;
+  if (!topp_on) {
+    z = c_sum<double>(pm, s.dred);
+    if (!topk_on) z += S_bulk * (double)inv_s;
+    if (t == 0) { s.vstar16 = 0xFFFFFFFFu; s.n_keep = 0; }
+  } else {
+    double ptot;
+    const double pre = c_excl_scan<double>(pm, s.dred, &ptot);
+    if (t == 0) { s.vstar16 = 0xFFFFFFFFu; s.ured[36] = 0; }
+    cbar();
+    // every thread whose range may hold the first class whose last member is
+    // dropped reports that class; the highest such key is the boundary
+    if (l0 < l1 && pre + pm >= (double)tp32 - 1e-9) {
+      double C = pre;
+      bool done = false;
+      for (int l = l0; l < l1 && !done; ++l) {
+        const uint32_t G = s.list[l];
+        for (int q = 7; q >= 0; --q) {
+          const uint32_t key = 8 * G + q;
+          if (key < keyk) { done = true; break; }
+          const uint32_t raw = raw16(key);
+          const uint32_t c = hist_count(s, raw);
+          if (!c) continue;
+          const float p = prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
+          const float cl = __fsub_rn(__double2float_rn(C + (double)c * (double)p), p);
+          if (!(cl < tp32)) { atomicMax(&s.ured[36], key + 1u); done = true; break; }
+          C += (double)c * (double)p;
+        }
+      }
+    }
+    cbar();
+    const uint32_t vk1 = s.ured[36];
+    if (vk1 == 0u && windowed && S_bulk > 0.0) return true;  // boundary below the window
+    if (vk1 != 0u && l0 < l1) {
+      const uint32_t vkey = vk1 - 1u;
+      const uint32_t Gv = vkey >> 3;
+      bool mine = false;
+      for (int l = l0; l < l1; ++l) mine |= (s.list[l] == Gv);
+      if (mine) {
+        double C = pre;
+        for (int l = l0; l < l1; ++l) {
+          const uint32_t G = s.list[l];
+          for (int q = 7; q >= 0; --q) {
+            const uint32_t key = 8 * G + q;
+            const uint32_t raw = raw16(key);
+            const uint32_t c = key >= keyk ? hist_count(s, raw) : 0u;
+            if (!c) continue;
+            const float p = prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
+            if (key == vkey) {
+              int lo = 0, hi = (int)c;   // largest n with keep(j) for all j < n
+              while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                const float cl = __fsub_rn(
+                    __double2float_rn(C + (double)(mid + 1) * (double)p), p);
+                if (cl < tp32) lo = mid + 1; else hi = mid;
+              }
+              int nk = lo;
+              if (nk == 0 && key == maxkey) nk = 1;   // the first sorted entry is always kept
+              s.vstar16 = vkey;
+              s.n_keep = nk;
+              s.vcount = (int)c;
+              s.z = C + (double)nk * (double)p;
+            }
+            C += (double)c * (double)p;
+          }
+        }
+      }
+    }
+    cbar();
+    if (s.vstar16 != 0xFFFFFFFFu &&
+        bits16_to_float(raw16(s.vstar16), P.dtype) < wlow) return true;
+    z = (s.vstar16 == 0xFFFFFFFFu) ? ptot : s.z;
+  }
+  cbar();
+  const uint32_t vstar16 = s.vstar16;
+  const float zf = fmaxf(__double2float_rn(z), 1e-12f);
+
+  // idx_cut: index of the n_keep-th member (ascending index) of the boundary class
+  int32_t idx_cut = (int32_t)NO_CUT;
+  if (vstar16 != 0xFFFFFFFFu) {
+    const int nk = s.n_keep;
+    if (nk == 0) idx_cut = -1;
+    else if (nk < s.vcount) {
+      const uint32_t r0 = raw16(vstar16);
+      const bool zero_cls = (r0 == 0u);
+      if (t == 0) s.found_cut = 0;
+      cbar();
+      uint32_t run = 0;
+      constexpr int PT = 32;
+      for (int base = 0; base < V; base += CT * PT) {
+        const int j0 = base + t * PT;
+        uint32_t c = 0;
+        for (int e = 0; e < PT; ++e) {
+          const int j = j0 + e;
+          if (j < V) {
+            const uint32_t r = __ldg(x + j);
+            c += (r == r0) || (zero_cls && r == 0x8000u);
+          }
+        }
+        uint32_t tot;
+        const uint32_t pre = c_excl_scan<uint32_t>(c, s.ured, &tot);
+        if (run + pre < (uint32_t)nk && run + pre + c >= (uint32_t)nk) {
+          uint32_t rr = run + pre;
+          for (int e = 0; e < PT; ++e) {
+            const int j = j0 + e;
+            if (j < V) {
+              const uint32_t r = __ldg(x + j);
+              if ((r == r0) || (zero_cls && r == 0x8000u)) {
+                if (++rr == (uint32_t)nk) { s.idx_cut = j; s.found_cut = 1; break; }
+              }
+            }
+          }
+        }
+        run += tot;
+        cbar();
+        if (s.found_cut) break;
+      }
+      idx_cut = s.idx_cut;
+    }
+  }
+
+  if (t == 0) {
+    VecStats o;
+    o.m = m;
+    o.inv_s = inv_s;
+    o.zf = zf;
+    o.kth = topk_on ? fkey(bits16_to_float(raw16(keyk), P.dtype)) : 0u;
+    o.vstar = vstar16 == 0xFFFFFFFFu ? 0u : fkey(bits16_to_float(raw16(vstar16), P.dtype));
+    o.idx_cut = vstar16 == 0xFFFFFFFFu ? (int32_t)NO_CUT : idx_cut;
+    o.argmax = -1;
+    o.flags = flags;
+    o.n_keep = vstar16 == 0xFFFFFFFFu ? -1 : s.n_keep;
+    o.pad[0] = o.pad[1] = 0;
+    float pp = 0.f;
+    if (probe >= 0 && probe < V) {
+      const float xv = bits16_to_float(__ldg(x + probe), P.dtype);
+      const uint32_t kx = fkey(xv);
+      const bool kept = kx >= o.kth &&
+                        (kx > o.vstar || (kx == o.vstar && probe <= (int64_t)o.idx_cut));
+      if (kept) pp = __fdiv_rn(prob_of(xv, P.T, m, inv_s), zf);
+    }
+    o.probe_p = pp;
+    P.stats[v] = o;
+  }
+  return false;
+}
+
+// Clear the groups listed as populated (and the correction table).
+__device__ void hist_clear_listed(HistSmem& s) {
+  const int nlist = (int)s.ured[35];
+  for (int l = threadIdx.x; l < nlist; l += CT) {
+    const uint32_t G = s.list[l];
+    const uint32_t wo = G >= 4096u ? 4u * (G - 4096u) : 0x7FFCu - 4u * G;
+    *reinterpret_cast<uint4*>(&s.hist[wo]) = make_uint4(0, 0, 0, 0);
+  }
+  if (threadIdx.x == 0) { s.ncorr = 0; s.corr_full = 0; }
+}
+
+__device__ void hist_clear_all(HistSmem& s) {
+  uint4* h = reinterpret_cast<uint4*>(s.hist);
+  for (int i = threadIdx.x; i < HIST_WORDS / 4; i += CT) h[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) { s.ncorr = 0; s.corr_full = 0; }
+}
+
+__global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  HistSmem& s = *reinterpret_cast<HistSmem*>(smem_raw);
+  const int t = threadIdx.x;
+  const int V = P.V;
+  const float c2 = 1.4426950408889634f / P.T;          // log2(e) / T
+  const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
+  // window (base-2 units below the running max) holding every class that can
+  // matter beyond the softmax sum
+  float a_top = 26.f;
+  if (topp_on) a_top = fmaxf(a_top, log2f(2.f * (float)V / (1.f - P.top_p)) + 1.f);
+  const float wtop = a_top / c2;
+
   for (int i = blockIdx.x * HT + t; i < P.n_ctr; i += gridDim.x * HT) P.zero_ctr[i] = 0;
-  hist_clear(s);
+  if (t < CT) hist_clear_all(s);
+  if (t == 0) {
+    for (int i = 0; i < NSLOT; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], NCW);
+    }
+    s.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   __syncthreads();
 
+  if (t >= CT) {
+    // ---------------- producer warp: stream this CTA's vectors into the ring
+    if (t == CT) {
+      uint32_t g = 0;
+      bool ok = true;
+      for (int v = blockIdx.x; v < P.nvec && ok; v += gridDim.x) {
+        int set, row, pos;
+        vec_locate(P.vs, v, &set, &row, &pos);
+        const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
+        const VecGeom gm(x, V);
+        const char* body = reinterpret_cast<const char*>(x + gm.head);
+        for (int c = 0; c < gm.nchunk; ++c, ++g) {
+          const int sl = g % NSLOT;
+          const uint32_t ph = (g / NSLOT) & 1u;
+          if (!mbar_wait(&s.empty[sl], ph ^ 1u, &s.abort_flag)) { ok = false; break; }
+          const uint32_t bytes = (uint32_t)min(SLOT, gm.nunits * 16 - c * SLOT);
+          mbar_expect_tx(&s.full[sl], bytes);
+          bulk_g2s(s.ring[sl], body + (size_t)c * SLOT, bytes, &s.full[sl]);
+        }
+      }
+      // on abort, let the copies already issued land before the CTA exits
+      if (!ok) {
+        for (uint32_t k = 0; k < NSLOT && k < g; ++k) {
+          const uint32_t gg = g - 1 - k;
+          int dummy = 0;
+          mbar_wait(&s.full[gg % NSLOT], (gg / NSLOT) & 1u, &dummy);
+        }
+        atomicOr(P.status, 1);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps
+  uint32_t g = 0;
   for (int v = blockIdx.x; v < P.nvec; v += gridDim.x) {
     int set, row, pos;
     vec_locate(P.vs, v, &set, &row, &pos);
     const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
     const int64_t probe = vec_probe(P.vs, set, row, pos);
-
-    hist_build<false>(s, x, V);
-    __syncthreads();
-    uint32_t total, maxkey;
-    // -0 joins +0 (one tie class per value)
-    if (t == 0) merge_signed_zero(s);
-    __syncthreads();
-    hist_pass_a(s, &total, &maxkey);
+    const VecGeom gm(x, V);
+    Stream st;
+    st.m = -INFINITY; st.mc = -INFINITY; st.thr = -INFINITY; st.bulk = 0.0; st.ntop = 0;
+    // ragged head / tail elements straight from global memory
+    const int nrag = gm.head + (V - gm.tail0);
+    for (int i = t; i < nrag; i += CT) {
+      const int j = i < gm.head ? i : gm.tail0 + (i - gm.head);
+      const uint32_t w[4] = {__ldg(x + j), 0u, 0u, 0u};
+      stream_group(s, st, w, 1, P.dtype, c2, wtop);
+    }
+    bool aborted = false;
+    for (int c = 0; c < gm.nchunk; ++c, ++g) {
+      const int sl = g % NSLOT;
+      if (!mbar_wait(&s.full[sl], (g / NSLOT) & 1u, &s.abort_flag)) { aborted = true; break; }
+      const int units = min(SLOT, gm.nunits * 16 - c * SLOT) >> 4;
+      const uint4* u4 = reinterpret_cast<const uint4*>(s.ring[sl]);
+      for (int u = t; u < units; u += CT) {
+        const uint4 w4 = u4[u];
+        const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+        stream_group(s, st, w, 8, P.dtype, c2, wtop);
+      }
+      __syncwarp();
+      if ((t & 31) == 0) mbar_arrive(&s.empty[sl]);
+    }
+    cbar();
+    if (aborted || s.abort_flag) {
+      if (t == 0) atomicOr(P.status, 1);
+      break;
+    }
     int flags = 0;
-    {
-      uint32_t csum = 0;
-      for (int i = 0; i < s.ncorr && i < NCORR_MAX; ++i) csum += (uint32_t)s.corr_add[i];
-      if (total + csum != (uint32_t)V) {
-        // a 16-bit counter wrapped: rebuild with wrap logging (rare: >65535 equal values)
-        __syncthreads();
-        hist_clear(s);
-        __syncthreads();
-        hist_build<true>(s, x, V);
-        __syncthreads();
-        if (t == 0) merge_signed_zero(s);
-        __syncthreads();
-        hist_pass_a(s, &total, &maxkey);
-        flags |= 1;
-      }
-    }
-    __syncthreads();
-    // fold corrections into segment counts / occupancy (all lanes see the same ncorr)
-    if (t == 0) {
-      const int n = min(s.ncorr, NCORR_MAX);
-      for (int i = 0; i < n; ++i) {
-        const uint32_t key = key16(s.corr_raw[i]);
-        const uint32_t G = key >> 3;
-        s.segc[G >> 4] += (uint32_t)s.corr_add[i];
-        s.occ[G >> 4] |= (uint16_t)(1u << (G & 15u));
-        if (s.corr_add[i] > 0 && key > maxkey) maxkey = key;
-      }
-      s.ured[34] = maxkey;
-      if (s.corr_full) flags |= 2;
-    }
-    __syncthreads();
-    maxkey = s.ured[34];
-    const float m = scaled_logit(bits16_to_float(raw16(maxkey), P.dtype), P.T);
-
-    // list of populated groups in descending key order: thread t handles segment 511-t
-    {
-      const int seg = HT - 1 - t;
-      const uint32_t o = s.occ[seg];
-      uint32_t tot;
-      uint32_t off = block_excl_scan<uint32_t>(__popc(o), s.ured, &tot);
-      for (int j = 15; j >= 0; --j)
-        if (o & (1u << j)) s.list[off++] = (uint16_t)(16 * seg + j);
-      __syncthreads();
-      if (t == 0) s.ured[35] = tot;
-      __syncthreads();
-    }
-    const int nlist = (int)s.ured[35];
-    const int per = (nlist + HT - 1) / HT;
-    const int l0 = min(nlist, t * per), l1 = min(nlist, l0 + per);
-
-    // top-k threshold (by counts, descending keys)
-    uint32_t keyk = 0;
-    if (topk_on) {
-      uint32_t c = 0;
-      for (int l = l0; l < l1; ++l) {
-        const uint32_t G = s.list[l];
-        for (int q = 7; q >= 0; --q) c += hist_count(s, raw16(8 * G + q));
-      }
-      uint32_t tot;
-      const uint32_t pre = block_excl_scan<uint32_t>(c, s.ured, &tot);
-      if (t == 0) s.keyk16 = 0;
-      __syncthreads();
-      if (pre < (uint32_t)P.top_k && pre + c >= (uint32_t)P.top_k) {
-        uint32_t run = pre;
-        for (int l = l0; l < l1 && run < (uint32_t)P.top_k; ++l) {
-          const uint32_t G = s.list[l];
-          for (int q = 7; q >= 0; --q) {
-            const uint32_t key = 8 * G + q;
-            run += hist_count(s, raw16(key));
-            if (run >= (uint32_t)P.top_k) { s.keyk16 = key; break; }
-          }
-        }
-      }
-      __syncthreads();
-      keyk = s.keyk16;
-    }
-
-    // softmax normaliser S over every element
-    double es = 0.0;
-    for (int l = l0; l < l1; ++l) {
-      const uint32_t G = s.list[l];
-      for (int q = 7; q >= 0; --q) {
-        const uint32_t raw = raw16(8 * G + q);
-        const uint32_t c = hist_count(s, raw);
-        if (c) es += (double)c * (double)softmax_num(bits16_to_float(raw, P.dtype), P.T, m);
-      }
-    }
-    const double S = block_sum<double>(es, s.dred);
-    const float inv_s = __double2float_rn(1.0 / S);
-
-    // kept mass (keys >= keyk) per thread, in p units
-    double pm = 0.0;
-    for (int l = l0; l < l1; ++l) {
-      const uint32_t G = s.list[l];
-      for (int q = 7; q >= 0; --q) {
-        const uint32_t key = 8 * G + q;
-        if (key < keyk) continue;
-        const uint32_t raw = raw16(key);
-        const uint32_t c = hist_count(s, raw);
-        if (c) pm += (double)c * (double)prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
-      }
-    }
-    double z;
-    if (!topp_on) {
-      z = block_sum<double>(pm, s.dred);
-      if (t == 0) { s.vstar16 = 0xFFFFFFFFu; s.n_keep = 0; }
+    bool redo = finalize_vector(s, P, st, v, x, probe, c2, wtop, true, flags);
+    cbar();
+    if (redo) {
+      // exact rebuild with every element counted (rare)
+      hist_clear_all(s);
+      cbar();
+      hist_build_all(s, x, V);
+      cbar();
+      Stream all;
+      all.m = -INFINITY; all.mc = -INFINITY; all.thr = -INFINITY; all.bulk = 0.0;
+      all.ntop = 0;
+      for (int j = t; j < V; j += CT) ++all.ntop;
+      finalize_vector(s, P, all, v, x, probe, c2, wtop, false, 1);
+      cbar();
+      hist_clear_all(s);
     } else {
-      double ptot;
-      const double pre = block_excl_scan<double>(pm, s.dred, &ptot);
-      if (t == 0) { s.vstar16 = 0xFFFFFFFFu; s.ured[36] = 0; }
-      __syncthreads();
-      // walk: every thread whose range may hold the first class whose last member
-      // is dropped reports that class; the highest such key is the boundary.
-      if (l0 < l1 && pre + pm >= (double)tp32 - 1e-9) {
-        double C = pre;
-        bool done = false;
-        for (int l = l0; l < l1 && !done; ++l) {
-          const uint32_t G = s.list[l];
-          for (int q = 7; q >= 0; --q) {
-            const uint32_t key = 8 * G + q;
-            if (key < keyk) { done = true; break; }
-            const uint32_t raw = raw16(key);
-            const uint32_t c = hist_count(s, raw);
-            if (!c) continue;
-            const float p = prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
-            const float cl = __fsub_rn(__double2float_rn(C + (double)c * (double)p), p);
-            if (!(cl < tp32)) { atomicMax(&s.ured[36], key + 1u); done = true; break; }
-            C += (double)c * (double)p;
-          }
-        }
-      }
-      __syncthreads();
-      const uint32_t vk1 = s.ured[36];
-      // owner of the boundary class computes how many of its members are kept
-      if (vk1 != 0u && l0 < l1) {
-        const uint32_t vkey = vk1 - 1u;
-        const uint32_t Gv = vkey >> 3;
-        bool mine = false;
-        for (int l = l0; l < l1; ++l) mine |= (s.list[l] == Gv);
-        if (mine) {
-          double C = pre;
-          for (int l = l0; l < l1; ++l) {
-            const uint32_t G = s.list[l];
-            for (int q = 7; q >= 0; --q) {
-              const uint32_t key = 8 * G + q;
-              const uint32_t raw = raw16(key);
-              const uint32_t c = key >= keyk ? hist_count(s, raw) : 0u;
-              if (!c) continue;
-              const float p = prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
-              if (key == vkey) {
-                // largest n in [0, c] with keep(j) for all j < n (keep is monotone)
-                int lo = 0, hi = (int)c;   // keep(lo-1) true, answer in [lo, hi]
-                while (lo < hi) {
-                  const int mid = (lo + hi) >> 1;   // test keep(mid)
-                  const float cl = __fsub_rn(
-                      __double2float_rn(C + (double)(mid + 1) * (double)p), p);
-                  if (cl < tp32) lo = mid + 1; else hi = mid;
-                }
-                int nk = lo;
-                if (nk == 0 && key == maxkey) nk = 1;   // the first sorted entry is always kept
-                s.vstar16 = vkey;
-                s.n_keep = nk;
-                s.vcount = (int)c;
-                s.z = C + (double)nk * (double)p;
-              }
-              C += (double)c * (double)p;
-            }
-          }
-        }
-      }
-      __syncthreads();
-      z = (s.vstar16 == 0xFFFFFFFFu) ? ptot : s.z;
+      hist_clear_listed(s);
     }
-    __syncthreads();
-    const uint32_t vstar16 = s.vstar16;
-    const float zf = fmaxf(__double2float_rn(z), 1e-12f);
-
-    // idx_cut: index of the n_keep-th member (ascending index) of the boundary class
-    int32_t idx_cut = (int32_t)NO_CUT;
-    if (vstar16 != 0xFFFFFFFFu) {
-      const int nk = s.n_keep;
-      if (nk == 0) idx_cut = -1;
-      else if (nk < s.vcount) {
-        const uint32_t r0 = raw16(vstar16);
-        const bool zero_cls = (r0 == 0u);
-        const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
-        if (t == 0) s.found_cut = 0;
-        __syncthreads();
-        uint32_t run = 0;
-        constexpr int PT = 32;                     // elements per thread per tile
-        for (int base = 0; base < V; base += HT * PT) {
-          const int j0 = base + t * PT;
-          uint32_t c = 0;
-          for (int e = 0; e < PT; ++e) {
-            const int j = j0 + e;
-            if (j < V) {
-              const uint32_t r = __ldg(xs + j);
-              c += (r == r0) || (zero_cls && r == 0x8000u);
-            }
-          }
-          uint32_t tot;
-          const uint32_t pre = block_excl_scan<uint32_t>(c, s.ured, &tot);
-          if (run + pre < (uint32_t)nk && run + pre + c >= (uint32_t)nk) {
-            uint32_t rr = run + pre;
-            for (int e = 0; e < PT; ++e) {
-              const int j = j0 + e;
-              if (j < V) {
-                const uint32_t r = __ldg(xs + j);
-                if ((r == r0) || (zero_cls && r == 0x8000u)) {
-                  if (++rr == (uint32_t)nk) { s.idx_cut = j; s.found_cut = 1; break; }
-                }
-              }
-            }
-          }
-          run += tot;
-          __syncthreads();
-          if (s.found_cut) break;
-        }
-        idx_cut = s.idx_cut;
-      }
-    }
-
-    if (t == 0) {
-      VecStats st;
-      st.m = m;
-      st.inv_s = inv_s;
-      st.zf = zf;
-      st.kth = topk_on ? fkey(bits16_to_float(raw16(keyk), P.dtype)) : 0u;
-      st.vstar = vstar16 == 0xFFFFFFFFu ? 0u : fkey(bits16_to_float(raw16(vstar16), P.dtype));
-      st.idx_cut = vstar16 == 0xFFFFFFFFu ? (int32_t)NO_CUT : idx_cut;
-      st.argmax = -1;
-      st.flags = flags;
-      st.n_keep = vstar16 == 0xFFFFFFFFu ? -1 : s.n_keep;
-      st.pad[0] = st.pad[1] = 0;
-      float pp = 0.f;
-      if (probe >= 0 && probe < V) {
-        const float xv = bits16_to_float(__ldg(reinterpret_cast<const unsigned short*>(x) + probe), P.dtype);
-        const uint32_t kx = fkey(xv);
-        const bool kept = kx >= st.kth &&
-                          (kx > st.vstar || (kx == st.vstar && probe <= (int64_t)st.idx_cut));
-        if (kept) pp = __fdiv_rn(prob_of(xv, P.T, m, inv_s), zf);
-      }
-      st.probe_p = pp;
-      P.stats[v] = st;
-    }
-    __syncthreads();
-    hist_clear(s);
-    __syncthreads();
+    cbar();
   }
 }
 
@@ -1014,7 +1258,7 @@ static int device_sms() {
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct WsLayout {
-  size_t stats, partial, counter, vcounter, rcounter, apartial, mat, total;
+  size_t status, stats, partial, counter, vcounter, rcounter, apartial, mat, total;
 };
 
 static int nch_for(int V) {
@@ -1025,6 +1269,7 @@ static int nch_for(int V) {
 static WsLayout ws_layout(int n_rows, int n_vec, int V, bool small) {
   WsLayout L;
   size_t off = 0;
+  L.status = off; off = 256;      // sticky device status word, same place for every shape
   L.stats = off; off = align256(off + (size_t)n_vec * sizeof(VecStats));
   L.partial = off; off = align256(off + (size_t)n_rows * NCH_MAX * 2 * sizeof(double));
   L.counter = off; off = align256(off + (size_t)n_rows * sizeof(int));
@@ -1059,6 +1304,7 @@ static int run_stats(const VecSet& vs, int nvec, int dtype, int V, float T, floa
   P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec; P.T = T; P.top_p = top_p;
   P.top_k = top_k; P.stats = stats;
   P.zero_ctr = reinterpret_cast<int*>(ws + L.counter); P.n_ctr = vs.nrows;
+  P.status = reinterpret_cast<int*>(ws + L.status);
   const int nsm = device_sms();
   const int grid = nvec < nsm ? nvec : nsm;
   hist_stats_kernel<<<grid, HT, sizeof(HistSmem), st>>>(P);

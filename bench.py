@@ -272,8 +272,9 @@ def main():
     plan = [GRAPH_CALLS] * (a.steps // GRAPH_CALLS)
     if a.steps % GRAPH_CALLS:
         plan.append(a.steps % GRAPH_CALLS)
-    for n in set(plan):
-        graph_of(n).replay()      # warm the graphs too
+    with torch.cuda.stream(s):
+        for n in set(plan):
+            graph_of(n).replay()      # warm the graphs too
     torch.cuda.synchronize(dev)
 
     ev0 = torch.cuda.Event(enable_timing=True)
@@ -281,7 +282,8 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+    # graphs replay on the current stream: keep replays and events on `s`
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk, torch.cuda.stream(s):
         ev0.record(s)
         for n in plan:
             graph_of(n).replay()

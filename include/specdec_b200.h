@@ -48,6 +48,12 @@ int sd_version(void);
  * need separate workspaces. */
 size_t sd_sampling_workspace_bytes(int n_rows, int n_vec, int V, int dtype);
 
+/* The first 4 bytes of a sampling workspace hold a sticky device status word:
+ * bit 0 is set when a kernel's bounded wait on its own copy pipeline timed out
+ * (the affected outputs are then invalid).  Kernels only ever set bits; the
+ * caller reads it at its convenience and clears it. */
+#define SD_STATUS_WAIT_TIMEOUT 1
+
 /*
  * Fused verify round: to_probs on every target/draft vector, the accept test
  * u < min(1, p(x)/max(q(x),1e-10)) with prefix-alive semantics, and the

@@ -60,10 +60,10 @@ def test_commit_and_device_errors():
     with pytest.raises(RuntimeError):
         c.check_errors()
     assert c.lengths.tolist() == [11, 25, 33, 44]
-    c.advance(30)                                              # beyond capacity: refused
+    c.advance(30)                        # row 3 would pass capacity: that row is refused
     with pytest.raises(RuntimeError):
         c.check_errors()
-    assert c.lengths.tolist() == [11, 25, 33, 44]
+    assert c.lengths.tolist() == [41, 55, 63, 44]
     c.set_lengths([60, 0, 0, 0])
     with pytest.raises(RuntimeError):
         c.advance(5)                                           # host-known: raises at once
