@@ -87,50 +87,84 @@ __device__ __forceinline__ int64_t vec_probe(const VecSet& vs, int set, int row,
 }
 
 // ---------------------------------------------------------------------------
-// histogram stats kernel (bf16 / fp16): persistent, TMA ring, producer warp
+// stats kernel (bf16 / fp16): persistent, TMA ring, producer warp, fused
+// row finish
 // ---------------------------------------------------------------------------
-// Per vector the consumer warps see every element once (from a shared-memory
-// ring filled by cp.async.bulk).  Elements within A_top base-2 units of the
-// running maximum ("top" elements) are counted exactly in a 65,536-bin
-// histogram of their 16-bit patterns; everything lower ("bulk") can never
-// reach the top-p boundary nor the top-k threshold checked below, and only
-// its softmax mass is needed: it is summed with ex2.approx relative to the
-// thread's running maximum (its share of S is <= V * 2^-A_top, so the
-// approximation moves S by < 4e-8 relative).  The exact per-class quantities
-// (S of the top classes, top-k key, top-p boundary class and how many of its
-// members are kept) are then computed per distinct value.  Any case the
-// window cannot decide (a top-k threshold below the window, a boundary not
-// found, a 16-bit counter wrap) rebuilds that vector's histogram with every
-// element counted, reading it again from global memory.
+// Streaming (every element once, from a shared-memory ring that a producer
+// warp fills with cp.async.bulk): elements within W_LIST base-2 units of the
+// thread's running maximum are appended (value, index) to a shared list; the
+// softmax mass of all lower elements is summed with ex2.approx relative to the
+// running maximum.  Per vector the list is sorted by (value desc, index asc) --
+// the order of the reference's sort with ties broken by index -- and the
+// reference's element-wise rules are applied to it directly: top-k (keep
+// p >= k-th value), top-p (keep while fl32(cum - p) < top_p, cum accumulated in
+// float64), renormalisation.  The kept set is described by its last element L
+// in that order: j is kept iff value_j > value_L or (value_j == value_L and
+// j <= index_L).  Elements of the list at or above M - W_LIST are complete
+// (every occurrence of those values is listed), so the rules are exact when
+// the boundary falls there; otherwise (boundary deeper, list overflow, top-k
+// beyond the list) the vector is recomputed exactly from a 65,536-bin count
+// histogram of all its elements read again from global memory.
+//
+// The CTA that finishes the last vector of a row then performs that row's
+// accept test and its residual / bonus draw.  Outside the nucleus of p the
+// residual max(p - q, 0) is zero, so the draw only walks p's kept elements in
+// index order (q gathered at those indices).
 constexpr int NCW = 16;                  // consumer warps
 constexpr int CT = NCW * 32;             // consumer threads
 constexpr int HT = CT + 32;              // + one producer warp
 constexpr int SLOT = 16384;              // bytes per ring slot
 constexpr int NSLOT = 4;
 constexpr long long WAIT_CYCLES = 1LL << 32;   // ~2 s at 2 GHz: bound on every wait
+constexpr int LIST_CAP = 8192;           // listed elements per vector
+constexpr int NUC_MAX = 4096;            // kept elements stored per vector for the draw
+constexpr float W_LIST = 12.f;           // list window, base-2 units below the maximum
+
+constexpr int F_FALLBACK = 1;            // exact full-histogram path taken
+constexpr int F_INEXACT = 2;             // that path's correction table overflowed
+constexpr int F_LISTED = 4;              // kept elements stored in the workspace
+constexpr int F_ALLKEPT = 8;             // no truncation: every element kept
+
+struct HistBuf {
+  uint32_t hist[HIST_WORDS];             // 128 KB: two 16-bit counters per word
+  uint16_t list[NGROUP];                 // populated key groups, descending key order
+  uint16_t occ[CT];                      // populated-group mask per 128-key segment
+};
+
+struct ListBuf {
+  unsigned long long key[LIST_CAP];      // (fkey(value) << 32) | ~index
+  float p[LIST_CAP];
+};
 
 struct HistSmem {
-  uint32_t hist[HIST_WORDS];           // 128 KB: two 16-bit counters per word
   alignas(128) unsigned char ring[NSLOT][SLOT];
-  uint16_t list[NGROUP];               // populated key groups, descending key order
-  uint16_t occ[CT];                    // populated-group mask per 128-key segment
+  union {
+    HistBuf h;
+    ListBuf l;
+  } u;
   uint32_t corr_raw[NCORR_MAX];
   int32_t corr_add[NCORR_MAX];
   double dred[40];
   uint32_t ured[40];
+  float fred[40];
   alignas(8) unsigned long long full[NSLOT];
   alignas(8) unsigned long long empty[NSLOT];
   int ncorr;
   int corr_full;
-  uint32_t keyk16;     // top-k threshold key (16-bit), 0 if inactive
-  uint32_t vstar16;    // boundary key (16-bit) or 0xFFFFFFFF if none
+  int nlist;
+  int abort_flag;
+  uint32_t keyk16;
+  uint32_t vstar16;
   int n_keep;
-  int vcount;          // count of the boundary class
-  double z;            // kept mass
+  int vcount;
+  double z;
   int32_t idx_cut;
   int found_cut;
-  int abort_flag;
-  int need_full;
+  int last_row;
+  int sc_n;
+  int sc_L;
+  long long sc_y;
+  double sc_pre;
 };
 
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
@@ -233,8 +267,41 @@ struct VecGeom {
   }
 };
 
+// inverse of fkey for finite non-NaN keys
+__device__ __forceinline__ float fkey_value(uint32_t k) {
+  const uint32_t b = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+  return __uint_as_float(b);
+}
+__device__ __forceinline__ unsigned long long list_key(float x, uint32_t idx) {
+  return ((unsigned long long)fkey(x) << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+__device__ __forceinline__ uint32_t list_idx(unsigned long long k) {
+  return 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
+}
+__device__ __forceinline__ float list_val(unsigned long long k) {
+  return fkey_value((uint32_t)(k >> 32));
+}
+
+// Bitonic sort of key[0..N) (N a power of two, <= LIST_CAP), consumer threads.
+__device__ void bitonic_sort(unsigned long long* key, int N, bool descending) {
+  for (int k2 = 2; k2 <= N; k2 <<= 1) {
+    for (int j2 = k2 >> 1; j2 > 0; j2 >>= 1) {
+      for (int i = threadIdx.x; i < N; i += CT) {
+        const int ixj = i ^ j2;
+        if (ixj > i) {
+          const unsigned long long a = key[i], b = key[ixj];
+          const bool up = ((i & k2) == 0) == descending;
+          if (up ? (a < b) : (a > b)) { key[i] = b; key[ixj] = a; }
+        }
+      }
+      cbar();
+    }
+  }
+}
+
+// ---- exact full-histogram path (fallback) ---------------------------------
 __device__ __forceinline__ uint32_t hist_field(const HistSmem& s, uint32_t raw) {
-  return (s.hist[raw >> 1] >> ((raw & 1u) << 4)) & 0xFFFFu;
+  return (s.u.h.hist[raw >> 1] >> ((raw & 1u) << 4)) & 0xFFFFu;
 }
 
 __device__ __forceinline__ uint32_t hist_count(const HistSmem& s, uint32_t raw) {
@@ -256,7 +323,7 @@ __device__ __forceinline__ void corr_log(HistSmem& s, uint32_t raw, int add) {
 __device__ void merge_signed_zero(HistSmem& s) {
   const uint32_t fneg0 = hist_field(s, 0x8000u);
   if (fneg0) {
-    s.hist[0x4000] &= 0xFFFF0000u;
+    s.u.h.hist[0x4000] &= 0xFFFF0000u;
     corr_log(s, 0u, (int)fneg0);
   }
   const int n = min(s.ncorr, NCORR_MAX);
@@ -264,78 +331,32 @@ __device__ void merge_signed_zero(HistSmem& s) {
     if (s.corr_raw[i] == 0x8000u) s.corr_raw[i] = 0u;
 }
 
-template <bool CHECKED>
-__device__ __forceinline__ void hist_add(HistSmem& s, uint32_t raw) {
+// Count one 16-bit pattern; a wrap of its 16-bit counter is logged in the
+// correction table (the returned old word shows it).
+__device__ __forceinline__ void hist_add_checked(HistSmem& s, uint32_t raw) {
   const uint32_t inc = 1u << ((raw & 1u) << 4);
-  if (!CHECKED) {
-    atomicAdd(&s.hist[raw >> 1], inc);
-  } else {
-    const uint32_t old = atomicAdd(&s.hist[raw >> 1], inc);
-    if ((raw & 1u) == 0u) {
-      if ((old & 0xFFFFu) == 0xFFFFu) {        // low counter wrapped, carried into high
-        corr_log(s, raw, 65536);
-        corr_log(s, raw + 1, -1);
-        if ((old >> 16) == 0xFFFFu) corr_log(s, raw + 1, 65536);
-      }
-    } else if ((old >> 16) == 0xFFFFu) {      // high counter wrapped out of the word
+  const uint32_t old = atomicAdd(&s.u.h.hist[raw >> 1], inc);
+  if ((raw & 1u) == 0u) {
+    if ((old & 0xFFFFu) == 0xFFFFu) {        // low counter wrapped, carried into high
       corr_log(s, raw, 65536);
+      corr_log(s, raw + 1, -1);
+      if ((old >> 16) == 0xFFFFu) corr_log(s, raw + 1, 65536);
     }
+  } else if ((old >> 16) == 0xFFFFu) {      // high counter wrapped out of the word
+    corr_log(s, raw, 65536);
   }
 }
 
-// Exact build of every element from global memory (the fallback path).
-__device__ void hist_build_all(HistSmem& s, const uint16_t* p, int V) {
-  for (int j = threadIdx.x; j < V; j += CT) hist_add<true>(s, __ldg(p + j));
-}
-
-// Per-thread streaming state of one vector.
-struct Stream {
-  float m;        // running max (logit units)
-  float mc;       // m * c2
-  float thr;      // m - wtop
-  double bulk;    // sum of 2^((x - m) c2) over bulk elements, relative to m
-  uint32_t ntop;  // elements counted in the histogram
-};
-
-__device__ __forceinline__ void stream_group(HistSmem& s, Stream& st, const uint32_t* w, int n,
-                                             int dtype, float c2, float wtop) {
-  float x[8];
-  uint32_t r[8];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    r[2 * q] = w[q] & 0xFFFFu;
-    r[2 * q + 1] = w[q] >> 16;
-  }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) x[e] = (e < n) ? bits16_to_float(r[e], dtype) : -INFINITY;
-  float gm = x[0];
-#pragma unroll
-  for (int e = 1; e < 8; ++e) gm = fmaxf(gm, x[e]);
-  if (gm > st.m) {
-    if (st.bulk != 0.0) st.bulk *= (double)ex2_approx((st.m - gm) * c2);
-    st.m = gm;
-    st.mc = gm * c2;
-    st.thr = gm - wtop;
-  }
-  float gs = 0.f;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    if (e < n) {
-      if (x[e] >= st.thr) {
-        hist_add<false>(s, r[e]);
-        ++st.ntop;
-      } else {
-        gs += ex2_approx(fmaf(x[e], c2, -st.mc));
-      }
-    }
-  }
-  st.bulk += (double)gs;
+__device__ void hist_clear_all(HistSmem& s) {
+  uint4* h = reinterpret_cast<uint4*>(s.u.h.hist);
+  for (int i = threadIdx.x; i < HIST_WORDS / 4; i += CT) h[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) { s.ncorr = 0; s.corr_full = 0; }
 }
 
 // Pass A: consumer thread t owns segment t = key groups [16t, 16t+16).
-__device__ void hist_pass_a(HistSmem& s, uint32_t* total_out, uint32_t* maxkey_out) {
+__device__ void hist_pass_a(HistSmem& s, uint32_t* maxkey_out) {
   const int t = threadIdx.x;
-  uint32_t cnt = 0, occ = 0, kmax = 0;
+  uint32_t occ = 0, kmax = 0;
   bool any = false;
 #pragma unroll 4
   for (int jj = 0; jj < 16; ++jj) {
@@ -343,19 +364,16 @@ __device__ void hist_pass_a(HistSmem& s, uint32_t* total_out, uint32_t* maxkey_o
     const uint32_t G = 16u * t + j;
     const bool pos = G >= 4096u;
     const uint32_t wo = pos ? 4u * (G - 4096u) : 0x7FFCu - 4u * G;
-    const uint4 w = *reinterpret_cast<const uint4*>(&s.hist[wo]);
+    const uint4 w = *reinterpret_cast<const uint4*>(&s.u.h.hist[wo]);
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-    uint32_t gsum = 0;
     int hi_idx = -1, lo_idx = 8;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint32_t f0 = ws[q] & 0xFFFFu, f1 = ws[q] >> 16;
-      gsum += f0 + f1;
       if (f0) { hi_idx = max(hi_idx, 2 * q); lo_idx = min(lo_idx, 2 * q); }
       if (f1) { hi_idx = max(hi_idx, 2 * q + 1); lo_idx = min(lo_idx, 2 * q + 1); }
     }
-    cnt += gsum;
-    if (gsum) {
+    if (hi_idx >= 0) {
       occ |= 1u << j;
       const uint32_t raw = 2u * wo + (pos ? (uint32_t)hi_idx : (uint32_t)lo_idx);
       const uint32_t key = key16(raw);
@@ -363,78 +381,69 @@ __device__ void hist_pass_a(HistSmem& s, uint32_t* total_out, uint32_t* maxkey_o
       any = true;
     }
   }
-  s.occ[t] = (uint16_t)occ;
-  *total_out = c_sum<uint32_t>(cnt, s.ured);
+  s.u.h.occ[t] = (uint16_t)occ;
   *maxkey_out = c_max<uint32_t>(any ? kmax : 0u, s.ured, 0u);
 }
 
-struct HistParams {
+struct StatsParams {
   VecSet vs;
   int dtype, V, nvec;
   float T, top_p;
   int top_k;
   VecStats* stats;
-  int* zero_ctr;       // completion counters of the kernel that follows; zeroed here
-  int n_ctr;
-  int* status;         // device status word: bit0 = a bounded wait timed out
+  unsigned long long* nuc;   // [nvec, NUC_MAX] kept elements (list keys)
+  int* row_ctr;              // [rows] vectors finished per row (zeroed before launch)
+  int* status;               // device status word: bit0 = a bounded wait timed out
+  // fused row finish (top-p / top-k modes)
+  int fused, k;
+  const float* u_acc; int64_t u_bs;
+  const float* u_res;
+  const uint8_t* alive;
+  int64_t* n_acc; int64_t* y; float* px; float* qx; float* y_prob;
 };
 
-// Everything after the histogram of one vector is built: exact per-class
-// quantities, the probe, and the stats record.  Returns true when the vector
-// must be rebuilt with every element counted.
-__device__ bool finalize_vector(HistSmem& s, const HistParams& P, const Stream& st, int v,
-                                const uint16_t* x, int64_t probe, float c2, float wtop,
-                                bool windowed, int flags) {
+// Exact per-class computation over the full histogram of vector x (every
+// element counted).  Writes the stats record; the kept set is not listed.
+__device__ void finalize_histogram(HistSmem& s, const StatsParams& P, int v, const uint16_t* x,
+                                   int64_t probe) {
   const int t = threadIdx.x;
   const int V = P.V;
   const bool topk_on = P.top_k > 0 && P.top_k < V;
   const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
   const float tp32 = P.top_p;
+  int flags = F_FALLBACK;
 
+  hist_clear_all(s);
+  cbar();
+  for (int j = t; j < V; j += CT) hist_add_checked(s, __ldg(x + j));
+  cbar();
   if (t == 0) merge_signed_zero(s);
   cbar();
-  uint32_t total, maxkey;
-  hist_pass_a(s, &total, &maxkey);
-  const uint32_t ntop = c_sum<uint32_t>(st.ntop, s.ured);
-  uint32_t csum = 0;
-  for (int i = 0; i < min(s.ncorr, NCORR_MAX); ++i) csum += (uint32_t)s.corr_add[i];
-  if (total + csum != ntop || s.corr_full) {
-    if (windowed) return true;          // a 16-bit counter wrapped: rebuild with wrap logging
-    flags |= 2;                         // rebuild itself overflowed its table: counts inexact
-  }
+  uint32_t maxkey;
+  hist_pass_a(s, &maxkey);
+  if (s.corr_full) flags |= F_INEXACT;
   cbar();
   if (t == 0) {
     const int n = min(s.ncorr, NCORR_MAX);
     for (int i = 0; i < n; ++i) {
       const uint32_t key = key16(s.corr_raw[i]);
       const uint32_t G = key >> 3;
-      s.occ[G >> 4] |= (uint16_t)(1u << (G & 15u));
+      s.u.h.occ[G >> 4] |= (uint16_t)(1u << (G & 15u));
       if (s.corr_add[i] > 0 && key > maxkey) maxkey = key;
     }
     s.ured[34] = maxkey;
   }
   cbar();
   maxkey = s.ured[34];
-  const float M = bits16_to_float(raw16(maxkey), P.dtype);
-  const float m = scaled_logit(M, P.T);
-  // classes with value >= M - wtop hold every occurrence; lower classes may
-  // have members in the bulk sum
-  const float wlow = windowed ? M - wtop : -INFINITY;
+  const float m = scaled_logit(bits16_to_float(raw16(maxkey), P.dtype), P.T);
 
-  // bulk mass relative to M (exp of the running-max offsets)
-  double sb = 0.0;
-  if (windowed && st.bulk > 0.0 && st.m > -INFINITY)
-    sb = st.bulk * (double)exp2f((st.m - M) * c2);
-  const double S_bulk = c_sum<double>(sb, s.dred);
-
-  // populated groups in descending key order: thread t handles segment CT-1-t
-  {
+  {   // populated groups in descending key order: thread t handles segment CT-1-t
     const int seg = CT - 1 - t;
-    const uint32_t o = s.occ[seg];
+    const uint32_t o = s.u.h.occ[seg];
     uint32_t tot;
     uint32_t off = c_excl_scan<uint32_t>(__popc(o), s.ured, &tot);
     for (int j = 15; j >= 0; --j)
-      if (o & (1u << j)) s.list[off++] = (uint16_t)(16 * seg + j);
+      if (o & (1u << j)) s.u.h.list[off++] = (uint16_t)(16 * seg + j);
     cbar();
     if (t == 0) s.ured[35] = tot;
     cbar();
@@ -443,22 +452,21 @@ __device__ bool finalize_vector(HistSmem& s, const HistParams& P, const Stream& 
   const int per = (nlist + CT - 1) / CT;
   const int l0 = min(nlist, t * per), l1 = min(nlist, l0 + per);
 
-  // top-k threshold (by counts, descending keys)
   uint32_t keyk = 0;
   if (topk_on) {
     uint32_t c = 0;
     for (int l = l0; l < l1; ++l) {
-      const uint32_t G = s.list[l];
+      const uint32_t G = s.u.h.list[l];
       for (int q = 7; q >= 0; --q) c += hist_count(s, raw16(8 * G + q));
     }
     uint32_t tot;
     const uint32_t pre = c_excl_scan<uint32_t>(c, s.ured, &tot);
-    if (t == 0) s.keyk16 = 0xFFFFFFFFu;
+    if (t == 0) s.keyk16 = 0;
     cbar();
     if (pre < (uint32_t)P.top_k && pre + c >= (uint32_t)P.top_k) {
       uint32_t run = pre;
       for (int l = l0; l < l1 && run < (uint32_t)P.top_k; ++l) {
-        const uint32_t G = s.list[l];
+        const uint32_t G = s.u.h.list[l];
         for (int q = 7; q >= 0; --q) {
           const uint32_t key = 8 * G + q;
           run += hist_count(s, raw16(key));
@@ -468,27 +476,23 @@ __device__ bool finalize_vector(HistSmem& s, const HistParams& P, const Stream& 
     }
     cbar();
     keyk = s.keyk16;
-    // the k-th value must be a complete class of the window
-    if (keyk == 0xFFFFFFFFu || bits16_to_float(raw16(keyk), P.dtype) < wlow) return true;
   }
 
-  // softmax normaliser S: exact over the histogram, plus the bulk
   double es = 0.0;
   for (int l = l0; l < l1; ++l) {
-    const uint32_t G = s.list[l];
+    const uint32_t G = s.u.h.list[l];
     for (int q = 7; q >= 0; --q) {
       const uint32_t raw = raw16(8 * G + q);
       const uint32_t c = hist_count(s, raw);
       if (c) es += (double)c * (double)softmax_num(bits16_to_float(raw, P.dtype), P.T, m);
     }
   }
-  const double S = c_sum<double>(es, s.dred) + S_bulk;
+  const double S = c_sum<double>(es, s.dred);
   const float inv_s = __double2float_rn(1.0 / S);
 
-  // kept mass (keys >= keyk) per thread, in p units
   double pm = 0.0;
   for (int l = l0; l < l1; ++l) {
-    const uint32_t G = s.list[l];
+    const uint32_t G = s.u.h.list[l];
     for (int q = 7; q >= 0; --q) {
       const uint32_t key = 8 * G + q;
       if (key < keyk) continue;
@@ -500,20 +504,17 @@ __device__ bool finalize_vector(HistSmem& s, const HistParams& P, const Stream& 
   double z;
   if (!topp_on) {
     z = c_sum<double>(pm, s.dred);
-    if (!topk_on) z += S_bulk * (double)inv_s;
     if (t == 0) { s.vstar16 = 0xFFFFFFFFu; s.n_keep = 0; }
   } else {
     double ptot;
     const double pre = c_excl_scan<double>(pm, s.dred, &ptot);
     if (t == 0) { s.vstar16 = 0xFFFFFFFFu; s.ured[36] = 0; }
     cbar();
-    // every thread whose range may hold the first class whose last member is
-    // dropped reports that class; the highest such key is the boundary
     if (l0 < l1 && pre + pm >= (double)tp32 - 1e-9) {
       double C = pre;
       bool done = false;
       for (int l = l0; l < l1 && !done; ++l) {
-        const uint32_t G = s.list[l];
+        const uint32_t G = s.u.h.list[l];
         for (int q = 7; q >= 0; --q) {
           const uint32_t key = 8 * G + q;
           if (key < keyk) { done = true; break; }
@@ -529,16 +530,15 @@ __device__ bool finalize_vector(HistSmem& s, const HistParams& P, const Stream& 
     }
     cbar();
     const uint32_t vk1 = s.ured[36];
-    if (vk1 == 0u && windowed && S_bulk > 0.0) return true;  // boundary below the window
     if (vk1 != 0u && l0 < l1) {
       const uint32_t vkey = vk1 - 1u;
       const uint32_t Gv = vkey >> 3;
       bool mine = false;
-      for (int l = l0; l < l1; ++l) mine |= (s.list[l] == Gv);
+      for (int l = l0; l < l1; ++l) mine |= (s.u.h.list[l] == Gv);
       if (mine) {
         double C = pre;
         for (int l = l0; l < l1; ++l) {
-          const uint32_t G = s.list[l];
+          const uint32_t G = s.u.h.list[l];
           for (int q = 7; q >= 0; --q) {
             const uint32_t key = 8 * G + q;
             const uint32_t raw = raw16(key);
@@ -566,15 +566,13 @@ __device__ bool finalize_vector(HistSmem& s, const HistParams& P, const Stream& 
       }
     }
     cbar();
-    if (s.vstar16 != 0xFFFFFFFFu &&
-        bits16_to_float(raw16(s.vstar16), P.dtype) < wlow) return true;
     z = (s.vstar16 == 0xFFFFFFFFu) ? ptot : s.z;
   }
   cbar();
   const uint32_t vstar16 = s.vstar16;
   const float zf = fmaxf(__double2float_rn(z), 1e-12f);
 
-  // idx_cut: index of the n_keep-th member (ascending index) of the boundary class
+  // index of the n_keep-th member (ascending index) of the boundary class
   int32_t idx_cut = (int32_t)NO_CUT;
   if (vstar16 != 0xFFFFFFFFu) {
     const int nk = s.n_keep;
@@ -627,8 +625,8 @@ __device__ bool finalize_vector(HistSmem& s, const HistParams& P, const Stream& 
     o.vstar = vstar16 == 0xFFFFFFFFu ? 0u : fkey(bits16_to_float(raw16(vstar16), P.dtype));
     o.idx_cut = vstar16 == 0xFFFFFFFFu ? (int32_t)NO_CUT : idx_cut;
     o.argmax = -1;
-    o.flags = flags;
-    o.n_keep = vstar16 == 0xFFFFFFFFu ? -1 : s.n_keep;
+    o.flags = flags | ((!topp_on && !topk_on) ? F_ALLKEPT : 0);
+    o.n_keep = -1;
     o.pad[0] = o.pad[1] = 0;
     float pp = 0.f;
     if (probe >= 0 && probe < V) {
@@ -641,47 +639,346 @@ __device__ bool finalize_vector(HistSmem& s, const HistParams& P, const Stream& 
     o.probe_p = pp;
     P.stats[v] = o;
   }
+  cbar();
+}
+
+// ---- streaming ---------------------------------------------------------------
+struct Stream {
+  float m;        // running max (logit units)
+  float mc;       // m * c2
+  float thr;      // m - wlist: listed at or above
+  double bulk;    // sum of 2^((x - m) c2) over unlisted elements, relative to m
+};
+
+template <int N>
+__device__ __forceinline__ void stream_group(HistSmem& s, Stream& st, const uint32_t* w,
+                                             uint32_t j0, int dtype, float c2, float wlist) {
+  float x[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint32_t r = (e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xFFFFu);
+    x[e] = (e < N) ? bits16_to_float(r, dtype) : -INFINITY;
+  }
+  float gm = x[0];
+#pragma unroll
+  for (int e = 1; e < N; ++e) gm = fmaxf(gm, x[e]);
+  if (gm > st.m) {
+    if (st.bulk != 0.0) st.bulk *= (double)ex2_approx((st.m - gm) * c2);
+    st.m = gm;
+    st.mc = gm * c2;
+    st.thr = gm - wlist;
+  }
+  float gs = 0.f;
+#pragma unroll
+  for (int e = 0; e < N; ++e) {
+    const bool listed = x[e] >= st.thr;
+    const float ev = ex2_approx(fmaf(x[e], c2, -st.mc));
+    gs += listed ? 0.f : ev;
+    if (listed) {
+      const int slot = atomicAdd(&s.nlist, 1);
+      if (slot < LIST_CAP) s.u.l.key[slot] = list_key(x[e], j0 + e);
+    }
+  }
+  st.bulk += (double)gs;
+}
+
+// Probability of element j of a vector under its stats (the kept predicate
+// and p' = fl(fl(e * inv_s) / zf)).
+__device__ __forceinline__ float stats_prob(const VecStats& st, const void* x, int dtype, float T,
+                                            int64_t j) {
+  const float xv = load_logit(x, dtype, j);
+  const uint32_t kx = fkey(xv);
+  const bool kept = kx >= st.kth && (kx > st.vstar || (kx == st.vstar && j <= (int64_t)st.idx_cut));
+  if (!kept) return 0.f;
+  return __fdiv_rn(prob_of(xv, T, st.m, st.inv_s), st.zf);
+}
+
+__device__ __forceinline__ VecStats load_stats_cg(const VecStats* p) {
+  VecStats o;
+  const int4* src = reinterpret_cast<const int4*>(p);
+  int4* dst = reinterpret_cast<int4*>(&o);
+  dst[0] = __ldcg(src);
+  dst[1] = __ldcg(src + 1);
+  dst[2] = __ldcg(src + 2);
+  return o;
+}
+
+// List-based exact computation (see the section comment).  Returns true when
+// the vector needs the exact full-histogram path.
+__device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& st, int v,
+                              const uint16_t* x, int64_t probe, float c2, float wlist) {
+  const int t = threadIdx.x;
+  const int V = P.V;
+  const bool topk_on = P.top_k > 0 && P.top_k < V;
+  const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
+  const float tp32 = P.top_p;
+  const int nl = s.nlist;
+  if (nl > LIST_CAP || nl < 1) return true;
+  const float M = c_max<float>(st.m, s.fred, -INFINITY);
+  int N = 1;
+  while (N < nl) N <<= 1;
+  for (int i = nl + t; i < N; i += CT) s.u.l.key[i] = 0ull;
+  cbar();
+  bitonic_sort(s.u.l.key, N, true);
+  const float m = scaled_logit(M, P.T);
+  double es = 0.0;
+  for (int i = t; i < nl; i += CT) {
+    const float e = softmax_num(list_val(s.u.l.key[i]), P.T, m);
+    s.u.l.p[i] = e;
+    es += (double)e;
+  }
+  double sb = 0.0;
+  if (st.bulk > 0.0 && st.m > -INFINITY) sb = st.bulk * (double)exp2f((st.m - M) * c2);
+  const double S_list = c_sum<double>(es, s.dred);
+  const double S_bulk = c_sum<double>(sb, s.dred);
+  const double S = S_list + S_bulk;
+  const float inv_s = __double2float_rn(1.0 / S);
+  const float wlow = M - wlist;
+  int ncomp = 0;
+  for (int i = t; i < nl; i += CT) {
+    s.u.l.p[i] = __fmul_rn(s.u.l.p[i], inv_s);
+    ncomp += list_val(s.u.l.key[i]) >= wlow;
+  }
+  ncomp = c_sum<int>(ncomp, reinterpret_cast<int*>(s.ured));
+  float kth_x = -INFINITY;
+  int n_eff = ncomp;
+  if (topk_on) {
+    if (P.top_k > ncomp) return true;
+    kth_x = list_val(s.u.l.key[P.top_k - 1]);
+    int c = 0;
+    for (int i = t; i < nl; i += CT) c += list_val(s.u.l.key[i]) >= kth_x;
+    n_eff = c_sum<int>(c, reinterpret_cast<int*>(s.ured));
+  }
+  int L = -1;
+  bool all_kept = false;
+  if (topp_on) {
+    if (t == 0) s.sc_L = 0x7FFFFFFF;
+    cbar();
+    double carry = 0.0;
+    for (int base = 0; base < n_eff; base += CT) {
+      const int i = base + t;
+      const float p = i < n_eff ? s.u.l.p[i] : 0.f;
+      double tot;
+      const double pre = c_excl_scan<double>((double)p, s.dred, &tot);
+      if (i < n_eff && i > 0) {
+        const float cl = __fsub_rn(__double2float_rn(carry + pre + (double)p), p);
+        if (!(cl < tp32)) atomicMin(&s.sc_L, i);
+      }
+      carry += tot;
+      cbar();
+      if (s.sc_L != 0x7FFFFFFF) break;
+    }
+    const int D = s.sc_L;
+    if (D != 0x7FFFFFFF) {
+      L = D - 1;
+    } else if (topk_on || ncomp == V) {
+      L = n_eff - 1;
+    } else {
+      return true;                 // the boundary lies below the complete part of the list
+    }
+  } else if (topk_on) {
+    L = n_eff - 1;
+  } else {
+    all_kept = true;
+  }
+  double zs = 0.0;
+  if (all_kept) {
+    for (int i = t; i < nl; i += CT) zs += (double)s.u.l.p[i];
+  } else {
+    for (int i = t; i <= L; i += CT) zs += (double)s.u.l.p[i];
+  }
+  double z = c_sum<double>(zs, s.dred);
+  if (all_kept) z += S_bulk * (double)inv_s;
+  const float zf = fmaxf(__double2float_rn(z), 1e-12f);
+  const bool listed = P.nuc != nullptr && !all_kept && L + 1 <= NUC_MAX;
+  if (listed) {
+    unsigned long long* dst = P.nuc + (int64_t)v * NUC_MAX;
+    for (int i = t; i <= L; i += CT) dst[i] = s.u.l.key[i];
+  }
+  if (t == 0) {
+    VecStats o;
+    o.m = m;
+    o.inv_s = inv_s;
+    o.zf = zf;
+    o.kth = topk_on ? fkey(kth_x) : 0u;
+    o.vstar = all_kept ? 0u : (uint32_t)(s.u.l.key[L] >> 32);
+    o.idx_cut = all_kept ? (int32_t)NO_CUT : (int32_t)list_idx(s.u.l.key[L]);
+    o.argmax = -1;
+    o.flags = (all_kept ? F_ALLKEPT : 0) | (listed ? F_LISTED : 0);
+    o.n_keep = all_kept ? -1 : L + 1;
+    o.pad[0] = o.pad[1] = 0;
+    o.probe_p = 0.f;
+    if (probe >= 0 && probe < V) o.probe_p = stats_prob(o, x, P.dtype, P.T, probe);
+    P.stats[v] = o;
+  }
+  cbar();
   return false;
 }
 
-// Clear the groups listed as populated (and the correction table).
-__device__ void hist_clear_listed(HistSmem& s) {
-  const int nlist = (int)s.ured[35];
-  for (int l = threadIdx.x; l < nlist; l += CT) {
-    const uint32_t G = s.list[l];
-    const uint32_t wo = G >= 4096u ? 4u * (G - 4096u) : 0x7FFCu - 4u * G;
-    *reinterpret_cast<uint4*>(&s.hist[wo]) = make_uint4(0, 0, 0, 0);
+// The row's accept test and its residual / bonus draw (consumer threads of the
+// CTA that finished the row's last vector).
+__device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
+  const int t = threadIdx.x;
+  const int npos0 = P.vs.npos[0], npos = P.vs.npos[0] + P.vs.npos[1];
+  const int vrow = row * npos;
+  const int k = P.k;
+  __threadfence();
+  if (t == 0) {
+    int n = 0;
+    bool alive = P.alive ? P.alive[row] != 0 : true;
+    for (int i = 0; i < k; ++i) {
+      const float pxi = __ldcg(&P.stats[vrow + i].probe_p);
+      const float qxi = __ldcg(&P.stats[vrow + npos0 + i].probe_p);
+      const float thr = fminf(__fdiv_rn(pxi, fmaxf(qxi, 1e-10f)), 1.0f);
+      if (P.px) P.px[row * k + i] = pxi;
+      if (P.qx) P.qx[row * k + i] = qxi;
+      if (alive && n == i && P.u_acc[row * P.u_bs + i] < thr) ++n; else alive = false;
+    }
+    s.sc_n = n;
   }
-  if (threadIdx.x == 0) { s.ncorr = 0; s.corr_full = 0; }
+  cbar();
+  const int n = s.sc_n;
+  const bool resid = n < k;
+  const int ppos = resid ? n : k;
+  const VecStats stp = load_stats_cg(P.stats + vrow + ppos);
+  VecStats stq = stp;
+  const void* xp = vec_ptr(P.vs, 0, row, ppos, P.dtype);
+  const void* xq = xp;
+  if (resid) {
+    stq = load_stats_cg(P.stats + vrow + npos0 + n);
+    xq = vec_ptr(P.vs, 1, row, n, P.dtype);
+  }
+  const double u = (double)P.u_res[row];
+  if (t == 0) s.sc_y = -1;
+  cbar();
+  if (stp.flags & F_LISTED) {
+    const int cnt = stp.n_keep;
+    int N = 1;
+    while (N < cnt) N <<= 1;
+    const unsigned long long* src = P.nuc + (int64_t)(vrow + ppos) * NUC_MAX;
+    for (int i = t; i < N; i += CT)
+      s.u.l.key[i] = i < cnt ? (unsigned long long)list_idx(__ldcg(src + i)) : ~0ull;
+    cbar();
+    bitonic_sort(s.u.l.key, N, false);        // kept elements in vocabulary order
+    double rs = 0.0;
+    for (int i = t; i < cnt; i += CT) {
+      const int64_t j = (int64_t)s.u.l.key[i];
+      const float pj = stats_prob(stp, xp, P.dtype, P.T, j);
+      float r = pj;
+      if (resid && pj != 0.f) r = fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+      s.u.l.p[i] = r;
+      rs += (double)r;
+    }
+    double R = c_sum<double>(rs, s.dred);
+    if (resid && __double2float_rn(R) <= 1e-9f) {        // sampling.py:86-89: fall back to p
+      rs = 0.0;
+      for (int i = t; i < cnt; i += CT) {
+        const float pj = stats_prob(stp, xp, P.dtype, P.T, (int64_t)s.u.l.key[i]);
+        s.u.l.p[i] = pj;
+        rs += (double)pj;
+      }
+      R = c_sum<double>(rs, s.dred);
+    }
+    const double tgt = u * R;
+    double carry = 0.0;
+    for (int base = 0; base < cnt; base += CT) {
+      const int i = base + t;
+      const float r = i < cnt ? s.u.l.p[i] : 0.f;
+      double tot;
+      const double pre = c_excl_scan<double>((double)r, s.dred, &tot);
+      if (i < cnt && carry + pre <= tgt && carry + pre + (double)r > tgt)
+        s.sc_y = (long long)s.u.l.key[i];
+      carry += tot;
+      cbar();
+      if (s.sc_y >= 0) break;
+    }
+    if (t == 0 && s.sc_y < 0) {
+      for (int i = cnt - 1; i >= 0; --i)
+        if (s.u.l.p[i] > 0.f) { s.sc_y = (long long)s.u.l.key[i]; break; }
+      if (s.sc_y < 0) s.sc_y = (long long)s.u.l.key[0];
+    }
+  } else {
+    // kept set not listed: two ordered passes over the whole vocabulary
+    constexpr int PT = 8;
+    double rs = 0.0, ps = 0.0;
+    for (int j = t; j < P.V; j += CT) {
+      const float pj = stats_prob(stp, xp, P.dtype, P.T, j);
+      ps += (double)pj;
+      if (resid && pj != 0.f) rs += (double)fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+    }
+    double R = c_sum<double>(rs, s.dred);
+    const double Pm = c_sum<double>(ps, s.dred);
+    const bool use_p = !resid || __double2float_rn(R) <= 1e-9f;
+    if (use_p) R = Pm;
+    const double tgt = u * R;
+    double carry = 0.0;
+    for (int base = 0; base < P.V; base += CT * PT) {
+      const int j0 = base + t * PT;
+      float r[PT];
+      double ls = 0.0;
+#pragma unroll
+      for (int e = 0; e < PT; ++e) {
+        const int j = j0 + e;
+        float v = 0.f;
+        if (j < P.V) {
+          v = stats_prob(stp, xp, P.dtype, P.T, j);
+          if (!use_p && v != 0.f) v = fmaxf(__fsub_rn(v, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+        }
+        r[e] = v;
+        ls += (double)v;
+      }
+      double tot;
+      const double pre = c_excl_scan<double>(ls, s.dred, &tot);
+      if (carry + pre <= tgt && carry + pre + ls > tgt) {
+        double run = carry + pre;
+#pragma unroll
+        for (int e = 0; e < PT; ++e) {
+          run += (double)r[e];
+          if (run > tgt) { s.sc_y = j0 + e; break; }
+        }
+      }
+      carry += tot;
+      cbar();
+      if (s.sc_y >= 0) break;
+    }
+    if (t == 0 && s.sc_y < 0) {
+      for (int j = P.V - 1; j >= 0; --j) {
+        float v = stats_prob(stp, xp, P.dtype, P.T, j);
+        if (!use_p && v != 0.f) v = fmaxf(__fsub_rn(v, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+        if (v > 0.f) { s.sc_y = j; break; }
+      }
+      if (s.sc_y < 0) s.sc_y = 0;
+    }
+  }
+  cbar();
+  if (t == 0) {
+    const int64_t yy = s.sc_y;
+    if (P.n_acc) P.n_acc[row] = n;
+    P.y[row] = yy;
+    if (P.y_prob) P.y_prob[row] = stats_prob(stp, xp, P.dtype, P.T, yy);
+    P.row_ctr[row] = 0;
+  }
+  cbar();
 }
 
-__device__ void hist_clear_all(HistSmem& s) {
-  uint4* h = reinterpret_cast<uint4*>(s.hist);
-  for (int i = threadIdx.x; i < HIST_WORDS / 4; i += CT) h[i] = make_uint4(0, 0, 0, 0);
-  if (threadIdx.x == 0) { s.ncorr = 0; s.corr_full = 0; }
-}
-
-__global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
+__global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   HistSmem& s = *reinterpret_cast<HistSmem*>(smem_raw);
   const int t = threadIdx.x;
   const int V = P.V;
   const float c2 = 1.4426950408889634f / P.T;          // log2(e) / T
-  const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
-  // window (base-2 units below the running max) holding every class that can
-  // matter beyond the softmax sum
-  float a_top = 26.f;
-  if (topp_on) a_top = fmaxf(a_top, log2f(2.f * (float)V / (1.f - P.top_p)) + 1.f);
-  const float wtop = a_top / c2;
+  const float wlist = W_LIST / c2;                      // list window in logit units
+  const int npos = P.vs.npos[0] + P.vs.npos[1];
 
-  for (int i = blockIdx.x * HT + t; i < P.n_ctr; i += gridDim.x * HT) P.zero_ctr[i] = 0;
-  if (t < CT) hist_clear_all(s);
   if (t == 0) {
     for (int i = 0; i < NSLOT; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], NCW);
     }
     s.abort_flag = 0;
+    s.nlist = 0;
+    s.ncorr = 0;
+    s.corr_full = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -728,13 +1025,12 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
     const int64_t probe = vec_probe(P.vs, set, row, pos);
     const VecGeom gm(x, V);
     Stream st;
-    st.m = -INFINITY; st.mc = -INFINITY; st.thr = -INFINITY; st.bulk = 0.0; st.ntop = 0;
-    // ragged head / tail elements straight from global memory
+    st.m = -INFINITY; st.mc = -INFINITY; st.thr = -INFINITY; st.bulk = 0.0;
     const int nrag = gm.head + (V - gm.tail0);
     for (int i = t; i < nrag; i += CT) {
       const int j = i < gm.head ? i : gm.tail0 + (i - gm.head);
       const uint32_t w[4] = {__ldg(x + j), 0u, 0u, 0u};
-      stream_group(s, st, w, 1, P.dtype, c2, wtop);
+      stream_group<1>(s, st, w, (uint32_t)j, P.dtype, c2, wlist);
     }
     bool aborted = false;
     for (int c = 0; c < gm.nchunk; ++c, ++g) {
@@ -742,10 +1038,11 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
       if (!mbar_wait(&s.full[sl], (g / NSLOT) & 1u, &s.abort_flag)) { aborted = true; break; }
       const int units = min(SLOT, gm.nunits * 16 - c * SLOT) >> 4;
       const uint4* u4 = reinterpret_cast<const uint4*>(s.ring[sl]);
+      const uint32_t jbase = (uint32_t)(gm.head + c * (SLOT / 2));
       for (int u = t; u < units; u += CT) {
         const uint4 w4 = u4[u];
         const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-        stream_group(s, st, w, 8, P.dtype, c2, wtop);
+        stream_group<8>(s, st, w, jbase + 8u * (uint32_t)u, P.dtype, c2, wlist);
       }
       __syncwarp();
       if ((t & 31) == 0) mbar_arrive(&s.empty[sl]);
@@ -755,25 +1052,16 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(HistParams P) {
       if (t == 0) atomicOr(P.status, 1);
       break;
     }
-    int flags = 0;
-    bool redo = finalize_vector(s, P, st, v, x, probe, c2, wtop, true, flags);
-    cbar();
-    if (redo) {
-      // exact rebuild with every element counted (rare)
-      hist_clear_all(s);
+    if (finalize_list(s, P, st, v, x, probe, c2, wlist)) finalize_histogram(s, P, v, x, probe);
+    // row bookkeeping: the CTA that completes a row draws for it
+    if (P.fused) {
+      __threadfence();
       cbar();
-      hist_build_all(s, x, V);
+      if (t == 0) s.last_row = atomicAdd(&P.row_ctr[row], 1) == npos - 1;
       cbar();
-      Stream all;
-      all.m = -INFINITY; all.mc = -INFINITY; all.thr = -INFINITY; all.bulk = 0.0;
-      all.ntop = 0;
-      for (int j = t; j < V; j += CT) ++all.ntop;
-      finalize_vector(s, P, all, v, x, probe, c2, wtop, false, 1);
-      cbar();
-      hist_clear_all(s);
-    } else {
-      hist_clear_listed(s);
+      if (s.last_row) finish_row(s, P, row);
     }
+    if (t == 0) s.nlist = 0;
     cbar();
   }
 }
@@ -1258,13 +1546,15 @@ static int device_sms() {
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct WsLayout {
-  size_t status, stats, partial, counter, vcounter, rcounter, apartial, mat, total;
+  size_t status, stats, partial, counter, vcounter, rcounter, apartial, mat, nuc, total;
 };
 
 static int nch_for(int V) {
   int n = (V + 4095) / 4096;
   return n < 1 ? 1 : (n > NCH_MAX ? NCH_MAX : n);
 }
+
+static bool use_small(int V, int dtype) { return V <= SMALLV_MAX || dtype == SD_DTYPE_F32; }
 
 static WsLayout ws_layout(int n_rows, int n_vec, int V, bool small) {
   WsLayout L;
@@ -1277,37 +1567,80 @@ static WsLayout ws_layout(int n_rows, int n_vec, int V, bool small) {
   L.rcounter = off; off = align256(off + (size_t)n_rows * sizeof(int));
   L.apartial = off; off = align256(off + (size_t)n_vec * NCH_MAX * sizeof(unsigned long long));
   L.mat = off; off = align256(off + (small ? (size_t)n_vec * V * sizeof(float) : 0));
+  L.nuc = off; off = align256(off + (small ? 0 : (size_t)n_vec * NUC_MAX * sizeof(unsigned long long)));
   L.total = off;
   return L;
 }
-
-static bool use_small(int V, int dtype) { return V <= SMALLV_MAX || dtype == SD_DTYPE_F32; }
 
 static int check_launch() {
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
 }
 
-// Stats for every vector of `vs` (non-greedy).
-static int run_stats(const VecSet& vs, int nvec, int dtype, int V, float T, float top_p, int top_k,
-                     const WsLayout& L, char* ws, cudaStream_t st) {
+// What a verify / draft call draws (to_probs passes none).
+struct DrawSpec {
+  int k;
+  const float* u_acc; int64_t u_bs;
+  const float* u_res;
+  const uint8_t* alive;
+  int64_t* n_acc; int64_t* y; float* px; float* qx; float* y_prob;
+};
+
+// Non-greedy path: stats for every vector of `vs`, then (if `draw`) each
+// row's accept test and draw.  Histogram-path truncated sampling draws inside
+// the stats kernel; otherwise a finish kernel follows.
+static int run_sampling(const VecSet& vs, int nvec, int dtype, int V, float T, float top_p,
+                        int top_k, const WsLayout& L, char* ws, cudaStream_t st,
+                        const DrawSpec* draw) {
   VecStats* stats = reinterpret_cast<VecStats*>(ws + L.stats);
-  if (use_small(V, dtype)) {
+  const bool small = use_small(V, dtype);
+  const int rows = vs.nrows;
+  bool need_finish = draw != nullptr;
+  if (small) {
     if (V > SMALLV_MAX) return SD_ENOTSUP;
     SmallParams P;
     P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec; P.T = T; P.top_p = top_p;
     P.top_k = top_k; P.stats = stats; P.mat = reinterpret_cast<float*>(ws + L.mat);
-    P.zero_ctr = reinterpret_cast<int*>(ws + L.counter); P.n_ctr = vs.nrows;
+    P.zero_ctr = reinterpret_cast<int*>(ws + L.counter); P.n_ctr = rows;
     small_stats_kernel<<<nvec, ST, 0, st>>>(P);
-    return check_launch();
+    if (int rc = check_launch()) return rc;
+  } else {
+    const bool truncated = (top_p > 0.0f && top_p < 1.0f) || (top_k > 0 && top_k < V);
+    const bool fused = draw != nullptr && truncated;
+    StatsParams P = {};
+    P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec; P.T = T; P.top_p = top_p;
+    P.top_k = top_k; P.stats = stats;
+    P.nuc = draw ? reinterpret_cast<unsigned long long*>(ws + L.nuc) : nullptr;
+    P.row_ctr = reinterpret_cast<int*>(ws + L.rcounter);
+    P.status = reinterpret_cast<int*>(ws + L.status);
+    P.fused = fused;
+    if (fused) {
+      P.k = draw->k; P.u_acc = draw->u_acc; P.u_bs = draw->u_bs; P.u_res = draw->u_res;
+      P.alive = draw->alive; P.n_acc = draw->n_acc; P.y = draw->y; P.px = draw->px;
+      P.qx = draw->qx; P.y_prob = draw->y_prob;
+      if (cudaMemsetAsync(ws + L.rcounter, 0, (size_t)rows * sizeof(int), st) != cudaSuccess)
+        return SD_ELAUNCH;
+    }
+    const int nsm = device_sms();
+    const int grid = nvec < nsm ? nvec : nsm;
+    hist_stats_kernel<<<grid, HT, sizeof(HistSmem), st>>>(P);
+    if (int rc = check_launch()) return rc;
+    need_finish = draw != nullptr && !fused;
+    if (need_finish &&
+        cudaMemsetAsync(ws + L.counter, 0, (size_t)rows * sizeof(int), st) != cudaSuccess)
+      return SD_ELAUNCH;
   }
-  HistParams P;
-  P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec; P.T = T; P.top_p = top_p;
-  P.top_k = top_k; P.stats = stats;
-  P.zero_ctr = reinterpret_cast<int*>(ws + L.counter); P.n_ctr = vs.nrows;
-  P.status = reinterpret_cast<int*>(ws + L.status);
-  const int nsm = device_sms();
-  const int grid = nvec < nsm ? nvec : nsm;
-  hist_stats_kernel<<<grid, HT, sizeof(HistSmem), st>>>(P);
+  if (!need_finish) return SD_OK;
+  FinishParams F;
+  F.vs = vs; F.dtype = dtype; F.V = V; F.k = draw->k;
+  F.nch = nch_for(V); F.chunk = (V + F.nch - 1) / F.nch;
+  F.T = T;
+  F.stats = stats;
+  F.mat = small ? reinterpret_cast<const float*>(ws + L.mat) : nullptr;
+  F.u_acc = draw->u_acc; F.u_bs = draw->u_bs; F.u_res = draw->u_res; F.alive = draw->alive;
+  F.n_acc = draw->n_acc; F.y = draw->y; F.px = draw->px; F.qx = draw->qx; F.y_prob = draw->y_prob;
+  F.partial = reinterpret_cast<double*>(ws + L.partial);
+  F.counter = reinterpret_cast<int*>(ws + L.counter);
+  finish_kernel<<<F.nch * rows, FT, 0, st>>>(F);
   return check_launch();
 }
 
@@ -1374,28 +1707,15 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
   }
   if (!drf) return SD_EINVAL;
   const int nvec = B * (2 * k + 1);
-  const bool small = use_small(V, dtype);
-  WsLayout L = ws_layout(B, nvec, V, small);
+  WsLayout L = ws_layout(B, nvec, V, use_small(V, dtype));
   if (workspace_bytes < L.total) return SD_ENOSPC;
   VecSet vs = {};
   vs.base[0] = tgt; vs.bs[0] = tgt_bs; vs.ps[0] = tgt_ps; vs.npos[0] = k + 1;
   vs.base[1] = drf; vs.bs[1] = drf_bs; vs.ps[1] = drf_ps; vs.npos[1] = k;
   vs.probe = xs; vs.probe_bs = xs_bs; vs.probe_npos[0] = k; vs.probe_npos[1] = k;
   vs.nrows = B;
-  rc = run_stats(vs, nvec, dtype, V, temperature, top_p, top_k, L, ws, st);
-  if (rc) return rc;
-  FinishParams F;
-  F.vs = vs; F.dtype = dtype; F.V = V; F.k = k;
-  F.nch = nch_for(V); F.chunk = (V + F.nch - 1) / F.nch;
-  F.T = temperature;
-  F.stats = reinterpret_cast<const VecStats*>(ws + L.stats);
-  F.mat = small ? reinterpret_cast<const float*>(ws + L.mat) : nullptr;
-  F.u_acc = u_acc; F.u_bs = u_bs; F.u_res = u_res; F.alive = alive;
-  F.n_acc = n_acc; F.y = y; F.px = px; F.qx = qx; F.y_prob = nullptr;
-  F.partial = reinterpret_cast<double*>(ws + L.partial);
-  F.counter = reinterpret_cast<int*>(ws + L.counter);
-  finish_kernel<<<F.nch * B, FT, 0, st>>>(F);
-  return check_launch();
+  DrawSpec d = {k, u_acc, u_bs, u_res, alive, n_acc, y, px, qx, nullptr};
+  return run_sampling(vs, nvec, dtype, V, temperature, top_p, top_k, L, ws, st, &d);
 }
 
 int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, int V,
@@ -1426,23 +1746,10 @@ int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, in
     argmax_kernel<<<P.nch * B, FT, 0, st>>>(P);
     return check_launch();
   }
-  const bool small = use_small(V, dtype);
-  WsLayout L = ws_layout(B, B, V, small);
+  WsLayout L = ws_layout(B, B, V, use_small(V, dtype));
   if (workspace_bytes < L.total) return SD_ENOSPC;
-  rc = run_stats(vs, B, dtype, V, temperature, top_p, top_k, L, ws, st);
-  if (rc) return rc;
-  FinishParams F;
-  F.vs = vs; F.dtype = dtype; F.V = V; F.k = 0;
-  F.nch = nch_for(V); F.chunk = (V + F.nch - 1) / F.nch;
-  F.T = temperature;
-  F.stats = reinterpret_cast<const VecStats*>(ws + L.stats);
-  F.mat = small ? reinterpret_cast<const float*>(ws + L.mat) : nullptr;
-  F.u_acc = nullptr; F.u_bs = 0; F.u_res = u; F.alive = nullptr;
-  F.n_acc = nullptr; F.y = x; F.px = nullptr; F.qx = nullptr; F.y_prob = qx;
-  F.partial = reinterpret_cast<double*>(ws + L.partial);
-  F.counter = reinterpret_cast<int*>(ws + L.counter);
-  finish_kernel<<<F.nch * B, FT, 0, st>>>(F);
-  return check_launch();
+  DrawSpec d = {0, nullptr, 0, u, nullptr, nullptr, x, nullptr, nullptr, qx};
+  return run_sampling(vs, B, dtype, V, temperature, top_p, top_k, L, ws, st, &d);
 }
 
 int sd_to_probs(const void* logits, int64_t row_stride, int dtype, int n_rows, int V,
@@ -1475,14 +1782,14 @@ int sd_to_probs(const void* logits, int64_t row_stride, int dtype, int n_rows, i
     A.vec_counter = reinterpret_cast<int*>(ws + L.vcounter);
     A.row_counter = reinterpret_cast<int*>(ws + L.rcounter);
     A.stats = reinterpret_cast<VecStats*>(ws + L.stats);
-    A.k = -1;   // stats only: per-row decision skipped (npos 1 row counter reaches 0 -> k<0)
+    A.k = -1;   // stats only: no per-row decision
     A.xs = nullptr; A.xs_bs = 0; A.u_acc = nullptr; A.u_bs = 0; A.alive = nullptr;
     A.n_acc = nullptr; A.y = nullptr; A.px = nullptr; A.qx = nullptr;
     if (zero_argmax_counters(L, n_rows, n_rows, ws, st)) return SD_ELAUNCH;
     argmax_kernel<<<A.nch * n_rows, FT, 0, st>>>(A);
     if ((rc = check_launch())) return rc;
   } else {
-    rc = run_stats(vs, n_rows, dtype, V, temperature, top_p, top_k, L, ws, st);
+    rc = run_sampling(vs, n_rows, dtype, V, temperature, top_p, top_k, L, ws, st, nullptr);
     if (rc) return rc;
   }
   probs_kernel<<<P.nch * n_rows, FT, 0, st>>>(P);
