@@ -1039,6 +1039,27 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
       const int units = min(SLOT, gm.nunits * 16 - c * SLOT) >> 4;
       const uint4* u4 = reinterpret_cast<const uint4*>(s.ring[sl]);
       const uint32_t jbase = (uint32_t)(gm.head + c * (SLOT / 2));
+      if (c == 0) {
+        // seed every thread's running max with the first chunk's maximum, so
+        // the list window starts near its final position
+        float cm = -INFINITY;
+        for (int u = t; u < units; u += CT) {
+          const uint4 w4 = u4[u];
+          const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t r = (e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xFFFFu);
+            cm = fmaxf(cm, bits16_to_float(r, P.dtype));
+          }
+        }
+        cm = c_max<float>(cm, s.fred, -INFINITY);
+        if (cm > st.m) {
+          if (st.bulk != 0.0) st.bulk *= (double)ex2_approx((st.m - cm) * c2);
+          st.m = cm;
+          st.mc = cm * c2;
+          st.thr = cm - wlist;
+        }
+      }
       for (int u = t; u < units; u += CT) {
         const uint4 w4 = u4[u];
         const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
@@ -1687,7 +1708,7 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
   char* ws = reinterpret_cast<char*>(workspace);
   if (greedy) {
     const int nvec = B * (k + 1);
-    WsLayout L = ws_layout(B, nvec, V, false);
+    WsLayout L = ws_layout(B, nvec, V, use_small(V, dtype));
     if (workspace_bytes < L.total) return SD_ENOSPC;
     VecSet vs = {};
     vs.base[0] = tgt; vs.bs[0] = tgt_bs; vs.ps[0] = tgt_ps; vs.npos[0] = k + 1;
@@ -1731,7 +1752,7 @@ int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, in
   vs.base[0] = logits; vs.bs[0] = row_stride; vs.ps[0] = 0; vs.npos[0] = 1; vs.npos[1] = 0;
   vs.nrows = B;
   if (!(temperature > 0.0f)) {
-    WsLayout L = ws_layout(B, B, V, false);
+    WsLayout L = ws_layout(B, B, V, use_small(V, dtype));
     if (workspace_bytes < L.total) return SD_ENOSPC;
     ArgmaxParams P;
     P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = B;
@@ -1766,7 +1787,7 @@ int sd_to_probs(const void* logits, int64_t row_stride, int dtype, int n_rows, i
   vs.nrows = n_rows;
   const bool greedy = !(temperature > 0.0f);
   const bool small = !greedy && use_small(V, dtype);
-  WsLayout L = ws_layout(n_rows, n_rows, V, small);
+  WsLayout L = ws_layout(n_rows, n_rows, V, use_small(V, dtype));
   if (workspace_bytes < L.total) return SD_ENOSPC;
   ProbsParams P;
   P.vs = vs; P.dtype = dtype; P.V = V; P.nch = nch_for(V); P.chunk = (V + P.nch - 1) / P.nch;
