@@ -131,9 +131,15 @@ struct HistBuf {
   uint16_t occ[CT];                      // populated-group mask per 128-key segment
 };
 
+constexpr int SEL_CAP = 4096;            // entries sorted per vector
+constexpr int NBIN = 49;                 // coarse depth bins: 4 per base-2 unit, + overflow
+
 struct ListBuf {
-  unsigned long long key[LIST_CAP];      // (fkey(value) << 32) | ~index
-  float p[LIST_CAP];
+  unsigned long long key[LIST_CAP];      // (fkey(value) << 32) | ~index, append order
+  unsigned long long sel[SEL_CAP];       // entries selected for sorting
+  float p[SEL_CAP];
+  float binmass[NBIN];
+  int bincnt[NBIN];
 };
 
 struct HistSmem {
@@ -152,6 +158,8 @@ struct HistSmem {
   int ncorr;
   int corr_full;
   int nlist;
+  int nsel;
+  uint32_t gkey;       // fkey of the CTA's running maximum of the current vector
   int abort_flag;
   uint32_t keyk16;
   uint32_t vstar16;
@@ -650,23 +658,44 @@ struct Stream {
   double bulk;    // sum of 2^((x - m) c2) over unlisted elements, relative to m
 };
 
+// Append `key` for the lanes with `pred` set: one shared atomic per warp.
+__device__ __forceinline__ void warp_append(int* counter, unsigned long long* buf, int cap,
+                                            bool pred, unsigned long long key) {
+  const unsigned mask = __ballot_sync(0xffffffffu, pred);
+  if (!mask) return;
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(mask) - 1;
+  int base = 0;
+  if (lane == leader) base = atomicAdd(counter, __popc(mask));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  if (pred) {
+    const int slot = base + __popc(mask & ((1u << lane) - 1u));
+    if (slot < cap) buf[slot] = key;
+  }
+}
+
+// One group of N (<= 8) elements; called by all 32 lanes of a warp (lanes with
+// no data pass N = 0 elements through `valid`).
 template <int N>
-__device__ __forceinline__ void stream_group(HistSmem& s, Stream& st, const uint32_t* w,
+__device__ __forceinline__ void stream_group(HistSmem& s, Stream& st, const uint32_t* w, bool valid,
                                              uint32_t j0, int dtype, float c2, float wlist) {
   float x[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const uint32_t r = (e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xFFFFu);
-    x[e] = (e < N) ? bits16_to_float(r, dtype) : -INFINITY;
+    x[e] = (valid && e < N) ? bits16_to_float(r, dtype) : -INFINITY;
   }
   float gm = x[0];
 #pragma unroll
   for (int e = 1; e < N; ++e) gm = fmaxf(gm, x[e]);
-  if (gm > st.m) {
-    if (st.bulk != 0.0) st.bulk *= (double)ex2_approx((st.m - gm) * c2);
-    st.m = gm;
-    st.mc = gm * c2;
-    st.thr = gm - wlist;
+  const float shared_m = fkey_value(*reinterpret_cast<volatile uint32_t*>(&s.gkey));
+  if (gm > shared_m) atomicMax(&s.gkey, fkey(gm));
+  const float mn = fmaxf(gm, shared_m);
+  if (mn > st.m) {
+    if (st.bulk != 0.0) st.bulk *= (double)ex2_approx((st.m - mn) * c2);
+    st.m = mn;
+    st.mc = mn * c2;
+    st.thr = mn - wlist;
   }
   float gs = 0.f;
 #pragma unroll
@@ -674,10 +703,7 @@ __device__ __forceinline__ void stream_group(HistSmem& s, Stream& st, const uint
     const bool listed = x[e] >= st.thr;
     const float ev = ex2_approx(fmaf(x[e], c2, -st.mc));
     gs += listed ? 0.f : ev;
-    if (listed) {
-      const int slot = atomicAdd(&s.nlist, 1);
-      if (slot < LIST_CAP) s.u.l.key[slot] = list_key(x[e], j0 + e);
-    }
+    warp_append(&s.nlist, s.u.l.key, LIST_CAP, listed, list_key(x[e], j0 + e));
   }
   st.bulk += (double)gs;
 }
@@ -711,89 +737,117 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
   const int V = P.V;
   const bool topk_on = P.top_k > 0 && P.top_k < V;
   const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
+  const bool all_kept = !topk_on && !topp_on;
   const float tp32 = P.top_p;
   const int nl = s.nlist;
   if (nl > LIST_CAP || nl < 1) return true;
-  const float M = c_max<float>(st.m, s.fred, -INFINITY);
-  int N = 1;
-  while (N < nl) N <<= 1;
-  for (int i = nl + t; i < N; i += CT) s.u.l.key[i] = 0ull;
-  cbar();
-  bitonic_sort(s.u.l.key, N, true);
+  const float M = fkey_value(s.gkey);                   // every element raised gkey
   const float m = scaled_logit(M, P.T);
-  double es = 0.0;
-  for (int i = t; i < nl; i += CT) {
-    const float e = softmax_num(list_val(s.u.l.key[i]), P.T, m);
-    s.u.l.p[i] = e;
-    es += (double)e;
-  }
-  double sb = 0.0;
-  if (st.bulk > 0.0 && st.m > -INFINITY) sb = st.bulk * (double)exp2f((st.m - M) * c2);
-  const double S_list = c_sum<double>(es, s.dred);
-  const double S_bulk = c_sum<double>(sb, s.dred);
-  const double S = S_list + S_bulk;
-  const float inv_s = __double2float_rn(1.0 / S);
   const float wlow = M - wlist;
-  int ncomp = 0;
+  if (t < NBIN) { s.u.l.binmass[t] = 0.f; s.u.l.bincnt[t] = 0; }
+  cbar();
+  // exact softmax numerators of the listed elements; complete ones are binned
+  // by depth below the maximum (4 bins per base-2 unit)
+  double es = 0.0;
+  if (st.bulk > 0.0 && st.m > -INFINITY) es = st.bulk * (double)exp2f((st.m - M) * c2);
   for (int i = t; i < nl; i += CT) {
-    s.u.l.p[i] = __fmul_rn(s.u.l.p[i], inv_s);
-    ncomp += list_val(s.u.l.key[i]) >= wlow;
+    const float xv = list_val(s.u.l.key[i]);
+    const float e = softmax_num(xv, P.T, m);
+    es += (double)e;
+    if (!all_kept && xv >= wlow) {
+      const int bin = min(NBIN - 1, (int)((M - xv) * c2 * 4.f));
+      atomicAdd(&s.u.l.binmass[bin], e);
+      atomicAdd(&s.u.l.bincnt[bin], 1);
+    }
   }
-  ncomp = c_sum<int>(ncomp, reinterpret_cast<int*>(s.ured));
-  float kth_x = -INFINITY;
-  int n_eff = ncomp;
-  if (topk_on) {
-    if (P.top_k > ncomp) return true;
-    kth_x = list_val(s.u.l.key[P.top_k - 1]);
-    int c = 0;
-    for (int i = t; i < nl; i += CT) c += list_val(s.u.l.key[i]) >= kth_x;
-    n_eff = c_sum<int>(c, reinterpret_cast<int*>(s.ured));
-  }
+  const double S = c_sum<double>(es, s.dred);
+  const float inv_s = __double2float_rn(1.0 / S);
   int L = -1;
-  bool all_kept = false;
-  if (topp_on) {
-    if (t == 0) s.sc_L = 0x7FFFFFFF;
-    cbar();
-    double carry = 0.0;
-    for (int base = 0; base < n_eff; base += CT) {
-      const int i = base + t;
-      const float p = i < n_eff ? s.u.l.p[i] : 0.f;
-      double tot;
-      const double pre = c_excl_scan<double>((double)p, s.dred, &tot);
-      if (i < n_eff && i > 0) {
-        const float cl = __fsub_rn(__double2float_rn(carry + pre + (double)p), p);
-        if (!(cl < tp32)) atomicMin(&s.sc_L, i);
+  float kth_x = -INFINITY;
+  if (!all_kept) {
+    // shallowest depth holding top_p of the mass and top_k elements, plus the
+    // next occupied bin (so the first dropped element is among those sorted)
+    if (t == 0) {
+      const double target = topp_on ? (double)tp32 * S * (1.0 + 1e-4) : 0.0;
+      double cm = 0.0;
+      int cc = 0, bstar = NBIN - 1;
+      for (int b = 0; b < NBIN; ++b) {
+        cm += (double)s.u.l.binmass[b];
+        cc += s.u.l.bincnt[b];
+        if (cm >= target && (!topk_on || cc >= P.top_k)) { bstar = b; break; }
       }
-      carry += tot;
+      for (int b = bstar + 1; b < NBIN; ++b)
+        if (s.u.l.bincnt[b] > 0) { bstar = b; break; }
+      s.ured[37] = (uint32_t)bstar;
+      s.nsel = 0;
+    }
+    cbar();
+    const int bstar = (int)s.ured[37];
+    const int iters = (nl + CT - 1) / CT;
+    for (int it = 0; it < iters; ++it) {
+      const int i = t + it * CT;
+      const unsigned long long key = i < nl ? s.u.l.key[i] : 0ull;
+      const float xv = list_val(key);
+      const bool take = i < nl && xv >= wlow && min(NBIN - 1, (int)((M - xv) * c2 * 4.f)) <= bstar;
+      warp_append(&s.nsel, s.u.l.sel, SEL_CAP, take, key);
+    }
+    cbar();
+    const int nsel = s.nsel;
+    if (nsel > SEL_CAP || nsel < 1) return true;
+    int N = 1;
+    while (N < nsel) N <<= 1;
+    for (int i = nsel + t; i < N; i += CT) s.u.l.sel[i] = 0ull;
+    cbar();
+    bitonic_sort(s.u.l.sel, N, true);
+    for (int i = t; i < nsel; i += CT)
+      s.u.l.p[i] = __fmul_rn(softmax_num(list_val(s.u.l.sel[i]), P.T, m), inv_s);
+    cbar();
+    int n_eff = nsel;
+    if (topk_on) {
+      if (P.top_k > nsel) return true;
+      kth_x = list_val(s.u.l.sel[P.top_k - 1]);
+      int c = 0;
+      for (int i = t; i < nsel; i += CT) c += list_val(s.u.l.sel[i]) >= kth_x;
+      n_eff = c_sum<int>(c, reinterpret_cast<int*>(s.ured));
+    }
+    if (topp_on) {
+      if (t == 0) s.sc_L = 0x7FFFFFFF;
       cbar();
-      if (s.sc_L != 0x7FFFFFFF) break;
-    }
-    const int D = s.sc_L;
-    if (D != 0x7FFFFFFF) {
-      L = D - 1;
-    } else if (topk_on || ncomp == V) {
-      L = n_eff - 1;
+      double carry = 0.0;
+      for (int base = 0; base < n_eff; base += CT) {
+        const int i = base + t;
+        const float p = i < n_eff ? s.u.l.p[i] : 0.f;
+        double tot;
+        const double pre = c_excl_scan<double>((double)p, s.dred, &tot);
+        if (i < n_eff && i > 0) {
+          const float cl = __fsub_rn(__double2float_rn(carry + pre + (double)p), p);
+          if (!(cl < tp32)) atomicMin(&s.sc_L, i);
+        }
+        carry += tot;
+        cbar();
+        if (s.sc_L != 0x7FFFFFFF) break;
+      }
+      const int D = s.sc_L;
+      if (D != 0x7FFFFFFF) L = D - 1;
+      else if (topk_on) L = n_eff - 1;
+      else return true;            // boundary below the sorted part: exact path
     } else {
-      return true;                 // the boundary lies below the complete part of the list
+      L = n_eff - 1;
     }
-  } else if (topk_on) {
-    L = n_eff - 1;
-  } else {
-    all_kept = true;
   }
-  double zs = 0.0;
+  double z;
   if (all_kept) {
-    for (int i = t; i < nl; i += CT) zs += (double)s.u.l.p[i];
+    z = S * (double)inv_s;
   } else {
+    double zs = 0.0;
     for (int i = t; i <= L; i += CT) zs += (double)s.u.l.p[i];
+    z = c_sum<double>(zs, s.dred);
   }
-  double z = c_sum<double>(zs, s.dred);
-  if (all_kept) z += S_bulk * (double)inv_s;
   const float zf = fmaxf(__double2float_rn(z), 1e-12f);
   const bool listed = P.nuc != nullptr && !all_kept && L + 1 <= NUC_MAX;
   if (listed) {
     unsigned long long* dst = P.nuc + (int64_t)v * NUC_MAX;
-    for (int i = t; i <= L; i += CT) dst[i] = s.u.l.key[i];
+    for (int i = t; i <= L; i += CT) dst[i] = s.u.l.sel[i];
   }
   if (t == 0) {
     VecStats o;
@@ -801,8 +855,8 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
     o.inv_s = inv_s;
     o.zf = zf;
     o.kth = topk_on ? fkey(kth_x) : 0u;
-    o.vstar = all_kept ? 0u : (uint32_t)(s.u.l.key[L] >> 32);
-    o.idx_cut = all_kept ? (int32_t)NO_CUT : (int32_t)list_idx(s.u.l.key[L]);
+    o.vstar = all_kept ? 0u : (uint32_t)(s.u.l.sel[L] >> 32);
+    o.idx_cut = all_kept ? (int32_t)NO_CUT : (int32_t)list_idx(s.u.l.sel[L]);
     o.argmax = -1;
     o.flags = (all_kept ? F_ALLKEPT : 0) | (listed ? F_LISTED : 0);
     o.n_keep = all_kept ? -1 : L + 1;
@@ -857,12 +911,12 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
     while (N < cnt) N <<= 1;
     const unsigned long long* src = P.nuc + (int64_t)(vrow + ppos) * NUC_MAX;
     for (int i = t; i < N; i += CT)
-      s.u.l.key[i] = i < cnt ? (unsigned long long)list_idx(__ldcg(src + i)) : ~0ull;
+      s.u.l.sel[i] = i < cnt ? (unsigned long long)list_idx(__ldcg(src + i)) : ~0ull;
     cbar();
-    bitonic_sort(s.u.l.key, N, false);        // kept elements in vocabulary order
+    bitonic_sort(s.u.l.sel, N, false);        // kept elements in vocabulary order
     double rs = 0.0;
     for (int i = t; i < cnt; i += CT) {
-      const int64_t j = (int64_t)s.u.l.key[i];
+      const int64_t j = (int64_t)s.u.l.sel[i];
       const float pj = stats_prob(stp, xp, P.dtype, P.T, j);
       float r = pj;
       if (resid && pj != 0.f) r = fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
@@ -873,7 +927,7 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
     if (resid && __double2float_rn(R) <= 1e-9f) {        // sampling.py:86-89: fall back to p
       rs = 0.0;
       for (int i = t; i < cnt; i += CT) {
-        const float pj = stats_prob(stp, xp, P.dtype, P.T, (int64_t)s.u.l.key[i]);
+        const float pj = stats_prob(stp, xp, P.dtype, P.T, (int64_t)s.u.l.sel[i]);
         s.u.l.p[i] = pj;
         rs += (double)pj;
       }
@@ -887,15 +941,15 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
       double tot;
       const double pre = c_excl_scan<double>((double)r, s.dred, &tot);
       if (i < cnt && carry + pre <= tgt && carry + pre + (double)r > tgt)
-        s.sc_y = (long long)s.u.l.key[i];
+        s.sc_y = (long long)s.u.l.sel[i];
       carry += tot;
       cbar();
       if (s.sc_y >= 0) break;
     }
     if (t == 0 && s.sc_y < 0) {
       for (int i = cnt - 1; i >= 0; --i)
-        if (s.u.l.p[i] > 0.f) { s.sc_y = (long long)s.u.l.key[i]; break; }
-      if (s.sc_y < 0) s.sc_y = (long long)s.u.l.key[0];
+        if (s.u.l.p[i] > 0.f) { s.sc_y = (long long)s.u.l.sel[i]; break; }
+      if (s.sc_y < 0) s.sc_y = (long long)s.u.l.sel[0];
     }
   } else {
     // kept set not listed: two ordered passes over the whole vocabulary
@@ -977,6 +1031,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
     }
     s.abort_flag = 0;
     s.nlist = 0;
+    s.gkey = 0u;
     s.ncorr = 0;
     s.corr_full = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1026,11 +1081,12 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
     const VecGeom gm(x, V);
     Stream st;
     st.m = -INFINITY; st.mc = -INFINITY; st.thr = -INFINITY; st.bulk = 0.0;
-    const int nrag = gm.head + (V - gm.tail0);
-    for (int i = t; i < nrag; i += CT) {
-      const int j = i < gm.head ? i : gm.tail0 + (i - gm.head);
-      const uint32_t w[4] = {__ldg(x + j), 0u, 0u, 0u};
-      stream_group<1>(s, st, w, (uint32_t)j, P.dtype, c2, wlist);
+    const int nrag = gm.head + (V - gm.tail0);        // < 16 ragged elements
+    if (t < 32 && nrag > 0) {
+      const bool valid = t < nrag;
+      const int j = !valid ? 0 : (t < gm.head ? t : gm.tail0 + (t - gm.head));
+      const uint32_t w[4] = {valid ? (uint32_t)__ldg(x + j) : 0u, 0u, 0u, 0u};
+      stream_group<1>(s, st, w, valid, (uint32_t)j, P.dtype, c2, wlist);
     }
     bool aborted = false;
     for (int c = 0; c < gm.nchunk; ++c, ++g) {
@@ -1053,6 +1109,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
           }
         }
         cm = c_max<float>(cm, s.fred, -INFINITY);
+        if (t == 0) atomicMax(&s.gkey, fkey(cm));
         if (cm > st.m) {
           if (st.bulk != 0.0) st.bulk *= (double)ex2_approx((st.m - cm) * c2);
           st.m = cm;
@@ -1060,10 +1117,13 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
           st.thr = cm - wlist;
         }
       }
-      for (int u = t; u < units; u += CT) {
-        const uint4 w4 = u4[u];
+      const int iters = (units + CT - 1) / CT;
+      for (int it = 0; it < iters; ++it) {
+        const int u = t + it * CT;
+        const bool valid = u < units;
+        const uint4 w4 = valid ? u4[u] : make_uint4(0, 0, 0, 0);
         const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-        stream_group<8>(s, st, w, jbase + 8u * (uint32_t)u, P.dtype, c2, wlist);
+        stream_group<8>(s, st, w, valid, jbase + 8u * (uint32_t)u, P.dtype, c2, wlist);
       }
       __syncwarp();
       if ((t & 31) == 0) mbar_arrive(&s.empty[sl]);
@@ -1082,7 +1142,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
       cbar();
       if (s.last_row) finish_row(s, P, row);
     }
-    if (t == 0) s.nlist = 0;
+    if (t == 0) { s.nlist = 0; s.gkey = 0u; }
     cbar();
   }
 }
