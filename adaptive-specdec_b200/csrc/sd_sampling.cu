@@ -110,14 +110,16 @@ __device__ __forceinline__ int64_t vec_probe(const VecSet& vs, int set, int row,
 // accept test and its residual / bonus draw.  Outside the nucleus of p the
 // residual max(p - q, 0) is zero, so the draw only walks p's kept elements in
 // index order (q gathered at those indices).
-constexpr int NCW = 16;                  // consumer warps
+constexpr int NCW = 8;                   // consumer warps
 constexpr int CT = NCW * 32;             // consumer threads
 constexpr int HT = CT + 32;              // + one producer warp
-constexpr int SLOT = 16384;              // bytes per ring slot
+constexpr int CTAS_PER_SM = 2;           // one CTA's per-vector work overlaps the other's streaming
+constexpr int GRID_MAX = 2 * 160;        // bound on the persistent grid (fallback buffers)
+constexpr int SLOT = 12288;              // bytes per ring slot
 constexpr int NSLOT = 4;
 constexpr long long WAIT_CYCLES = 1LL << 32;   // ~2 s at 2 GHz: bound on every wait
-constexpr int LIST_CAP = 8192;           // listed elements per vector
-constexpr int NUC_MAX = 4096;            // kept elements stored per vector for the draw
+constexpr int LIST_CAP = 4096;           // listed elements per vector
+constexpr int NUC_MAX = 2048;            // kept elements stored per vector for the draw
 constexpr float W_LIST = 12.f;           // list window, base-2 units below the maximum
 
 constexpr int F_FALLBACK = 1;            // exact full-histogram path taken
@@ -125,13 +127,16 @@ constexpr int F_INEXACT = 2;             // that path's correction table overflo
 constexpr int F_LISTED = 4;              // kept elements stored in the workspace
 constexpr int F_ALLKEPT = 8;             // no truncation: every element kept
 
+constexpr int NSEG = 512;                // 128-key segments of the 16-bit key space
+
+// Shared-memory part of the exact full-histogram path; the 65,536 counters
+// themselves live in a per-CTA global buffer (the path is rare).
 struct HistBuf {
-  uint32_t hist[HIST_WORDS];             // 128 KB: two 16-bit counters per word
   uint16_t list[NGROUP];                 // populated key groups, descending key order
-  uint16_t occ[CT];                      // populated-group mask per 128-key segment
+  uint16_t occ[NSEG];                    // populated-group mask per 128-key segment
 };
 
-constexpr int SEL_CAP = 4096;            // entries sorted per vector
+constexpr int SEL_CAP = 2048;            // entries sorted per vector
 constexpr int NBIN = 49;                 // coarse depth bins: 4 per base-2 unit, + overflow
 
 struct ListBuf {
@@ -155,6 +160,7 @@ struct HistSmem {
   float fred[40];
   alignas(8) unsigned long long full[NSLOT];
   alignas(8) unsigned long long empty[NSLOT];
+  uint32_t* gh;        // this CTA's global 65,536-counter histogram (fallback path)
   int ncorr;
   int corr_full;
   int nlist;
@@ -175,7 +181,7 @@ struct HistSmem {
   double sc_pre;
 };
 
-__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 template <typename T>
 __device__ __forceinline__ T c_sum(T v, T* red) {
@@ -309,7 +315,7 @@ __device__ void bitonic_sort(unsigned long long* key, int N, bool descending) {
 
 // ---- exact full-histogram path (fallback) ---------------------------------
 __device__ __forceinline__ uint32_t hist_field(const HistSmem& s, uint32_t raw) {
-  return (s.u.h.hist[raw >> 1] >> ((raw & 1u) << 4)) & 0xFFFFu;
+  return (__ldcg(&s.gh[raw >> 1]) >> ((raw & 1u) << 4)) & 0xFFFFu;
 }
 
 __device__ __forceinline__ uint32_t hist_count(const HistSmem& s, uint32_t raw) {
@@ -331,7 +337,7 @@ __device__ __forceinline__ void corr_log(HistSmem& s, uint32_t raw, int add) {
 __device__ void merge_signed_zero(HistSmem& s) {
   const uint32_t fneg0 = hist_field(s, 0x8000u);
   if (fneg0) {
-    s.u.h.hist[0x4000] &= 0xFFFF0000u;
+    s.gh[0x4000] &= 0xFFFF0000u;
     corr_log(s, 0u, (int)fneg0);
   }
   const int n = min(s.ncorr, NCORR_MAX);
@@ -343,7 +349,7 @@ __device__ void merge_signed_zero(HistSmem& s) {
 // correction table (the returned old word shows it).
 __device__ __forceinline__ void hist_add_checked(HistSmem& s, uint32_t raw) {
   const uint32_t inc = 1u << ((raw & 1u) << 4);
-  const uint32_t old = atomicAdd(&s.u.h.hist[raw >> 1], inc);
+  const uint32_t old = atomicAdd(&s.gh[raw >> 1], inc);
   if ((raw & 1u) == 0u) {
     if ((old & 0xFFFFu) == 0xFFFFu) {        // low counter wrapped, carried into high
       corr_log(s, raw, 65536);
@@ -356,40 +362,41 @@ __device__ __forceinline__ void hist_add_checked(HistSmem& s, uint32_t raw) {
 }
 
 __device__ void hist_clear_all(HistSmem& s) {
-  uint4* h = reinterpret_cast<uint4*>(s.u.h.hist);
+  uint4* h = reinterpret_cast<uint4*>(s.gh);
   for (int i = threadIdx.x; i < HIST_WORDS / 4; i += CT) h[i] = make_uint4(0, 0, 0, 0);
   if (threadIdx.x == 0) { s.ncorr = 0; s.corr_full = 0; }
+  __threadfence_block();
 }
 
-// Pass A: consumer thread t owns segment t = key groups [16t, 16t+16).
+// Pass A: segments seg = t, t + CT, ... (segment = key groups [16 seg, 16 seg + 16)).
 __device__ void hist_pass_a(HistSmem& s, uint32_t* maxkey_out) {
-  const int t = threadIdx.x;
-  uint32_t occ = 0, kmax = 0;
+  uint32_t kmax = 0;
   bool any = false;
-#pragma unroll 4
-  for (int jj = 0; jj < 16; ++jj) {
-    const int j = (jj + t) & 15;                 // bank-conflict-free order
-    const uint32_t G = 16u * t + j;
-    const bool pos = G >= 4096u;
-    const uint32_t wo = pos ? 4u * (G - 4096u) : 0x7FFCu - 4u * G;
-    const uint4 w = *reinterpret_cast<const uint4*>(&s.u.h.hist[wo]);
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-    int hi_idx = -1, lo_idx = 8;
+  for (int seg = threadIdx.x; seg < NSEG; seg += CT) {
+    uint32_t occ = 0;
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t G = 16u * seg + j;
+      const bool pos = G >= 4096u;
+      const uint32_t wo = pos ? 4u * (G - 4096u) : 0x7FFCu - 4u * G;
+      const uint4 w = __ldcg(reinterpret_cast<const uint4*>(&s.gh[wo]));
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      int hi_idx = -1, lo_idx = 8;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t f0 = ws[q] & 0xFFFFu, f1 = ws[q] >> 16;
-      if (f0) { hi_idx = max(hi_idx, 2 * q); lo_idx = min(lo_idx, 2 * q); }
-      if (f1) { hi_idx = max(hi_idx, 2 * q + 1); lo_idx = min(lo_idx, 2 * q + 1); }
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t f0 = ws[q] & 0xFFFFu, f1 = ws[q] >> 16;
+        if (f0) { hi_idx = max(hi_idx, 2 * q); lo_idx = min(lo_idx, 2 * q); }
+        if (f1) { hi_idx = max(hi_idx, 2 * q + 1); lo_idx = min(lo_idx, 2 * q + 1); }
+      }
+      if (hi_idx >= 0) {
+        occ |= 1u << j;
+        const uint32_t raw = 2u * wo + (pos ? (uint32_t)hi_idx : (uint32_t)lo_idx);
+        const uint32_t key = key16(raw);
+        kmax = any ? max(kmax, key) : key;
+        any = true;
+      }
     }
-    if (hi_idx >= 0) {
-      occ |= 1u << j;
-      const uint32_t raw = 2u * wo + (pos ? (uint32_t)hi_idx : (uint32_t)lo_idx);
-      const uint32_t key = key16(raw);
-      kmax = any ? max(kmax, key) : key;
-      any = true;
-    }
+    s.u.h.occ[seg] = (uint16_t)occ;
   }
-  s.u.h.occ[t] = (uint16_t)occ;
   *maxkey_out = c_max<uint32_t>(any ? kmax : 0u, s.ured, 0u);
 }
 
@@ -400,6 +407,7 @@ struct StatsParams {
   int top_k;
   VecStats* stats;
   unsigned long long* nuc;   // [nvec, NUC_MAX] kept elements (list keys)
+  uint32_t* ghist;           // [grid, 32768] counters for the exact fallback path
   int* row_ctr;              // [rows] vectors finished per row (zeroed before launch)
   int* status;               // device status word: bit0 = a bounded wait timed out
   // fused row finish (top-p / top-k modes)
@@ -445,13 +453,22 @@ __device__ void finalize_histogram(HistSmem& s, const StatsParams& P, int v, con
   maxkey = s.ured[34];
   const float m = scaled_logit(bits16_to_float(raw16(maxkey), P.dtype), P.T);
 
-  {   // populated groups in descending key order: thread t handles segment CT-1-t
-    const int seg = CT - 1 - t;
-    const uint32_t o = s.u.h.occ[seg];
+  {   // populated groups in descending key order: thread t handles segments
+      // NSEG-1-(2t), NSEG-2-(2t) (two consecutive segments, descending)
+    constexpr int SPT = NSEG / CT;
+    uint32_t o[SPT];
+    uint32_t cnt = 0;
+    for (int q = 0; q < SPT; ++q) {
+      o[q] = s.u.h.occ[NSEG - 1 - (SPT * t + q)];
+      cnt += __popc(o[q]);
+    }
     uint32_t tot;
-    uint32_t off = c_excl_scan<uint32_t>(__popc(o), s.ured, &tot);
-    for (int j = 15; j >= 0; --j)
-      if (o & (1u << j)) s.u.h.list[off++] = (uint16_t)(16 * seg + j);
+    uint32_t off = c_excl_scan<uint32_t>(cnt, s.ured, &tot);
+    for (int q = 0; q < SPT; ++q) {
+      const int seg = NSEG - 1 - (SPT * t + q);
+      for (int j = 15; j >= 0; --j)
+        if (o[q] & (1u << j)) s.u.h.list[off++] = (uint16_t)(16 * seg + j);
+    }
     cbar();
     if (t == 0) s.ured[35] = tot;
     cbar();
@@ -674,16 +691,22 @@ __device__ __forceinline__ void warp_append(int* counter, unsigned long long* bu
   }
 }
 
-// One group of N (<= 8) elements; called by all 32 lanes of a warp (lanes with
-// no data pass N = 0 elements through `valid`).
-template <int N>
+template <int DT>
+__device__ __forceinline__ float b16f(uint32_t b) {
+  if (DT == SD_DTYPE_BF16) return __uint_as_float(b << 16);
+  return __half2float(__ushort_as_half((unsigned short)b));
+}
+
+// One group of N (<= 8) elements; called by all 32 lanes of a warp (lanes
+// without data pass valid = false).
+template <int DT, int N>
 __device__ __forceinline__ void stream_group(HistSmem& s, Stream& st, const uint32_t* w, bool valid,
-                                             uint32_t j0, int dtype, float c2, float wlist) {
+                                             uint32_t j0, float c2, float wlist) {
   float x[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
+  for (int e = 0; e < N; ++e) {
     const uint32_t r = (e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xFFFFu);
-    x[e] = (valid && e < N) ? bits16_to_float(r, dtype) : -INFINITY;
+    x[e] = valid ? b16f<DT>(r) : -INFINITY;
   }
   float gm = x[0];
 #pragma unroll
@@ -697,15 +720,22 @@ __device__ __forceinline__ void stream_group(HistSmem& s, Stream& st, const uint
     st.mc = mn * c2;
     st.thr = mn - wlist;
   }
-  float gs = 0.f;
+  bool lf[8];
+  bool any = false;
+  float g0 = 0.f, g1 = 0.f;
 #pragma unroll
   for (int e = 0; e < N; ++e) {
-    const bool listed = x[e] >= st.thr;
+    lf[e] = x[e] >= st.thr;
+    any |= lf[e];
     const float ev = ex2_approx(fmaf(x[e], c2, -st.mc));
-    gs += listed ? 0.f : ev;
-    warp_append(&s.nlist, s.u.l.key, LIST_CAP, listed, list_key(x[e], j0 + e));
+    if (e & 1) g1 += lf[e] ? 0.f : ev; else g0 += lf[e] ? 0.f : ev;
   }
-  st.bulk += (double)gs;
+  st.bulk += (double)(g0 + g1);
+  if (__any_sync(0xffffffffu, any)) {
+#pragma unroll
+    for (int e = 0; e < N; ++e)
+      warp_append(&s.nlist, s.u.l.key, LIST_CAP, lf[e], list_key(x[e], j0 + e));
+  }
 }
 
 // Probability of element j of a vector under its stats (the kept predicate
@@ -1015,7 +1045,8 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
   cbar();
 }
 
-__global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
+template <int DT>
+__global__ void __launch_bounds__(HT, CTAS_PER_SM) hist_stats_kernel(StatsParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   HistSmem& s = *reinterpret_cast<HistSmem*>(smem_raw);
   const int t = threadIdx.x;
@@ -1029,6 +1060,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], NCW);
     }
+    s.gh = P.ghist + (size_t)blockIdx.x * HIST_WORDS;
     s.abort_flag = 0;
     s.nlist = 0;
     s.gkey = 0u;
@@ -1086,7 +1118,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
       const bool valid = t < nrag;
       const int j = !valid ? 0 : (t < gm.head ? t : gm.tail0 + (t - gm.head));
       const uint32_t w[4] = {valid ? (uint32_t)__ldg(x + j) : 0u, 0u, 0u, 0u};
-      stream_group<1>(s, st, w, valid, (uint32_t)j, P.dtype, c2, wlist);
+      stream_group<DT, 1>(s, st, w, valid, (uint32_t)j, c2, wlist);
     }
     bool aborted = false;
     for (int c = 0; c < gm.nchunk; ++c, ++g) {
@@ -1105,7 +1137,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const uint32_t r = (e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xFFFFu);
-            cm = fmaxf(cm, bits16_to_float(r, P.dtype));
+            cm = fmaxf(cm, b16f<DT>(r));
           }
         }
         cm = c_max<float>(cm, s.fred, -INFINITY);
@@ -1123,7 +1155,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
         const bool valid = u < units;
         const uint4 w4 = valid ? u4[u] : make_uint4(0, 0, 0, 0);
         const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-        stream_group<8>(s, st, w, valid, jbase + 8u * (uint32_t)u, P.dtype, c2, wlist);
+        stream_group<DT, 8>(s, st, w, valid, jbase + 8u * (uint32_t)u, c2, wlist);
       }
       __syncwarp();
       if ((t & 31) == 0) mbar_arrive(&s.empty[sl]);
@@ -1617,8 +1649,10 @@ static int device_sms() {
     g_num_sms[dev] = n > 0 ? n : 148;
   }
   if (!g_attr_set[dev]) {
-    cudaFuncSetAttribute(hist_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)sizeof(HistSmem));
+    cudaFuncSetAttribute(hist_stats_kernel<SD_DTYPE_BF16>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(HistSmem));
+    cudaFuncSetAttribute(hist_stats_kernel<SD_DTYPE_F16>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(HistSmem));
     g_attr_set[dev] = true;
   }
   return g_num_sms[dev];
@@ -1627,7 +1661,7 @@ static int device_sms() {
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct WsLayout {
-  size_t status, stats, partial, counter, vcounter, rcounter, apartial, mat, nuc, total;
+  size_t status, stats, partial, counter, vcounter, rcounter, apartial, mat, nuc, ghist, total;
 };
 
 static int nch_for(int V) {
@@ -1649,6 +1683,8 @@ static WsLayout ws_layout(int n_rows, int n_vec, int V, bool small) {
   L.apartial = off; off = align256(off + (size_t)n_vec * NCH_MAX * sizeof(unsigned long long));
   L.mat = off; off = align256(off + (small ? (size_t)n_vec * V * sizeof(float) : 0));
   L.nuc = off; off = align256(off + (small ? 0 : (size_t)n_vec * NUC_MAX * sizeof(unsigned long long)));
+  L.ghist = off;
+  off = align256(off + (small ? 0 : (size_t)GRID_MAX * HIST_WORDS * sizeof(uint32_t)));
   L.total = off;
   return L;
 }
@@ -1701,9 +1737,15 @@ static int run_sampling(const VecSet& vs, int nvec, int dtype, int V, float T, f
       if (cudaMemsetAsync(ws + L.rcounter, 0, (size_t)rows * sizeof(int), st) != cudaSuccess)
         return SD_ELAUNCH;
     }
+    P.ghist = reinterpret_cast<uint32_t*>(ws + L.ghist);
     const int nsm = device_sms();
-    const int grid = nvec < nsm ? nvec : nsm;
-    hist_stats_kernel<<<grid, HT, sizeof(HistSmem), st>>>(P);
+    int grid = CTAS_PER_SM * nsm;
+    if (grid > GRID_MAX) grid = GRID_MAX;
+    if (grid > nvec) grid = nvec;
+    if (dtype == SD_DTYPE_BF16)
+      hist_stats_kernel<SD_DTYPE_BF16><<<grid, HT, sizeof(HistSmem), st>>>(P);
+    else
+      hist_stats_kernel<SD_DTYPE_F16><<<grid, HT, sizeof(HistSmem), st>>>(P);
     if (int rc = check_launch()) return rc;
     need_finish = draw != nullptr && !fused;
     if (need_finish &&
