@@ -115,8 +115,9 @@ constexpr int CT = NCW * 32;             // consumer threads
 constexpr int HT = CT + 32;              // + one producer warp
 constexpr int CTAS_PER_SM = 2;           // one CTA's per-vector work overlaps the other's streaming
 constexpr int GRID_MAX = 2 * 160;        // bound on the persistent grid (fallback buffers)
-constexpr int SLOT = 12288;              // bytes per ring slot
-constexpr int NSLOT = 4;
+constexpr int GPS = 4;                   // 16-byte groups per consumer thread per ring slot
+constexpr int SLOT = GPS * 16 * 256;     // bytes per ring slot (16 KB)
+constexpr int NSLOT = 3;
 constexpr long long WAIT_CYCLES = 1LL << 32;   // ~2 s at 2 GHz: bound on every wait
 constexpr int LIST_CAP = 4096;           // listed elements per vector
 constexpr int NUC_MAX = 2048;            // kept elements stored per vector for the draw
@@ -165,6 +166,7 @@ struct HistSmem {
   int corr_full;
   int nlist;
   int nsel;
+  int wcnt[CT];        // list entries per consumer thread segment
   uint32_t gkey;       // fkey of the CTA's running maximum of the current vector
   int abort_flag;
   uint32_t keyk16;
@@ -668,11 +670,14 @@ __device__ void finalize_histogram(HistSmem& s, const StatsParams& P, int v, con
 }
 
 // ---- streaming ---------------------------------------------------------------
+constexpr int SEG = LIST_CAP / CT;       // list slots owned by each consumer thread
+
 struct Stream {
   float m;        // running max (logit units)
   float mc;       // m * c2
   float thr;      // m - wlist: listed at or above
   double bulk;    // sum of 2^((x - m) c2) over unlisted elements, relative to m
+  int wcnt;       // elements this thread has listed
 };
 
 // Append `key` for the lanes with `pred` set: one shared atomic per warp.
@@ -697,45 +702,77 @@ __device__ __forceinline__ float b16f(uint32_t b) {
   return __half2float(__ushort_as_half((unsigned short)b));
 }
 
-// One group of N (<= 8) elements; called by all 32 lanes of a warp (lanes
-// without data pass valid = false).
-template <int DT, int N>
-__device__ __forceinline__ void stream_group(HistSmem& s, Stream& st, const uint32_t* w, bool valid,
-                                             uint32_t j0, float c2, float wlist) {
-  float x[8];
+// Raise this thread's running max to mn (> st.m), rescaling its bulk sums.
+__device__ __forceinline__ void raise_max(Stream& st, float mn, float c2, float wlist, float& a0,
+                                          float& a1) {
+  const float f = ex2_approx((st.m - mn) * c2);      // 0 when st.m = -inf
+  st.bulk *= (double)f;
+  a0 *= f;
+  a1 *= f;
+  st.m = mn;
+  st.mc = mn * c2;
+  st.thr = mn - wlist;
+}
+
+// Append this thread's flagged elements to its own list slots.
+__device__ __forceinline__ void list_elems(HistSmem& s, Stream& st, const float* x, uint32_t lf,
+                                           uint32_t j0) {
+  unsigned long long* seg = s.u.l.key + threadIdx.x * SEG;
 #pragma unroll
-  for (int e = 0; e < N; ++e) {
-    const uint32_t r = (e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xFFFFu);
-    x[e] = valid ? b16f<DT>(r) : -INFINITY;
+  for (int e = 0; e < 8; ++e) {
+    if ((lf >> e) & 1u) {
+      if (st.wcnt < SEG) seg[st.wcnt] = list_key(x[e], j0 + e);
+      ++st.wcnt;
+    }
   }
-  float gm = x[0];
+}
+
+// G groups of 8 elements (w[4g..4g+3]); lanes without data pass valid = 0.
+// a0 / a1 accumulate the bulk mass relative to st.m.
+template <int DT, int G>
+__device__ __forceinline__ void stream_groups(HistSmem& s, Stream& st, const uint32_t* w,
+                                              const bool* valid, const uint32_t* j0, float c2,
+                                              float wlist, float& a0, float& a1) {
+  float x[G][8];
 #pragma unroll
-  for (int e = 1; e < N; ++e) gm = fmaxf(gm, x[e]);
-  const float shared_m = fkey_value(*reinterpret_cast<volatile uint32_t*>(&s.gkey));
-  if (gm > shared_m) atomicMax(&s.gkey, fkey(gm));
-  const float mn = fmaxf(gm, shared_m);
-  if (mn > st.m) {
-    if (st.bulk != 0.0) st.bulk *= (double)ex2_approx((st.m - mn) * c2);
-    st.m = mn;
-    st.mc = mn * c2;
-    st.thr = mn - wlist;
-  }
-  bool lf[8];
-  bool any = false;
-  float g0 = 0.f, g1 = 0.f;
+  for (int g = 0; g < G; ++g) {
 #pragma unroll
-  for (int e = 0; e < N; ++e) {
-    lf[e] = x[e] >= st.thr;
-    any |= lf[e];
-    const float ev = ex2_approx(fmaf(x[e], c2, -st.mc));
-    if (e & 1) g1 += lf[e] ? 0.f : ev; else g0 += lf[e] ? 0.f : ev;
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t r = (e & 1) ? (w[4 * g + (e >> 1)] >> 16) : (w[4 * g + (e >> 1)] & 0xFFFFu);
+      x[g][e] = valid[g] ? b16f<DT>(r) : -INFINITY;
+    }
   }
-  st.bulk += (double)(g0 + g1);
-  if (__any_sync(0xffffffffu, any)) {
+  float gm = -INFINITY;
 #pragma unroll
-    for (int e = 0; e < N; ++e)
-      warp_append(&s.nlist, s.u.l.key, LIST_CAP, lf[e], list_key(x[e], j0 + e));
+  for (int g = 0; g < G; ++g)
+    gm = fmaxf(gm, fmaxf(fmaxf(fmaxf(x[g][0], x[g][1]), fmaxf(x[g][2], x[g][3])),
+                         fmaxf(fmaxf(x[g][4], x[g][5]), fmaxf(x[g][6], x[g][7]))));
+  if (gm > st.m) {                                   // rare once the window has settled
+    atomicMax(&s.gkey, fkey(gm));
+    raise_max(st, gm, c2, wlist, a0, a1);
   }
+  uint32_t lf[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    lf[g] = 0u;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const bool listed = x[g][e] >= st.thr;
+      lf[g] |= (uint32_t)listed << e;
+      const float ev = ex2_approx(fmaf(x[g][e], c2, -st.mc));
+      if (e & 1) a1 += listed ? 0.f : ev; else a0 += listed ? 0.f : ev;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+    if (lf[g]) list_elems(s, st, x[g], lf[g], j0[g]);
+}
+
+// Start of a ring slot: adopt the CTA's running max if it is ahead.
+__device__ __forceinline__ void sync_max(HistSmem& s, Stream& st, float c2, float wlist) {
+  const float sm = fkey_value(*reinterpret_cast<volatile uint32_t*>(&s.gkey));
+  float a0 = 0.f, a1 = 0.f;
+  if (sm > st.m) raise_max(st, sm, c2, wlist, a0, a1);
 }
 
 // Probability of element j of a vector under its stats (the kept predicate
@@ -780,7 +817,8 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
   // by depth below the maximum (4 bins per base-2 unit)
   double es = 0.0;
   if (st.bulk > 0.0 && st.m > -INFINITY) es = st.bulk * (double)exp2f((st.m - M) * c2);
-  for (int i = t; i < nl; i += CT) {
+  for (int i = t; i < LIST_CAP; i += CT) {
+    if ((i % SEG) >= s.wcnt[i / SEG]) continue;
     const float xv = list_val(s.u.l.key[i]);
     const float e = softmax_num(xv, P.T, m);
     es += (double)e;
@@ -813,12 +851,12 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
     }
     cbar();
     const int bstar = (int)s.ured[37];
-    const int iters = (nl + CT - 1) / CT;
-    for (int it = 0; it < iters; ++it) {
+    for (int it = 0; it < LIST_CAP / CT; ++it) {
       const int i = t + it * CT;
-      const unsigned long long key = i < nl ? s.u.l.key[i] : 0ull;
+      const bool in = (i % SEG) < s.wcnt[i / SEG];
+      const unsigned long long key = in ? s.u.l.key[i] : 0ull;
       const float xv = list_val(key);
-      const bool take = i < nl && xv >= wlow && min(NBIN - 1, (int)((M - xv) * c2 * 4.f)) <= bstar;
+      const bool take = in && xv >= wlow && min(NBIN - 1, (int)((M - xv) * c2 * 4.f)) <= bstar;
       warp_append(&s.nsel, s.u.l.sel, SEL_CAP, take, key);
     }
     cbar();
@@ -1112,13 +1150,18 @@ __global__ void __launch_bounds__(HT, CTAS_PER_SM) hist_stats_kernel(StatsParams
     const int64_t probe = vec_probe(P.vs, set, row, pos);
     const VecGeom gm(x, V);
     Stream st;
-    st.m = -INFINITY; st.mc = -INFINITY; st.thr = -INFINITY; st.bulk = 0.0;
+    st.m = -INFINITY; st.mc = -INFINITY; st.thr = -INFINITY; st.bulk = 0.0; st.wcnt = 0;
     const int nrag = gm.head + (V - gm.tail0);        // < 16 ragged elements
     if (t < 32 && nrag > 0) {
       const bool valid = t < nrag;
       const int j = !valid ? 0 : (t < gm.head ? t : gm.tail0 + (t - gm.head));
       const uint32_t w[4] = {valid ? (uint32_t)__ldg(x + j) : 0u, 0u, 0u, 0u};
-      stream_group<DT, 1>(s, st, w, valid, (uint32_t)j, c2, wlist);
+      float a0 = 0.f, a1 = 0.f;
+      const uint32_t wv[4] = {w[0], 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u};   // -inf padding
+      const bool vv[1] = {valid};
+      const uint32_t jj[1] = {(uint32_t)j};
+      stream_groups<DT, 1>(s, st, wv, vv, jj, c2, wlist, a0, a1);
+      st.bulk += (double)(a0 + a1);
     }
     bool aborted = false;
     for (int c = 0; c < gm.nchunk; ++c, ++g) {
@@ -1142,23 +1185,31 @@ __global__ void __launch_bounds__(HT, CTAS_PER_SM) hist_stats_kernel(StatsParams
         }
         cm = c_max<float>(cm, s.fred, -INFINITY);
         if (t == 0) atomicMax(&s.gkey, fkey(cm));
-        if (cm > st.m) {
-          if (st.bulk != 0.0) st.bulk *= (double)ex2_approx((st.m - cm) * c2);
-          st.m = cm;
-          st.mc = cm * c2;
-          st.thr = cm - wlist;
-        }
+        cbar();
       }
-      const int iters = (units + CT - 1) / CT;
-      for (int it = 0; it < iters; ++it) {
-        const int u = t + it * CT;
-        const bool valid = u < units;
-        const uint4 w4 = valid ? u4[u] : make_uint4(0, 0, 0, 0);
-        const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-        stream_group<DT, 8>(s, st, w, valid, jbase + 8u * (uint32_t)u, c2, wlist);
+      sync_max(s, st, c2, wlist);
+      float a0 = 0.f, a1 = 0.f;
+      uint32_t w[4 * GPS];
+      bool valid[GPS];
+      uint32_t j0[GPS];
+#pragma unroll
+      for (int g = 0; g < GPS; ++g) {
+        const int u = t + g * CT;
+        valid[g] = u < units;
+        const uint4 w4 = valid[g] ? u4[u] : make_uint4(0, 0, 0, 0);
+        w[4 * g] = w4.x; w[4 * g + 1] = w4.y; w[4 * g + 2] = w4.z; w[4 * g + 3] = w4.w;
+        j0[g] = jbase + 8u * (uint32_t)u;
       }
+      stream_groups<DT, GPS>(s, st, w, valid, j0, c2, wlist, a0, a1);
+      st.bulk += (double)(a0 + a1);
       __syncwarp();
       if ((t & 31) == 0) mbar_arrive(&s.empty[sl]);
+    }
+    s.wcnt[t] = st.wcnt;
+    {
+      const int tot = c_sum<int>(st.wcnt, reinterpret_cast<int*>(s.ured));
+      const int ovf = c_max<int>(st.wcnt > SEG ? 1 : 0, reinterpret_cast<int*>(s.ured), 0);
+      if (t == 0) s.nlist = ovf ? LIST_CAP + 1 : tot;
     }
     cbar();
     if (aborted || s.abort_flag) {
