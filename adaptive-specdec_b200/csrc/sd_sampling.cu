@@ -52,7 +52,8 @@ struct VecStats {
   int32_t argmax;   // greedy: first index of the maximum
   int32_t flags;    // bit0: histogram overflow path taken; bit1: correction table full
   int32_t n_keep;   // kept members of the boundary class (diagnostics)
-  int32_t pad[2];
+  int32_t fb_why;   // FB_* reason when the histogram path ran, else 0
+  int32_t pad;
 };
 static_assert(sizeof(VecStats) == 48, "VecStats layout");
 
@@ -119,11 +120,17 @@ constexpr int GPS = 4;                   // 16-byte groups per consumer thread p
 constexpr int SLOT = GPS * 16 * 256;     // bytes per ring slot (16 KB)
 constexpr int NSLOT = 3;
 constexpr long long WAIT_CYCLES = 1LL << 32;   // ~2 s at 2 GHz: bound on every wait
-constexpr int LIST_CAP = 4096;           // listed elements per vector
-constexpr int NUC_MAX = 2048;            // kept elements stored per vector for the draw
+constexpr int LIST_CAP = 2048;           // listed elements per vector
+constexpr int REC_CAP = 2048;            // hot (lane, ring slot) records per vector
+constexpr int NUC_MAX = 1024;            // kept elements stored per vector for the draw
 constexpr float W_LIST = 12.f;           // list window, base-2 units below the maximum
 
 constexpr int F_FALLBACK = 1;            // exact full-histogram path taken
+// why the list path handed a vector to the histogram path (VecStats.fb_why)
+constexpr int FB_RECORDS = 1;            // more hot records than REC_CAP
+constexpr int FB_LIST = 2;               // more listed elements than LIST_CAP
+constexpr int FB_SELECT = 3;             // more selected elements than SEL_CAP
+constexpr int FB_BOUNDARY = 4;           // top-p / top-k boundary outside the sorted part
 constexpr int F_INEXACT = 2;             // that path's correction table overflowed
 constexpr int F_LISTED = 4;              // kept elements stored in the workspace
 constexpr int F_ALLKEPT = 8;             // no truncation: every element kept
@@ -137,15 +144,21 @@ struct HistBuf {
   uint16_t occ[NSEG];                    // populated-group mask per 128-key segment
 };
 
-constexpr int SEL_CAP = 2048;            // entries sorted per vector
+constexpr int SEL_CAP = 1024;            // entries sorted per vector
 constexpr int NBIN = 49;                 // coarse depth bins: 4 per base-2 unit, + overflow
+constexpr int NBIN_PAD = 64;             // two bins per lane of one warp
 
+// Hot records: consumer thread t of ring chunk c (rec_ct = c << 16 | t) held
+// elements with y(x) >= rec_y under offset rec_r, excluded from its bulk sum.
 struct ListBuf {
-  unsigned long long key[LIST_CAP];      // (fkey(value) << 32) | ~index, append order
+  uint32_t rec_ct[REC_CAP];
+  float rec_y[REC_CAP];
+  float rec_r[REC_CAP];
+  unsigned long long key[LIST_CAP];      // (fkey(value) << 32) | ~index
   unsigned long long sel[SEL_CAP];       // entries selected for sorting
   float p[SEL_CAP];
-  float binmass[NBIN];
-  int bincnt[NBIN];
+  unsigned long long binfx[NBIN_PAD];    // depth-bin mass, 2^-40 fixed point
+  int bincnt[NBIN_PAD];
 };
 
 struct HistSmem {
@@ -164,9 +177,10 @@ struct HistSmem {
   uint32_t* gh;        // this CTA's global 65,536-counter histogram (fallback path)
   int ncorr;
   int corr_full;
-  int nlist;
   int nsel;
-  int wcnt[CT];        // list entries per consumer thread segment
+  int nrec;            // hot records of the current vector
+  int fb_why;          // FB_* reason of the last hand-over to the histogram path
+  int nkey;            // listed elements of the current vector
   uint32_t gkey;       // fkey of the CTA's running maximum of the current vector
   int abort_flag;
   uint32_t keyk16;
@@ -654,7 +668,8 @@ __device__ void finalize_histogram(HistSmem& s, const StatsParams& P, int v, con
     o.argmax = -1;
     o.flags = flags | ((!topp_on && !topk_on) ? F_ALLKEPT : 0);
     o.n_keep = -1;
-    o.pad[0] = o.pad[1] = 0;
+    o.fb_why = s.fb_why;
+    o.pad = 0;
     float pp = 0.f;
     if (probe >= 0 && probe < V) {
       const float xv = bits16_to_float(__ldg(x + probe), P.dtype);
@@ -670,14 +685,13 @@ __device__ void finalize_histogram(HistSmem& s, const StatsParams& P, int v, con
 }
 
 // ---- streaming ---------------------------------------------------------------
-constexpr int SEG = LIST_CAP / CT;       // list slots owned by each consumer thread
 
 struct Stream {
-  float m;        // running max (logit units)
-  float mc;       // m * c2
-  float thr;      // m - wlist: listed at or above
-  double bulk;    // sum of 2^((x - m) c2) over unlisted elements, relative to m
-  int wcnt;       // elements this thread has listed
+  float Rc2;      // exponent offset of the bulk sum: y(x) = x c2 - Rc2 (-inf until set)
+  float m;        // this lane's running max (logit units)
+  float Y;        // y(m - wlist): elements with y(x) >= Y are listed
+  uint32_t pkey;  // largest key this warp has published to the CTA max
+  double bulk;    // sum of 2^y(x) over the unlisted elements
 };
 
 // Append `key` for the lanes with `pred` set: one shared atomic per warp.
@@ -696,83 +710,168 @@ __device__ __forceinline__ void warp_append(int* counter, unsigned long long* bu
   }
 }
 
+// low / high element of a packed pair as float
 template <int DT>
-__device__ __forceinline__ float b16f(uint32_t b) {
-  if (DT == SD_DTYPE_BF16) return __uint_as_float(b << 16);
-  return __half2float(__ushort_as_half((unsigned short)b));
+__device__ __forceinline__ float lo16(uint32_t w) {
+  if (DT == SD_DTYPE_BF16) return __uint_as_float(w << 16);
+  return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu)));
+}
+template <int DT>
+__device__ __forceinline__ float hi16(uint32_t w) {
+  if (DT == SD_DTYPE_BF16) return __uint_as_float(w & 0xFFFF0000u);
+  return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+// packed pair of -inf
+template <int DT>
+__device__ __forceinline__ constexpr uint32_t neg_inf2() {
+  return DT == SD_DTYPE_BF16 ? 0xFF80FF80u : 0xFC00FC00u;
+}
+// element-wise max of two packed pairs
+template <int DT>
+__device__ __forceinline__ uint32_t pmax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if (DT == SD_DTYPE_BF16) asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// (y0, y1) = (x0, x1) * c + (d0, d1) on the paired FP32 pipe (each an IEEE fma)
+__device__ __forceinline__ void fma2(float& y0, float& y1, float x0, float x1, float c, float d0,
+                                     float d1) {
+  asm("{\n .reg .b64 A, B, C, D;\n mov.b64 A, {%2, %3};\n mov.b64 B, {%4, %4};\n"
+      " mov.b64 C, {%5, %6};\n fma.rn.f32x2 D, A, B, C;\n mov.b64 {%0, %1}, D;\n}"
+      : "=f"(y0), "=f"(y1) : "f"(x0), "f"(x1), "f"(c), "f"(d0), "f"(d1));
+}
+// (a0, a1) += (b0, b1)
+__device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n .reg .b64 A, B, D;\n mov.b64 A, {%0, %1};\n mov.b64 B, {%2, %3};\n"
+      " add.rn.f32x2 D, A, B;\n mov.b64 {%0, %1}, D;\n}"
+      : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
 }
 
-// Raise this thread's running max to mn (> st.m), rescaling its bulk sums.
-__device__ __forceinline__ void raise_max(Stream& st, float mn, float c2, float wlist, float& a0,
-                                          float& a1) {
-  const float f = ex2_approx((st.m - mn) * c2);      // 0 when st.m = -inf
-  st.bulk *= (double)f;
-  a0 *= f;
-  a1 *= f;
+// Base-2 exponent of an element relative to the bulk reference,
+// y(x) = x (c2h + c2l) - Rc2 with c2h + c2l = log2(e) / T to ~2^-48 and
+// c2h, c2l > 0.  Monotone non-decreasing in x (a composition of two fmas with
+// positive multipliers), so x >= thr implies y(x) >= y(thr); y(-inf) = -inf.
+__device__ __forceinline__ float yof(float x, float c2h, float c2l, float Rc2) {
+  return fmaf(x, c2h, fmaf(x, c2l, -Rc2));
+}
+__device__ __forceinline__ void yof2(float& y0, float& y1, float x0, float x1, float c2h,
+                                     float c2l, float Rc2) {
+  float i0, i1;
+  fma2(i0, i1, x0, x1, c2l, -Rc2, -Rc2);
+  fma2(y0, y1, x0, x1, c2h, i0, i1);
+}
+
+// Raise this lane's running max (list threshold follows).
+__device__ __forceinline__ void raise_m(Stream& st, float mn, float c2h, float c2l, float wlist) {
   st.m = mn;
-  st.mc = mn * c2;
-  st.thr = mn - wlist;
+  st.Y = yof(mn - wlist, c2h, c2l, st.Rc2);
 }
 
-// Append this thread's flagged elements to its own list slots.
-__device__ __forceinline__ void list_elems(HistSmem& s, Stream& st, const float* x, uint32_t lf,
-                                           uint32_t j0) {
-  unsigned long long* seg = s.u.l.key + threadIdx.x * SEG;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    if ((lf >> e) & 1u) {
-      if (st.wcnt < SEG) seg[st.wcnt] = list_key(x[e], j0 + e);
-      ++st.wcnt;
-    }
-  }
+// Fix the bulk reference of a lane that has none yet (its first finite element).
+__device__ __forceinline__ void set_ref(Stream& st, float r, float c2h, float c2l, float wlist) {
+  st.Rc2 = r * c2h;
+  st.m = fmaxf(st.m, r);
+  st.Y = yof(st.m - wlist, c2h, c2l, st.Rc2);
 }
 
-// G groups of 8 elements (w[4g..4g+3]); lanes without data pass valid = 0.
-// a0 / a1 accumulate the bulk mass relative to st.m.
+// Lane maximum of 4G packed words.
 template <int DT, int G>
-__device__ __forceinline__ void stream_groups(HistSmem& s, Stream& st, const uint32_t* w,
-                                              const bool* valid, const uint32_t* j0, float c2,
-                                              float wlist, float& a0, float& a1) {
-  float x[G][8];
+__device__ __forceinline__ float lane_max(const uint32_t* w, uint32_t* pm1) {
+  uint32_t pm[2 * G];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int i = 0; i < 2 * G; ++i) pm1[i] = pm[i] = pmax2<DT>(w[2 * i], w[2 * i + 1]);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const uint32_t r = (e & 1) ? (w[4 * g + (e >> 1)] >> 16) : (w[4 * g + (e >> 1)] & 0xFFFFu);
-      x[g][e] = valid[g] ? b16f<DT>(r) : -INFINITY;
+  for (int n = 2 * G; n > 1; n >>= 1) {
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) pm[i] = pmax2<DT>(pm[i], pm[i + n / 2]);
+  }
+  return fmaxf(lo16<DT>(pm[0]), hi16<DT>(pm[0]));
+}
+
+// 2^y summed over the elements of 4G packed words with y < Y (those with
+// y >= Y are listed instead).
+template <int DT, int G>
+__device__ __forceinline__ float bulk_words(const uint32_t* w, float c2h, float c2l, float Rc2,
+                                            float Y) {
+  float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4 * G; ++i) {
+    float y0, y1;
+    yof2(y0, y1, lo16<DT>(w[i]), hi16<DT>(w[i]), c2h, c2l, Rc2);
+    const float e0 = ex2_approx(y0 >= Y ? -INFINITY : y0);
+    const float e1 = ex2_approx(y1 >= Y ? -INFINITY : y1);
+    if (i & 1) add2(b2, b3, e0, e1); else add2(b0, b1, e0, e1);
+  }
+  return (b0 + b2) + (b1 + b3);
+}
+
+// One pass over 4G packed words per lane; groups without data hold -inf
+// pairs.  Called by whole warps.  RING: the words are lane t's 16-byte units
+// t + q * CT of ring chunk `chunk` of the vector body; a lane that
+// holds elements with y >= Y leaves a hot record and the list is built from
+// the records after the vector (one shared atomic per warp here).  Otherwise
+// (the < 16 ragged elements, one per lane in the low half of w[0], index jr)
+// the element itself is appended to the list.
+template <int DT, int G, bool RING>
+__device__ __forceinline__ void stream_words(HistSmem& s, Stream& st, const uint32_t* w,
+                                             uint32_t chunk, uint32_t jr, float c2h, float c2l,
+                                             float wlist) {
+  const int lane = threadIdx.x & 31;
+  uint32_t pm1[2 * G];
+  const float gm = lane_max<DT, G>(w, pm1);
+  if (st.Rc2 == -INFINITY && gm > -INFINITY) set_ref(st, gm, c2h, c2l, wlist);
+  const bool have = st.Rc2 != -INFINITY;
+  float b = 0.f, ygm = -INFINITY, Y = st.Y;
+  if (have) {
+    b = bulk_words<DT, G>(w, c2h, c2l, st.Rc2, Y);
+    ygm = yof(gm, c2h, c2l, st.Rc2);
+    if (ygm > 64.f) {
+      // far above the reference: move it up so that no partial sum overflows
+      // and redo this lane's words (a logit tens of units above everything
+      // seen before in the vector)
+      const float nr = st.Rc2 + (ygm - 32.f);
+      st.bulk *= exp2((double)st.Rc2 - (double)nr);
+      st.Rc2 = nr;
+      st.Y = Y = yof(st.m - wlist, c2h, c2l, nr);
+      b = bulk_words<DT, G>(w, c2h, c2l, nr, Y);
+      ygm = yof(gm, c2h, c2l, nr);
     }
+    st.bulk += (double)b;
   }
-  float gm = -INFINITY;
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-    gm = fmaxf(gm, fmaxf(fmaxf(fmaxf(x[g][0], x[g][1]), fmaxf(x[g][2], x[g][3])),
-                         fmaxf(fmaxf(x[g][4], x[g][5]), fmaxf(x[g][6], x[g][7]))));
-  if (gm > st.m) {                                   // rare once the window has settled
-    atomicMax(&s.gkey, fkey(gm));
-    raise_max(st, gm, c2, wlist, a0, a1);
-  }
-  uint32_t lf[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    lf[g] = 0u;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const bool listed = x[g][e] >= st.thr;
-      lf[g] |= (uint32_t)listed << e;
-      const float ev = ex2_approx(fmaf(x[g][e], c2, -st.mc));
-      if (e & 1) a1 += listed ? 0.f : ev; else a0 += listed ? 0.f : ev;
+  const bool hot = have && ygm >= Y;
+  if (RING) {
+    const unsigned hm = __ballot_sync(0xffffffffu, hot);
+    if (hm) {
+      const int leader = __ffs(hm) - 1;
+      int base = 0;
+      if (lane == leader) base = atomicAdd(&s.nrec, __popc(hm));
+      base = __shfl_sync(0xffffffffu, base, leader) + __popc(hm & ((1u << lane) - 1u));
+      if (hot && base < REC_CAP) {
+        s.u.l.rec_ct[base] = chunk << 16 | (uint32_t)threadIdx.x;
+        s.u.l.rec_y[base] = Y;
+        s.u.l.rec_r[base] = st.Rc2;
+      }
     }
+  } else {
+    const float xv = lo16<DT>(w[0]);                  // the lane's only element
+    warp_append(&s.nkey, s.u.l.key, LIST_CAP, hot && yof(xv, c2h, c2l, st.Rc2) >= Y,
+                list_key(xv, jr));
   }
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-    if (lf[g]) list_elems(s, st, x[g], lf[g], j0[g]);
+  if (gm > st.m) raise_m(st, gm, c2h, c2l, wlist);
+  const uint32_t wk = __reduce_max_sync(0xffffffffu, fkey(gm));
+  if (wk > st.pkey) {                                 // warp-uniform
+    if (lane == 0) atomicMax(&s.gkey, wk);
+    st.pkey = wk;
+  }
 }
 
 // Start of a ring slot: adopt the CTA's running max if it is ahead.
-__device__ __forceinline__ void sync_max(HistSmem& s, Stream& st, float c2, float wlist) {
-  const float sm = fkey_value(*reinterpret_cast<volatile uint32_t*>(&s.gkey));
-  float a0 = 0.f, a1 = 0.f;
-  if (sm > st.m) raise_max(st, sm, c2, wlist, a0, a1);
+__device__ __forceinline__ void sync_max(HistSmem& s, Stream& st, float c2h, float c2l,
+                                         float wlist) {
+  const uint32_t gk = *reinterpret_cast<volatile uint32_t*>(&s.gkey);
+  const float gv = fkey_value(gk);
+  if (st.Rc2 != -INFINITY && gv > st.m) raise_m(st, gv, c2h, c2l, wlist);
 }
 
 // Probability of element j of a vector under its stats (the kept predicate
@@ -798,118 +897,264 @@ __device__ __forceinline__ VecStats load_stats_cg(const VecStats* p) {
 
 // List-based exact computation (see the section comment).  Returns true when
 // the vector needs the exact full-histogram path.
+__device__ __forceinline__ int depth_bin(float M, float xv, float c2) {
+  return min(NBIN - 1, (int)((M - xv) * c2 * 4.f));
+}
+
+// Descending sort of one key per lane across a warp (bitonic network).
+__device__ __forceinline__ unsigned long long warp_sort_desc(unsigned long long key) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k2 = 2; k2 <= 32; k2 <<= 1) {
+#pragma unroll
+    for (int j2 = k2 >> 1; j2 > 0; j2 >>= 1) {
+      const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, j2);
+      const bool lower = (lane & j2) == 0;
+      const bool desc = (lane & k2) == 0;             // this half of the merge sorts descending
+      const bool take_max = lower == desc;
+      key = take_max ? (o > key ? o : key) : (o < key ? o : key);
+    }
+  }
+  return key;
+}
+
+// p' of element j (logit xv) under `o`: the kept predicate and fl(fl(e * inv_s) / zf).
+__device__ __forceinline__ float stats_prob_x(const VecStats& o, float xv, float T, int64_t j) {
+  const uint32_t kx = fkey(xv);
+  const bool kept = kx >= o.kth && (kx > o.vstar || (kx == o.vstar && j <= (int64_t)o.idx_cut));
+  return kept ? __fdiv_rn(prob_of(xv, T, o.m, o.inv_s), o.zf) : 0.f;
+}
+
+__device__ __forceinline__ bool fallback_why(HistSmem& s, int why) {
+  if (threadIdx.x == 0) s.fb_why = why;
+  return true;
+}
+
+template <int DT>
 __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& st, int v,
-                              const uint16_t* x, int64_t probe, float c2, float wlist) {
-  const int t = threadIdx.x;
+                              const uint16_t* x, int64_t probe, float c2, float c2l, float wlist) {
+  const int t = threadIdx.x, lane = t & 31;
   const int V = P.V;
   const bool topk_on = P.top_k > 0 && P.top_k < V;
   const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
   const bool all_kept = !topk_on && !topp_on;
   const float tp32 = P.top_p;
-  const int nl = s.nlist;
-  if (nl > LIST_CAP || nl < 1) return true;
+  // the list: the elements of the hot records (re-read, mostly from L2) with
+  // y >= Y under the record's offset, after the ragged ones already there;
+  // one record per thread per round, one shared atomic per warp per round
+  {
+    const int nrec = s.nrec;
+    if (nrec > REC_CAP) return fallback_why(s, FB_RECORDS);
+    const VecGeom g(x, V);
+    for (int base = 0; base < nrec; base += CT) {
+      const int r = base + t;
+      const bool rin = r < nrec;
+      uint32_t ct = 0u;
+      float ry = INFINITY, rr = 0.f;
+      if (rin) { ct = s.u.l.rec_ct[r]; ry = s.u.l.rec_y[r]; rr = s.u.l.rec_r[r]; }
+      const uint32_t j00 = (uint32_t)g.head + (ct >> 16) * (uint32_t)(SLOT / 2) + 8u * (ct & 0xFFFFu);
+      uint4 v4[GPS];
+#pragma unroll
+      for (int q = 0; q < GPS; ++q) {
+        const uint32_t j0 = j00 + 8u * (uint32_t)(q * CT);
+        v4[q] = make_uint4(0u, 0u, 0u, 0u);
+        if (rin && (int)j0 + 8 <= g.tail0) v4[q] = __ldg(reinterpret_cast<const uint4*>(x + j0));
+      }
+      static_assert(GPS == 4, "record listing selects among four 16-byte units");
+      uint32_t mask = 0u;
+#pragma unroll
+      for (int q = 0; q < GPS; ++q) {
+        const uint32_t ww[4] = {v4[q].x, v4[q].y, v4[q].z, v4[q].w};
+        const bool qin = rin && (int)(j00 + 8u * (uint32_t)(q * CT)) + 8 <= g.tail0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float xv = (e & 1) ? hi16<DT>(ww[e >> 1]) : lo16<DT>(ww[e >> 1]);
+          if (qin && yof(xv, c2, c2l, rr) >= ry) mask |= 1u << (q * 8 + e);
+        }
+      }
+      const int cnt = __popc(mask);
+      const int incl = warp_incl_scan<int>(cnt);
+      int wbase = 0;
+      if (lane == 31 && incl > 0) wbase = atomicAdd(&s.nkey, incl);
+      int o = __shfl_sync(0xffffffffu, wbase, 31) + incl - cnt;
+      while (mask) {
+        const int b = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        const int q = b >> 3, e = b & 7;
+        const uint4 vq = q == 0 ? v4[0] : q == 1 ? v4[1] : q == 2 ? v4[2] : v4[3];
+        const uint32_t wq = (e >> 1) == 0 ? vq.x : (e >> 1) == 1 ? vq.y : (e >> 1) == 2 ? vq.z : vq.w;
+        const float xv = (e & 1) ? hi16<DT>(wq) : lo16<DT>(wq);
+        if (o < LIST_CAP) s.u.l.key[o] = list_key(xv, j00 + 8u * (uint32_t)(q * CT) + (uint32_t)e);
+        ++o;
+      }
+    }
+    cbar();
+  }
+  const int nl = s.nkey;
+  if (nl > LIST_CAP || nl < 1) return fallback_why(s, FB_LIST);
+  // the probe's logit, requested now so that its latency overlaps the list work
+  const bool has_probe = probe >= 0 && probe < V;
+  float xprobe = 0.f;
+  if (t == 0 && has_probe) xprobe = bits16_to_float(__ldg(x + probe), P.dtype);
   const float M = fkey_value(s.gkey);                   // every element raised gkey
   const float m = scaled_logit(M, P.T);
   const float wlow = M - wlist;
-  if (t < NBIN) { s.u.l.binmass[t] = 0.f; s.u.l.bincnt[t] = 0; }
+  if (t < NBIN_PAD) { s.u.l.binfx[t] = 0ull; s.u.l.bincnt[t] = 0; }
   cbar();
-  // exact softmax numerators of the listed elements; complete ones are binned
-  // by depth below the maximum (4 bins per base-2 unit)
+  // exact softmax numerators of the listed elements (each thread its own list
+  // slots, then the shared overflow); complete ones are binned by depth below
+  // the maximum (4 bins per base-2 unit), mass in 2^-40 fixed point
   double es = 0.0;
-  if (st.bulk > 0.0 && st.m > -INFINITY) es = st.bulk * (double)exp2f((st.m - M) * c2);
-  for (int i = t; i < LIST_CAP; i += CT) {
-    if ((i % SEG) >= s.wcnt[i / SEG]) continue;
-    const float xv = list_val(s.u.l.key[i]);
-    const float e = softmax_num(xv, P.T, m);
+  // bulk terms are 2^(x c2 - Rc2); the listed ones exp(x / T - m)
+  if (st.bulk > 0.0 && st.Rc2 != -INFINITY)
+    es = st.bulk * exp2((double)st.Rc2 - (double)m * 1.4426950408889634);
+  auto tally = [&](unsigned long long key) {
+    const float xv = list_val(key);
+    const float e = softmax_num(xv, P.T, m);           // <= 1: xv <= M
     es += (double)e;
     if (!all_kept && xv >= wlow) {
-      const int bin = min(NBIN - 1, (int)((M - xv) * c2 * 4.f));
-      atomicAdd(&s.u.l.binmass[bin], e);
+      const int bin = depth_bin(M, xv, c2);
       atomicAdd(&s.u.l.bincnt[bin], 1);
+      atomicAdd(&s.u.l.binfx[bin], (unsigned long long)__float2ull_rn(e * 0x1p40f));
     }
-  }
+  };
+  for (int i = t; i < nl; i += CT) tally(s.u.l.key[i]);
   const double S = c_sum<double>(es, s.dred);
   const float inv_s = __double2float_rn(1.0 / S);
   int L = -1;
   float kth_x = -INFINITY;
+  double z = 0.0;
   if (!all_kept) {
-    // shallowest depth holding top_p of the mass and top_k elements, plus the
-    // next occupied bin (so the first dropped element is among those sorted)
-    if (t == 0) {
-      const double target = topp_on ? (double)tp32 * S * (1.0 + 1e-4) : 0.0;
-      double cm = 0.0;
-      int cc = 0, bstar = NBIN - 1;
-      for (int b = 0; b < NBIN; ++b) {
-        cm += (double)s.u.l.binmass[b];
-        cc += s.u.l.bincnt[b];
-        if (cm >= target && (!topk_on || cc >= P.top_k)) { bstar = b; break; }
+    if (t < 32) {
+      // shallowest depth bin holding top_p of the mass and top_k elements,
+      // plus the next occupied bin (so the first dropped element is among
+      // those sorted); lane l owns bins 2l and 2l+1
+      const unsigned long long f0 = s.u.l.binfx[2 * lane], f1 = s.u.l.binfx[2 * lane + 1];
+      const int c0 = s.u.l.bincnt[2 * lane], c1 = s.u.l.bincnt[2 * lane + 1];
+      const unsigned long long fi = warp_incl_scan<unsigned long long>(f0 + f1);
+      const int ci = warp_incl_scan<int>(c0 + c1);
+      const unsigned long long fe = fi - f0 - f1;
+      const int ce = ci - c0 - c1;
+      const double target = topp_on ? (double)tp32 * S * (1.0 + 1e-4) * 0x1p40 : 0.0;
+      const bool ok0 = (double)(fe + f0) >= target && (!topk_on || ce + c0 >= P.top_k);
+      const bool ok1 = (double)fi >= target && (!topk_on || ci >= P.top_k);
+      const unsigned okm = __ballot_sync(0xffffffffu, ok0 || ok1);
+      int bstar = NBIN - 1;
+      if (okm) {
+        const int fl = __ffs(okm) - 1;
+        bstar = 2 * fl + (__shfl_sync(0xffffffffu, ok0, fl) ? 0 : 1);
       }
-      for (int b = bstar + 1; b < NBIN; ++b)
-        if (s.u.l.bincnt[b] > 0) { bstar = b; break; }
-      s.ured[37] = (uint32_t)bstar;
-      s.nsel = 0;
+      const unsigned n0 = __ballot_sync(0xffffffffu, c0 > 0 && 2 * lane > bstar);
+      const unsigned n1 = __ballot_sync(0xffffffffu, c1 > 0 && 2 * lane + 1 > bstar);
+      int nb = NBIN_PAD;
+      if (n0) nb = min(nb, 2 * (__ffs(n0) - 1));
+      if (n1) nb = min(nb, 2 * (__ffs(n1) - 1) + 1);
+      if (nb < NBIN) bstar = nb;
+      // no occupied bin after bstar: the sorted part is the whole window, so
+      // the first element after it lies below the window
+      if (lane == 0) { s.ured[37] = (uint32_t)bstar; s.ured[36] = nb >= NBIN; s.nsel = 0; }
     }
     cbar();
     const int bstar = (int)s.ured[37];
-    for (int it = 0; it < LIST_CAP / CT; ++it) {
-      const int i = t + it * CT;
-      const bool in = (i % SEG) < s.wcnt[i / SEG];
+    const bool whole = s.ured[36] != 0u;
+    // all of the window sorted and its mass clear of top_p: every element of
+    // it is kept, the next one (outside) is the first dropped
+    const double tp_clear = (double)tp32 + 2e-6;
+    for (int base = 0; base < nl; base += CT) {
+      const int i = base + t;
+      const bool in = i < nl;
       const unsigned long long key = in ? s.u.l.key[i] : 0ull;
-      const float xv = list_val(key);
-      const bool take = in && xv >= wlow && min(NBIN - 1, (int)((M - xv) * c2 * 4.f)) <= bstar;
-      warp_append(&s.nsel, s.u.l.sel, SEL_CAP, take, key);
+      const float xv = in ? list_val(key) : -INFINITY;
+      warp_append(&s.nsel, s.u.l.sel, SEL_CAP, in && xv >= wlow && depth_bin(M, xv, c2) <= bstar,
+                  key);
     }
     cbar();
     const int nsel = s.nsel;
-    if (nsel > SEL_CAP || nsel < 1) return true;
-    int N = 1;
-    while (N < nsel) N <<= 1;
-    for (int i = nsel + t; i < N; i += CT) s.u.l.sel[i] = 0ull;
-    cbar();
-    bitonic_sort(s.u.l.sel, N, true);
-    for (int i = t; i < nsel; i += CT)
-      s.u.l.p[i] = __fmul_rn(softmax_num(list_val(s.u.l.sel[i]), P.T, m), inv_s);
-    cbar();
-    int n_eff = nsel;
-    if (topk_on) {
-      if (P.top_k > nsel) return true;
-      kth_x = list_val(s.u.l.sel[P.top_k - 1]);
-      int c = 0;
-      for (int i = t; i < nsel; i += CT) c += list_val(s.u.l.sel[i]) >= kth_x;
-      n_eff = c_sum<int>(c, reinterpret_cast<int*>(s.ured));
-    }
-    if (topp_on) {
-      if (t == 0) s.sc_L = 0x7FFFFFFF;
-      cbar();
-      double carry = 0.0;
-      for (int base = 0; base < n_eff; base += CT) {
-        const int i = base + t;
-        const float p = i < n_eff ? s.u.l.p[i] : 0.f;
-        double tot;
-        const double pre = c_excl_scan<double>((double)p, s.dred, &tot);
-        if (i < n_eff && i > 0) {
-          const float cl = __fsub_rn(__double2float_rn(carry + pre + (double)p), p);
-          if (!(cl < tp32)) atomicMin(&s.sc_L, i);
+    if (nsel > SEL_CAP || nsel < 1) return fallback_why(s, FB_SELECT);
+    if (nsel <= 32) {
+      // one warp: register sort, shuffle scans
+      if (t < 32) {
+        unsigned long long key = lane < nsel ? s.u.l.sel[lane] : 0ull;
+        key = warp_sort_desc(key);
+        s.u.l.sel[lane] = key;
+        const bool valid = lane < nsel;
+        const float xv = valid ? list_val(key) : 0.f;
+        const float p = valid ? __fmul_rn(softmax_num(xv, P.T, m), inv_s) : 0.f;
+        int n_eff = nsel, Lw = -1;
+        bool exact = false;
+        float kx = -INFINITY;
+        if (topk_on) {
+          if (P.top_k > nsel) {
+            exact = true;
+          } else {
+            kx = __shfl_sync(0xffffffffu, xv, P.top_k - 1);
+            n_eff = __popc(__ballot_sync(0xffffffffu, valid && xv >= kx));
+          }
         }
-        carry += tot;
-        cbar();
-        if (s.sc_L != 0x7FFFFFFF) break;
+        Lw = n_eff - 1;
+        if (!exact && topp_on) {
+          const double incl = warp_incl_scan<double>(lane < n_eff ? (double)p : 0.0);
+          const float cl = __fsub_rn(__double2float_rn(incl), p);
+          const unsigned dm = __ballot_sync(0xffffffffu, lane < n_eff && lane > 0 && !(cl < tp32));
+          const double last = __shfl_sync(0xffffffffu, incl, n_eff - 1);
+          if (dm) Lw = __ffs(dm) - 2;
+          else if (!topk_on && !(whole && last >= tp_clear)) exact = true;   // boundary deeper
+        }
+        const double zs = warp_sum<double>(lane <= Lw ? (double)p : 0.0);
+        if (lane == 0) { s.sc_L = exact ? -1 : Lw; s.z = zs; s.fred[39] = kx; }
       }
-      const int D = s.sc_L;
-      if (D != 0x7FFFFFFF) L = D - 1;
-      else if (topk_on) L = n_eff - 1;
-      else return true;            // boundary below the sorted part: exact path
+      cbar();
+      if (s.sc_L < 0) return fallback_why(s, FB_BOUNDARY);
+      L = s.sc_L;
+      kth_x = s.fred[39];
+      z = s.z;
     } else {
-      L = n_eff - 1;
+      int N = 1;
+      while (N < nsel) N <<= 1;
+      for (int i = nsel + t; i < N; i += CT) s.u.l.sel[i] = 0ull;
+      cbar();
+      bitonic_sort(s.u.l.sel, N, true);
+      for (int i = t; i < nsel; i += CT)
+        s.u.l.p[i] = __fmul_rn(softmax_num(list_val(s.u.l.sel[i]), P.T, m), inv_s);
+      cbar();
+      int n_eff = nsel;
+      if (topk_on) {
+        if (P.top_k > nsel) return fallback_why(s, FB_BOUNDARY);
+        kth_x = list_val(s.u.l.sel[P.top_k - 1]);
+        int c = 0;
+        for (int i = t; i < nsel; i += CT) c += list_val(s.u.l.sel[i]) >= kth_x;
+        n_eff = c_sum<int>(c, reinterpret_cast<int*>(s.ured));
+      }
+      if (topp_on) {
+        if (t == 0) s.sc_L = 0x7FFFFFFF;
+        cbar();
+        double carry = 0.0;
+        for (int base = 0; base < n_eff; base += CT) {
+          const int i = base + t;
+          const float p = i < n_eff ? s.u.l.p[i] : 0.f;
+          double tot;
+          const double pre = c_excl_scan<double>((double)p, s.dred, &tot);
+          if (i < n_eff && i > 0) {
+            const float cl = __fsub_rn(__double2float_rn(carry + pre + (double)p), p);
+            if (!(cl < tp32)) atomicMin(&s.sc_L, i);
+          }
+          carry += tot;
+          cbar();
+          if (s.sc_L != 0x7FFFFFFF) break;
+        }
+        const int D = s.sc_L;
+        if (D != 0x7FFFFFFF) L = D - 1;
+        else if (topk_on || (whole && carry >= tp_clear)) L = n_eff - 1;
+        else return fallback_why(s, FB_BOUNDARY);   // boundary below the sorted part
+      } else {
+        L = n_eff - 1;
+      }
+      double zs = 0.0;
+      for (int i = t; i <= L; i += CT) zs += (double)s.u.l.p[i];
+      z = c_sum<double>(zs, s.dred);
     }
-  }
-  double z;
-  if (all_kept) {
-    z = S * (double)inv_s;
   } else {
-    double zs = 0.0;
-    for (int i = t; i <= L; i += CT) zs += (double)s.u.l.p[i];
-    z = c_sum<double>(zs, s.dred);
+    z = S * (double)inv_s;
   }
   const float zf = fmaxf(__double2float_rn(z), 1e-12f);
   const bool listed = P.nuc != nullptr && !all_kept && L + 1 <= NUC_MAX;
@@ -928,9 +1173,9 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
     o.argmax = -1;
     o.flags = (all_kept ? F_ALLKEPT : 0) | (listed ? F_LISTED : 0);
     o.n_keep = all_kept ? -1 : L + 1;
-    o.pad[0] = o.pad[1] = 0;
-    o.probe_p = 0.f;
-    if (probe >= 0 && probe < V) o.probe_p = stats_prob(o, x, P.dtype, P.T, probe);
+    o.fb_why = 0;
+    o.pad = 0;
+    o.probe_p = has_probe ? stats_prob_x(o, xprobe, P.T, probe) : 0.f;
     P.stats[v] = o;
   }
   cbar();
@@ -945,18 +1190,26 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
   const int vrow = row * npos;
   const int k = P.k;
   __threadfence();
-  if (t == 0) {
-    int n = 0;
-    bool alive = P.alive ? P.alive[row] != 0 : true;
-    for (int i = 0; i < k; ++i) {
-      const float pxi = __ldcg(&P.stats[vrow + i].probe_p);
-      const float qxi = __ldcg(&P.stats[vrow + npos0 + i].probe_p);
-      const float thr = fminf(__fdiv_rn(pxi, fmaxf(qxi, 1e-10f)), 1.0f);
-      if (P.px) P.px[row * k + i] = pxi;
-      if (P.qx) P.qx[row * k + i] = qxi;
-      if (alive && n == i && P.u_acc[row * P.u_bs + i] < thr) ++n; else alive = false;
+  if (t < 32) {
+    // accepted prefix: one lane per draft position
+    const int lane = t;
+    int n = k;
+    for (int base = 0; base < k; base += 32) {
+      const int i = base + lane;
+      bool acc = false;
+      if (i < k) {
+        const float pxi = __ldcg(&P.stats[vrow + i].probe_p);
+        const float qxi = __ldcg(&P.stats[vrow + npos0 + i].probe_p);
+        const float thr = fminf(__fdiv_rn(pxi, fmaxf(qxi, 1e-10f)), 1.0f);
+        if (P.px) P.px[row * k + i] = pxi;
+        if (P.qx) P.qx[row * k + i] = qxi;
+        acc = P.u_acc[row * P.u_bs + i] < thr;
+      }
+      const unsigned rm = __ballot_sync(0xffffffffu, i < k && !acc);
+      if (rm && n == k) n = base + __ffs(rm) - 1;
     }
-    s.sc_n = n;
+    if (P.alive && P.alive[row] == 0) n = 0;
+    if (lane == 0) s.sc_n = n;
   }
   cbar();
   const int n = s.sc_n;
@@ -971,6 +1224,59 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
     xq = vec_ptr(P.vs, 1, row, n, P.dtype);
   }
   const double u = (double)P.u_res[row];
+  if ((stp.flags & F_LISTED) && stp.n_keep <= 32) {
+    // p's kept set fits one warp: values come with the stored keys, q is
+    // gathered at those indices, register sort into vocabulary order
+    if (t < 32) {
+      const int lane = t;
+      const int cnt = stp.n_keep;
+      const bool valid = lane < cnt;
+      const unsigned long long key =
+          valid ? __ldcg(P.nuc + (int64_t)(vrow + ppos) * NUC_MAX + lane) : 0ull;
+      int jj = valid ? (int)list_idx(key) : 0x7FFFFFFF;
+      float pp = valid ? __fdiv_rn(prob_of(list_val(key), P.T, stp.m, stp.inv_s), stp.zf) : 0.f;
+      float rr = pp;
+      if (resid && valid && pp != 0.f)
+        rr = fmaxf(__fsub_rn(pp, stats_prob(stq, xq, P.dtype, P.T, jj)), 0.f);
+#pragma unroll
+      for (int k2 = 2; k2 <= 32; k2 <<= 1) {
+#pragma unroll
+        for (int j2 = k2 >> 1; j2 > 0; j2 >>= 1) {
+          const int oj = __shfl_xor_sync(0xffffffffu, jj, j2);
+          const float orr = __shfl_xor_sync(0xffffffffu, rr, j2);
+          const float opp = __shfl_xor_sync(0xffffffffu, pp, j2);
+          const bool take_min = ((lane & j2) == 0) == ((lane & k2) == 0);
+          if (take_min ? (oj < jj) : (oj > jj)) { jj = oj; rr = orr; pp = opp; }
+        }
+      }
+      double R = warp_sum<double>((double)rr);
+      if (resid && __double2float_rn(R) <= 1e-9f) {         // sampling.py:86-89: fall back to p
+        rr = pp;
+        R = warp_sum<double>((double)pp);
+      }
+      const double tgt = u * R;
+      const double pre = warp_incl_scan<double>((double)rr) - (double)rr;
+      const unsigned hm =
+          __ballot_sync(0xffffffffu, lane < cnt && pre <= tgt && pre + (double)rr > tgt);
+      int ly = 0;
+      if (hm) {
+        ly = __ffs(hm) - 1;
+      } else {
+        const unsigned pm = __ballot_sync(0xffffffffu, lane < cnt && rr > 0.f);
+        if (pm) ly = 31 - __clz(pm);
+      }
+      const int yy = __shfl_sync(0xffffffffu, jj, ly);
+      const float ypp = __shfl_sync(0xffffffffu, pp, ly);
+      if (lane == 0) {
+        if (P.n_acc) P.n_acc[row] = n;
+        P.y[row] = yy;
+        if (P.y_prob) P.y_prob[row] = ypp;
+        P.row_ctr[row] = 0;
+      }
+    }
+    cbar();
+    return;
+  }
   if (t == 0) s.sc_y = -1;
   cbar();
   if (stp.flags & F_LISTED) {
@@ -1089,7 +1395,11 @@ __global__ void __launch_bounds__(HT, CTAS_PER_SM) hist_stats_kernel(StatsParams
   HistSmem& s = *reinterpret_cast<HistSmem*>(smem_raw);
   const int t = threadIdx.x;
   const int V = P.V;
-  const float c2 = 1.4426950408889634f / P.T;          // log2(e) / T
+  // log2(e) / T as c2 + c2l, c2 rounded down so that c2l > 0: y(x) is then
+  // monotone and y(-inf) = -inf (a negative c2l would give -inf + inf)
+  const double c2d = 1.4426950408889634 / (double)P.T;
+  const float c2 = __double2float_rd(c2d);
+  const float c2l = fmaxf((float)(c2d - (double)c2), __int_as_float(1));
   const float wlist = W_LIST / c2;                      // list window in logit units
   const int npos = P.vs.npos[0] + P.vs.npos[1];
 
@@ -1100,7 +1410,9 @@ __global__ void __launch_bounds__(HT, CTAS_PER_SM) hist_stats_kernel(StatsParams
     }
     s.gh = P.ghist + (size_t)blockIdx.x * HIST_WORDS;
     s.abort_flag = 0;
-    s.nlist = 0;
+    s.nrec = 0;
+    s.nkey = 0;
+    s.fb_why = 0;
     s.gkey = 0u;
     s.ncorr = 0;
     s.corr_full = 0;
@@ -1150,73 +1462,77 @@ __global__ void __launch_bounds__(HT, CTAS_PER_SM) hist_stats_kernel(StatsParams
     const int64_t probe = vec_probe(P.vs, set, row, pos);
     const VecGeom gm(x, V);
     Stream st;
-    st.m = -INFINITY; st.mc = -INFINITY; st.thr = -INFINITY; st.bulk = 0.0; st.wcnt = 0;
-    const int nrag = gm.head + (V - gm.tail0);        // < 16 ragged elements
-    if (t < 32 && nrag > 0) {
-      const bool valid = t < nrag;
-      const int j = !valid ? 0 : (t < gm.head ? t : gm.tail0 + (t - gm.head));
-      const uint32_t w[4] = {valid ? (uint32_t)__ldg(x + j) : 0u, 0u, 0u, 0u};
-      float a0 = 0.f, a1 = 0.f;
-      const uint32_t wv[4] = {w[0], 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u};   // -inf padding
-      const bool vv[1] = {valid};
-      const uint32_t jj[1] = {(uint32_t)j};
-      stream_groups<DT, 1>(s, st, wv, vv, jj, c2, wlist, a0, a1);
-      st.bulk += (double)(a0 + a1);
-    }
+    st.Rc2 = -INFINITY; st.m = -INFINITY; st.Y = INFINITY; st.pkey = 0u;
+    st.bulk = 0.0;
     bool aborted = false;
     for (int c = 0; c < gm.nchunk; ++c, ++g) {
       const int sl = g % NSLOT;
-      if (!mbar_wait(&s.full[sl], (g / NSLOT) & 1u, &s.abort_flag)) { aborted = true; break; }
-      const int units = min(SLOT, gm.nunits * 16 - c * SLOT) >> 4;
+      // warp-uniform: stream_words works on whole warps
+      bool okw = __all_sync(0xffffffffu, mbar_wait(&s.full[sl], (g / NSLOT) & 1u, &s.abort_flag));
+      const int units = okw ? min(SLOT, gm.nunits * 16 - c * SLOT) >> 4 : 0;
       const uint4* u4 = reinterpret_cast<const uint4*>(s.ring[sl]);
       const uint32_t jbase = (uint32_t)(gm.head + c * (SLOT / 2));
-      if (c == 0) {
-        // seed every thread's running max with the first chunk's maximum, so
-        // the list window starts near its final position
-        float cm = -INFINITY;
-        for (int u = t; u < units; u += CT) {
-          const uint4 w4 = u4[u];
-          const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+      uint32_t w[4 * GPS];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const uint32_t r = (e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xFFFFu);
-            cm = fmaxf(cm, b16f<DT>(r));
+      for (int q = 0; q < GPS; ++q) {
+        const int u = t + q * CT;
+        const uint32_t n2 = neg_inf2<DT>();
+        const uint4 w4 = u < units ? u4[u] : make_uint4(n2, n2, n2, n2);
+        w[4 * q] = w4.x; w[4 * q + 1] = w4.y; w[4 * q + 2] = w4.z; w[4 * q + 3] = w4.w;
+      }
+      if (c == 0) {
+        // the CTA-wide maximum of the chunks already in the ring: bulk
+        // reference of every lane and the first list threshold
+        uint32_t pm1[2 * GPS];
+        float lm = lane_max<DT, GPS>(w, pm1);
+        const int nseed = min(NSLOT, gm.nchunk);
+#pragma unroll 1
+        for (int i = 1; i < nseed; ++i) {
+          const uint32_t gi = g + (uint32_t)i;
+          okw = okw && __all_sync(0xffffffffu, mbar_wait(&s.full[gi % NSLOT], (gi / NSLOT) & 1u,
+                                                          &s.abort_flag));
+          if (okw) {
+            const int ui = min(SLOT, gm.nunits * 16 - i * SLOT) >> 4;
+            const uint4* wi4 = reinterpret_cast<const uint4*>(s.ring[gi % NSLOT]);
+            uint32_t wi[4 * GPS];
+#pragma unroll
+            for (int q = 0; q < GPS; ++q) {
+              const int u = t + q * CT;
+              const uint32_t n2 = neg_inf2<DT>();
+              const uint4 w4 = u < ui ? wi4[u] : make_uint4(n2, n2, n2, n2);
+              wi[4 * q] = w4.x; wi[4 * q + 1] = w4.y; wi[4 * q + 2] = w4.z; wi[4 * q + 3] = w4.w;
+            }
+            lm = fmaxf(lm, lane_max<DT, GPS>(wi, pm1));
           }
         }
-        cm = c_max<float>(cm, s.fred, -INFINITY);
-        if (t == 0) atomicMax(&s.gkey, fkey(cm));
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, fkey(lm));
+        if ((t & 31) == 0) atomicMax(&s.gkey, wk);
         cbar();
+        const float r = fkey_value(*reinterpret_cast<volatile uint32_t*>(&s.gkey));
+        if (r > -INFINITY) set_ref(st, r, c2, c2l, wlist);
       }
-      sync_max(s, st, c2, wlist);
-      float a0 = 0.f, a1 = 0.f;
-      uint32_t w[4 * GPS];
-      bool valid[GPS];
-      uint32_t j0[GPS];
-#pragma unroll
-      for (int g = 0; g < GPS; ++g) {
-        const int u = t + g * CT;
-        valid[g] = u < units;
-        const uint4 w4 = valid[g] ? u4[u] : make_uint4(0, 0, 0, 0);
-        w[4 * g] = w4.x; w[4 * g + 1] = w4.y; w[4 * g + 2] = w4.z; w[4 * g + 3] = w4.w;
-        j0[g] = jbase + 8u * (uint32_t)u;
-      }
-      stream_groups<DT, GPS>(s, st, w, valid, j0, c2, wlist, a0, a1);
-      st.bulk += (double)(a0 + a1);
+      if (!okw) { aborted = true; break; }
+      sync_max(s, st, c2, c2l, wlist);
+      stream_words<DT, GPS, true>(s, st, w, (uint32_t)c, 0u, c2, c2l, wlist);
       __syncwarp();
       if ((t & 31) == 0) mbar_arrive(&s.empty[sl]);
     }
-    s.wcnt[t] = st.wcnt;
-    {
-      const int tot = c_sum<int>(st.wcnt, reinterpret_cast<int*>(s.ured));
-      const int ovf = c_max<int>(st.wcnt > SEG ? 1 : 0, reinterpret_cast<int*>(s.ured), 0);
-      if (t == 0) s.nlist = ovf ? LIST_CAP + 1 : tot;
+    // ragged head / tail elements (< 16 of them), warp 0
+    const int nrag = gm.head + (V - gm.tail0);
+    if (t < 32 && nrag > 0 && !aborted) {
+      const bool valid = t < nrag;
+      const int j = !valid ? 0 : (t < gm.head ? t : gm.tail0 + (t - gm.head));
+      constexpr uint32_t NEG16 = neg_inf2<DT>() & 0xFFFFu;
+      const uint32_t lo = valid ? (uint32_t)__ldg(x + j) : NEG16;
+      const uint32_t wv[4] = {lo | (NEG16 << 16), neg_inf2<DT>(), neg_inf2<DT>(), neg_inf2<DT>()};
+      stream_words<DT, 1, false>(s, st, wv, 0u, (uint32_t)j, c2, c2l, wlist);
     }
     cbar();
     if (aborted || s.abort_flag) {
       if (t == 0) atomicOr(P.status, 1);
       break;
     }
-    if (finalize_list(s, P, st, v, x, probe, c2, wlist)) finalize_histogram(s, P, v, x, probe);
+    if (finalize_list<DT>(s, P, st, v, x, probe, c2, c2l, wlist)) finalize_histogram(s, P, v, x, probe);
     // row bookkeeping: the CTA that completes a row draws for it
     if (P.fused) {
       __threadfence();
@@ -1225,7 +1541,7 @@ __global__ void __launch_bounds__(HT, CTAS_PER_SM) hist_stats_kernel(StatsParams
       cbar();
       if (s.last_row) finish_row(s, P, row);
     }
-    if (t == 0) { s.nlist = 0; s.gkey = 0u; }
+    if (t == 0) { s.nrec = 0; s.nkey = 0; s.gkey = 0u; }
     cbar();
   }
 }
@@ -1346,7 +1662,7 @@ __global__ void __launch_bounds__(ST) small_stats_kernel(SmallParams P) {
     VecStats st;
     st.m = m; st.inv_s = inv_s; st.zf = zf;
     st.kth = 0; st.vstar = 0; st.idx_cut = (int32_t)NO_CUT; st.argmax = -1;
-    st.flags = 0; st.n_keep = -1; st.pad[0] = st.pad[1] = 0;
+    st.flags = 0; st.n_keep = -1; st.fb_why = 0; st.pad = 0;
     st.probe_p = (probe >= 0 && probe < V) ? out[probe] : 0.f;
     P.stats[v] = st;
   }
@@ -1404,7 +1720,7 @@ __global__ void __launch_bounds__(FT) argmax_kernel(ArgmaxParams P) {
     VecStats st;
     st.m = 0.f; st.inv_s = 1.f; st.zf = 1.f; st.probe_p = 0.f;
     st.kth = 0; st.vstar = 0; st.idx_cut = (int32_t)NO_CUT; st.argmax = am;
-    st.flags = 0; st.n_keep = -1; st.pad[0] = st.pad[1] = 0;
+    st.flags = 0; st.n_keep = -1; st.fb_why = 0; st.pad = 0;
     P.stats[v] = st;
     __threadfence();
     const int per = P.vs.npos[0];
