@@ -1471,7 +1471,6 @@ __global__ void __launch_bounds__(HT, CTAS_PER_SM) hist_stats_kernel(StatsParams
       bool okw = __all_sync(0xffffffffu, mbar_wait(&s.full[sl], (g / NSLOT) & 1u, &s.abort_flag));
       const int units = okw ? min(SLOT, gm.nunits * 16 - c * SLOT) >> 4 : 0;
       const uint4* u4 = reinterpret_cast<const uint4*>(s.ring[sl]);
-      const uint32_t jbase = (uint32_t)(gm.head + c * (SLOT / 2));
       uint32_t w[4 * GPS];
 #pragma unroll
       for (int q = 0; q < GPS; ++q) {
@@ -1673,7 +1672,7 @@ __global__ void __launch_bounds__(ST) small_stats_kernel(SmallParams P) {
 // ---------------------------------------------------------------------------
 struct ArgmaxParams {
   VecSet vs;           // set 0 only
-  int dtype, V, nvec, nch, chunk;
+  int dtype, V, nvec, nch, cu;   // nch blocks per vector, cu 16-byte units per block
   unsigned long long* partial;   // [nvec, nch]
   int* vec_counter;              // [nvec]
   int* row_counter;              // [rows]
@@ -1686,19 +1685,86 @@ struct ArgmaxParams {
   int64_t* n_acc; int64_t* y; float* px; float* qx;
 };
 
+template <int DT>
+__device__ __forceinline__ unsigned long long argmax_key(float x, int j) {
+  return ((unsigned long long)fkey(x) << 32) | (0xFFFFFFFFu - (uint32_t)j);
+}
+
+// Element-wise max of two packed 16-bit pairs, NaN propagating.
+template <int DT>
+__device__ __forceinline__ uint32_t pmax2_nan(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if (DT == SD_DTYPE_BF16) asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Argmax (first index of the maximum, NaN counting as the largest value) of a
+// vector: block c of the vector reads 16-byte units [c cu, (c+1) cu) of its
+// aligned body with vectorised loads (block 0 also the unaligned head, the
+// last block the tail).  For 16-bit logits a packed max of each unit's eight
+// elements skips the per-element keys unless the unit can hold a new maximum.
+template <int DT>
 __global__ void __launch_bounds__(FT) argmax_kernel(ArgmaxParams P) {
   __shared__ unsigned long long ured[40];
   __shared__ int last;
+  constexpr int ESZ = DT == SD_DTYPE_F32 ? 4 : 2;
+  constexpr int EPU = 16 / ESZ;
   const int c = blockIdx.x % P.nch, v = blockIdx.x / P.nch, t = threadIdx.x;
+  const int V = P.V;
   int set, row, pos;
   vec_locate(P.vs, v, &set, &row, &pos);
-  const void* x = vec_ptr(P.vs, set, row, pos, P.dtype);
-  const int j0 = c * P.chunk, j1 = min(P.V, j0 + P.chunk);
+  const char* xb = reinterpret_cast<const char*>(vec_ptr(P.vs, set, row, pos, DT));
+  int head = (int)(((16u - (uint32_t)(reinterpret_cast<uintptr_t>(xb) & 15u)) & 15u) / ESZ);
+  if (head > V) head = V;
+  const int nunits = (V - head) / EPU;
+  const int tail0 = head + nunits * EPU;
   unsigned long long best = 0ull;
-  for (int j = j0 + t; j < j1; j += FT) {
-    const unsigned long long key = ((unsigned long long)fkey(load_logit(x, P.dtype, j)) << 32) |
-                                   (0xFFFFFFFFu - (uint32_t)j);
-    best = key > best ? key : best;
+  if (c == 0 && t < head) best = argmax_key<DT>(load_logit(xb, DT, t), t);
+  if (c == P.nch - 1 && t < V - tail0) {
+    const unsigned long long kk = argmax_key<DT>(load_logit(xb, DT, tail0 + t), tail0 + t);
+    best = kk > best ? kk : best;
+  }
+  // lanes skip a unit unless it can reach the warp's best value so far
+  // (ties included: the first index among equal values is decided by keys)
+  uint32_t wthr = __reduce_max_sync(0xffffffffu, (uint32_t)(best >> 32));
+  const uint4* body = reinterpret_cast<const uint4*>(xb + (size_t)head * ESZ);
+  const int u1 = min((c + 1) * P.cu, nunits);
+  const int ub = c * P.cu + (t & ~31);                 // the warp iterates uniformly
+#pragma unroll 4
+  for (int uw = ub; uw < u1; uw += FT) {
+    const int u = uw + (t & 31);
+    uint32_t mk = 0u;                                   // key of the unit's maximum (0: no data)
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (u < u1) {
+      w = __ldg(body + u);
+      if (DT == SD_DTYPE_F32) {
+        mk = fkey(fmaxf(fmaxf(__uint_as_float(w.x), __uint_as_float(w.y)),
+                        fmaxf(__uint_as_float(w.z), __uint_as_float(w.w))));
+        const bool nan = __uint_as_float(w.x) != __uint_as_float(w.x) ||
+                         __uint_as_float(w.y) != __uint_as_float(w.y) ||
+                         __uint_as_float(w.z) != __uint_as_float(w.z) ||
+                         __uint_as_float(w.w) != __uint_as_float(w.w);
+        if (nan) mk = 0xFFFFFFFFu;
+      } else {
+        const uint32_t m = pmax2_nan<DT>(pmax2_nan<DT>(w.x, w.y), pmax2_nan<DT>(w.z, w.w));
+        const float lo = lo16<DT>(m), hi = hi16<DT>(m);
+        mk = (lo != lo || hi != hi) ? 0xFFFFFFFFu : fkey(fmaxf(lo, hi));
+      }
+    }
+    if (u < u1 && (mk >= wthr || mk == 0xFFFFFFFFu)) {   // may hold (or tie) the maximum
+      const int j0 = head + u * EPU;
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < EPU; ++e) {
+        float xv;
+        if (DT == SD_DTYPE_F32) xv = __uint_as_float(ww[e]);
+        else xv = (e & 1) ? hi16<DT>(ww[e >> 1]) : lo16<DT>(ww[e >> 1]);
+        const unsigned long long kk = argmax_key<DT>(xv, j0 + e);
+        best = kk > best ? kk : best;
+      }
+    }
+    wthr = __reduce_max_sync(0xffffffffu, (uint32_t)(best >> 32));
   }
   best = block_max<unsigned long long>(best, ured, 0ull);
   if (t == 0) {
@@ -2031,6 +2097,24 @@ struct WsLayout {
   size_t status, stats, partial, counter, vcounter, rcounter, apartial, mat, nuc, ghist, total;
 };
 
+// Argmax geometry: blocks per vector and 16-byte units per block (a multiple
+// of FT, at most NCH_MAX blocks).
+struct ArgmaxGeom {
+  int nch, cu;
+};
+static ArgmaxGeom argmax_geom(int V, int dtype) {
+  const int epu = dtype == SD_DTYPE_F32 ? 4 : 8;
+  const int units = V / epu + 1;
+  ArgmaxGeom g;
+  g.cu = 8 * FT;
+  g.nch = (units + g.cu - 1) / g.cu;
+  if (g.nch > NCH_MAX) {
+    g.nch = NCH_MAX;
+    g.cu = ((units + g.nch - 1) / g.nch + FT - 1) / FT * FT;
+  }
+  return g;
+}
+
 static int nch_for(int V) {
   int n = (V + 4095) / 4096;
   return n < 1 ? 1 : (n > NCH_MAX ? NCH_MAX : n);
@@ -2059,6 +2143,14 @@ static WsLayout ws_layout(int n_rows, int n_vec, int V, bool small) {
 static int check_launch() {
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
 }
+
+static int launch_argmax(const ArgmaxParams& P, cudaStream_t st) {
+  if (P.dtype == SD_DTYPE_BF16) argmax_kernel<SD_DTYPE_BF16><<<P.nch * P.nvec, FT, 0, st>>>(P);
+  else if (P.dtype == SD_DTYPE_F16) argmax_kernel<SD_DTYPE_F16><<<P.nch * P.nvec, FT, 0, st>>>(P);
+  else argmax_kernel<SD_DTYPE_F32><<<P.nch * P.nvec, FT, 0, st>>>(P);
+  return check_launch();
+}
+
 
 // What a verify / draft call draws (to_probs passes none).
 struct DrawSpec {
@@ -2142,6 +2234,34 @@ static int zero_argmax_counters(const WsLayout& L, int nvec, int nrows, char* ws
   return 0;
 }
 
+// Greedy verify round over caller-provided buffers: argmax of every target
+// vector, then per row the accepted prefix and the emitted token.  The two
+// counter arrays must hold zeros on entry (zeroed here on the stream).
+static int launch_greedy_verify(const void* tgt, int64_t tgt_bs, int64_t tgt_ps, int dtype,
+                                const int64_t* xs, int64_t xs_bs, const float* u_acc,
+                                int64_t u_bs, const uint8_t* alive, int B, int k, int V,
+                                int64_t* n_acc, int64_t* y, float* px, float* qx,
+                                VecStats* stats, unsigned long long* partial, int* vcounter,
+                                int* rcounter, cudaStream_t st) {
+  const int nvec = B * (k + 1);
+  VecSet vs = {};
+  vs.base[0] = tgt; vs.bs[0] = tgt_bs; vs.ps[0] = tgt_ps; vs.npos[0] = k + 1;
+  vs.npos[1] = 0; vs.nrows = B;
+  ArgmaxParams P;
+  P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec;
+  const ArgmaxGeom ag = argmax_geom(V, dtype);
+  P.nch = ag.nch; P.cu = ag.cu;
+  P.partial = partial;
+  P.vec_counter = vcounter;
+  P.row_counter = rcounter;
+  P.stats = stats;
+  P.k = k; P.xs = xs; P.xs_bs = xs_bs; P.u_acc = u_acc; P.u_bs = u_bs; P.alive = alive;
+  P.n_acc = n_acc; P.y = y; P.px = px; P.qx = qx;
+  if (cudaMemsetAsync(vcounter, 0, (size_t)nvec * sizeof(int), st) != cudaSuccess) return SD_ELAUNCH;
+  if (cudaMemsetAsync(rcounter, 0, (size_t)B * sizeof(int), st) != cudaSuccess) return SD_ELAUNCH;
+  return launch_argmax(P, st);
+}
+
 static int validate_common(int dtype, int V, float T) {
   if (dtype != SD_DTYPE_F32 && dtype != SD_DTYPE_F16 && dtype != SD_DTYPE_BF16) return SD_EINVAL;
   if (V <= 0 || V > (1 << 21)) return SD_EINVAL;
@@ -2179,21 +2299,11 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
     const int nvec = B * (k + 1);
     WsLayout L = ws_layout(B, nvec, V, use_small(V, dtype));
     if (workspace_bytes < L.total) return SD_ENOSPC;
-    VecSet vs = {};
-    vs.base[0] = tgt; vs.bs[0] = tgt_bs; vs.ps[0] = tgt_ps; vs.npos[0] = k + 1;
-    vs.npos[1] = 0; vs.nrows = B;
-    ArgmaxParams P;
-    P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec;
-    P.nch = nch_for(V); P.chunk = (V + P.nch - 1) / P.nch;
-    P.partial = reinterpret_cast<unsigned long long*>(ws + L.apartial);
-    P.vec_counter = reinterpret_cast<int*>(ws + L.vcounter);
-    P.row_counter = reinterpret_cast<int*>(ws + L.rcounter);
-    P.stats = reinterpret_cast<VecStats*>(ws + L.stats);
-    P.k = k; P.xs = xs; P.xs_bs = xs_bs; P.u_acc = u_acc; P.u_bs = u_bs; P.alive = alive;
-    P.n_acc = n_acc; P.y = y; P.px = px; P.qx = qx;
-    if (zero_argmax_counters(L, nvec, B, ws, st)) return SD_ELAUNCH;
-    argmax_kernel<<<P.nch * nvec, FT, 0, st>>>(P);
-    return check_launch();
+    return launch_greedy_verify(tgt, tgt_bs, tgt_ps, dtype, xs, xs_bs, u_acc, u_bs, alive, B, k, V,
+                                n_acc, y, px, qx, reinterpret_cast<VecStats*>(ws + L.stats),
+                                reinterpret_cast<unsigned long long*>(ws + L.apartial),
+                                reinterpret_cast<int*>(ws + L.vcounter),
+                                reinterpret_cast<int*>(ws + L.rcounter), st);
   }
   if (!drf) return SD_EINVAL;
   const int nvec = B * (2 * k + 1);
@@ -2225,7 +2335,8 @@ int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, in
     if (workspace_bytes < L.total) return SD_ENOSPC;
     ArgmaxParams P;
     P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = B;
-    P.nch = nch_for(V); P.chunk = (V + P.nch - 1) / P.nch;
+    const ArgmaxGeom ag = argmax_geom(V, dtype);
+    P.nch = ag.nch; P.cu = ag.cu;
     P.partial = reinterpret_cast<unsigned long long*>(ws + L.apartial);
     P.vec_counter = reinterpret_cast<int*>(ws + L.vcounter);
     P.row_counter = reinterpret_cast<int*>(ws + L.rcounter);
@@ -2233,8 +2344,7 @@ int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, in
     P.k = 0; P.xs = nullptr; P.xs_bs = 0; P.u_acc = nullptr; P.u_bs = 0; P.alive = nullptr;
     P.n_acc = nullptr; P.y = x; P.px = nullptr; P.qx = qx;
     if (zero_argmax_counters(L, B, B, ws, st)) return SD_ELAUNCH;
-    argmax_kernel<<<P.nch * B, FT, 0, st>>>(P);
-    return check_launch();
+    return launch_argmax(P, st);
   }
   WsLayout L = ws_layout(B, B, V, use_small(V, dtype));
   if (workspace_bytes < L.total) return SD_ENOSPC;
@@ -2267,7 +2377,8 @@ int sd_to_probs(const void* logits, int64_t row_stride, int dtype, int n_rows, i
   if (greedy) {
     ArgmaxParams A;
     A.vs = vs; A.dtype = dtype; A.V = V; A.nvec = n_rows;
-    A.nch = P.nch; A.chunk = P.chunk;
+    const ArgmaxGeom ag = argmax_geom(V, dtype);
+    A.nch = ag.nch; A.cu = ag.cu;
     A.partial = reinterpret_cast<unsigned long long*>(ws + L.apartial);
     A.vec_counter = reinterpret_cast<int*>(ws + L.vcounter);
     A.row_counter = reinterpret_cast<int*>(ws + L.rcounter);
@@ -2276,8 +2387,7 @@ int sd_to_probs(const void* logits, int64_t row_stride, int dtype, int n_rows, i
     A.xs = nullptr; A.xs_bs = 0; A.u_acc = nullptr; A.u_bs = 0; A.alive = nullptr;
     A.n_acc = nullptr; A.y = nullptr; A.px = nullptr; A.qx = nullptr;
     if (zero_argmax_counters(L, n_rows, n_rows, ws, st)) return SD_ELAUNCH;
-    argmax_kernel<<<A.nch * n_rows, FT, 0, st>>>(A);
-    if ((rc = check_launch())) return rc;
+    if ((rc = launch_argmax(A, st))) return rc;
   } else {
     rc = run_sampling(vs, n_rows, dtype, V, temperature, top_p, top_k, L, ws, st, nullptr);
     if (rc) return rc;

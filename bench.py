@@ -242,15 +242,11 @@ def main():
         tgt, drf = W.cfg2_logits(B, K_DRAFT, VOCAB, seed=100 * rank + i, device=dev)
         xs, _ = S.draft_sample(drf.reshape(-1, VOCAB), torch.rand(B * K_DRAFT, device=dev), T, tp)
         ua, ur = W.uniforms(B, K_DRAFT, seed=100 * rank + i, device=dev)
-        out = (torch.empty(B, dtype=torch.long, device=dev), torch.empty(B, dtype=torch.long,
-                                                                        device=dev))
-        bufs.append((tgt, drf, xs.view(B, K_DRAFT), ua, ur, out))
+        bufs.append((tgt, drf, xs.view(B, K_DRAFT), ua, ur))
 
     def call(i):
-        tgt, drf, xs, ua, ur, out = bufs[i % NBUF]
-        n, y = S.verify_sample(tgt, drf, xs, ua, ur, T, tp)
-        out[0].copy_(n)
-        out[1].copy_(y)
+        tgt, drf, xs, ua, ur = bufs[i % NBUF]
+        return S.verify_sample(tgt, drf, xs, ua, ur, T, tp)
 
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream(dev))
@@ -297,9 +293,22 @@ def main():
         ms = float(t.item())
     ms_step = ms / a.steps
     value = world * B * a.steps / (ms / 1e3)
-    calls_s = 1e3 / ms_step
     bytes_call = W.bytes_per_verify(B, K_DRAFT, VOCAB, greedy=greedy)
-    gbs = bytes_call * calls_s / 1e9
+
+    # the dominant kernel alone: each verify call is one stats / argmax kernel
+    # (plus a few-hundred-byte memset of its row counters), timed call by call
+    # with events on the stream it is launched on
+    n_k = max(20, min(a.steps, 200))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n_k)]
+    with torch.cuda.stream(s):
+        for i, (k0, k1) in enumerate(evs):
+            k0.record(s)
+            call(i)
+            k1.record(s)
+        torch.cuda.synchronize(dev)
+    k_ms = statistics.mean(k0.elapsed_time(k1) for k0, k1 in evs)
+    gbs = bytes_call / (k_ms * 1e-3) / 1e9
     peaks = {}
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
@@ -311,7 +320,7 @@ def main():
     # end to end through the public API from pinned host buffers
     host = []
     for i in range(NBUF):
-        tgt, drf, xs, ua, ur, _ = bufs[i]
+        tgt, drf, xs, ua, ur = bufs[i]
         host.append(tuple(t.cpu().pin_memory() for t in (tgt, drf, xs, ua, ur)))
     dev_in = [tuple(torch.empty_like(t, device=dev) for t in host[0]) for _ in range(NBUF)]
     res = [(torch.empty(B, dtype=torch.long).pin_memory(),
@@ -351,19 +360,20 @@ def main():
     prof = ROOT / "profiles" / ("verify_greedy_traffic.json" if greedy else "verify_sample_traffic.json")
     if prof.exists():
         traffic = json.loads(prof.read_text()).get("bytes_per_call")
-    launches_per_step = 1 if greedy else 2
+    launches_per_step = 1             # our kernels per verify call (the stats or argmax kernel)
     line = {
         "metric": metric_name(a.mode), "value": value, "unit": "rows/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded config-2 logits, see specdec/workloads.py)",
         "config": workload_config(a.mode, world),
-        "hbm_gbs": gbs,
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                      "frac": gbs / peak, "traffic": traffic,
                      "peak_source": peak_src,
-                     "scope": "the whole verify call (all its kernels); algorithmic bytes "
-                              f"{bytes_call} per call = every logits element read once"},
+                     "kernel": "argmax_kernel" if greedy else "hist_stats_kernel",
+                     "kernel_ms": k_ms,
+                     "scope": f"algorithmic bytes {bytes_call} per call (every logits element "
+                              "read once) / mean event-timed duration of one verify call"},
         "e2e": {"value": world * B * n_e2e / (e2e_ms / 1e3), "unit": "rows/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 2 * B * 8, "steps": n_e2e},
         "gpu_launches": launches_per_step * a.steps,
