@@ -27,6 +27,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "sd_common.cuh"
 
 namespace sd {
@@ -2262,6 +2264,41 @@ static int launch_greedy_verify(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
   return launch_argmax(P, st);
 }
 
+// Fixed device scratch of sd_verify_greedy_static (one copy per device, in
+// this library's module): stats, chunk maxima and the two counter arrays.
+static __device__ __align__(256) unsigned char g_static_scratch[SD_STATIC_SCRATCH_BYTES];
+
+struct StaticLayout {
+  size_t stats, partial, vcounter, rcounter, total;
+};
+static StaticLayout static_layout(int B, int nvec, int nch) {
+  StaticLayout L;
+  size_t off = 0;
+  L.stats = off; off = align256(off + (size_t)nvec * sizeof(VecStats));
+  L.partial = off; off = align256(off + (size_t)nvec * nch * sizeof(unsigned long long));
+  L.vcounter = off; off = align256(off + (size_t)nvec * sizeof(int));
+  L.rcounter = off; off = align256(off + (size_t)B * sizeof(int));
+  L.total = off;
+  return L;
+}
+
+// Address of g_static_scratch on the current device, looked up once per device.
+static std::mutex g_static_mu;
+static void* g_static_ptr[SD_MAX_DEVICES];
+
+static int static_scratch(char** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= SD_MAX_DEVICES) return SD_ELAUNCH;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (g_static_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || p == nullptr) return SD_ELAUNCH;
+    g_static_ptr[dev] = p;
+  }
+  *out = reinterpret_cast<char*>(g_static_ptr[dev]);
+  return SD_OK;
+}
+
 static int validate_common(int dtype, int V, float T) {
   if (dtype != SD_DTYPE_F32 && dtype != SD_DTYPE_F16 && dtype != SD_DTYPE_BF16) return SD_EINVAL;
   if (V <= 0 || V > (1 << 21)) return SD_EINVAL;
@@ -2316,6 +2353,25 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
   vs.nrows = B;
   DrawSpec d = {k, u_acc, u_bs, u_res, alive, n_acc, y, px, qx, nullptr};
   return run_sampling(vs, nvec, dtype, V, temperature, top_p, top_k, L, ws, st, &d);
+}
+
+int sd_verify_greedy_static(const void* tgt, int64_t tgt_bs, int64_t tgt_ps, int dtype,
+                            const int64_t* xs, int64_t xs_bs, const float* u_acc, int64_t u_bs,
+                            const uint8_t* alive, int B, int k, int V, int64_t* n_acc,
+                            int64_t* y, float* px, float* qx, void* stream) {
+  int rc = validate_common(dtype, V, 0.0f);
+  if (rc) return rc;
+  if (B <= 0 || k < 1 || k > 64 || !tgt || !xs || !u_acc || !n_acc || !y) return SD_EINVAL;
+  const StaticLayout L = static_layout(B, B * (k + 1), argmax_geom(V, dtype).nch);
+  if (L.total > SD_STATIC_SCRATCH_BYTES) return SD_ENOSPC;
+  char* ws = nullptr;
+  if ((rc = static_scratch(&ws))) return rc;
+  return launch_greedy_verify(tgt, tgt_bs, tgt_ps, dtype, xs, xs_bs, u_acc, u_bs, alive, B, k, V,
+                              n_acc, y, px, qx, reinterpret_cast<VecStats*>(ws + L.stats),
+                              reinterpret_cast<unsigned long long*>(ws + L.partial),
+                              reinterpret_cast<int*>(ws + L.vcounter),
+                              reinterpret_cast<int*>(ws + L.rcounter),
+                              reinterpret_cast<cudaStream_t>(stream));
 }
 
 int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, int V,

@@ -84,6 +84,26 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * No counterpart in the reference (added entry point).  The greedy verify
+ * round of sd_verify_sample (temperature <= 0: u_res, draft logits, top-p and
+ * top-k unused; same arguments, results and error codes otherwise) with no
+ * workspace argument: its scratch is a fixed SD_STATIC_SCRATCH_BYTES device
+ * array inside this library, one per device, whose address is looked up once
+ * per device (cudaGetSymbolAddress) on the first call there.  The call
+ * allocates no memory.  Returns SD_ENOSPC when the shape needs more scratch
+ * than that (about B*(k+1)*(48 + 8*chunks) bytes, chunks <= 64).
+ * Calls that overlap on one device (other streams, other host threads) share
+ * the scratch and race: serialise them.  Make the first call on each device
+ * before capturing it into a CUDA graph (the symbol lookup is not captured).
+ */
+#define SD_STATIC_SCRATCH_BYTES (1u << 20)
+#define SD_MAX_DEVICES 64
+int sd_verify_greedy_static(const void* tgt, int64_t tgt_bs, int64_t tgt_ps, int dtype,
+                            const int64_t* xs, int64_t xs_bs, const float* u_acc, int64_t u_bs,
+                            const uint8_t* alive, int B, int k, int V, int64_t* n_acc,
+                            int64_t* y, float* px, float* qx, void* stream);
+
+/*
  * One draft step: x[b] ~ to_probs(logits[b]) drawn by inverse CDF with u[b],
  * and qx[b] = q(x[b]).  Replaces reference specdec/engine.py:250-251 and 256
  * (to_probs, sample_from_probs, gather_prob for the confidence product).
