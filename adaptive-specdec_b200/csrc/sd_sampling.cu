@@ -90,46 +90,53 @@ __device__ __forceinline__ int64_t vec_probe(const VecSet& vs, int set, int row,
 }
 
 // ---------------------------------------------------------------------------
-// stats kernel (bf16 / fp16): persistent, TMA ring, producer warp, fused
-// row finish
+// stats kernel (bf16 / fp16): persistent, one CTA per SM, three warp roles
 // ---------------------------------------------------------------------------
-// Streaming (every element once, from a shared-memory ring that a producer
-// warp fills with cp.async.bulk): elements within W_LIST base-2 units of the
-// thread's running maximum are appended (value, index) to a shared list; the
-// softmax mass of all lower elements is summed with ex2.approx relative to the
-// running maximum.  Per vector the list is sorted by (value desc, index asc) --
-// the order of the reference's sort with ties broken by index -- and the
-// reference's element-wise rules are applied to it directly: top-k (keep
-// p >= k-th value), top-p (keep while fl32(cum - p) < top_p, cum accumulated in
-// float64), renormalisation.  The kept set is described by its last element L
-// in that order: j is kept iff value_j > value_L or (value_j == value_L and
-// j <= index_L).  Elements of the list at or above M - W_LIST are complete
-// (every occurrence of those values is listed), so the rules are exact when
-// the boundary falls there; otherwise (boundary deeper, list overflow, top-k
-// beyond the list) the vector is recomputed exactly from a 65,536-bin count
-// histogram of all its elements read again from global memory.
+// Warp 0 (producer) streams each vector's 16-byte-aligned body into a ring of
+// NSLOT shared-memory slots with cp.async.bulk.  Warps 1..NSW (streaming) read
+// every element once from the ring: each lane sums 2^(x c2 - Rc2) over the
+// elements below its list threshold (the running maximum minus W_LIST base-2
+// units) against a per-vector reference Rc2, and a lane holding elements at
+// or above the threshold leaves a record (lane, threshold, reference) for
+// the slot.  Before refilling a slot the producer turns that slot's records
+// into list entries (value, index) straight from the ring.  The FNW finalize
+// warps then take a finished vector (its list, the streaming warps' partial
+// sums, its maximum) while the next one streams: they sort the list by
+// (value desc, index asc) -- the order of the reference's sort with ties
+// broken by index -- and apply the reference's element-wise rules to it:
+// top-k (keep p >= k-th value), top-p (keep while fl32(cum - p) < top_p, cum
+// in float64), renormalisation.  The kept set is described by its last
+// element L in that order: j is kept iff value_j > value_L or (value_j ==
+// value_L and j <= index_L).  Every element at or above M - W_LIST is listed,
+// so the rules are exact when the boundary falls there; otherwise (boundary
+// deeper, list overflow, top-k beyond the list) the vector is recomputed
+// exactly from a 65,536-bin count histogram of all its elements read again
+// from global memory.  Two vectors are in flight per CTA (two list sets).
 //
 // The CTA that finishes the last vector of a row then performs that row's
-// accept test and its residual / bonus draw.  Outside the nucleus of p the
-// residual max(p - q, 0) is zero, so the draw only walks p's kept elements in
-// index order (q gathered at those indices).
-constexpr int NCW = 8;                   // consumer warps
-constexpr int CT = NCW * 32;             // consumer threads
-constexpr int HT = CT + 32;              // + one producer warp
-constexpr int CTAS_PER_SM = 2;           // one CTA's per-vector work overlaps the other's streaming
-constexpr int GRID_MAX = 2 * 160;        // bound on the persistent grid (fallback buffers)
-constexpr int GPS = 4;                   // 16-byte groups per consumer thread per ring slot
-constexpr int SLOT = GPS * 16 * 256;     // bytes per ring slot (16 KB)
-constexpr int NSLOT = 3;
+// accept test and its residual / bonus draw (finalize warps).  Outside the
+// nucleus of p the residual max(p - q, 0) is zero, so the draw only walks p's
+// kept elements in index order (q gathered at those indices).
+constexpr int NSW = 15;                  // streaming warps
+constexpr int ST_N = NSW * 32;           // streaming threads
+constexpr int ST0 = 32;                  // first streaming thread (warp 0 produces)
+constexpr int NCW = 4;                   // finalize warps
+constexpr int CT = NCW * 32;             // finalize threads
+constexpr int FIN0 = ST0 + ST_N;         // first finalize thread
+constexpr int HT = FIN0 + CT;            // threads per CTA
+constexpr int GRID_MAX = 160;            // bound on the persistent grid (fallback buffers)
+constexpr int GPS = 4;                   // 16-byte units per streaming lane per ring slot
+constexpr int SLOT = GPS * 16 * ST_N;    // bytes per ring slot (30 KB)
+constexpr int NSLOT = 4;
 constexpr long long WAIT_CYCLES = 1LL << 32;   // ~2 s at 2 GHz: bound on every wait
-constexpr int LIST_CAP = 2048;           // listed elements per vector
-constexpr int REC_CAP = 2048;            // hot (lane, ring slot) records per vector
+constexpr int LIST_CAP = 3072;           // listed elements per vector
 constexpr int NUC_MAX = 1024;            // kept elements stored per vector for the draw
 constexpr float W_LIST = 12.f;           // list window, base-2 units below the maximum
 
+static_assert(FIN0 % 32 == 0, "finalize warps start on a warp boundary");
+
 constexpr int F_FALLBACK = 1;            // exact full-histogram path taken
 // why the list path handed a vector to the histogram path (VecStats.fb_why)
-constexpr int FB_RECORDS = 1;            // more hot records than REC_CAP
 constexpr int FB_LIST = 2;               // more listed elements than LIST_CAP
 constexpr int FB_SELECT = 3;             // more selected elements than SEL_CAP
 constexpr int FB_BOUNDARY = 4;           // top-p / top-k boundary outside the sorted part
@@ -147,24 +154,32 @@ struct HistBuf {
 };
 
 constexpr int SEL_CAP = 1024;            // entries sorted per vector
+constexpr int RANK_MAX = 512;            // row draw by direct prefix sums up to this many kept
 constexpr int NBIN = 49;                 // coarse depth bins: 4 per base-2 unit, + overflow
 constexpr int NBIN_PAD = 64;             // two bins per lane of one warp
 
-// Hot records: consumer thread t of ring chunk c (rec_ct = c << 16 | t) held
-// elements with y(x) >= rec_y under offset rec_r, excluded from its bulk sum.
+// Finalize-warp scratch of the list path.
 struct ListBuf {
-  uint32_t rec_ct[REC_CAP];
-  float rec_y[REC_CAP];
-  float rec_r[REC_CAP];
-  unsigned long long key[LIST_CAP];      // (fkey(value) << 32) | ~index
+  float ecache[LIST_CAP];                // exact softmax numerator of each window key
   unsigned long long sel[SEL_CAP];       // entries selected for sorting
   float p[SEL_CAP];
   unsigned long long binfx[NBIN_PAD];    // depth-bin mass, 2^-40 fixed point
   int bincnt[NBIN_PAD];
 };
 
+// What the streaming warps hand to the finalize warps for one vector (two
+// of these alternate).
+struct VecHand {
+  unsigned long long key[LIST_CAP];      // (fkey(value) << 32) | ~index
+  double wbulk[NSW];                     // per streaming warp: sum of 2^(y - (wrc2 - Rc2))
+  float wrc2[NSW];                       // per streaming warp: its common offset (-inf: none)
+  uint32_t gkey;                         // fkey of the vector's running maximum
+  int nkey;                              // listed elements
+};
+
 struct HistSmem {
   alignas(128) unsigned char ring[NSLOT][SLOT];
+  VecHand hand[2];
   union {
     HistBuf h;
     ListBuf l;
@@ -176,15 +191,16 @@ struct HistSmem {
   float fred[40];
   alignas(8) unsigned long long full[NSLOT];
   alignas(8) unsigned long long empty[NSLOT];
+  alignas(8) unsigned long long streamed[2];   // the streaming warps finished a vector
+  alignas(8) unsigned long long freed[2];      // the finalize warps released its hand-over
   uint32_t* gh;        // this CTA's global 65,536-counter histogram (fallback path)
   int ncorr;
   int corr_full;
   int nsel;
-  int nrec;            // hot records of the current vector
+  int npre;           // kept elements above the sorted part of the list path
   int fb_why;          // FB_* reason of the last hand-over to the histogram path
-  int nkey;            // listed elements of the current vector
-  uint32_t gkey;       // fkey of the CTA's running maximum of the current vector
   int abort_flag;
+  int fin_skip;        // finalize warps: skip the work of this vector (after an abort)
   uint32_t keyk16;
   uint32_t vstar16;
   int n_keep;
@@ -199,11 +215,20 @@ struct HistSmem {
   double sc_pre;
 };
 
-__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+static_assert(sizeof(HistSmem) <= 227 * 1024, "stats kernel shared memory");
+
+// Index of this thread within the finalize warps.
+__device__ __forceinline__ int ftid() { return (int)threadIdx.x - FIN0; }
+
+// barrier of the finalize warps
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+// barrier of the streaming warps
+__device__ __forceinline__ void sbar() { asm volatile("bar.sync 1, 480;" ::: "memory"); }
+static_assert(CT == 128 && ST_N == 480, "named barrier thread counts");
 
 template <typename T>
 __device__ __forceinline__ T c_sum(T v, T* red) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, wid = ftid() >> 5;
   v = warp_sum(v);
   cbar();
   if (lane == 0) red[wid] = v;
@@ -214,7 +239,7 @@ __device__ __forceinline__ T c_sum(T v, T* red) {
 
 template <typename T>
 __device__ __forceinline__ T c_max(T v, T* red, T lowest) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, wid = ftid() >> 5;
   v = warp_max(v);
   cbar();
   if (lane == 0) red[wid] = v;
@@ -225,7 +250,7 @@ __device__ __forceinline__ T c_max(T v, T* red, T lowest) {
 
 template <typename T>
 __device__ __forceinline__ T c_excl_scan(T v, T* red, T* total) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, wid = ftid() >> 5;
   T inc = warp_incl_scan(v);
   cbar();
   if (lane == 31) red[wid] = inc;
@@ -273,6 +298,13 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* b, uint32_t parity
     }
   }
 }
+// Non-blocking: has the phase of parity `parity` completed?
+__device__ __forceinline__ bool mbar_test(unsigned long long* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+               " selp.u32 %0, 1, 0, p;\n}" : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          unsigned long long* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -318,7 +350,7 @@ __device__ __forceinline__ float list_val(unsigned long long k) {
 __device__ void bitonic_sort(unsigned long long* key, int N, bool descending) {
   for (int k2 = 2; k2 <= N; k2 <<= 1) {
     for (int j2 = k2 >> 1; j2 > 0; j2 >>= 1) {
-      for (int i = threadIdx.x; i < N; i += CT) {
+      for (int i = ftid(); i < N; i += CT) {
         const int ixj = i ^ j2;
         if (ixj > i) {
           const unsigned long long a = key[i], b = key[ixj];
@@ -381,8 +413,8 @@ __device__ __forceinline__ void hist_add_checked(HistSmem& s, uint32_t raw) {
 
 __device__ void hist_clear_all(HistSmem& s) {
   uint4* h = reinterpret_cast<uint4*>(s.gh);
-  for (int i = threadIdx.x; i < HIST_WORDS / 4; i += CT) h[i] = make_uint4(0, 0, 0, 0);
-  if (threadIdx.x == 0) { s.ncorr = 0; s.corr_full = 0; }
+  for (int i = ftid(); i < HIST_WORDS / 4; i += CT) h[i] = make_uint4(0, 0, 0, 0);
+  if (ftid() == 0) { s.ncorr = 0; s.corr_full = 0; }
   __threadfence_block();
 }
 
@@ -390,7 +422,7 @@ __device__ void hist_clear_all(HistSmem& s) {
 __device__ void hist_pass_a(HistSmem& s, uint32_t* maxkey_out) {
   uint32_t kmax = 0;
   bool any = false;
-  for (int seg = threadIdx.x; seg < NSEG; seg += CT) {
+  for (int seg = ftid(); seg < NSEG; seg += CT) {
     uint32_t occ = 0;
     for (int j = 0; j < 16; ++j) {
       const uint32_t G = 16u * seg + j;
@@ -440,7 +472,7 @@ struct StatsParams {
 // element counted).  Writes the stats record; the kept set is not listed.
 __device__ void finalize_histogram(HistSmem& s, const StatsParams& P, int v, const uint16_t* x,
                                    int64_t probe) {
-  const int t = threadIdx.x;
+  const int t = ftid();
   const int V = P.V;
   const bool topk_on = P.top_k > 0 && P.top_k < V;
   const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
@@ -791,43 +823,48 @@ __device__ __forceinline__ float lane_max(const uint32_t* w, uint32_t* pm1) {
   return fmaxf(lo16<DT>(pm[0]), hi16<DT>(pm[0]));
 }
 
-// 2^y summed over the elements of 4G packed words with y < Y (those with
-// y >= Y are listed instead).
+// 2^y summed over the elements of 4G packed words with y < Y; the elements
+// with y >= Y are excluded and flagged in lmask (bit 2i + h: word i, low /
+// high half), to be listed instead.
 template <int DT, int G>
 __device__ __forceinline__ float bulk_words(const uint32_t* w, float c2h, float c2l, float Rc2,
-                                            float Y) {
+                                            float Y, uint32_t& lmask) {
   float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+  uint32_t m = 0u;
 #pragma unroll
   for (int i = 0; i < 4 * G; ++i) {
     float y0, y1;
     yof2(y0, y1, lo16<DT>(w[i]), hi16<DT>(w[i]), c2h, c2l, Rc2);
-    const float e0 = ex2_approx(y0 >= Y ? -INFINITY : y0);
-    const float e1 = ex2_approx(y1 >= Y ? -INFINITY : y1);
+    const bool l0 = y0 >= Y, l1 = y1 >= Y;
+    if (l0) m |= 1u << (2 * i);
+    if (l1) m |= 2u << (2 * i);
+    const float e0 = ex2_approx(l0 ? -INFINITY : y0);
+    const float e1 = ex2_approx(l1 ? -INFINITY : y1);
     if (i & 1) add2(b2, b3, e0, e1); else add2(b0, b1, e0, e1);
   }
+  lmask = m;
   return (b0 + b2) + (b1 + b3);
 }
 
 // One pass over 4G packed words per lane; groups without data hold -inf
-// pairs.  Called by whole warps.  RING: the words are lane t's 16-byte units
-// t + q * CT of ring chunk `chunk` of the vector body; a lane that
-// holds elements with y >= Y leaves a hot record and the list is built from
-// the records after the vector (one shared atomic per warp here).  Otherwise
-// (the < 16 ragged elements, one per lane in the low half of w[0], index jr)
-// the element itself is appended to the list.
+// pairs.  Called by whole streaming warps.  RING: the words are streaming
+// thread st's 16-byte units st + q * ST_N of ring slot `slot`, whose first
+// element has vocabulary index jbase; a lane that flagged elements lists them
+// itself, re-reading each from the slot.  Otherwise (the < 16 ragged
+// elements, one per lane in the low half of w[0], index jr) the lane's
+// element is listed the same way.
 template <int DT, int G, bool RING>
-__device__ __forceinline__ void stream_words(HistSmem& s, Stream& st, const uint32_t* w,
-                                             uint32_t chunk, uint32_t jr, float c2h, float c2l,
-                                             float wlist) {
+__device__ __forceinline__ void stream_words(HistSmem& s, VecHand& H, Stream& st,
+                                             const uint32_t* w, int slot, uint32_t jbase,
+                                             uint32_t jr, float c2h, float c2l, float wlist) {
   const int lane = threadIdx.x & 31;
   uint32_t pm1[2 * G];
   const float gm = lane_max<DT, G>(w, pm1);
   if (st.Rc2 == -INFINITY && gm > -INFINITY) set_ref(st, gm, c2h, c2l, wlist);
-  const bool have = st.Rc2 != -INFINITY;
-  float b = 0.f, ygm = -INFINITY, Y = st.Y;
-  if (have) {
-    b = bulk_words<DT, G>(w, c2h, c2l, st.Rc2, Y);
-    ygm = yof(gm, c2h, c2l, st.Rc2);
+  uint32_t lmask = 0u;
+  if (st.Rc2 != -INFINITY) {
+    float b = bulk_words<DT, G>(w, c2h, c2l, st.Rc2, st.Y, lmask);
+    const float ygm = yof(gm, c2h, c2l, st.Rc2);
     if (ygm > 64.f) {
       // far above the reference: move it up so that no partial sum overflows
       // and redo this lane's words (a logit tens of units above everything
@@ -835,43 +872,45 @@ __device__ __forceinline__ void stream_words(HistSmem& s, Stream& st, const uint
       const float nr = st.Rc2 + (ygm - 32.f);
       st.bulk *= exp2((double)st.Rc2 - (double)nr);
       st.Rc2 = nr;
-      st.Y = Y = yof(st.m - wlist, c2h, c2l, nr);
-      b = bulk_words<DT, G>(w, c2h, c2l, nr, Y);
-      ygm = yof(gm, c2h, c2l, nr);
+      st.Y = yof(st.m - wlist, c2h, c2l, nr);
+      b = bulk_words<DT, G>(w, c2h, c2l, nr, st.Y, lmask);
     }
     st.bulk += (double)b;
   }
-  const bool hot = have && ygm >= Y;
+  // the flagged elements (rare: only near the running maximum), one shared
+  // atomic each
   if (RING) {
-    const unsigned hm = __ballot_sync(0xffffffffu, hot);
-    if (hm) {
-      const int leader = __ffs(hm) - 1;
-      int base = 0;
-      if (lane == leader) base = atomicAdd(&s.nrec, __popc(hm));
-      base = __shfl_sync(0xffffffffu, base, leader) + __popc(hm & ((1u << lane) - 1u));
-      if (hot && base < REC_CAP) {
-        s.u.l.rec_ct[base] = chunk << 16 | (uint32_t)threadIdx.x;
-        s.u.l.rec_y[base] = Y;
-        s.u.l.rec_r[base] = st.Rc2;
-      }
+    if (lmask) {
+      const uint32_t* ring32 = reinterpret_cast<const uint32_t*>(s.ring[slot]);
+      const int tl = (int)threadIdx.x - ST0;
+      do {
+        const int bit = __ffs(lmask) - 1;
+        lmask &= lmask - 1u;
+        const int i = bit >> 1, h = bit & 1;
+        const int unit = tl + (i >> 2) * ST_N;
+        const uint32_t ww = ring32[unit * 4 + (i & 3)];
+        const float xv = h ? hi16<DT>(ww) : lo16<DT>(ww);
+        const int o = atomicAdd(&H.nkey, 1);
+        if (o < LIST_CAP)
+          H.key[o] = list_key(xv, jbase + 8u * (uint32_t)unit + 2u * (uint32_t)(i & 3) + (uint32_t)h);
+      } while (lmask);
     }
-  } else {
-    const float xv = lo16<DT>(w[0]);                  // the lane's only element
-    warp_append(&s.nkey, s.u.l.key, LIST_CAP, hot && yof(xv, c2h, c2l, st.Rc2) >= Y,
-                list_key(xv, jr));
+  } else if (lmask & 1u) {                            // the lane's only element
+    const int o = atomicAdd(&H.nkey, 1);
+    if (o < LIST_CAP) H.key[o] = list_key(lo16<DT>(w[0]), jr);
   }
   if (gm > st.m) raise_m(st, gm, c2h, c2l, wlist);
   const uint32_t wk = __reduce_max_sync(0xffffffffu, fkey(gm));
   if (wk > st.pkey) {                                 // warp-uniform
-    if (lane == 0) atomicMax(&s.gkey, wk);
+    if (lane == 0) atomicMax(&H.gkey, wk);
     st.pkey = wk;
   }
 }
 
-// Start of a ring slot: adopt the CTA's running max if it is ahead.
-__device__ __forceinline__ void sync_max(HistSmem& s, Stream& st, float c2h, float c2l,
+// Start of a ring slot: adopt the vector's running max if it is ahead.
+__device__ __forceinline__ void sync_max(VecHand& H, Stream& st, float c2h, float c2l,
                                          float wlist) {
-  const uint32_t gk = *reinterpret_cast<volatile uint32_t*>(&s.gkey);
+  const uint32_t gk = *reinterpret_cast<volatile uint32_t*>(&H.gkey);
   const float gv = fkey_value(gk);
   if (st.Rc2 != -INFINITY && gv > st.m) raise_m(st, gv, c2h, c2l, wlist);
 }
@@ -928,118 +967,83 @@ __device__ __forceinline__ float stats_prob_x(const VecStats& o, float xv, float
 }
 
 __device__ __forceinline__ bool fallback_why(HistSmem& s, int why) {
-  if (threadIdx.x == 0) s.fb_why = why;
+  if (ftid() == 0) s.fb_why = why;
   return true;
 }
 
-template <int DT>
-__device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& st, int v,
-                              const uint16_t* x, int64_t probe, float c2, float c2l, float wlist) {
-  const int t = threadIdx.x, lane = t & 31;
+__device__ bool finalize_list(HistSmem& s, VecHand& H, const StatsParams& P, int v,
+                              const uint16_t* x, int64_t probe, float c2, float wlist) {
+  const int t = ftid(), lane = t & 31;
   const int V = P.V;
   const bool topk_on = P.top_k > 0 && P.top_k < V;
   const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
   const bool all_kept = !topk_on && !topp_on;
   const float tp32 = P.top_p;
-  // the list: the elements of the hot records (re-read, mostly from L2) with
-  // y >= Y under the record's offset, after the ragged ones already there;
-  // one record per thread per round, one shared atomic per warp per round
-  {
-    const int nrec = s.nrec;
-    if (nrec > REC_CAP) return fallback_why(s, FB_RECORDS);
-    const VecGeom g(x, V);
-    for (int base = 0; base < nrec; base += CT) {
-      const int r = base + t;
-      const bool rin = r < nrec;
-      uint32_t ct = 0u;
-      float ry = INFINITY, rr = 0.f;
-      if (rin) { ct = s.u.l.rec_ct[r]; ry = s.u.l.rec_y[r]; rr = s.u.l.rec_r[r]; }
-      const uint32_t j00 = (uint32_t)g.head + (ct >> 16) * (uint32_t)(SLOT / 2) + 8u * (ct & 0xFFFFu);
-      uint4 v4[GPS];
-#pragma unroll
-      for (int q = 0; q < GPS; ++q) {
-        const uint32_t j0 = j00 + 8u * (uint32_t)(q * CT);
-        v4[q] = make_uint4(0u, 0u, 0u, 0u);
-        if (rin && (int)j0 + 8 <= g.tail0) v4[q] = __ldg(reinterpret_cast<const uint4*>(x + j0));
-      }
-      static_assert(GPS == 4, "record listing selects among four 16-byte units");
-      uint32_t mask = 0u;
-#pragma unroll
-      for (int q = 0; q < GPS; ++q) {
-        const uint32_t ww[4] = {v4[q].x, v4[q].y, v4[q].z, v4[q].w};
-        const bool qin = rin && (int)(j00 + 8u * (uint32_t)(q * CT)) + 8 <= g.tail0;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float xv = (e & 1) ? hi16<DT>(ww[e >> 1]) : lo16<DT>(ww[e >> 1]);
-          if (qin && yof(xv, c2, c2l, rr) >= ry) mask |= 1u << (q * 8 + e);
-        }
-      }
-      const int cnt = __popc(mask);
-      const int incl = warp_incl_scan<int>(cnt);
-      int wbase = 0;
-      if (lane == 31 && incl > 0) wbase = atomicAdd(&s.nkey, incl);
-      int o = __shfl_sync(0xffffffffu, wbase, 31) + incl - cnt;
-      while (mask) {
-        const int b = __ffs(mask) - 1;
-        mask &= mask - 1u;
-        const int q = b >> 3, e = b & 7;
-        const uint4 vq = q == 0 ? v4[0] : q == 1 ? v4[1] : q == 2 ? v4[2] : v4[3];
-        const uint32_t wq = (e >> 1) == 0 ? vq.x : (e >> 1) == 1 ? vq.y : (e >> 1) == 2 ? vq.z : vq.w;
-        const float xv = (e & 1) ? hi16<DT>(wq) : lo16<DT>(wq);
-        if (o < LIST_CAP) s.u.l.key[o] = list_key(xv, j00 + 8u * (uint32_t)(q * CT) + (uint32_t)e);
-        ++o;
-      }
-    }
-    cbar();
-  }
-  const int nl = s.nkey;
+  const int nl = H.nkey;
   if (nl > LIST_CAP || nl < 1) return fallback_why(s, FB_LIST);
   // the probe's logit, requested now so that its latency overlaps the list work
   const bool has_probe = probe >= 0 && probe < V;
   float xprobe = 0.f;
   if (t == 0 && has_probe) xprobe = bits16_to_float(__ldg(x + probe), P.dtype);
-  const float M = fkey_value(s.gkey);                   // every element raised gkey
+  const float M = fkey_value(H.gkey);                   // every element raised gkey
   const float m = scaled_logit(M, P.T);
   const float wlow = M - wlist;
   if (t < NBIN_PAD) { s.u.l.binfx[t] = 0ull; s.u.l.bincnt[t] = 0; }
+  if (t == 0) { s.nsel = 0; s.npre = 0; }
   cbar();
-  // exact softmax numerators of the listed elements (each thread its own list
-  // slots, then the shared overflow); complete ones are binned by depth below
-  // the maximum (4 bins per base-2 unit), mass in 2^-40 fixed point
+  // exact softmax numerators of the listed elements of the window (at or
+  // above M - W_LIST), binned by depth below the maximum (4 bins per base-2
+  // unit, mass in 2^-40 fixed point).  The streaming warps' bulk sums are
+  // relative to their offsets wrc2 (terms 2^(x c2 - wrc2)); the listed terms
+  // are exp(x / T - m).
   double es = 0.0;
-  // bulk terms are 2^(x c2 - Rc2); the listed ones exp(x / T - m)
-  if (st.bulk > 0.0 && st.Rc2 != -INFINITY)
-    es = st.bulk * exp2((double)st.Rc2 - (double)m * 1.4426950408889634);
-  auto tally = [&](unsigned long long key) {
-    const float xv = list_val(key);
-    const float e = softmax_num(xv, P.T, m);           // <= 1: xv <= M
-    es += (double)e;
-    if (!all_kept && xv >= wlow) {
-      const int bin = depth_bin(M, xv, c2);
-      atomicAdd(&s.u.l.bincnt[bin], 1);
-      atomicAdd(&s.u.l.binfx[bin], (unsigned long long)__float2ull_rn(e * 0x1p40f));
+  if (t < NSW && H.wbulk[t] > 0.0 && H.wrc2[t] != -INFINITY)
+    es = H.wbulk[t] * exp2((double)H.wrc2[t] - (double)m * 1.4426950408889634);
+  // keys below the window only add to S: the ex2 form of the bulk sum
+  const float mc2 = (float)((double)m * 1.4426950408889634);
+  for (int i = t; i < nl; i += CT) {
+    const float xv = list_val(H.key[i]);
+    float e;
+    if (!(xv >= wlow)) {
+      e = ex2_approx(fmaf(xv, c2, -mc2));
+    } else {
+      e = softmax_num(xv, P.T, m);                      // <= 1: xv <= M
+      s.u.l.ecache[i] = e;
+      if (!all_kept) {
+        const int bin = depth_bin(M, xv, c2);
+        atomicAdd(&s.u.l.bincnt[bin], 1);
+        atomicAdd(&s.u.l.binfx[bin], (unsigned long long)__float2ull_rn(e * 0x1p40f));
+      }
     }
-  };
-  for (int i = t; i < nl; i += CT) tally(s.u.l.key[i]);
+    es += (double)e;
+  }
   const double S = c_sum<double>(es, s.dred);
   const float inv_s = __double2float_rn(1.0 / S);
-  int L = -1;
+  int L = -1;                                            // last kept, sorted-part index
   float kth_x = -INFINITY;
   double z = 0.0;
+  int npre = 0;                                          // kept elements above the sorted part
   if (!all_kept) {
     if (t < 32) {
-      // shallowest depth bin holding top_p of the mass and top_k elements,
-      // plus the next occupied bin (so the first dropped element is among
-      // those sorted); lane l owns bins 2l and 2l+1
+      // Bins, lane l owning 2l and 2l+1.  bstar: the shallowest bin holding
+      // top_p of the mass (with 1e-4 slack) and top_k elements, plus the next
+      // occupied bin, so the first dropped element is sorted.  bL: the first
+      // bin where the top-p or top-k boundary can lie; every element of the
+      // bins before it is kept (its exclusive mass is below top_p by the
+      // slack and it ranks within top_k), in any order.
       const unsigned long long f0 = s.u.l.binfx[2 * lane], f1 = s.u.l.binfx[2 * lane + 1];
       const int c0 = s.u.l.bincnt[2 * lane], c1 = s.u.l.bincnt[2 * lane + 1];
       const unsigned long long fi = warp_incl_scan<unsigned long long>(f0 + f1);
       const int ci = warp_incl_scan<int>(c0 + c1);
       const unsigned long long fe = fi - f0 - f1;
       const int ce = ci - c0 - c1;
-      const double target = topp_on ? (double)tp32 * S * (1.0 + 1e-4) * 0x1p40 : 0.0;
-      const bool ok0 = (double)(fe + f0) >= target && (!topk_on || ce + c0 >= P.top_k);
-      const bool ok1 = (double)fi >= target && (!topk_on || ci >= P.top_k);
+      // thresholds in fixed point (the bins hold at most 2^52)
+      const double hi_d = topp_on ? (double)tp32 * S * (1.0 + 1e-4) * 0x1p40 : 0.0;
+      const double lo_d = (double)tp32 * S * (1.0 - 1e-4) * 0x1p40;
+      const unsigned long long hi_t = hi_d >= 0x1p60 ? ~0ull : (unsigned long long)ceil(hi_d);
+      const unsigned long long lo_t = lo_d >= 0x1p60 ? ~0ull : (unsigned long long)ceil(lo_d);
+      const bool ok0 = fe + f0 >= hi_t && (!topk_on || ce + c0 >= P.top_k);
+      const bool ok1 = fi >= hi_t && (!topk_on || ci >= P.top_k);
       const unsigned okm = __ballot_sync(0xffffffffu, ok0 || ok1);
       int bstar = NBIN - 1;
       if (okm) {
@@ -1052,25 +1056,53 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
       if (n0) nb = min(nb, 2 * (__ffs(n0) - 1));
       if (n1) nb = min(nb, 2 * (__ffs(n1) - 1) + 1);
       if (nb < NBIN) bstar = nb;
-      // no occupied bin after bstar: the sorted part is the whole window, so
-      // the first element after it lies below the window
-      if (lane == 0) { s.ured[37] = (uint32_t)bstar; s.ured[36] = nb >= NBIN; s.nsel = 0; }
+      // first bin reaching the lower mass bound / holding the top_k-th element
+      int bL = NBIN_PAD;
+      auto first_bin = [&](bool a0, bool a1) {
+        const unsigned mm = __ballot_sync(0xffffffffu, a0 || a1);
+        if (!mm) return NBIN_PAD;
+        const int fl = __ffs(mm) - 1;
+        return 2 * fl + (__shfl_sync(0xffffffffu, a0, fl) ? 0 : 1);
+      };
+      if (topp_on) bL = min(bL, first_bin(fe + f0 >= lo_t, fi >= lo_t));
+      if (topk_on) bL = min(bL, first_bin(ce + c0 >= P.top_k, ci >= P.top_k));
+      if (bL > bstar) bL = bstar;
+      if (lane == 0) {
+        s.ured[37] = (uint32_t)bstar;
+        s.ured[36] = nb >= NBIN;
+        s.ured[35] = (uint32_t)bL;
+      }
     }
     cbar();
     const int bstar = (int)s.ured[37];
     const bool whole = s.ured[36] != 0u;
+    const int bL = (int)s.ured[35];
     // all of the window sorted and its mass clear of top_p: every element of
     // it is kept, the next one (outside) is the first dropped
     const double tp_clear = (double)tp32 + 2e-6;
+    unsigned long long* nuc = P.nuc != nullptr ? P.nuc + (int64_t)v * NUC_MAX : nullptr;
+    double zp = 0.0;
     for (int base = 0; base < nl; base += CT) {
       const int i = base + t;
       const bool in = i < nl;
-      const unsigned long long key = in ? s.u.l.key[i] : 0ull;
+      const unsigned long long key = in ? H.key[i] : 0ull;
       const float xv = in ? list_val(key) : -INFINITY;
-      warp_append(&s.nsel, s.u.l.sel, SEL_CAP, in && xv >= wlow && depth_bin(M, xv, c2) <= bstar,
-                  key);
+      const int bin = (in && xv >= wlow) ? depth_bin(M, xv, c2) : NBIN_PAD;
+      const bool pre = bin < bL;
+      if (pre) zp += (double)__fmul_rn(s.u.l.ecache[i], inv_s);
+      // kept for sure: straight into the stored kept set (order is free there)
+      const unsigned pm = __ballot_sync(0xffffffffu, pre);
+      if (pm) {
+        const int leader = __ffs(pm) - 1;
+        int b0 = 0;
+        if (lane == leader) b0 = atomicAdd(&s.npre, __popc(pm));
+        const int o = __shfl_sync(0xffffffffu, b0, leader) + __popc(pm & ((1u << lane) - 1u));
+        if (pre && nuc != nullptr && o < NUC_MAX) nuc[o] = key;
+      }
+      warp_append(&s.nsel, s.u.l.sel, SEL_CAP, bin >= bL && bin <= bstar, key);
     }
-    cbar();
+    const double zpre = c_sum<double>(zp, s.dred);     // (its barriers publish nsel, npre)
+    npre = s.npre;
     const int nsel = s.nsel;
     if (nsel > SEL_CAP || nsel < 1) return fallback_why(s, FB_SELECT);
     if (nsel <= 32) {
@@ -1086,23 +1118,30 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
         bool exact = false;
         float kx = -INFINITY;
         if (topk_on) {
-          if (P.top_k > nsel) {
+          const int kl = P.top_k - 1 - npre;
+          if (kl < 0 || kl >= nsel) {
             exact = true;
           } else {
-            kx = __shfl_sync(0xffffffffu, xv, P.top_k - 1);
+            kx = __shfl_sync(0xffffffffu, xv, kl);
             n_eff = __popc(__ballot_sync(0xffffffffu, valid && xv >= kx));
           }
         }
         Lw = n_eff - 1;
         if (!exact && topp_on) {
-          const double incl = warp_incl_scan<double>(lane < n_eff ? (double)p : 0.0);
+          const double incl = zpre + warp_incl_scan<double>(lane < n_eff ? (double)p : 0.0);
           const float cl = __fsub_rn(__double2float_rn(incl), p);
-          const unsigned dm = __ballot_sync(0xffffffffu, lane < n_eff && lane > 0 && !(cl < tp32));
+          const unsigned dm = __ballot_sync(0xffffffffu,
+                                            lane < n_eff && npre + lane > 0 && !(cl < tp32));
           const double last = __shfl_sync(0xffffffffu, incl, n_eff - 1);
-          if (dm) Lw = __ffs(dm) - 2;
-          else if (!topk_on && !(whole && last >= tp_clear)) exact = true;   // boundary deeper
+          if (dm) {
+            const int D = __ffs(dm) - 1;
+            if (D == 0) exact = true;                    // boundary above the sorted part
+            else Lw = D - 1;
+          } else if (!topk_on && !(whole && last >= tp_clear)) {
+            exact = true;                                // boundary deeper
+          }
         }
-        const double zs = warp_sum<double>(lane <= Lw ? (double)p : 0.0);
+        const double zs = zpre + warp_sum<double>(lane <= Lw ? (double)p : 0.0);
         if (lane == 0) { s.sc_L = exact ? -1 : Lw; s.z = zs; s.fred[39] = kx; }
       }
       cbar();
@@ -1121,8 +1160,9 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
       cbar();
       int n_eff = nsel;
       if (topk_on) {
-        if (P.top_k > nsel) return fallback_why(s, FB_BOUNDARY);
-        kth_x = list_val(s.u.l.sel[P.top_k - 1]);
+        const int kl = P.top_k - 1 - npre;
+        if (kl < 0 || kl >= nsel) return fallback_why(s, FB_BOUNDARY);
+        kth_x = list_val(s.u.l.sel[kl]);
         int c = 0;
         for (int i = t; i < nsel; i += CT) c += list_val(s.u.l.sel[i]) >= kth_x;
         n_eff = c_sum<int>(c, reinterpret_cast<int*>(s.ured));
@@ -1130,13 +1170,13 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
       if (topp_on) {
         if (t == 0) s.sc_L = 0x7FFFFFFF;
         cbar();
-        double carry = 0.0;
+        double carry = zpre;
         for (int base = 0; base < n_eff; base += CT) {
           const int i = base + t;
           const float p = i < n_eff ? s.u.l.p[i] : 0.f;
           double tot;
           const double pre = c_excl_scan<double>((double)p, s.dred, &tot);
-          if (i < n_eff && i > 0) {
+          if (i < n_eff && npre + i > 0) {
             const float cl = __fsub_rn(__double2float_rn(carry + pre + (double)p), p);
             if (!(cl < tp32)) atomicMin(&s.sc_L, i);
           }
@@ -1145,23 +1185,25 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
           if (s.sc_L != 0x7FFFFFFF) break;
         }
         const int D = s.sc_L;
+        if (D == 0) return fallback_why(s, FB_BOUNDARY);   // boundary above the sorted part
         if (D != 0x7FFFFFFF) L = D - 1;
         else if (topk_on || (whole && carry >= tp_clear)) L = n_eff - 1;
-        else return fallback_why(s, FB_BOUNDARY);   // boundary below the sorted part
+        else return fallback_why(s, FB_BOUNDARY);         // boundary below the sorted part
       } else {
         L = n_eff - 1;
       }
       double zs = 0.0;
       for (int i = t; i <= L; i += CT) zs += (double)s.u.l.p[i];
-      z = c_sum<double>(zs, s.dred);
+      z = zpre + c_sum<double>(zs, s.dred);
     }
   } else {
     z = S * (double)inv_s;
   }
   const float zf = fmaxf(__double2float_rn(z), 1e-12f);
-  const bool listed = P.nuc != nullptr && !all_kept && L + 1 <= NUC_MAX;
+  const int nkept = npre + L + 1;
+  const bool listed = P.nuc != nullptr && !all_kept && nkept <= NUC_MAX;
   if (listed) {
-    unsigned long long* dst = P.nuc + (int64_t)v * NUC_MAX;
+    unsigned long long* dst = P.nuc + (int64_t)v * NUC_MAX + npre;
     for (int i = t; i <= L; i += CT) dst[i] = s.u.l.sel[i];
   }
   if (t == 0) {
@@ -1174,7 +1216,7 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
     o.idx_cut = all_kept ? (int32_t)NO_CUT : (int32_t)list_idx(s.u.l.sel[L]);
     o.argmax = -1;
     o.flags = (all_kept ? F_ALLKEPT : 0) | (listed ? F_LISTED : 0);
-    o.n_keep = all_kept ? -1 : L + 1;
+    o.n_keep = all_kept ? -1 : nkept;
     o.fb_why = 0;
     o.pad = 0;
     o.probe_p = has_probe ? stats_prob_x(o, xprobe, P.T, probe) : 0.f;
@@ -1187,7 +1229,7 @@ __device__ bool finalize_list(HistSmem& s, const StatsParams& P, const Stream& s
 // The row's accept test and its residual / bonus draw (consumer threads of the
 // CTA that finished the row's last vector).
 __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
-  const int t = threadIdx.x;
+  const int t = ftid();
   const int npos0 = P.vs.npos[0], npos = P.vs.npos[0] + P.vs.npos[1];
   const int vrow = row * npos;
   const int k = P.k;
@@ -1281,7 +1323,69 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
   }
   if (t == 0) s.sc_y = -1;
   cbar();
-  if (stp.flags & F_LISTED) {
+  if ((stp.flags & F_LISTED) && stp.n_keep <= RANK_MAX) {
+    // p's kept set (values from the stored keys, q gathered at their
+    // indices); each element's exclusive prefix in vocabulary order is summed
+    // directly over the set (no sort): the draw is the element whose
+    // [prefix, prefix + r) holds u * R
+    constexpr int PER = RANK_MAX / CT;
+    const int cnt = stp.n_keep;
+    const unsigned long long* src = P.nuc + (int64_t)(vrow + ppos) * NUC_MAX;
+    float* ra = s.u.l.p;                       // r, then p at RANK_MAX
+    double rs = 0.0, ps = 0.0;
+    uint32_t jmine[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int i = t + q * CT;
+      jmine[q] = 0xFFFFFFFFu;
+      if (i < cnt) {
+        const unsigned long long key = __ldcg(src + i);
+        const uint32_t j = list_idx(key);
+        const float pj = __fdiv_rn(prob_of(list_val(key), P.T, stp.m, stp.inv_s), stp.zf);
+        float r = pj;
+        if (resid && pj != 0.f)
+          r = fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, (int64_t)j)), 0.f);
+        s.u.l.sel[i] = j;
+        ra[i] = r;
+        ra[RANK_MAX + i] = pj;
+        rs += (double)r;
+        ps += (double)pj;
+        jmine[q] = j;
+      }
+    }
+    if (t == 0) { s.ured[29] = 0xFFFFFFFFu; s.ured[30] = 0xFFFFFFFFu; s.ured[31] = 0u; }
+    double R = c_sum<double>(rs, s.dred);
+    const double Pm = c_sum<double>(ps, s.dred);
+    const bool use_p = !resid || __double2float_rn(R) <= 1e-9f;   // sampling.py:86-89
+    if (use_p) { R = Pm; ra += RANK_MAX; }
+    const double tgt = u * R;
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int i = t + q * CT;
+      if (i < cnt) {
+        const uint32_t j = jmine[q];
+        double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+        int k = 0;
+        for (; k + 4 <= cnt; k += 4) {
+          if ((uint32_t)s.u.l.sel[k] < j) a0 += (double)ra[k];
+          if ((uint32_t)s.u.l.sel[k + 1] < j) a1 += (double)ra[k + 1];
+          if ((uint32_t)s.u.l.sel[k + 2] < j) a2 += (double)ra[k + 2];
+          if ((uint32_t)s.u.l.sel[k + 3] < j) a3 += (double)ra[k + 3];
+        }
+        for (; k < cnt; ++k)
+          if ((uint32_t)s.u.l.sel[k] < j) a0 += (double)ra[k];
+        const double pre = (a0 + a1) + (a2 + a3);
+        const float r = ra[i];
+        if (pre <= tgt && pre + (double)r > tgt) atomicMin(&s.ured[30], j);
+        if (r > 0.f) atomicMax(&s.ured[31], j + 1u);
+        atomicMin(&s.ured[29], j);
+      }
+    }
+    cbar();
+    if (t == 0)
+      s.sc_y = s.ured[30] != 0xFFFFFFFFu ? (long long)s.ured[30]
+               : s.ured[31] > 0u ? (long long)(s.ured[31] - 1u) : (long long)s.ured[29];
+  } else if (stp.flags & F_LISTED) {
     const int cnt = stp.n_keep;
     int N = 1;
     while (N < cnt) N <<= 1;
@@ -1392,10 +1496,9 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
 }
 
 template <int DT>
-__global__ void __launch_bounds__(HT, CTAS_PER_SM) hist_stats_kernel(StatsParams P) {
+__global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   HistSmem& s = *reinterpret_cast<HistSmem*>(smem_raw);
-  const int t = threadIdx.x;
   const int V = P.V;
   // log2(e) / T as c2 + c2l, c2 rounded down so that c2l > 0: y(x) is then
   // monotone and y(-inf) = -inf (a negative c2l would give -inf + inf)
@@ -1405,146 +1508,189 @@ __global__ void __launch_bounds__(HT, CTAS_PER_SM) hist_stats_kernel(StatsParams
   const float wlist = W_LIST / c2;                      // list window in logit units
   const int npos = P.vs.npos[0] + P.vs.npos[1];
 
-  if (t == 0) {
+  if (threadIdx.x == 0) {
     for (int i = 0; i < NSLOT; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], NCW);
+      mbar_init(&s.empty[i], NSW);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.streamed[i], NSW);
+      mbar_init(&s.freed[i], 1);
+      s.hand[i].nkey = 0;
+      s.hand[i].gkey = 0u;
     }
     s.gh = P.ghist + (size_t)blockIdx.x * HIST_WORDS;
     s.abort_flag = 0;
-    s.nrec = 0;
-    s.nkey = 0;
     s.fb_why = 0;
-    s.gkey = 0u;
     s.ncorr = 0;
     s.corr_full = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  if (t >= CT) {
-    // ---------------- producer warp: stream this CTA's vectors into the ring
-    if (t == CT) {
-      uint32_t g = 0;
-      bool ok = true;
-      for (int v = blockIdx.x; v < P.nvec && ok; v += gridDim.x) {
-        int set, row, pos;
-        vec_locate(P.vs, v, &set, &row, &pos);
-        const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
-        const VecGeom gm(x, V);
-        const char* body = reinterpret_cast<const char*>(x + gm.head);
-        for (int c = 0; c < gm.nchunk; ++c, ++g) {
-          const int sl = g % NSLOT;
-          const uint32_t ph = (g / NSLOT) & 1u;
-          if (!mbar_wait(&s.empty[sl], ph ^ 1u, &s.abort_flag)) { ok = false; break; }
+  if (threadIdx.x < ST0) {
+    // ---------------- producer warp (lane 0): ring refills
+    if (threadIdx.x != 0) return;
+    bool ok = true;
+    uint32_t g = 0, issued = 0;
+    for (int v = blockIdx.x; v < P.nvec; v += gridDim.x) {
+      int set, row, pos;
+      vec_locate(P.vs, v, &set, &row, &pos);
+      const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
+      const VecGeom gm(x, V);
+      const char* body = reinterpret_cast<const char*>(x + gm.head);
+      for (int c = 0; c < gm.nchunk; ++c, ++g) {
+        const int sl = g % NSLOT;
+        if (g >= NSLOT)
+          ok = ok && mbar_wait(&s.empty[sl], ((g - NSLOT) / NSLOT) & 1u, &s.abort_flag);
+        if (ok) {
           const uint32_t bytes = (uint32_t)min(SLOT, gm.nunits * 16 - c * SLOT);
           mbar_expect_tx(&s.full[sl], bytes);
           bulk_g2s(s.ring[sl], body + (size_t)c * SLOT, bytes, &s.full[sl]);
+          issued = g + 1;
         }
       }
-      // on abort, let the copies already issued land before the CTA exits
-      if (!ok) {
-        for (uint32_t k = 0; k < NSLOT && k < g; ++k) {
-          const uint32_t gg = g - 1 - k;
-          int dummy = 0;
-          mbar_wait(&s.full[gg % NSLOT], (gg / NSLOT) & 1u, &dummy);
+    }
+    if (!ok) {
+      // after an abort, let the copies already issued land before the CTA exits
+      for (uint32_t gg = issued > (uint32_t)NSLOT ? issued - NSLOT : 0u; gg < issued; ++gg) {
+        int dummy = 0;
+        mbar_wait(&s.full[gg % NSLOT], (gg / NSLOT) & 1u, &dummy);
+      }
+      atomicOr(P.status, 1);
+    }
+    return;
+  }
+
+  if (threadIdx.x < FIN0) {
+    // ---------------- streaming warps
+    const int t = threadIdx.x - ST0;
+    const int lane = t & 31, wl = t >> 5;
+    uint32_t g = 0;
+    int vl = 0;
+    for (int v = blockIdx.x; v < P.nvec; v += gridDim.x, ++vl) {
+      VecHand& H = s.hand[vl & 1];
+      if (vl >= 2)                                   // wait until the finalize warps release it
+        __all_sync(0xffffffffu, mbar_wait(&s.freed[vl & 1], ((vl >> 1) - 1) & 1, &s.abort_flag));
+      int set, row, pos;
+      vec_locate(P.vs, v, &set, &row, &pos);
+      const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
+      const VecGeom gm(x, V);
+      Stream st;
+      st.Rc2 = -INFINITY; st.m = -INFINITY; st.Y = INFINITY; st.pkey = 0u;
+      st.bulk = 0.0;
+      for (int c = 0; c < gm.nchunk; ++c, ++g) {
+        const int sl = g % NSLOT;
+        const bool okw = __all_sync(0xffffffffu, mbar_wait(&s.full[sl], (g / NSLOT) & 1u, &s.abort_flag));
+        const int units = okw ? min(SLOT, gm.nunits * 16 - c * SLOT) >> 4 : 0;
+        const uint4* u4 = reinterpret_cast<const uint4*>(s.ring[sl]);
+        uint32_t w[4 * GPS];
+#pragma unroll
+        for (int q = 0; q < GPS; ++q) {
+          const int u = t + q * ST_N;
+          const uint32_t n2 = neg_inf2<DT>();
+          const uint4 w4 = u < units ? u4[u] : make_uint4(n2, n2, n2, n2);
+          w[4 * q] = w4.x; w[4 * q + 1] = w4.y; w[4 * q + 2] = w4.z; w[4 * q + 3] = w4.w;
         }
-        atomicOr(P.status, 1);
+        if (c == 0) {
+          // the maximum of the chunks already in the ring (no waiting for the
+          // later ones): bulk reference of every lane and the first list
+          // threshold
+          uint32_t pm1[2 * GPS];
+          float lm = lane_max<DT, GPS>(w, pm1);
+          const int nseed = min(NSLOT, gm.nchunk);
+#pragma unroll 1
+          for (int i = 1; i < nseed; ++i) {
+            const uint32_t gi = g + (uint32_t)i;
+            const bool oki = __all_sync(0xffffffffu, mbar_test(&s.full[gi % NSLOT], (gi / NSLOT) & 1u));
+            if (oki) {
+              const int ui = min(SLOT, gm.nunits * 16 - i * SLOT) >> 4;
+              const uint4* wi4 = reinterpret_cast<const uint4*>(s.ring[gi % NSLOT]);
+              uint32_t wi[4 * GPS];
+#pragma unroll
+              for (int q = 0; q < GPS; ++q) {
+                const int u = t + q * ST_N;
+                const uint32_t n2 = neg_inf2<DT>();
+                const uint4 w4 = u < ui ? wi4[u] : make_uint4(n2, n2, n2, n2);
+                wi[4 * q] = w4.x; wi[4 * q + 1] = w4.y; wi[4 * q + 2] = w4.z; wi[4 * q + 3] = w4.w;
+              }
+              lm = fmaxf(lm, lane_max<DT, GPS>(wi, pm1));
+            }
+          }
+          const uint32_t wk = __reduce_max_sync(0xffffffffu, fkey(lm));
+          if (lane == 0) atomicMax(&H.gkey, wk);
+          sbar();
+          const float r = fkey_value(*reinterpret_cast<volatile uint32_t*>(&H.gkey));
+          if (r > -INFINITY) set_ref(st, r, c2, c2l, wlist);
+        }
+        if (okw) {
+          sync_max(H, st, c2, c2l, wlist);
+          stream_words<DT, GPS, true>(s, H, st, w, sl, (uint32_t)(gm.head + c * (SLOT / 2)), 0u,
+                                      c2, c2l, wlist);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[sl]);
+      }
+      // ragged head / tail elements (< 16 of them), first streaming warp
+      const int nrag = gm.head + (V - gm.tail0);
+      if (wl == 0 && nrag > 0) {
+        const bool valid = lane < nrag;
+        const int j = !valid ? 0 : (lane < gm.head ? lane : gm.tail0 + (lane - gm.head));
+        constexpr uint32_t NEG16 = neg_inf2<DT>() & 0xFFFFu;
+        const uint32_t lo = valid ? (uint32_t)__ldg(x + j) : NEG16;
+        const uint32_t wv[4] = {lo | (NEG16 << 16), neg_inf2<DT>(), neg_inf2<DT>(), neg_inf2<DT>()};
+        stream_words<DT, 1, false>(s, H, st, wv, 0, 0u, (uint32_t)j, c2, c2l, wlist);
+      }
+      // the warp's bulk sum, relative to the largest offset among its lanes
+      float wr = st.Rc2;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) wr = fmaxf(wr, __shfl_xor_sync(0xffffffffu, wr, o));
+      double b = 0.0;
+      if (st.Rc2 != -INFINITY && st.bulk > 0.0) b = st.bulk * exp2((double)st.Rc2 - (double)wr);
+      b = warp_sum(b);
+      if (lane == 0) {
+        H.wbulk[wl] = b;
+        H.wrc2[wl] = wr;
+        mbar_arrive(&s.streamed[vl & 1]);
       }
     }
     return;
   }
 
-  // ---------------- consumer warps
-  uint32_t g = 0;
-  for (int v = blockIdx.x; v < P.nvec; v += gridDim.x) {
-    int set, row, pos;
-    vec_locate(P.vs, v, &set, &row, &pos);
-    const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
-    const int64_t probe = vec_probe(P.vs, set, row, pos);
-    const VecGeom gm(x, V);
-    Stream st;
-    st.Rc2 = -INFINITY; st.m = -INFINITY; st.Y = INFINITY; st.pkey = 0u;
-    st.bulk = 0.0;
-    bool aborted = false;
-    for (int c = 0; c < gm.nchunk; ++c, ++g) {
-      const int sl = g % NSLOT;
-      // warp-uniform: stream_words works on whole warps
-      bool okw = __all_sync(0xffffffffu, mbar_wait(&s.full[sl], (g / NSLOT) & 1u, &s.abort_flag));
-      const int units = okw ? min(SLOT, gm.nunits * 16 - c * SLOT) >> 4 : 0;
-      const uint4* u4 = reinterpret_cast<const uint4*>(s.ring[sl]);
-      uint32_t w[4 * GPS];
-#pragma unroll
-      for (int q = 0; q < GPS; ++q) {
-        const int u = t + q * CT;
-        const uint32_t n2 = neg_inf2<DT>();
-        const uint4 w4 = u < units ? u4[u] : make_uint4(n2, n2, n2, n2);
-        w[4 * q] = w4.x; w[4 * q + 1] = w4.y; w[4 * q + 2] = w4.z; w[4 * q + 3] = w4.w;
-      }
-      if (c == 0) {
-        // the CTA-wide maximum of the chunks already in the ring: bulk
-        // reference of every lane and the first list threshold
-        uint32_t pm1[2 * GPS];
-        float lm = lane_max<DT, GPS>(w, pm1);
-        const int nseed = min(NSLOT, gm.nchunk);
-#pragma unroll 1
-        for (int i = 1; i < nseed; ++i) {
-          const uint32_t gi = g + (uint32_t)i;
-          okw = okw && __all_sync(0xffffffffu, mbar_wait(&s.full[gi % NSLOT], (gi / NSLOT) & 1u,
-                                                          &s.abort_flag));
-          if (okw) {
-            const int ui = min(SLOT, gm.nunits * 16 - i * SLOT) >> 4;
-            const uint4* wi4 = reinterpret_cast<const uint4*>(s.ring[gi % NSLOT]);
-            uint32_t wi[4 * GPS];
-#pragma unroll
-            for (int q = 0; q < GPS; ++q) {
-              const int u = t + q * CT;
-              const uint32_t n2 = neg_inf2<DT>();
-              const uint4 w4 = u < ui ? wi4[u] : make_uint4(n2, n2, n2, n2);
-              wi[4 * q] = w4.x; wi[4 * q + 1] = w4.y; wi[4 * q + 2] = w4.z; wi[4 * q + 3] = w4.w;
-            }
-            lm = fmaxf(lm, lane_max<DT, GPS>(wi, pm1));
-          }
-        }
-        const uint32_t wk = __reduce_max_sync(0xffffffffu, fkey(lm));
-        if ((t & 31) == 0) atomicMax(&s.gkey, wk);
+  // ---------------- finalize warps: list -> stats -> row draw, one vector
+  // behind the streaming warps
+  const int t = ftid();
+  int vl = 0;
+  for (int v = blockIdx.x; v < P.nvec; v += gridDim.x, ++vl) {
+    VecHand& H = s.hand[vl & 1];
+    const uint32_t par = (vl >> 1) & 1;
+    if (!mbar_wait(&s.streamed[vl & 1], par, &s.abort_flag)) s.abort_flag = 1;
+    cbar();
+    if (t == 0) s.fin_skip = *reinterpret_cast<volatile int*>(&s.abort_flag);
+    cbar();
+    if (!s.fin_skip) {
+      int set, row, pos;
+      vec_locate(P.vs, v, &set, &row, &pos);
+      const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
+      const int64_t probe = vec_probe(P.vs, set, row, pos);
+      if (finalize_list(s, H, P, v, x, probe, c2, wlist)) finalize_histogram(s, P, v, x, probe);
+      // row bookkeeping: the CTA that completes a row draws for it
+      if (P.fused) {
+        __threadfence();
         cbar();
-        const float r = fkey_value(*reinterpret_cast<volatile uint32_t*>(&s.gkey));
-        if (r > -INFINITY) set_ref(st, r, c2, c2l, wlist);
+        if (t == 0) s.last_row = atomicAdd(&P.row_ctr[row], 1) == npos - 1;
+        cbar();
+        if (s.last_row) finish_row(s, P, row);
       }
-      if (!okw) { aborted = true; break; }
-      sync_max(s, st, c2, c2l, wlist);
-      stream_words<DT, GPS, true>(s, st, w, (uint32_t)c, 0u, c2, c2l, wlist);
-      __syncwarp();
-      if ((t & 31) == 0) mbar_arrive(&s.empty[sl]);
-    }
-    // ragged head / tail elements (< 16 of them), warp 0
-    const int nrag = gm.head + (V - gm.tail0);
-    if (t < 32 && nrag > 0 && !aborted) {
-      const bool valid = t < nrag;
-      const int j = !valid ? 0 : (t < gm.head ? t : gm.tail0 + (t - gm.head));
-      constexpr uint32_t NEG16 = neg_inf2<DT>() & 0xFFFFu;
-      const uint32_t lo = valid ? (uint32_t)__ldg(x + j) : NEG16;
-      const uint32_t wv[4] = {lo | (NEG16 << 16), neg_inf2<DT>(), neg_inf2<DT>(), neg_inf2<DT>()};
-      stream_words<DT, 1, false>(s, st, wv, 0u, (uint32_t)j, c2, c2l, wlist);
     }
     cbar();
-    if (aborted || s.abort_flag) {
-      if (t == 0) atomicOr(P.status, 1);
-      break;
+    if (t == 0) {
+      H.nkey = 0;
+      H.gkey = 0u;
+      mbar_arrive(&s.freed[vl & 1]);
     }
-    if (finalize_list<DT>(s, P, st, v, x, probe, c2, c2l, wlist)) finalize_histogram(s, P, v, x, probe);
-    // row bookkeeping: the CTA that completes a row draws for it
-    if (P.fused) {
-      __threadfence();
-      cbar();
-      if (t == 0) s.last_row = atomicAdd(&P.row_ctr[row], 1) == npos - 1;
-      cbar();
-      if (s.last_row) finish_row(s, P, row);
-    }
-    if (t == 0) { s.nrec = 0; s.nkey = 0; s.gkey = 0u; }
-    cbar();
   }
+  if (t == 0 && s.abort_flag) atomicOr(P.status, 1);
 }
 
 // ---------------------------------------------------------------------------
@@ -2200,7 +2346,7 @@ static int run_sampling(const VecSet& vs, int nvec, int dtype, int V, float T, f
     }
     P.ghist = reinterpret_cast<uint32_t*>(ws + L.ghist);
     const int nsm = device_sms();
-    int grid = CTAS_PER_SM * nsm;
+    int grid = nsm;
     if (grid > GRID_MAX) grid = GRID_MAX;
     if (grid > nvec) grid = nvec;
     if (dtype == SD_DTYPE_BF16)
