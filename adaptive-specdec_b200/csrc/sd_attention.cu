@@ -10,7 +10,9 @@
 // Work decomposition: one CTA per (row, kv head, key split).  The CTA holds the
 // R = qlen * (Hq / Hkv) query rows that share the kv head (grouped-query), so
 // every K/V element is read from HBM once per split.  Splits write partial
-// (max, sum, acc) to the workspace; a combine kernel merges them.
+// (max, sum, acc) to the workspace; a combine kernel merges them.  bf16 with
+// head_dim 128 runs on the tensor cores (attn_mma_kernel); other shapes and
+// fp32 on the CUDA cores (attn_split_kernel).
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -192,6 +194,275 @@ __global__ void __launch_bounds__(AT) attn_combine_kernel(AttnParams P) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core path (bf16, head_dim 128, R = qlen * group <= 32 query rows)
+// ---------------------------------------------------------------------------
+// One CTA per (row, kv head, split of SPLIT_KEYS keys), 4 warps.  Per tile of
+// 64 keys each warp takes 16 keys and computes S^T = K Q^T (keys on the M
+// side, the <= 32 query rows of the kv head on N, so only N pads), the online
+// softmax per query row in base 2, and O^T += V^T P^T with P^T moved into the
+// B-operand layout by a register transpose.  K / V tiles are double-buffered
+// in shared memory by cp.async with a 16-byte-chunk XOR swizzle (conflict-free
+// ldmatrix).  The four warps' (max, sum, O) merge in shared memory and the
+// split's partial goes to the same workspace layout as the CUDA-core path.
+constexpr int MT_KEYS = 64;              // keys per tile (16 per warp)
+constexpr int MT_THREADS = 128;
+constexpr int MT_D = 128;
+
+struct MmaSmem {
+  union {
+    struct {
+      __nv_bfloat16 k[2][MT_KEYS * MT_D];
+      __nv_bfloat16 v[2][MT_KEYS * MT_D];
+    } kv;
+    float o[4][32][MT_D];                // per-warp O (rows x d) for the merge
+  } u;
+  __nv_bfloat16 q[32 * MT_D];
+  float ms[4][32], ls[4][32];
+};
+
+// byte offset of 16-byte chunk c of row r in a swizzled [rows][128] bf16 tile
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return (uint32_t)(r * (MT_D * 2) + ((c ^ (r & 7)) << 4));
+}
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool in) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+               :: "r"(dst), "l"(src), "r"(in ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldm_x4(uint32_t addr, uint32_t& a0, uint32_t& a1, uint32_t& a2,
+                                       uint32_t& a3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3) : "r"(addr));
+}
+__device__ __forceinline__ void ldm_x4_t(uint32_t addr, uint32_t& a0, uint32_t& a1, uint32_t& a2,
+                                         uint32_t& a3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3) : "r"(addr));
+}
+__device__ __forceinline__ void ldm_x2(uint32_t addr, uint32_t& b0, uint32_t& b1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
+               : "=r"(b0), "=r"(b1) : "r"(addr));
+}
+__device__ __forceinline__ uint32_t movm_t(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+// D = A (16x16, row) * B (16x8, col) + D, bf16 in, fp32 accumulate
+__device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+               "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(MT_THREADS) attn_mma_kernel(AttnParams P) {
+  extern __shared__ __align__(128) unsigned char mma_smem[];
+  MmaSmem& S = *reinterpret_cast<MmaSmem*>(mma_smem);
+  const int split = blockIdx.x % P.nsplit;
+  const int bh = blockIdx.x / P.nsplit;
+  const int h = bh % P.Hkv, b = bh / P.Hkv;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int R = P.R;
+  int kmax = 0;
+  for (int j = 0; j < P.qlen; ++j) kmax = max(kmax, row_limit(P, b, j));
+  const int s0 = split * SPLIT_KEYS, s1 = min(kmax, s0 + SPLIT_KEYS);
+  const int64_t pbase = (((int64_t)b * P.Hkv + h) * P.nsplit + split) * R;
+  if (s0 >= s1) {                                      // nothing live in this split
+    for (int r = t; r < R; r += MT_THREADS) {
+      P.part_ml[(pbase + r) * 2] = -INFINITY;
+      P.part_ml[(pbase + r) * 2 + 1] = 0.f;
+    }
+    return;
+  }
+  const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(P.k) +
+                            ((int64_t)b * P.Hkv + h) * P.C * MT_D;
+  const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(P.v) +
+                            ((int64_t)b * P.Hkv + h) * P.C * MT_D;
+  auto load_tile = [&](int tile, int buf) {
+    const int key0 = s0 + tile * MT_KEYS;
+    const uint32_t kd = smem_addr(S.u.kv.k[buf]), vd = smem_addr(S.u.kv.v[buf]);
+    for (int i = t; i < MT_KEYS * 16; i += MT_THREADS) {
+      const int kk = i >> 4, c = i & 15;
+      const bool in = key0 + kk < s1;
+      const int64_t row = in ? key0 + kk : s0;         // a valid address when nothing is read
+      cp_async16(kd + sw_off(kk, c), kb + row * MT_D + 8 * c, in);
+      cp_async16(vd + sw_off(kk, c), vb + row * MT_D + 8 * c, in);
+    }
+    cp_async_commit();
+  };
+  const int ntiles = (s1 - s0 + MT_KEYS - 1) / MT_KEYS;
+  load_tile(0, 0);
+  if (ntiles > 1) load_tile(1, 1);
+  // the kv head's query rows r = j * group + g (zero rows up to 8 * NT)
+  const __nv_bfloat16* Q = reinterpret_cast<const __nv_bfloat16*>(P.q);
+  for (int i = t; i < 32 * 16; i += MT_THREADS) {
+    const int r = i >> 4, c = i & 15;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (r < R) {
+      const int j = r / P.group, hq = h * P.group + r % P.group;
+      v = *reinterpret_cast<const uint4*>(Q + b * P.qbs + hq * P.qhs + j * P.qqs + 8 * c);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<char*>(S.q) + sw_off(r, c)) = v;
+  }
+  __syncthreads();
+  uint32_t qf[8][NT][2];
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      ldm_x2(smem_addr(S.q) + sw_off(8 * nt + (lane & 7), 2 * ks + ((lane >> 3) & 1)),
+             qf[ks][nt][0], qf[ks][nt][1]);
+  // this thread's query-row columns r = 8 nt + 2 (lane % 4) + e
+  float mrow[NT][2], lrow[NT][2];
+  int lim[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int r = 8 * nt + 2 * (lane & 3) + e;
+      mrow[nt][e] = -INFINITY;
+      lrow[nt][e] = 0.f;
+      lim[nt][e] = r < R ? row_limit(P, b, r / P.group) : 0;
+    }
+  float o[8][NT][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.f;
+  const float sl2 = P.scale * 1.4426950408889634f;
+  const int krow0 = 16 * w;                            // this warp's keys within a tile
+  for (int tile = 0; tile < ntiles; ++tile) {
+    const int buf = tile & 1;
+    if (tile + 1 < ntiles) cp_async_wait<1>(); else cp_async_wait<0>();
+    __syncthreads();
+    const uint32_t kbase = smem_addr(S.u.kv.k[buf]), vbase = smem_addr(S.u.kv.v[buf]);
+    // S^T = K Q^T for the warp's 16 keys
+    float sc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[nt][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      ldm_x4(kbase + sw_off(krow0 + (lane & 15), 2 * ks + (lane >> 4)), a0, a1, a2, a3);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma16816(sc[nt], a0, a1, a2, a3, qf[ks][nt][0], qf[ks][nt][1]);
+    }
+    // online softmax per query row (base 2), over the warp's keys
+    const int kg = s0 + tile * MT_KEYS + krow0 + (lane >> 2);
+    uint32_t pb[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int le = min(lim[nt][e], s1);
+        const float sa = kg < le ? sc[nt][e] * sl2 : -INFINITY;
+        const float sb = kg + 8 < le ? sc[nt][2 + e] * sl2 : -INFINITY;
+        float mx = fmaxf(sa, sb);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mold = mrow[nt][e];
+        const float mnew = fmaxf(mold, mx);
+        const float alpha = mnew == -INFINITY ? 1.f : (mold == -INFINITY ? 0.f : ex2f(mold - mnew));
+        const float pa = sa == -INFINITY ? 0.f : ex2f(sa - mnew);
+        const float pbv = sb == -INFINITY ? 0.f : ex2f(sb - mnew);
+        lrow[nt][e] = lrow[nt][e] * alpha + pa + pbv;
+        mrow[nt][e] = mnew;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          o[mt][nt][e] *= alpha;
+          o[mt][nt][2 + e] *= alpha;
+        }
+        sc[nt][e] = pa;
+        sc[nt][2 + e] = pbv;
+      }
+      // P^T (keys x rows) into the B-operand layout
+      pb[nt][0] = movm_t(pack_bf16(sc[nt][0], sc[nt][1]));
+      pb[nt][1] = movm_t(pack_bf16(sc[nt][2], sc[nt][3]));
+    }
+    // O^T += V^T P^T over the head dimension (8 m-tiles of 16)
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      uint32_t a0, a1, a2, a3;
+      ldm_x4_t(vbase + sw_off(krow0 + (lane & 7) + ((lane >> 4) << 3), 2 * mt + ((lane >> 3) & 1)),
+               a0, a1, a2, a3);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma16816(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+    }
+    __syncthreads();                                   // the buffer is refilled next
+    if (tile + 2 < ntiles) load_tile(tile + 2, buf);
+  }
+  // row sums over the lanes that share a column; merge the four warps
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float l = lrow[nt][e];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      lrow[nt][e] = l;
+    }
+  __syncthreads();                                     // K / V buffers become the merge area
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int r = 8 * nt + 2 * (lane & 3) + e;
+      if (lane < 4) { S.ms[w][r] = mrow[nt][e]; S.ls[w][r] = lrow[nt][e]; }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        S.u.o[w][r][16 * mt + (lane >> 2)] = o[mt][nt][e];
+        S.u.o[w][r][16 * mt + (lane >> 2) + 8] = o[mt][nt][2 + e];
+      }
+    }
+  __syncthreads();
+  for (int idx = t; idx < R * MT_D; idx += MT_THREADS) {
+    const int r = idx >> 7, d = idx & (MT_D - 1);
+    float m = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) m = fmaxf(m, S.ms[q][r]);
+    float acc = 0.f, l = 0.f;
+    if (m != -INFINITY) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (S.ms[q][r] == -INFINITY) continue;
+        const float f = ex2f(S.ms[q][r] - m);
+        acc += f * S.u.o[q][r][d];
+        l += f * S.ls[q][r];
+      }
+    }
+    P.part_acc[(pbase + r) * MT_D + d] = acc;
+    if (d == 0) {
+      P.part_ml[(pbase + r) * 2] = m == -INFINITY ? -INFINITY : m * 0.6931471805599453f;
+      P.part_ml[(pbase + r) * 2 + 1] = l;
+    }
+  }
+}
+
 static int nsplit_for(int C, int qlen) {
   const int maxkeys = C + qlen;
   return (maxkeys + SPLIT_KEYS - 1) / SPLIT_KEYS;
@@ -234,6 +505,38 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
   P.part_acc = ws;
   P.part_ml = ws + (size_t)B * Hkv * P.nsplit * P.R * D;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // tensor-core path: bf16, head_dim 128, <= 32 query rows per kv head,
+  // 16-byte aligned rows
+  const bool mma_ok = dtype == SD_DTYPE_BF16 && D == MT_D && P.R <= 32 &&
+                      (reinterpret_cast<uintptr_t>(q) & 15) == 0 && qbs % 8 == 0 &&
+                      qhs % 8 == 0 && qqs % 8 == 0 &&
+                      (reinterpret_cast<uintptr_t>(kcache) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(vcache) & 15) == 0;
+  if (mma_ok) {
+    P.nrc = 1;
+    const unsigned g = (unsigned)(B * Hkv * P.nsplit);
+    const int sm = (int)sizeof(MmaSmem);
+    switch ((P.R + 7) / 8) {
+      case 1:
+        cudaFuncSetAttribute(attn_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        attn_mma_kernel<1><<<g, MT_THREADS, sm, st>>>(P);
+        break;
+      case 2:
+        cudaFuncSetAttribute(attn_mma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        attn_mma_kernel<2><<<g, MT_THREADS, sm, st>>>(P);
+        break;
+      case 3:
+        cudaFuncSetAttribute(attn_mma_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        attn_mma_kernel<3><<<g, MT_THREADS, sm, st>>>(P);
+        break;
+      default:
+        cudaFuncSetAttribute(attn_mma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+        attn_mma_kernel<4><<<g, MT_THREADS, sm, st>>>(P);
+        break;
+    }
+    attn_combine_kernel<__nv_bfloat16><<<B * Hkv, AT, 0, st>>>(P);
+    return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+  }
   const unsigned grid = (unsigned)(B * Hkv * P.nrc * P.nsplit);
   if (dtype == SD_DTYPE_BF16) {
     const size_t sm = sizeof(AttnSmem<__nv_bfloat16>);

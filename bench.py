@@ -44,7 +44,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="sample", choices=["sample", "greedy"])
+    ap.add_argument("--mode", default="sample", choices=["sample", "greedy", "attn"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -215,10 +215,67 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def attn_bench(a):
+    """--mode attn: verify attention at config 3 (one layer of the Qwen3-8B
+    shape: B=64 rows, 32 query / 8 kv heads x 128, 5 queries per row, context
+    lengths uniform in [512, 8192]), one GPU.  Algorithmic bytes: every live
+    K and V row read once, plus Q and the output."""
+    import torch
+    from specdec import attention as A
+    from specdec import workloads as W
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, Hq, Hkv, D, ql = 64, 32, 8, 128, 5
+    lens = W.attn_lengths(B, seed=0)
+    C = int(lens.max()) + ql + 3
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(B, Hq, ql, D, generator=g, device=dev).to(torch.bfloat16)
+    kc = torch.randn(B, Hkv, C, D, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, C, D, generator=g, device=dev).to(torch.bfloat16)
+    lens_d = lens.to(dev)
+    out = torch.empty(B, ql, Hq, D, dtype=torch.bfloat16, device=dev)
+    live = int((lens + ql).sum())
+    bytes_call = live * Hkv * D * 2 * 2 + 2 * q.numel() * 2
+    flops_call = sum(4 * Hq * ql * (int(n) + (ql + 1) // 2) * D for n in lens)
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        for _ in range(max(3, a.warmup)):
+            A.verify_attention(q, kc, vc, lens_d, out=out)
+        torch.cuda.synchronize(dev)
+        steps = max(5, min(a.steps, 200))
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index or 0) as clk:
+            e0.record(s)
+            for _ in range(steps):
+                A.verify_attention(q, kc, vc, lens_d, out=out)
+            e1.record(s)
+            torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    gbs = bytes_call / (ms * 1e-3) / 1e9
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs") or 6650.0
+    print(json.dumps({
+        "metric": "verify attention GB/s (config 3, one layer: B=64, 32q/8kv x 128, 5 queries, "
+                  "len U[512,8192])", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": steps,
+        "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q / k / v)",
+        "config": {"workload": "config 3 verify attention, one layer", "rows": B, "Hq": Hq,
+                   "Hkv": Hkv, "head_dim": D, "queries": ql, "live_keys": live,
+                   "l2": "one layer reads >1 GB of K/V (> 126 MB L2)"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "tflops": flops_call / (ms * 1e-3) / 1e12,
+                     "scope": f"{bytes_call} algorithmic bytes per call / event-timed call"},
+        "gpu_launches": 2 * steps, "clocks": clk.summary()}))
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         return reference_arm(a)
+    if a.mode == "attn":
+        return attn_bench(a)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
