@@ -167,31 +167,30 @@ __global__ void __launch_bounds__(AT) attn_split_kernel(AttnParams P) {
   }
 }
 
+// Merge of the splits: one CTA per (row, kv head, query row), one thread per
+// head-dim element (blockDim.x = D).
 template <typename T>
-__global__ void __launch_bounds__(AT) attn_combine_kernel(AttnParams P) {
-  const int bh = blockIdx.x;
+__global__ void attn_combine_kernel(AttnParams P) {
+  const int r = blockIdx.x % P.R, bh = blockIdx.x / P.R;
   const int h = bh % P.Hkv, b = bh / P.Hkv;
-  const int D = P.D, R = P.R;
-  for (int i = threadIdx.x; i < R * D; i += AT) {
-    const int r = i / D, d = i % D;
-    const int64_t base = ((int64_t)b * P.Hkv + h) * P.nsplit * R;
-    float m = -INFINITY;
-    for (int s = 0; s < P.nsplit; ++s) m = fmaxf(m, P.part_ml[(base + (int64_t)s * R + r) * 2]);
-    float l = 0.f, a = 0.f;
-    if (m != -INFINITY) {
-      for (int s = 0; s < P.nsplit; ++s) {
-        const int64_t o = base + (int64_t)s * R + r;
-        const float ms = P.part_ml[o * 2];
-        if (ms == -INFINITY) continue;
-        const float w = __expf(ms - m);
-        l += w * P.part_ml[o * 2 + 1];
-        a += w * P.part_acc[o * D + d];
-      }
+  const int d = threadIdx.x;
+  const int64_t base = ((int64_t)b * P.Hkv + h) * P.nsplit * P.R + r;
+  float m = -INFINITY;
+  for (int sp = 0; sp < P.nsplit; ++sp) m = fmaxf(m, P.part_ml[(base + (int64_t)sp * P.R) * 2]);
+  float l = 0.f, a = 0.f;
+  if (m != -INFINITY) {
+    for (int sp = 0; sp < P.nsplit; ++sp) {
+      const int64_t o = base + (int64_t)sp * P.R;
+      const float ms = P.part_ml[o * 2];
+      if (ms == -INFINITY) continue;
+      const float w = __expf(ms - m);
+      l += w * P.part_ml[o * 2 + 1];
+      a += w * P.part_acc[o * P.D + d];
     }
-    const int j = r / P.group, hq = h * P.group + r % P.group;
-    const float y = l > 0.f ? a / l : 0.f;
-    reinterpret_cast<T*>(P.out)[b * P.obs + j * P.oqs + hq * P.ohs + d] = from_f<T>(y);
   }
+  const int j = r / P.group, hq = h * P.group + r % P.group;
+  const float y = l > 0.f ? a / l : 0.f;
+  reinterpret_cast<T*>(P.out)[b * P.obs + j * P.oqs + hq * P.ohs + d] = from_f<T>(y);
 }
 
 // ---------------------------------------------------------------------------
@@ -274,7 +273,7 @@ __device__ __forceinline__ float ex2f(float x) {
 }
 
 template <int NT>
-__global__ void __launch_bounds__(MT_THREADS) attn_mma_kernel(AttnParams P) {
+__global__ void __launch_bounds__(MT_THREADS, NT <= 3 ? 3 : 2) attn_mma_kernel(AttnParams P) {
   extern __shared__ __align__(128) unsigned char mma_smem[];
   MmaSmem& S = *reinterpret_cast<MmaSmem*>(mma_smem);
   const int split = blockIdx.x % P.nsplit;
@@ -324,13 +323,7 @@ __global__ void __launch_bounds__(MT_THREADS) attn_mma_kernel(AttnParams P) {
     *reinterpret_cast<uint4*>(reinterpret_cast<char*>(S.q) + sw_off(r, c)) = v;
   }
   __syncthreads();
-  uint32_t qf[8][NT][2];
-#pragma unroll
-  for (int ks = 0; ks < 8; ++ks)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-      ldm_x2(smem_addr(S.q) + sw_off(8 * nt + (lane & 7), 2 * ks + ((lane >> 3) & 1)),
-             qf[ks][nt][0], qf[ks][nt][1]);
+  const uint32_t qbase = smem_addr(S.q);
   // this thread's query-row columns r = 8 nt + 2 (lane % 4) + e
   float mrow[NT][2], lrow[NT][2];
   int lim[NT][2];
@@ -368,7 +361,11 @@ __global__ void __launch_bounds__(MT_THREADS) attn_mma_kernel(AttnParams P) {
       uint32_t a0, a1, a2, a3;
       ldm_x4(kbase + sw_off(krow0 + (lane & 15), 2 * ks + (lane >> 4)), a0, a1, a2, a3);
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) mma16816(sc[nt], a0, a1, a2, a3, qf[ks][nt][0], qf[ks][nt][1]);
+      for (int nt = 0; nt < NT; ++nt) {
+        uint32_t q0, q1;                               // Q fragments, re-read from shared memory
+        ldm_x2(qbase + sw_off(8 * nt + (lane & 7), 2 * ks + ((lane >> 3) & 1)), q0, q1);
+        mma16816(sc[nt], a0, a1, a2, a3, q0, q1);
+      }
     }
     // online softmax per query row (base 2), over the warp's keys
     const int kg = s0 + tile * MT_KEYS + krow0 + (lane >> 2);
@@ -391,10 +388,12 @@ __global__ void __launch_bounds__(MT_THREADS) attn_mma_kernel(AttnParams P) {
         const float pbv = sb == -INFINITY ? 0.f : ex2f(sb - mnew);
         lrow[nt][e] = lrow[nt][e] * alpha + pa + pbv;
         mrow[nt][e] = mnew;
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {   // the running max moved somewhere
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          o[mt][nt][e] *= alpha;
-          o[mt][nt][2 + e] *= alpha;
+          for (int mt = 0; mt < 8; ++mt) {
+            o[mt][nt][e] *= alpha;
+            o[mt][nt][2 + e] *= alpha;
+          }
         }
         sc[nt][e] = pa;
         sc[nt][2 + e] = pbv;
@@ -534,7 +533,7 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
         attn_mma_kernel<4><<<g, MT_THREADS, sm, st>>>(P);
         break;
     }
-    attn_combine_kernel<__nv_bfloat16><<<B * Hkv, AT, 0, st>>>(P);
+    attn_combine_kernel<__nv_bfloat16><<<B * Hkv * P.R, D, 0, st>>>(P);
     return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
   }
   const unsigned grid = (unsigned)(B * Hkv * P.nrc * P.nsplit);
@@ -543,13 +542,13 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
     cudaFuncSetAttribute(attn_split_kernel<__nv_bfloat16>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     attn_split_kernel<__nv_bfloat16><<<grid, AT, sm, st>>>(P);
-    attn_combine_kernel<__nv_bfloat16><<<B * Hkv, AT, 0, st>>>(P);
+    attn_combine_kernel<__nv_bfloat16><<<B * Hkv * P.R, D, 0, st>>>(P);
   } else {
     const size_t sm = sizeof(AttnSmem<float>);
     cudaFuncSetAttribute(attn_split_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)sm);
     attn_split_kernel<float><<<grid, AT, sm, st>>>(P);
-    attn_combine_kernel<float><<<B * Hkv, AT, 0, st>>>(P);
+    attn_combine_kernel<float><<<B * Hkv * P.R, D, 0, st>>>(P);
   }
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
 }

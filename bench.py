@@ -46,6 +46,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="sample", choices=["sample", "greedy", "attn"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attn-rows", type=int, default=64, help="--mode attn: rows (config 3: 64)")
     return ap.parse_args()
 
 
@@ -226,7 +227,7 @@ def attn_bench(a):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    B, Hq, Hkv, D, ql = 64, 32, 8, 128, 5
+    B, Hq, Hkv, D, ql = a.attn_rows, 32, 8, 128, 5
     lens = W.attn_lengths(B, seed=0)
     C = int(lens.max()) + ql + 3
     g = torch.Generator(device=dev).manual_seed(0)
@@ -261,7 +262,8 @@ def attn_bench(a):
                   "len U[512,8192])", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": steps,
         "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q / k / v)",
-        "config": {"workload": "config 3 verify attention, one layer", "rows": B, "Hq": Hq,
+        "config": {"workload": "config 3 verify attention, one layer" + ("" if B == 64 else
+                   f" ({B} rows)"), "rows": B, "Hq": Hq,
                    "Hkv": Hkv, "head_dim": D, "queries": ql, "live_keys": live,
                    "l2": "one layer reads >1 GB of K/V (> 126 MB L2)"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
