@@ -17,6 +17,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "specdec_b200.h"
 
 namespace sd {
@@ -47,6 +49,11 @@ struct AttnParams {
   void* out; int64_t obs, oqs, ohs;
   float* part_acc;   // [B, Hkv, nsplit, R, D]
   float* part_ml;    // [B, Hkv, nsplit, R, 2]
+  int* split_done;   // [B, Hkv] pieces finished (tensor-core path; zeroed per call)
+  int* rowpre;       // [B + 1] exclusive prefix of 64-key tiles per row (tensor-core path)
+  int* rowkmax;      // [B] live-key bound of each row (tensor-core path)
+  int npiece;        // partial slots per (row, kv head) on the tensor-core path
+  int out_vec4;      // out is 8-byte aligned and its strides are multiples of 4 elements
 };
 
 __device__ __forceinline__ int row_limit(const AttnParams& P, int b, int j) {
@@ -202,9 +209,14 @@ __global__ void attn_combine_kernel(AttnParams P) {
 // softmax per query row in base 2, and O^T += V^T P^T with P^T moved into the
 // B-operand layout by a register transpose.  K / V tiles are double-buffered
 // in shared memory by cp.async with a 16-byte-chunk XOR swizzle (conflict-free
-// ldmatrix).  The four warps' (max, sum, O) merge in shared memory and the
-// split's partial goes to the same workspace layout as the CUDA-core path.
+// ldmatrix).  The four warps' (max, sum, O) merge in shared memory.  A row
+// whose live keys fit one split writes its output directly; otherwise each
+// split leaves a partial (max, sum, O) in the workspace and the split that
+// finishes last for its (row, kv head), found by an atomic counter, merges
+// them while they are still in L2 — no separate combine launch.
 constexpr int MT_KEYS = 64;              // keys per tile (16 per warp)
+constexpr int MT_MIN_SHARE = SPLIT_KEYS / MT_KEYS;  // fewest tiles per CTA
+constexpr float MT_HEADROOM = 8.f;       // lazy-rescale headroom of the running max (base 2)
 constexpr int MT_THREADS = 128;
 constexpr int MT_D = 128;
 
@@ -218,6 +230,8 @@ struct MmaSmem {
   } u;
   __nv_bfloat16 q[32 * MT_D];
   float ms[4][32], ls[4][32];
+  int last;                              // this CTA finished its (row, kv head) last
+  int seg_b;                             // row of the CTA's first tile
 };
 
 // byte offset of 16-byte chunk c of row r in a swizzled [rows][128] bf16 tile
@@ -272,199 +286,389 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
-template <int NT>
-__global__ void __launch_bounds__(MT_THREADS, NT <= 3 ? 3 : 2) attn_mma_kernel(AttnParams P) {
-  extern __shared__ __align__(128) unsigned char mma_smem[];
-  MmaSmem& S = *reinterpret_cast<MmaSmem*>(mma_smem);
-  const int split = blockIdx.x % P.nsplit;
-  const int bh = blockIdx.x / P.nsplit;
-  const int h = bh % P.Hkv, b = bh / P.Hkv;
-  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+// Merge the partials (max, sum, O) of a (row, kv head)'s pieces into the
+// output: one warp per query row; lanes own pieces for (max, sum), then four
+// head-dim elements each for O (float4), eight pieces' loads in flight.
+__device__ __noinline__ void merge_pieces(const AttnParams& P, int b, int h, int np, int w,
+                                          int lane, __nv_bfloat16* out) {
   const int R = P.R;
-  int kmax = 0;
-  for (int j = 0; j < P.qlen; ++j) kmax = max(kmax, row_limit(P, b, j));
-  const int s0 = split * SPLIT_KEYS, s1 = min(kmax, s0 + SPLIT_KEYS);
-  const int64_t pbase = (((int64_t)b * P.Hkv + h) * P.nsplit + split) * R;
-  if (s0 >= s1) {                                      // nothing live in this split
-    for (int r = t; r < R; r += MT_THREADS) {
-      P.part_ml[(pbase + r) * 2] = -INFINITY;
-      P.part_ml[(pbase + r) * 2 + 1] = 0.f;
-    }
-    return;
-  }
-  const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(P.k) +
-                            ((int64_t)b * P.Hkv + h) * P.C * MT_D;
-  const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(P.v) +
-                            ((int64_t)b * P.Hkv + h) * P.C * MT_D;
-  auto load_tile = [&](int tile, int buf) {
-    const int key0 = s0 + tile * MT_KEYS;
-    const uint32_t kd = smem_addr(S.u.kv.k[buf]), vd = smem_addr(S.u.kv.v[buf]);
-    for (int i = t; i < MT_KEYS * 16; i += MT_THREADS) {
-      const int kk = i >> 4, c = i & 15;
-      const bool in = key0 + kk < s1;
-      const int64_t row = in ? key0 + kk : s0;         // a valid address when nothing is read
-      cp_async16(kd + sw_off(kk, c), kb + row * MT_D + 8 * c, in);
-      cp_async16(vd + sw_off(kk, c), vb + row * MT_D + 8 * c, in);
-    }
-    cp_async_commit();
-  };
-  const int ntiles = (s1 - s0 + MT_KEYS - 1) / MT_KEYS;
-  load_tile(0, 0);
-  if (ntiles > 1) load_tile(1, 1);
-  // the kv head's query rows r = j * group + g (zero rows up to 8 * NT)
-  const __nv_bfloat16* Q = reinterpret_cast<const __nv_bfloat16*>(P.q);
-  for (int i = t; i < 32 * 16; i += MT_THREADS) {
-    const int r = i >> 4, c = i & 15;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (r < R) {
-      const int j = r / P.group, hq = h * P.group + r % P.group;
-      v = *reinterpret_cast<const uint4*>(Q + b * P.qbs + hq * P.qhs + j * P.qqs + 8 * c);
-    }
-    *reinterpret_cast<uint4*>(reinterpret_cast<char*>(S.q) + sw_off(r, c)) = v;
-  }
-  __syncthreads();
-  const uint32_t qbase = smem_addr(S.q);
-  // this thread's query-row columns r = 8 nt + 2 (lane % 4) + e
-  float mrow[NT][2], lrow[NT][2];
-  int lim[NT][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int r = 8 * nt + 2 * (lane & 3) + e;
-      mrow[nt][e] = -INFINITY;
-      lrow[nt][e] = 0.f;
-      lim[nt][e] = r < R ? row_limit(P, b, r / P.group) : 0;
-    }
-  float o[8][NT][4];
-#pragma unroll
-  for (int mt = 0; mt < 8; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.f;
-  const float sl2 = P.scale * 1.4426950408889634f;
-  const int krow0 = 16 * w;                            // this warp's keys within a tile
-  for (int tile = 0; tile < ntiles; ++tile) {
-    const int buf = tile & 1;
-    if (tile + 1 < ntiles) cp_async_wait<1>(); else cp_async_wait<0>();
-    __syncthreads();
-    const uint32_t kbase = smem_addr(S.u.kv.k[buf]), vbase = smem_addr(S.u.kv.v[buf]);
-    // S^T = K Q^T for the warp's 16 keys
-    float sc[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sc[nt][e] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      uint32_t a0, a1, a2, a3;
-      ldm_x4(kbase + sw_off(krow0 + (lane & 15), 2 * ks + (lane >> 4)), a0, a1, a2, a3);
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        uint32_t q0, q1;                               // Q fragments, re-read from shared memory
-        ldm_x2(qbase + sw_off(8 * nt + (lane & 7), 2 * ks + ((lane >> 3) & 1)), q0, q1);
-        mma16816(sc[nt], a0, a1, a2, a3, q0, q1);
+  const int64_t base0 = ((int64_t)b * P.Hkv + h) * P.npiece * R;
+  for (int r = w; r < R; r += MT_THREADS / 32) {
+    float mx = -INFINITY, ll = 0.f, ms0 = -INFINITY;
+    for (int c0 = 0; c0 < np; c0 += 32) {              // per lane, online over its pieces
+      const int sp = c0 + lane;
+      if (sp < np) {
+        const float ms = __ldcg(&P.part_ml[(base0 + (int64_t)sp * R + r) * 2]);
+        const float lv = __ldcg(&P.part_ml[(base0 + (int64_t)sp * R + r) * 2 + 1]);
+        if (c0 == 0) ms0 = ms;
+        if (ms != -INFINITY) {
+          const float mn = fmaxf(mx, ms);
+          ll = (mx == -INFINITY ? 0.f : ll * __expf(mx - mn)) + lv * __expf(ms - mn);
+          mx = mn;
+        }
       }
     }
-    // online softmax per query row (base 2), over the warp's keys
-    const int kg = s0 + tile * MT_KEYS + krow0 + (lane >> 2);
-    uint32_t pb[NT][2];
+    float gm = mx;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int o = 16; o; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+    float L = mx == -INFINITY ? 0.f : ll * __expf(mx - gm);
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int le = min(lim[nt][e], s1);
-        const float sa = kg < le ? sc[nt][e] * sl2 : -INFINITY;
-        const float sb = kg + 8 < le ? sc[nt][2 + e] * sl2 : -INFINITY;
-        float mx = fmaxf(sa, sb);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float mold = mrow[nt][e];
-        const float mnew = fmaxf(mold, mx);
-        const float alpha = mnew == -INFINITY ? 1.f : (mold == -INFINITY ? 0.f : ex2f(mold - mnew));
-        const float pa = sa == -INFINITY ? 0.f : ex2f(sa - mnew);
-        const float pbv = sb == -INFINITY ? 0.f : ex2f(sb - mnew);
-        lrow[nt][e] = lrow[nt][e] * alpha + pa + pbv;
-        mrow[nt][e] = mnew;
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {   // the running max moved somewhere
+    for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (L > 0.f) {
+      for (int c0 = 0; c0 < np; c0 += 32) {
+        const int sp = c0 + lane;
+        float ms = ms0;
+        if (c0 > 0) ms = sp < np ? __ldcg(&P.part_ml[(base0 + (int64_t)sp * R + r) * 2]) : -INFINITY;
+        const float f = (sp < np && ms != -INFINITY) ? __expf(ms - gm) : 0.f;
+        const int n = min(32, np - c0);
+        for (int i0 = 0; i0 < n; i0 += 8) {
+          float4 v[8];
 #pragma unroll
-          for (int mt = 0; mt < 8; ++mt) {
-            o[mt][nt][e] *= alpha;
-            o[mt][nt][2 + e] *= alpha;
+          for (int u = 0; u < 8; ++u)
+            v[u] = i0 + u < n ? __ldcg(reinterpret_cast<const float4*>(
+                                    P.part_acc + (base0 + (int64_t)(c0 + i0 + u) * R + r) * MT_D) +
+                                lane)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float fu = __shfl_sync(0xffffffffu, f, (i0 + u) & 31);
+            a.x += fu * v[u].x; a.y += fu * v[u].y; a.z += fu * v[u].z; a.w += fu * v[u].w;
           }
         }
-        sc[nt][e] = pa;
-        sc[nt][2 + e] = pbv;
       }
-      // P^T (keys x rows) into the B-operand layout
-      pb[nt][0] = movm_t(pack_bf16(sc[nt][0], sc[nt][1]));
-      pb[nt][1] = movm_t(pack_bf16(sc[nt][2], sc[nt][3]));
     }
-    // O^T += V^T P^T over the head dimension (8 m-tiles of 16)
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      uint32_t a0, a1, a2, a3;
-      ldm_x4_t(vbase + sw_off(krow0 + (lane & 7) + ((lane >> 4) << 3), 2 * mt + ((lane >> 3) & 1)),
-               a0, a1, a2, a3);
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) mma16816(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+    const float il = L > 0.f ? 1.f / L : 0.f;
+    const int j = r / P.group, hq = h * P.group + r % P.group;
+    const __nv_bfloat162 y0 = __floats2bfloat162_rn(a.x * il, a.y * il);
+    const __nv_bfloat162 y1 = __floats2bfloat162_rn(a.z * il, a.w * il);
+    __nv_bfloat16* dst = out + b * P.obs + j * P.oqs + hq * P.ohs + 4 * lane;
+    if (P.out_vec4) {
+      uint2 pk;
+      pk.x = *reinterpret_cast<const uint32_t*>(&y0);
+      pk.y = *reinterpret_cast<const uint32_t*>(&y1);
+      *reinterpret_cast<uint2*>(dst) = pk;
+    } else {
+      dst[0] = y0.x; dst[1] = y0.y; dst[2] = y1.x; dst[3] = y1.y;
     }
-    __syncthreads();                                   // the buffer is refilled next
-    if (tile + 2 < ntiles) load_tile(tile + 2, buf);
   }
-  // row sums over the lanes that share a column; merge the four warps
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float l = lrow[nt][e];
-      l += __shfl_xor_sync(0xffffffffu, l, 4);
-      l += __shfl_xor_sync(0xffffffffu, l, 8);
-      l += __shfl_xor_sync(0xffffffffu, l, 16);
-      lrow[nt][e] = l;
+}
+
+// One CTA for the whole call: per row b the live-key bound kmax_b (the
+// largest limit over its queries), the exclusive prefix of its 64-key tile
+// counts (rowpre[B] = tiles per kv head summed over rows), the split counters
+// zeroed, and a zero output for rows without a live key.
+__global__ void __launch_bounds__(1024) attn_plan_kernel(AttnParams P) {
+  __shared__ int wsum[32];
+  __shared__ int carry;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  if (t == 0) carry = 0;
+  for (int i = t; i < P.B * P.Hkv; i += 1024) P.split_done[i] = 0;
+  __syncthreads();
+  for (int b0 = 0; b0 < P.B; b0 += 1024) {
+    const int b = b0 + t;
+    int km = 0;
+    if (b < P.B) {
+      for (int j = 0; j < P.qlen; ++j) km = max(km, row_limit(P, b, j));
+      P.rowkmax[b] = km;
     }
-  __syncthreads();                                     // K / V buffers become the merge area
+    const int tiles = (km + MT_KEYS - 1) / MT_KEYS;
+    int x = tiles;                                     // inclusive scan within the warp
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int s = wsum[lane];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int r = 8 * nt + 2 * (lane & 3) + e;
-      if (lane < 4) { S.ms[w][r] = mrow[nt][e]; S.ls[w][r] = lrow[nt][e]; }
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += y;
+      }
+      wsum[lane] = s;
+    }
+    __syncthreads();
+    const int excl = carry + (w ? wsum[w - 1] : 0) + x - tiles;
+    if (b < P.B) P.rowpre[b] = excl;
+    __syncthreads();
+    if (t == 1023) carry = excl + tiles;
+    __syncthreads();
+  }
+  if (t == 0) P.rowpre[P.B] = carry;
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.out);
+  for (int b = 0; b < P.B; ++b) {
+    if (P.rowkmax[b] != 0) continue;
+    for (int idx = t; idx < P.Hq * P.qlen * MT_D; idx += 1024) {
+      const int d = idx % MT_D, jh = idx / MT_D, j = jh % P.qlen, hq = jh / P.qlen;
+      out[b * P.obs + j * P.oqs + hq * P.ohs + d] = __float2bfloat16(0.f);
+    }
+  }
+}
+
+// Persistent, stream-K style: the 64-key tiles of every (row, kv head) are laid
+// end to end (row-major, kv head inner) and each CTA takes one contiguous run
+// of `share` tiles, so every CTA streams the same number of K/V bytes whatever
+// the row lengths.  A run crosses (row, kv head) boundaries as segments; a
+// (row, kv head) covered by one CTA writes its output directly, otherwise
+// each piece leaves a partial and the piece that finishes last merges them.
+template <int NT>
+__global__ void __launch_bounds__(MT_THREADS, NT <= 3 ? 3 : 2)
+attn_mma_kernel(const __grid_constant__ AttnParams P) {
+  extern __shared__ __align__(128) unsigned char mma_smem[];
+  MmaSmem& S = *reinterpret_cast<MmaSmem*>(mma_smem);
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int R = P.R, Hkv = P.Hkv;
+  const int total = P.rowpre[P.B] * Hkv;
+  const int share = max(MT_MIN_SHARE, (total + (int)gridDim.x - 1) / (int)gridDim.x);
+  const int t0 = (int)blockIdx.x * share;
+  if (t0 >= total) return;
+  const int t1 = min(total, t0 + share);
+  for (int b = t; b < P.B; b += MT_THREADS)            // the row holding tile t0
+    if (P.rowpre[b] * Hkv <= t0 && t0 < P.rowpre[b + 1] * Hkv) S.seg_b = b;
+  __syncthreads();
+  int b = S.seg_b;
+  int tb = P.rowpre[b + 1] - P.rowpre[b];              // tiles per kv head in row b
+  int h = (t0 - P.rowpre[b] * Hkv) / tb;
+  int off = (t0 - P.rowpre[b] * Hkv) % tb;
+  int tt = t0;
+  const __nv_bfloat16* Q = reinterpret_cast<const __nv_bfloat16*>(P.q);
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.out);
+  const float sl2 = P.scale * 1.4426950408889634f;
+  const int krow0 = 16 * w;                            // this warp's keys within a tile
+  while (true) {
+    const int nseg = min(tb - off, t1 - tt);           // tiles of this segment
+    const int s0 = off * MT_KEYS, s1 = min(P.rowkmax[b], (off + nseg) * MT_KEYS);
+    const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(P.k) +
+                              ((int64_t)b * Hkv + h) * P.C * MT_D;
+    const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(P.v) +
+                              ((int64_t)b * Hkv + h) * P.C * MT_D;
+    auto load_tile = [&](int tile, int buf) {
+      const int key0 = s0 + tile * MT_KEYS;
+      const uint32_t kd = smem_addr(S.u.kv.k[buf]), vd = smem_addr(S.u.kv.v[buf]);
+      for (int i = t; i < MT_KEYS * 16; i += MT_THREADS) {
+        const int kk = i >> 4, c = i & 15;
+        const bool in = key0 + kk < s1;
+        const int64_t row = in ? key0 + kk : s0;       // a valid address when nothing is read
+        cp_async16(kd + sw_off(kk, c), kb + row * MT_D + 8 * c, in);
+        cp_async16(vd + sw_off(kk, c), vb + row * MT_D + 8 * c, in);
+      }
+      cp_async_commit();
+    };
+    load_tile(0, 0);
+    if (nseg > 1) load_tile(1, 1);
+    // the kv head's query rows r = j * group + g (zero rows up to 8 * NT)
+    for (int i = t; i < 32 * 16; i += MT_THREADS) {
+      const int r = i >> 4, c = i & 15;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < R) {
+        const int j = r / P.group, hq = h * P.group + r % P.group;
+        v = *reinterpret_cast<const uint4*>(Q + b * P.qbs + hq * P.qhs + j * P.qqs + 8 * c);
+      }
+      *reinterpret_cast<uint4*>(reinterpret_cast<char*>(S.q) + sw_off(r, c)) = v;
+    }
+    __syncthreads();
+    const uint32_t qbase = smem_addr(S.q);
+    // this thread's query-row columns r = 8 nt + 2 (lane % 4) + e
+    float mrow[NT][2], lrow[NT][2];
+    int lim[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int r = 8 * nt + 2 * (lane & 3) + e;
+        mrow[nt][e] = -INFINITY;
+        lrow[nt][e] = 0.f;
+        lim[nt][e] = r < R ? min(row_limit(P, b, r / P.group), s1) : 0;
+      }
+    float o[8][NT][4];
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.f;
+    for (int tile = 0; tile < nseg; ++tile) {
+      const int buf = tile & 1;
+      if (tile + 1 < nseg) cp_async_wait<1>(); else cp_async_wait<0>();
+      __syncthreads();
+      const uint32_t kbase = smem_addr(S.u.kv.k[buf]), vbase = smem_addr(S.u.kv.v[buf]);
+      // S^T = K Q^T for the warp's 16 keys
+      float sc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[nt][e] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a0, a1, a2, a3;
+        ldm_x4(kbase + sw_off(krow0 + (lane & 15), 2 * ks + (lane >> 4)), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          uint32_t q0, q1;                             // Q fragments, re-read from shared memory
+          ldm_x2(qbase + sw_off(8 * nt + (lane & 7), 2 * ks + ((lane >> 3) & 1)), q0, q1);
+          mma16816(sc[nt], a0, a1, a2, a3, q0, q1);
+        }
+      }
+      // online softmax per query row (base 2), over the warp's keys
+      const int kg = s0 + tile * MT_KEYS + krow0 + (lane >> 2);
+      uint32_t pb[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int le = lim[nt][e];
+          const float sa = kg < le ? sc[nt][e] * sl2 : -INFINITY;
+          const float sb = kg + 8 < le ? sc[nt][2 + e] * sl2 : -INFINITY;
+          // lazy rescale: the reference max m of a query row moves only when a
+          // score exceeds it by more than MT_HEADROOM (base 2), so the common
+          // tile needs no cross-lane max; p = 2^(s - m) stays below 2^MT_HEADROOM
+          float mx = fmaxf(sa, sb);
+          if (__any_sync(0xffffffffu, mx > mrow[nt][e] + MT_HEADROOM)) {
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mold = mrow[nt][e];
+            const float mnew = fmaxf(mold, mx);
+            const float alpha =
+                mnew == -INFINITY ? 1.f : (mold == -INFINITY ? 0.f : ex2f(mold - mnew));
+            lrow[nt][e] *= alpha;
+            mrow[nt][e] = mnew;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+              o[mt][nt][e] *= alpha;
+              o[mt][nt][2 + e] *= alpha;
+            }
+          }
+          const float pa = sa == -INFINITY ? 0.f : ex2f(sa - mrow[nt][e]);
+          const float pbv = sb == -INFINITY ? 0.f : ex2f(sb - mrow[nt][e]);
+          lrow[nt][e] += pa + pbv;
+          sc[nt][e] = pa;
+          sc[nt][2 + e] = pbv;
+        }
+        // P^T (keys x rows) into the B-operand layout
+        pb[nt][0] = movm_t(pack_bf16(sc[nt][0], sc[nt][1]));
+        pb[nt][1] = movm_t(pack_bf16(sc[nt][2], sc[nt][3]));
+      }
+      // O^T += V^T P^T over the head dimension (8 m-tiles of 16)
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
-        S.u.o[w][r][16 * mt + (lane >> 2)] = o[mt][nt][e];
-        S.u.o[w][r][16 * mt + (lane >> 2) + 8] = o[mt][nt][2 + e];
+        uint32_t a0, a1, a2, a3;
+        ldm_x4_t(vbase + sw_off(krow0 + (lane & 7) + ((lane >> 4) << 3), 2 * mt + ((lane >> 3) & 1)),
+                 a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+      }
+      __syncthreads();                                 // the buffer is refilled next
+      if (tile + 2 < nseg) load_tile(tile + 2, buf);
+    }
+    // row sums over the lanes that share a column; merge the four warps
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float l = lrow[nt][e];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        lrow[nt][e] = l;
+      }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int r = 8 * nt + 2 * (lane & 3) + e;
+        if (lane < 4) { S.ms[w][r] = mrow[nt][e]; S.ls[w][r] = lrow[nt][e]; }
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          S.u.o[w][r][16 * mt + (lane >> 2)] = o[mt][nt][e];
+          S.u.o[w][r][16 * mt + (lane >> 2) + 8] = o[mt][nt][2 + e];
+        }
+      }
+    __syncthreads();
+    const int bh = b * Hkv + h;
+    const int Tb = P.rowpre[b] * Hkv + h * tb;         // first tile of this (row, kv head)
+    const int cfirst = Tb / share;
+    const int npieces = (Tb + tb - 1) / share - cfirst + 1;
+    const int64_t pbase = ((int64_t)bh * P.npiece + ((int)blockIdx.x - cfirst)) * R;
+    for (int idx = t; idx < R * MT_D; idx += MT_THREADS) {
+      const int r = idx >> 7, d = idx & (MT_D - 1);
+      float m = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) m = fmaxf(m, S.ms[q][r]);
+      float acc = 0.f, l = 0.f;
+      if (m != -INFINITY) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (S.ms[q][r] == -INFINITY) continue;
+          const float f = ex2f(S.ms[q][r] - m);
+          acc += f * S.u.o[q][r][d];
+          l += f * S.ls[q][r];
+        }
+      }
+      if (npieces == 1) {                              // the only piece: final output
+        const int j = r / P.group, hq = h * P.group + r % P.group;
+        out[b * P.obs + j * P.oqs + hq * P.ohs + d] = __float2bfloat16(l > 0.f ? acc / l : 0.f);
+        continue;
+      }
+      P.part_acc[(pbase + r) * MT_D + d] = acc;
+      if (d == 0) {
+        P.part_ml[(pbase + r) * 2] = m == -INFINITY ? -INFINITY : m * 0.6931471805599453f;
+        P.part_ml[(pbase + r) * 2 + 1] = l;
       }
     }
-  __syncthreads();
-  for (int idx = t; idx < R * MT_D; idx += MT_THREADS) {
-    const int r = idx >> 7, d = idx & (MT_D - 1);
-    float m = -INFINITY;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) m = fmaxf(m, S.ms[q][r]);
-    float acc = 0.f, l = 0.f;
-    if (m != -INFINITY) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (S.ms[q][r] == -INFINITY) continue;
-        const float f = ex2f(S.ms[q][r] - m);
-        acc += f * S.u.o[q][r][d];
-        l += f * S.ls[q][r];
+    if (npieces > 1) {
+      __threadfence();
+      __syncthreads();
+      if (t == 0) S.last = atomicAdd(&P.split_done[bh], 1) == npieces - 1;
+      __syncthreads();
+      if (S.last) {
+        __threadfence();
+        merge_pieces(P, b, h, npieces, w, lane, out);
       }
     }
-    P.part_acc[(pbase + r) * MT_D + d] = acc;
-    if (d == 0) {
-      P.part_ml[(pbase + r) * 2] = m == -INFINITY ? -INFINITY : m * 0.6931471805599453f;
-      P.part_ml[(pbase + r) * 2 + 1] = l;
+    tt += nseg;
+    if (tt >= t1) break;
+    off = 0;
+    if (++h == Hkv) {
+      h = 0;
+      do { ++b; } while (P.rowpre[b + 1] == P.rowpre[b]);
+      tb = P.rowpre[b + 1] - P.rowpre[b];
     }
+    __syncthreads();                                   // merge area and Q are rewritten next
   }
 }
 
 static int nsplit_for(int C, int qlen) {
   const int maxkeys = C + qlen;
   return (maxkeys + SPLIT_KEYS - 1) / SPLIT_KEYS;
+}
+
+// Persistent grid of the tensor-core kernel: SMs x resident CTAs, looked up
+// once per device.
+template <int NT>
+static int launch_mma(const AttnParams& P, cudaStream_t st) {
+  static std::atomic<int> grid_of[SD_MAX_DEVICES];
+  const int sm = (int)sizeof(MmaSmem);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SD_ELAUNCH;
+  if (cudaFuncSetAttribute(attn_mma_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) !=
+      cudaSuccess)
+    return SD_ELAUNCH;
+  int g = dev < SD_MAX_DEVICES ? grid_of[dev].load() : 0;
+  if (g == 0) {
+    int nsm = 0, occ = 0;
+    if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, attn_mma_kernel<NT>, MT_THREADS, sm) !=
+            cudaSuccess)
+      return SD_ELAUNCH;
+    g = nsm * (occ > 0 ? occ : 1);
+    if (dev < SD_MAX_DEVICES) grid_of[dev].store(g);
+  }
+  attn_mma_kernel<NT><<<g, MT_THREADS, sm, st>>>(P);
+  return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
 }
 
 }  // namespace sd
@@ -476,8 +680,9 @@ extern "C" {
 size_t sd_verify_attn_workspace_bytes(int B, int Hq, int Hkv, int D, int C, int qlen) {
   if (B <= 0 || Hkv <= 0 || Hq % Hkv) return 0;
   const int R = qlen * (Hq / Hkv);
-  const size_t ns = (size_t)nsplit_for(C, qlen);
-  return (size_t)B * Hkv * ns * R * (D + 2) * sizeof(float) + 256;
+  const size_t np = (size_t)nsplit_for(C, qlen) + 1;   // pieces per (row, kv head), either path
+  return (size_t)B * Hkv * np * R * (D + 2) * sizeof(float) +
+         ((size_t)B * Hkv + 2 * (size_t)B + 1) * sizeof(int) + 256;
 }
 
 int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const void* kcache,
@@ -500,9 +705,15 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
   P.R = qlen * P.group; P.nsplit = nsplit_for(C, qlen); P.scale = scale;
   P.nrc = (P.R + RMAX - 1) / RMAX;
   P.out = out; P.obs = obs; P.oqs = oqs; P.ohs = ohs;
+  P.out_vec4 = (reinterpret_cast<uintptr_t>(out) & 7) == 0 && obs % 4 == 0 && oqs % 4 == 0 &&
+               ohs % 4 == 0;
   float* ws = reinterpret_cast<float*>(workspace);
   P.part_acc = ws;
-  P.part_ml = ws + (size_t)B * Hkv * P.nsplit * P.R * D;
+  P.npiece = P.nsplit + 1;
+  P.part_ml = ws + (size_t)B * Hkv * P.npiece * P.R * D;
+  P.split_done = reinterpret_cast<int*>(P.part_ml + (size_t)B * Hkv * P.npiece * P.R * 2);
+  P.rowpre = P.split_done + (size_t)B * Hkv;
+  P.rowkmax = P.rowpre + B + 1;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // tensor-core path: bf16, head_dim 128, <= 32 query rows per kv head,
   // 16-byte aligned rows
@@ -513,28 +724,13 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
                       (reinterpret_cast<uintptr_t>(vcache) & 15) == 0;
   if (mma_ok) {
     P.nrc = 1;
-    const unsigned g = (unsigned)(B * Hkv * P.nsplit);
-    const int sm = (int)sizeof(MmaSmem);
+    attn_plan_kernel<<<1, 1024, 0, st>>>(P);
     switch ((P.R + 7) / 8) {
-      case 1:
-        cudaFuncSetAttribute(attn_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-        attn_mma_kernel<1><<<g, MT_THREADS, sm, st>>>(P);
-        break;
-      case 2:
-        cudaFuncSetAttribute(attn_mma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-        attn_mma_kernel<2><<<g, MT_THREADS, sm, st>>>(P);
-        break;
-      case 3:
-        cudaFuncSetAttribute(attn_mma_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-        attn_mma_kernel<3><<<g, MT_THREADS, sm, st>>>(P);
-        break;
-      default:
-        cudaFuncSetAttribute(attn_mma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-        attn_mma_kernel<4><<<g, MT_THREADS, sm, st>>>(P);
-        break;
+      case 1: return launch_mma<1>(P, st);
+      case 2: return launch_mma<2>(P, st);
+      case 3: return launch_mma<3>(P, st);
+      default: return launch_mma<4>(P, st);
     }
-    attn_combine_kernel<__nv_bfloat16><<<B * Hkv * P.R, D, 0, st>>>(P);
-    return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
   }
   const unsigned grid = (unsigned)(B * Hkv * P.nrc * P.nsplit);
   if (dtype == SD_DTYPE_BF16) {

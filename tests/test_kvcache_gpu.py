@@ -125,6 +125,35 @@ def test_verify_attention_matches_reference_rule(dt, tol):
     assert torch.equal(out, out2)
 
 
+def test_verify_attention_tensor_core_splits_and_caps():
+    """bf16, head_dim 128 (the tensor-core path): rows with no live key, one
+    split, several splits and a 6-key last split; repeated calls reuse the
+    per-call split counters."""
+    g = torch.Generator(device=DEV).manual_seed(3)
+    B, Hq, Hkv, D, C, ql = 5, 32, 8, 128, 3000, 5
+    lens = torch.tensor([0, 1020, 2500, 7, 1500], device=DEV)
+    valid = torch.tensor([0, 1022, 3000, 3, 1030], device=DEV)
+    q = torch.randn(B, Hq, ql, D, generator=g, device=DEV).to(torch.bfloat16)
+    kc = torch.randn(B, Hkv, C, D, generator=g, device=DEV).to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, C, D, generator=g, device=DEV).to(torch.bfloat16)
+    ref = _ref_attention(q, kc, vc, lens, valid, D ** -0.5)
+    out = A.verify_attention(q, kc, vc, lens, valid=valid, scale=D ** -0.5)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
+    assert torch.count_nonzero(out[0]) == 0
+    for _ in range(3):
+        again = A.verify_attention(q, kc, vc, lens, valid=valid, scale=D ** -0.5)
+        assert torch.equal(again, out)
+    # NaN in every slot outside the live windows (never-written cache memory)
+    # must not reach the output
+    kc2, vc2 = kc.clone(), vc.clone()
+    for b in range(B):
+        n = min(int(lens[b]) + ql, int(valid[b]))
+        kc2[b, :, n:] = float("nan")
+        vc2[b, :, n:] = float("nan")
+    out2 = A.verify_attention(q, kc2, vc2, lens, valid=valid, scale=D ** -0.5)
+    assert torch.equal(out2, out)
+
+
 def test_prefill_valid_cap():
     g = torch.Generator(device=DEV).manual_seed(2)
     B, Hq, Hkv, D, C, ql = 3, 4, 2, 8, 16, 7
