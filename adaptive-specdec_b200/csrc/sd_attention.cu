@@ -7,12 +7,12 @@
 // Here each row reads only its own live keys: row b, query j attends to cache
 // slots [0, min(lengths[b] + j + 1, valid[b])).
 //
-// Work decomposition: one CTA per (row, kv head, key split).  The CTA holds the
-// R = qlen * (Hq / Hkv) query rows that share the kv head (grouped-query), so
-// every K/V element is read from HBM once per split.  Splits write partial
-// (max, sum, acc) to the workspace; a combine kernel merges them.  bf16 with
-// head_dim 128 runs on the tensor cores (attn_mma_kernel); other shapes and
-// fp32 on the CUDA cores (attn_split_kernel).
+// A CTA holds the R = qlen * (Hq / Hkv) query rows that share a kv head
+// (grouped-query), so every live K/V element is read from HBM once.  bf16 with
+// head_dim 128 runs on the tensor cores (attn_plan_kernel + the persistent
+// attn_mma_kernel, which merges its own partials); other shapes and fp32 run
+// on the CUDA cores (attn_split_kernel, one CTA per (row, kv head, key
+// split), then attn_combine_kernel).
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -360,16 +360,18 @@ __device__ __noinline__ void merge_pieces(const AttnParams& P, int b, int h, int
 // zeroed, and a zero output for rows without a live key.
 __global__ void __launch_bounds__(1024) attn_plan_kernel(AttnParams P) {
   __shared__ int wsum[32];
-  __shared__ int carry;
+  __shared__ int carry, nzero;
+  __shared__ int zrow[1024];                           // rows of this chunk without a live key
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   if (t == 0) carry = 0;
   for (int i = t; i < P.B * P.Hkv; i += 1024) P.split_done[i] = 0;
   __syncthreads();
   for (int b0 = 0; b0 < P.B; b0 += 1024) {
     const int b = b0 + t;
+    if (t == 0) nzero = 0;
     int km = 0;
     if (b < P.B) {
-      for (int j = 0; j < P.qlen; ++j) km = max(km, row_limit(P, b, j));
+      km = row_limit(P, b, P.qlen - 1);                // the limit grows with the query index
       P.rowkmax[b] = km;
     }
     const int tiles = (km + MT_KEYS - 1) / MT_KEYS;
@@ -392,20 +394,24 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(AttnParams P) {
     }
     __syncthreads();
     const int excl = carry + (w ? wsum[w - 1] : 0) + x - tiles;
-    if (b < P.B) P.rowpre[b] = excl;
+    if (b < P.B) {
+      P.rowpre[b] = excl;
+      if (km == 0) zrow[atomicAdd(&nzero, 1)] = b;
+    }
     __syncthreads();
     if (t == 1023) carry = excl + tiles;
+    // rows without a live key get a zero output (no CTA of the main kernel visits them)
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.out);
+    for (int z = 0; z < nzero; ++z) {
+      const int bz = zrow[z];
+      for (int idx = t; idx < P.Hq * P.qlen * MT_D; idx += 1024) {
+        const int d = idx % MT_D, jh = idx / MT_D, j = jh % P.qlen, hq = jh / P.qlen;
+        out[bz * P.obs + j * P.oqs + hq * P.ohs + d] = __float2bfloat16(0.f);
+      }
+    }
     __syncthreads();
   }
   if (t == 0) P.rowpre[P.B] = carry;
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.out);
-  for (int b = 0; b < P.B; ++b) {
-    if (P.rowkmax[b] != 0) continue;
-    for (int idx = t; idx < P.Hq * P.qlen * MT_D; idx += 1024) {
-      const int d = idx % MT_D, jh = idx / MT_D, j = jh % P.qlen, hq = jh / P.qlen;
-      out[b * P.obs + j * P.oqs + hq * P.ohs + d] = __float2bfloat16(0.f);
-    }
-  }
 }
 
 // Persistent, stream-K style: the 64-key tiles of every (row, kv head) are laid

@@ -6,24 +6,24 @@
 //
 // Design
 // ------
-// * bf16 / fp16 logits at any vocabulary size: one CTA per logits vector builds
-//   an EXACT count histogram over the 65,536 possible 16-bit values in shared
-//   memory (two 16-bit counters per 32-bit word, one shared-memory atomic per
-//   element).  Every element of a bin has the same logit, hence the same
-//   probability, so the softmax normaliser, the top-k threshold and the top-p
-//   nucleus (including how many members of the boundary tie class are kept)
-//   are computed per distinct value, with float64 sums, and never need a sort.
-//   Tie order inside the boundary class is ascending vocabulary index; the
-//   index of the last kept member (idx_cut) is found by one ordered scan.
+// * bf16 / fp16 logits at any vocabulary size (the verify round's case): a
+//   persistent stats kernel reads every logits element exactly once and
+//   produces, per vector, the softmax normaliser, the top-k / top-p kept set
+//   and the probe probability, without sorting the vocabulary (see the stats
+//   kernel section below).  An exact 65,536-bin count histogram of the
+//   vector's 16-bit values backs it up for the rare vectors the list cannot
+//   decide.  The CTA that finishes a row's last vector performs that row's
+//   accept test and its residual / bonus draw.
 // * fp32 / any dtype with V <= SMALLV_MAX: one CTA per vector computes every
 //   probability, sorts (p desc, index asc) with a bitonic sort in shared memory
 //   and materialises the final probabilities in the workspace.
 // * greedy (T <= 0): only the target argmax is needed; the draft logits are
 //   never read.
-// * the finish kernel runs per (row, vocabulary chunk): it decides the accepted
-//   prefix from the per-vector probe probabilities p_i(x_i), q_i(x_i), sums the
-//   residual (or bonus) mass of its chunk, and the last chunk of a row to
-//   finish performs the inverse-CDF draw.  No CTA ever waits on another.
+// * the finish kernel (small-V, fp32 and histogram paths) runs per (row,
+//   vocabulary chunk): it decides the accepted prefix from the per-vector
+//   probe probabilities p_i(x_i), q_i(x_i), sums the residual (or bonus) mass
+//   of its chunk, and the last chunk of a row to finish performs the
+//   inverse-CDF draw.  No CTA ever waits on another CTA.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -93,25 +93,28 @@ __device__ __forceinline__ int64_t vec_probe(const VecSet& vs, int set, int row,
 // stats kernel (bf16 / fp16): persistent, one CTA per SM, three warp roles
 // ---------------------------------------------------------------------------
 // Warp 0 (producer) streams each vector's 16-byte-aligned body into a ring of
-// NSLOT shared-memory slots with cp.async.bulk.  Warps 1..NSW (streaming) read
-// every element once from the ring: each lane sums 2^(x c2 - Rc2) over the
-// elements below its list threshold (the running maximum minus W_LIST base-2
-// units) against a per-vector reference Rc2, and a lane holding elements at
-// or above the threshold leaves a record (lane, threshold, reference) for
-// the slot.  Before refilling a slot the producer turns that slot's records
-// into list entries (value, index) straight from the ring.  The FNW finalize
-// warps then take a finished vector (its list, the streaming warps' partial
-// sums, its maximum) while the next one streams: they sort the list by
-// (value desc, index asc) -- the order of the reference's sort with ties
-// broken by index -- and apply the reference's element-wise rules to it:
-// top-k (keep p >= k-th value), top-p (keep while fl32(cum - p) < top_p, cum
-// in float64), renormalisation.  The kept set is described by its last
-// element L in that order: j is kept iff value_j > value_L or (value_j ==
-// value_L and j <= index_L).  Every element at or above M - W_LIST is listed,
-// so the rules are exact when the boundary falls there; otherwise (boundary
-// deeper, list overflow, top-k beyond the list) the vector is recomputed
-// exactly from a 65,536-bin count histogram of all its elements read again
-// from global memory.  Two vectors are in flight per CTA (two list sets).
+// NSLOT shared-memory slots with cp.async.bulk (mbarrier completion, bounded
+// waits).  Warps 1..NSW (streaming) read every element once from the ring:
+// each lane sums 2^(x c2 - Rc2) over its elements below the list threshold
+// (the vector's running maximum minus W_LIST base-2 units) against a
+// per-vector reference Rc2, and lists the elements at or above it itself,
+// re-reading them from the slot: a list entry is (order key, vocabulary
+// index).  The NCW finalize warps take a finished vector (its list, the
+// streaming warps' partial sums, its maximum) while the next one streams.
+// They compute S exactly (the bulk mass plus expf over the listed elements,
+// float64), place the listed elements in coarse depth bins, sort only the
+// bins that can hold the top-k / top-p boundary by (value desc, index asc) --
+// the order of the reference's sort with ties broken by index -- and apply
+// the reference's element-wise rules there: top-k (keep p >= k-th value),
+// top-p (keep while fl32(cum - p) < top_p, cum in float64), renormalisation.
+// The kept set is described by its last element L in that order: j is kept
+// iff value_j > value_L or (value_j == value_L and j <= index_L).  Every
+// element at or above M - W_LIST is listed, so the rules are exact when the
+// boundary falls there; otherwise (boundary deeper, list overflow, top-k
+// beyond the list) the vector is recomputed exactly from a 65,536-bin count
+// histogram of all its elements read again from global memory
+// (VecStats.fb_why records why).  Two vectors are in flight per CTA (two
+// hand-over sets).
 //
 // The CTA that finishes the last vector of a row then performs that row's
 // accept test and its residual / bonus draw (finalize warps).  Outside the
