@@ -40,7 +40,29 @@ _SIGNATURES = {
     "sd_verify_attn": ([_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
                         _i32, _f32, _vp, _i64, _i64, _i64, _i32, _vp, _sz, _vp], _i32),
     "sd_verify_attn_workspace_bytes": ([_i32, _i32, _i32, _i32, _i32, _i32], _sz),
+    "sd_shard_workspace_bytes": ([_i32, _i32, _i32], _sz),
+    "sd_shard_send_bytes": ([_i32, _i32, _i32, _i32, _i32], _sz),
+    "sd_shard_phase": ([_vp, _i32, _vp, _vp, _vp], _i32),
 }
+
+SHARD_MAX_RANKS = 16          # SD_SHARD_MAX_RANKS
+SHARD_BOUNDARY_CAP = 128      # SD_SHARD_BOUNDARY_CAP
+SHARD_STATUS_FALLBACK = 2     # SD_SHARD_STATUS_FALLBACK
+
+
+class ShardArgs(ctypes.Structure):
+    """sd_shard_args (include/specdec_b200.h)."""
+    _fields_ = [("tgt", _vp), ("tgt_bs", _i64), ("tgt_ps", _i64),
+                ("drf", _vp), ("drf_bs", _i64), ("drf_ps", _i64),
+                ("dtype", _i32),
+                ("xs", _vp), ("xs_bs", _i64),
+                ("u_acc", _vp), ("u_bs", _i64),
+                ("u_res", _vp), ("alive", _vp),
+                ("B", _i32), ("k", _i32), ("V", _i32), ("rank", _i32), ("nranks", _i32),
+                ("v_start", _i32 * (SHARD_MAX_RANKS + 1)),
+                ("temperature", _f32), ("top_p", _f32), ("top_k", _i32),
+                ("n_acc", _vp), ("y", _vp),
+                ("workspace", _vp), ("workspace_bytes", _sz)]
 
 _lib = None
 _lock = threading.Lock()

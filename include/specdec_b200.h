@@ -188,6 +188,73 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs,
 
 size_t sd_verify_attn_workspace_bytes(int B, int Hq, int Hkv, int D, int C, int qlen);
 
+/*
+ * Vocabulary-sharded verify round: the SPMD form of sd_verify_sample for a
+ * vocab-parallel LM head.  Rank r holds columns [v_start[r], v_start[r+1]) of
+ * every target and draft logits vector; every rank ends with the n_acc and y
+ * that sd_verify_sample gives on the full vectors (same arithmetic, same
+ * exemptions).  The reference verifies on one device only; this replaces
+ * specdec/engine.py:282-303 when the logits arrive vocab-sharded.
+ *
+ * The round is a fixed sequence of local phases; between two phases the
+ * caller runs one collective over all ranks on the phase's send buffer
+ * (sd_shard_send_bytes) and passes the result as the next phase's recv:
+ *
+ *   temperature > 0:  P1 -> all_gather -> P2 -> all_reduce(sum, float64)
+ *                     -> P3 -> all_gather -> P4 -> all_gather
+ *                     -> P5 -> all_reduce(max, int64) -> P6
+ *   temperature <= 0: P1 -> all_reduce(max, int64) -> P6
+ *
+ * all_gather concatenates the ranks' buffers in rank order.  What crosses
+ * the ranks: P1 each shard's maximum and the draft tokens' logits; P2 the
+ * shard's softmax normaliser and a 128-bin depth histogram of its mass
+ * (16 base-2 units below the global maximum); P3 the shard's mass above the
+ * top-p boundary bins and its elements inside them (at most
+ * SD_SHARD_BOUNDARY_CAP per vector); P4 the shard's residual mass per row;
+ * P5 the drawn token from the shard that holds it.  Greedy needs only the
+ * per-shard argmax.  top_k must be 0 (SD_ENOTSUP otherwise).
+ *
+ * When the top-p boundary lies deeper than the histogram window or a shard
+ * holds more boundary elements than the cap, the round cannot be decided
+ * from these messages: P6 then sets SD_SHARD_STATUS_FALLBACK in the status
+ * word (the first 4 bytes of the workspace, identical on every rank) and
+ * the caller re-runs the round on gathered full vectors.
+ */
+#define SD_SHARD_MAX_RANKS 16
+#define SD_SHARD_BOUNDARY_CAP 128
+#define SD_SHARD_STATUS_FALLBACK 2
+typedef struct sd_shard_args {
+  const void* tgt;              /* [B, k+1, Vr] local slice, element strides (tgt_bs, tgt_ps, 1) */
+  int64_t tgt_bs, tgt_ps;
+  const void* drf;              /* [B, k, Vr] local slice (unused when temperature <= 0) */
+  int64_t drf_bs, drf_ps;
+  int dtype;                    /* SD_DTYPE_BF16 or SD_DTYPE_F16 */
+  const int64_t* xs;            /* [B, k] draft tokens, global vocabulary ids */
+  int64_t xs_bs;
+  const float* u_acc;           /* [B, k] */
+  int64_t u_bs;
+  const float* u_res;           /* [B] */
+  const uint8_t* alive;         /* [B] or NULL */
+  int B, k, V, rank, nranks;
+  int v_start[SD_SHARD_MAX_RANKS + 1];   /* v_start[0] = 0, v_start[nranks] = V */
+  float temperature, top_p;
+  int top_k;
+  int64_t* n_acc;               /* [B] out (written by P6) */
+  int64_t* y;                   /* [B] out (written by P6) */
+  void* workspace;
+  size_t workspace_bytes;
+} sd_shard_args;
+
+size_t sd_shard_workspace_bytes(int B, int k, int nranks);
+/* Bytes this rank contributes to the collective that follows phase `phase`
+ * (1..5); the collective's result is nranks times that for an all_gather and
+ * the same size for an all_reduce.  0 when no collective follows. */
+size_t sd_shard_send_bytes(int B, int k, int nranks, int greedy, int phase);
+/* Run local phase `phase` (1..6).  recv: the previous collective's result
+ * (NULL for P1); send: this phase's send buffer (NULL for P6). */
+int sd_shard_phase(const sd_shard_args* args, int phase, const void* recv, void* send,
+                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif
