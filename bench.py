@@ -44,7 +44,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="sample", choices=["sample", "greedy", "attn"])
+    ap.add_argument("--mode", default="sample",
+                    choices=["sample", "greedy", "attn", "vshard", "vshard-greedy"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-rows", type=int, default=64, help="--mode attn: rows (config 3: 64)")
     return ap.parse_args()
@@ -272,12 +273,113 @@ def attn_bench(a):
         "gpu_launches": 2 * steps, "clocks": clk.summary()}))
 
 
+def vshard_bench(a):
+    """--mode vshard / vshard-greedy: the vocabulary-sharded verify round.
+
+    Every rank holds V/N columns of the same config-2 batch (B=64, k=4) and
+    runs specdec.sharded.verify_sharded: the local phase kernels plus the
+    round's NCCL collectives (5 for sampling, 1 for greedy) and the host read
+    of the status word.  Total work is fixed as N grows (strong scaling);
+    value = rows verified per second by the whole job, device-timed with CUDA
+    events on the current stream, max over ranks.
+    """
+    import torch
+    import torch.distributed as dist
+    from specdec import sampling as S
+    from specdec import sharded as SH
+    from specdec import workloads as W
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from datetime import timedelta
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    greedy = a.mode == "vshard-greedy"
+    T, tp = (0.0, 1.0) if greedy else (T_SAMPLE, TOP_P)
+    vs = SH.even_split(VOCAB, world)
+    sl = slice(vs[rank], vs[rank + 1])
+    inputs = []
+    for i in range(NBUF):
+        tgt, drf = W.cfg2_logits(B, K_DRAFT, VOCAB, seed=i, device=dev)
+        xs, _ = S.draft_sample(drf.reshape(-1, VOCAB), torch.rand(
+            B * K_DRAFT, generator=torch.Generator(device=dev).manual_seed(i), device=dev), T, tp)
+        ua, ur = W.uniforms(B, K_DRAFT, seed=i, device=dev)
+        inputs.append((tgt[..., sl].contiguous(), drf[..., sl].contiguous(),
+                       xs.view(B, K_DRAFT), ua, ur))
+        del tgt, drf
+    comm = SH.ProcessGroupCollectives() if world > 1 else _SelfComm()
+    backend = SH.CudaShardBackend(dev)
+
+    def step(i):
+        t, d, xs, ua, ur = inputs[i % NBUF]
+        return SH.verify_sharded(t, None if greedy else d, xs, ua, ur, vs, comm, temperature=T,
+                                 top_p=tp, backend=backend)
+
+    for i in range(max(3, a.warmup)):
+        step(i)
+    torch.cuda.synchronize(dev)
+    steps = max(5, min(a.steps, 2000))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index or 0) as clk:
+        e0.record()
+        for i in range(steps):
+            step(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    per_rank = W.bytes_per_verify(B, K_DRAFT, vs[rank + 1] - vs[rank], greedy=greedy)
+    line = {
+        "metric": "vocab-sharded verify rows/s (B=64,k=4,V=151936 bf16, " +
+                  ("greedy)" if greedy else "T=0.7 top-p 0.9)"),
+        "value": B * steps / (ms / 1e3), "unit": "rows/s", "n_gpus": world, "steps": steps,
+        "warmup": a.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded config-2 logits, see specdec/workloads.py)",
+        "config": {"workload": "config 2 verify round, vocabulary sharded " +
+                               ("(greedy)" if greedy else "(T=0.7 top-p 0.9)"),
+                   "rows": B, "k": K_DRAFT, "vocab": VOCAB, "columns_per_gpu": vs[1] - vs[0],
+                   "parallelism": f"vocab-sharded x{world}, "
+                                  f"{1 if greedy else 5} collectives per round",
+                   "logits_bytes_per_gpu": per_rank},
+        "gpu_launches": (2 if greedy else 7) * steps, "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+class _SelfComm:
+    """Collectives of a one-rank job (identity)."""
+    nranks, rank = 1, 0
+
+    def all_gather(self, t):
+        return t
+
+    def all_reduce_sum(self, t):
+        return t
+
+    def all_reduce_max(self, t):
+        return t
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         return reference_arm(a)
     if a.mode == "attn":
         return attn_bench(a)
+    if a.mode.startswith("vshard"):
+        return vshard_bench(a)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
