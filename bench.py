@@ -45,7 +45,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="sample",
-                    choices=["sample", "greedy", "attn", "vshard", "vshard-greedy"])
+                    choices=["sample", "greedy", "attn", "vshard", "vshard-greedy", "engine"])
+    ap.add_argument("--new-tokens", type=int, default=256, help="--mode engine: tokens per row")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-rows", type=int, default=64, help="--mode attn: rows (config 3: 64)")
     return ap.parse_args()
@@ -358,6 +359,75 @@ def vshard_bench(a):
         dist.destroy_process_group()
 
 
+def engine_bench(a):
+    """--mode engine: config 4, the whole speculative round through the engine.
+
+    Random-init bf16 models (N(0, 0.02), no checkpoints offline) with the
+    Qwen3-8B target shape (36 layers, 4096 hidden, 32/8 heads x 128, FFN
+    12288, V 151936, RMSNorm, rope theta 1e6) and the Qwen3-0.6B draft shape
+    (28 layers, 1024 hidden, 16/8 heads x 128, FFN 3072); B=32 rows of 512
+    random prompt ids, k=4, --new-tokens per row, T=0.7 top-p 0.9.  Every
+    attention, KV append / rollback and sampling step runs on this package's
+    kernels; the projections and MLPs are torch / cuBLAS.  value = accepted
+    (emitted) tokens per second over the whole generate call, timed with CUDA
+    events around it (one step = one generate call).
+    """
+    import torch
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from specdec.engine import SamplingConfig, SpecDecodeEngine
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    common = dict(vocab_size=VOCAB, head_dim=128, num_key_value_heads=8, rope_theta=1e6,
+                  max_position_embeddings=8192, rms_norm_eps=1e-6, initializer_range=0.02)
+    tcfg = Qwen3Config(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
+                       num_attention_heads=32, tie_word_embeddings=False, **common)
+    dcfg = Qwen3Config(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                       num_attention_heads=16, tie_word_embeddings=True, **common)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        target = Qwen3ForCausalLM(tcfg).to(torch.bfloat16).eval()
+        draft = Qwen3ForCausalLM(dcfg).to(torch.bfloat16).eval()
+
+    class _Tok:
+        eos_token_id = None
+
+    Bq, P, k = 32, 512, 4
+    new = max(8, a.new_tokens)
+    # rows that finish early keep one cache slot per round until the slowest row
+    # ends (the reference's rollback leaves k - n_acc with n_acc = 0 for them),
+    # so a row can reach P + 2 * new
+    eng = SpecDecodeEngine(target, draft, _Tok(), device=dev, capacity=P + 2 * new + 2 * k + 8)
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, VOCAB, (Bq, P), generator=g)
+    plen = torch.full((Bq,), P, dtype=torch.long)
+    sp = SamplingConfig(temperature=T_SAMPLE, top_p=TOP_P)
+    eng.generate(ids, plen, 16, sampling=sp, seed=0, k_fixed=k)          # warm-up
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index or 0) as clk:
+        e0.record()
+        _, st = eng.generate(ids, plen, new, sampling=sp, seed=1, k_fixed=k)
+        e1.record()
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    d = st.to_dict()
+    print(json.dumps({
+        "metric": "accepted tok/s (config 4: Qwen3-8B / Qwen3-0.6B shapes, B=32, k=4)",
+        "value": st.emitted / (ms / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": 1,
+        "warmup": 1, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0,0.02), random prompt ids)",
+        "config": {"workload": "config 4 full speculative round", "rows": Bq, "prompt": P,
+                   "new_tokens": new, "k": k, "temperature": T_SAMPLE, "top_p": TOP_P,
+                   "target": "Qwen3-8B shape (random init)",
+                   "draft": "Qwen3-0.6B shape (random init)"},
+        "engine": {key: d[key] for key in ("rounds", "emitted", "acceptance_rate",
+                                           "mean_accepted_len", "draft_forwards",
+                                           "target_forwards")},
+        "clocks": clk.summary()}))
+
+
 class _SelfComm:
     """Collectives of a one-rank job (identity)."""
     nranks, rank = 1, 0
@@ -380,6 +450,8 @@ def main():
         return attn_bench(a)
     if a.mode.startswith("vshard"):
         return vshard_bench(a)
+    if a.mode == "engine":
+        return engine_bench(a)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
