@@ -20,7 +20,13 @@ What runs where:
 * attention reads the ragged cache through the verify-attention kernel
   (models are switched to attn_implementation "specdec_b200");
 * the one designed host sync per round reads n_acc, y and the drafted ids
-  together (the reference reads them at engine.py:309, :322-323).
+  together (the reference reads them at engine.py:309, :322-323);
+* with ``cuda_graphs=True`` (the default) every fixed-shape step after the
+  first round -- each draft step (forward, cache advance, draw), the
+  commit-only draft forward and the target verify forward -- replays a CUDA
+  graph captured once per generate call: nothing in them reads the device
+  lengths back, so the eager per-layer launch overhead of the HF forwards
+  (most of a round's time at small batch) is paid once.
 
 Draws use uniforms from the round's torch.Generator, so runs are reproducible
 for a seed; the random stream differs from the reference's multinomial calls,
@@ -111,6 +117,78 @@ class RunStats:
         }
 
 
+class _RoundGraphs:
+    """CUDA graphs of one generate call's fixed-shape round steps.
+
+    Static buffers carry the inputs and outputs across replays: ``feed`` (the
+    token each draft step consumes), ``u`` (draft uniforms), ``xs`` / ``qx``
+    (drafted ids and q(x)), ``vin[k]`` (the target's [B, k+1] verify input)
+    and ``vlog[k]`` (its logits).  A graph is captured on first use, after the
+    eager first round has created every workspace, and is then replayed; a
+    capture records the kernels without running them.  The caches' host
+    mirrors are invalidated so that no step touches host state.
+    """
+
+    def __init__(self, eng, B, k_max, dcache, tcache, drf_buf, T, tp, tk):
+        dev = eng.device
+        self.eng, self.B = eng, B
+        self.dcache, self.tcache, self.drf_buf = dcache, tcache, drf_buf
+        self.T, self.tp, self.tk = T, tp, tk
+        self.pool = torch.cuda.graph_pool_handle()
+        self.feed = torch.zeros(B, 1, dtype=torch.long, device=dev)
+        self.u = torch.zeros(k_max, B, dtype=torch.float32, device=dev)
+        self.xs = torch.zeros(B, k_max, dtype=torch.long, device=dev)
+        self.qx = torch.ones(k_max, B, dtype=torch.float32, device=dev)
+        self.rows0 = torch.zeros(B, dtype=torch.long, device=dev)
+        self.vin, self.vlog, self.graphs = {}, {}, {}
+        self.stream = torch.cuda.Stream(device=dev)
+
+    def _run(self, key, body):
+        self.dcache.invalidate_host()
+        self.tcache.invalidate_host()
+        g = self.graphs.get(key)
+        if g is None:
+            g = torch.cuda.CUDAGraph()
+            self.stream.wait_stream(torch.cuda.current_stream(self.eng.device))
+            with torch.cuda.graph(g, pool=self.pool, stream=self.stream):
+                body()
+            torch.cuda.current_stream(self.eng.device).wait_stream(self.stream)
+            self.graphs[key] = g
+        g.replay()
+
+    def draft_step(self, i):
+        e, B = self.eng, self.B
+
+        def body():
+            logits = e._forward(e.draft, self.dcache, self.feed)[:, -1]
+            self.dcache.advance(1)
+            self.drf_buf[:, i].copy_(logits)
+            x, q = draft_sample(self.drf_buf[:, i], self.u[i], self.T, self.tp, self.tk)
+            self.xs[:, i].copy_(x)
+            self.qx[i].copy_(q)
+            self.feed.copy_(x.view(B, 1))
+        self._run(("draft", i), body)
+
+    def draft_commit(self):
+        e = self.eng
+
+        def body():
+            e._forward(e.draft, self.dcache, self.feed, rows_last=self.rows0)
+            self.dcache.advance(1)
+        self._run(("commit",), body)
+
+    def target(self, k):
+        e = self.eng
+        if k not in self.vin:
+            self.vin[k] = torch.zeros(self.B, k + 1, dtype=torch.long, device=e.device)
+
+        def body():
+            self.vlog[k] = e._forward(e.target, self.tcache, self.vin[k])
+            self.tcache.advance(k + 1)
+        self._run(("target", k), body)
+        return self.vlog[k]
+
+
 class _NullCtx:
     def __enter__(self):
         return None
@@ -123,7 +201,7 @@ class SpecDecodeEngine:
     """Speculative decoding for a (target, draft) pair sharing a tokenizer."""
 
     def __init__(self, target, draft, tokenizer, device=None, capacity=4096, nvtx=False,
-                 time_phases=False):
+                 time_phases=False, cuda_graphs=True):
         self.target = target.eval()
         self.draft = draft.eval()
         self.tok = tokenizer
@@ -134,6 +212,7 @@ class SpecDecodeEngine:
         self.capacity = capacity
         self.nvtx = nvtx
         self.time_phases = time_phases
+        self.cuda_graphs = bool(cuda_graphs)
         tcfg, dcfg = target.config, draft.config
         if tcfg.vocab_size != dcfg.vocab_size:
             raise ValueError(
@@ -168,8 +247,11 @@ class SpecDecodeEngine:
         """
         q = tokens.shape[1]
         mask = cache.attn_mask(q, model.dtype, valid=valid)
+        # cache_position given explicitly: derived from the cache it would read
+        # the device lengths back on the host (and could not be graph-captured)
         hidden = model.model(input_ids=tokens, position_ids=cache.positions(q),
                              attention_mask=mask, past_key_values=cache,
+                             cache_position=cache.cache_position(q),
                              use_cache=True).last_hidden_state
         if rows_last is not None:
             hidden = hidden[torch.arange(hidden.shape[0], device=hidden.device), rows_last]
@@ -221,48 +303,82 @@ class SpecDecodeEngine:
         done_l = [int(pend_l[b]) in self.eos_ids for b in range(B)]
         st.emitted += B
         drf_buf = None
+        graphs = None
+        K_BUF = 8
 
         while not all(done_l):
             k = int(k_fixed) if k_fixed is not None else controller.propose_k()
             k = max(1, k)
             r0 = time.perf_counter()
             if drf_buf is None or drf_buf.shape[1] < k:
-                drf_buf = torch.empty(B, max(k, 8), self.vocab_size, dtype=self.draft.dtype,
+                drf_buf = torch.empty(B, max(k, K_BUF), self.vocab_size, dtype=self.draft.dtype,
                                       device=dev)
-            xs = torch.empty(B, k, dtype=torch.long, device=dev)
-            feed = pending.view(B, 1)
+                graphs = None                      # graphs write into drf_buf
+            # the first round (and any round after drf_buf grew) runs eagerly and
+            # warms every workspace; later rounds replay graphs
+            use_g = self.cuda_graphs and st.rounds > 0 and graphs is not None
+            if self.cuda_graphs and graphs is None and st.rounds > 0:
+                graphs = _RoundGraphs(self, B, drf_buf.shape[1], dcache, tcache, drf_buf,
+                                      T, tp, tk)
+                use_g = True
             conf = torch.ones(B, device=dev)
             u_draft = torch.rand(k, B, generator=gen, device=dev)
             d0 = time.perf_counter()
             k_eff = k
             with self._range("draft_loop"):
-                for i in range(k):
-                    logits = self._forward(self.draft, dcache, feed)[:, -1]
+                if use_g:
+                    graphs.feed.copy_(pending.view(B, 1))
+                    graphs.u[:k].copy_(u_draft)
+                    for i in range(k):
+                        graphs.draft_step(i)
+                        st.draft_forwards += 1
+                        if controller is not None:
+                            conf = conf * graphs.qx[i]
+                            if controller.should_stop_drafting(i + 1, conf):
+                                k_eff = i + 1
+                                break
+                    graphs.draft_commit()
+                    st.draft_forwards += 1
+                    xs = graphs.xs[:, :k_eff]
+                else:
+                    xs = torch.empty(B, k, dtype=torch.long, device=dev)
+                    feed = pending.view(B, 1)
+                    for i in range(k):
+                        logits = self._forward(self.draft, dcache, feed)[:, -1]
+                        dcache.advance(1)
+                        st.draft_forwards += 1
+                        drf_buf[:, i].copy_(logits)
+                        x, qx = draft_sample(drf_buf[:, i], u_draft[i], T, tp, tk)
+                        xs[:, i] = x
+                        feed = x.view(B, 1)
+                        if controller is not None:
+                            conf = conf * qx
+                            if controller.should_stop_drafting(i + 1, conf):
+                                k_eff = i + 1
+                                break
+                    # commit-only forward: puts the last drafted token in the draft cache
+                    self._forward(self.draft, dcache, feed,
+                                  rows_last=torch.zeros(B, dtype=torch.long, device=dev))
                     dcache.advance(1)
                     st.draft_forwards += 1
-                    drf_buf[:, i].copy_(logits)
-                    x, qx = draft_sample(drf_buf[:, i], u_draft[i], T, tp, tk)
-                    xs[:, i] = x
-                    feed = x.view(B, 1)
-                    if controller is not None:
-                        conf = conf * qx
-                        if controller.should_stop_drafting(i + 1, conf):
-                            k_eff = i + 1
-                            break
-                # commit-only forward: puts the last drafted token in the draft cache
-                self._forward(self.draft, dcache, feed,
-                              rows_last=torch.zeros(B, dtype=torch.long, device=dev))
-                dcache.advance(1)
-                st.draft_forwards += 1
+                    xs = xs[:, :k_eff]
             self._sync_phase()
             st.t_draft += time.perf_counter() - d0
-            xs = xs[:, :k_eff]
 
             v0 = time.perf_counter()
             with self._range("verify"):
-                verify_in = torch.cat([pending.view(B, 1), xs], dim=1)
-                vlog = self._forward(self.target, tcache, verify_in)
-                tcache.advance(k_eff + 1)
+                if use_g:
+                    if k_eff not in graphs.vin:
+                        graphs.vin[k_eff] = torch.zeros(B, k_eff + 1, dtype=torch.long,
+                                                        device=dev)
+                    vin = graphs.vin[k_eff]
+                    vin[:, :1].copy_(pending.view(B, 1))
+                    vin[:, 1:].copy_(xs)
+                    vlog = graphs.target(k_eff)
+                else:
+                    verify_in = torch.cat([pending.view(B, 1), xs], dim=1)
+                    vlog = self._forward(self.target, tcache, verify_in)
+                    tcache.advance(k_eff + 1)
                 st.target_forwards += 1
             self._sync_phase()
             st.t_target += time.perf_counter() - v0

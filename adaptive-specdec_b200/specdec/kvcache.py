@@ -86,7 +86,7 @@ class _RaggedLayer(CacheLayerMixin):
         return self.parent.get_mask_sizes(query_length, layer_idx)
 
     def get_seq_length(self):
-        return self.parent.max_len if self.is_initialized else 0
+        return self.parent.get_seq_length() if self.is_initialized else 0
 
     def get_max_cache_shape(self):
         return self.parent.capacity
@@ -124,6 +124,11 @@ class RaggedCache(Cache):
             self._host = self.lengths.to("cpu")
             self._host_valid = True
         return self._host
+
+    def invalidate_host(self):
+        """Forget the host mirror (the next host read syncs once).  Steps that
+        are replayed from CUDA graphs change the device lengths only."""
+        self._host_valid = False
 
     @property
     def lengths_cpu(self):
@@ -249,6 +254,12 @@ class RaggedCache(Cache):
 
     # ---- Cache interface ---------------------------------------------------
     def get_seq_length(self, layer_idx: int = 0):
+        # On the kernel path transformers only feeds this to mask construction,
+        # which the registered mask function skips: answer from the host mirror
+        # when it is valid and never read the device lengths back (so forwards
+        # stay free of host syncs and can be graph-captured).
+        if self.attn_impl == "specdec_b200":
+            return int(self._host.max()) if self._host_valid and self.batch_size else 0
         return self.max_len
 
     def get_mask_sizes(self, query_length, layer_idx=0):

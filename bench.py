@@ -397,7 +397,8 @@ def engine_bench(a):
     # rows that finish early keep one cache slot per round until the slowest row
     # ends (the reference's rollback leaves k - n_acc with n_acc = 0 for them),
     # so a row can reach P + 2 * new
-    eng = SpecDecodeEngine(target, draft, _Tok(), device=dev, capacity=P + 2 * new + 2 * k + 8)
+    eng = SpecDecodeEngine(target, draft, _Tok(), device=dev, capacity=P + 2 * new + 2 * k + 8,
+                           time_phases=True)
     g = torch.Generator().manual_seed(1)
     ids = torch.randint(0, VOCAB, (Bq, P), generator=g)
     plen = torch.full((Bq,), P, dtype=torch.long)
@@ -424,7 +425,8 @@ def engine_bench(a):
                    "draft": "Qwen3-0.6B shape (random init)"},
         "engine": {key: d[key] for key in ("rounds", "emitted", "acceptance_rate",
                                            "mean_accepted_len", "draft_forwards",
-                                           "target_forwards")},
+                                           "target_forwards", "t_draft", "t_target",
+                                           "t_total")},
         "clocks": clk.summary()}))
 
 
