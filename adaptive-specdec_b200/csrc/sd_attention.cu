@@ -16,8 +16,11 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstdlib>
 
 #include "specdec_b200.h"
 
@@ -54,6 +57,8 @@ struct AttnParams {
   int* rowkmax;      // [B] live-key bound of each row (tensor-core path)
   int npiece;        // partial slots per (row, kv head) on the tensor-core path
   int out_vec4;      // out is 8-byte aligned and its strides are multiples of 4 elements
+  int tile_keys;     // keys per tile of the tensor-core schedule (plan kernel)
+  int* status;       // sticky: bit 0 = a bounded wait of the tcgen05 kernel gave up
 };
 
 __device__ __forceinline__ int row_limit(const AttnParams& P, int b, int j) {
@@ -363,7 +368,10 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(AttnParams P) {
   __shared__ int carry, nzero;
   __shared__ int zrow[1024];                           // rows of this chunk without a live key
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-  if (t == 0) carry = 0;
+  if (t == 0) {
+    carry = 0;
+    *P.status = 0;
+  }
   for (int i = t; i < P.B * P.Hkv; i += 1024) P.split_done[i] = 0;
   __syncthreads();
   for (int b0 = 0; b0 < P.B; b0 += 1024) {
@@ -374,7 +382,7 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(AttnParams P) {
       km = row_limit(P, b, P.qlen - 1);                // the limit grows with the query index
       P.rowkmax[b] = km;
     }
-    const int tiles = (km + MT_KEYS - 1) / MT_KEYS;
+    const int tiles = (km + P.tile_keys - 1) / P.tile_keys;
     int x = tiles;                                     // inclusive scan within the warp
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -647,6 +655,553 @@ attn_mma_kernel(const __grid_constant__ AttnParams P) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// tcgen05 path (bf16, head_dim 128, R <= 32 query rows per kv head)
+// ---------------------------------------------------------------------------
+// Same stream-K schedule as attn_mma_kernel, with 128-key tiles.  Per tile:
+//   S^T[128 keys, 32] = K_tile[128, 128 d] . Q^T        (tcgen05.mma, M=128 N=32,
+//                        A = K tile K-major, B = Q K-major, both 128B-swizzled;
+//                        accumulator in TMEM, double-buffered)
+//   softmax: thread t of the 4 softmax warps owns key t (TMEM lane t): 32
+//            scores in registers, lazy reference max per query row (moved
+//            only when a score passes it by TC_HEADROOM, a CTA-wide vote),
+//            p = 2^(s - m) written to shared memory as P^T (MN-major, 16 B
+//            per thread and row group)
+//   O^T[128 d, 32] += V^T[128 d, 128 keys] . P^T       (tcgen05.mma, A = the V
+//                        tile MN-major 128B-swizzled, B = P^T MN-major; O in
+//                        TMEM for the whole segment)
+// K / V tiles arrive by TMA (2D tensor maps over the caches viewed as
+// [B * Hkv * C, 128], 64-column boxes, 128B swizzle, no multicast) into a
+// TC_NST-stage ring.  Warp roles: 0-3 softmax + epilogue (TMEM lane quarter
+// = warp), 4 TMA producer, 5 MMA issuer (one elected thread each).  Every
+// wait is bounded; on expiry the CTA records SD attention error bit 0 and
+// drains.
+constexpr int TC_KEYS = 128;             // keys per tile
+constexpr int TC_N = 32;                 // query rows per kv head (padded)
+constexpr int TC_NST = 3;                // K/V ring stages
+constexpr int TC_THREADS = 192;
+constexpr int TC_MIN_SHARE = SPLIT_KEYS / TC_KEYS;
+constexpr float TC_HEADROOM = 8.f;
+constexpr uint32_t TC_TMEM_COLS = 128;   // S0, S1, O0, O1 (32 columns each)
+constexpr long long TC_WAIT = 1LL << 31; // cycles (~1 s) before a wait gives up
+
+struct TcSmem {
+  alignas(1024) unsigned char k[TC_NST][2][TC_KEYS * 128];   // [stage][64-col box][128 rows x 128 B]
+  alignas(1024) unsigned char v[TC_NST][2][TC_KEYS * 128];
+  alignas(1024) unsigned char q[2][2][TC_N * 128];           // Q per segment parity, 2 boxes
+  alignas(1024) unsigned char p[2][4 * 2048];                // P^T, MN-major, double-buffered
+  alignas(8) unsigned long long full[TC_NST], empty[TC_NST];
+  alignas(8) unsigned long long sfull[2], sfree[2], pfull[2];
+  // oready[g & 1]: GEMM2 of tile g done.  Two barriers so that every wait on
+  // one sees at most two of its phases outstanding (a tile's sfull commit
+  // already covers the GEMM2 two tiles back).
+  alignas(8) unsigned long long oready[2], qfull, fin;
+  float red[4][TC_N];                                        // cross-warp row reductions
+  uint32_t tmem;
+  int seg_b;
+  int abort_;
+  int last;
+};
+static_assert(sizeof(TcSmem) + 1024 <= 227 * 1024, "tcgen05 attention shared memory");
+
+__device__ __forceinline__ uint32_t tc_sw128(int row, int col) {  // element offset in a 64-col box
+  return (uint32_t)(row * 128 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2);
+}
+__device__ __forceinline__ uint64_t tc_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                            uint32_t layout) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46) |
+         ((uint64_t)(layout & 7) << 61);
+}
+// kind::f16 instruction descriptor: bf16 A and B, f32 D, M x N, majors
+__host__ __device__ constexpr uint32_t tc_idesc(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, int acc) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+               " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+               :: "r"(d), "l"(a), "l"(b), "r"(id), "r"(acc) : "memory");
+}
+__device__ __forceinline__ void tc_commit(unsigned long long* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_bar_init(unsigned long long* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void tc_arrive(unsigned long long* bar) {
+  asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}"
+               :: "r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_expect_tx(unsigned long long* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+               :: "r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+// Has the phase of parity `par` completed?  (non-blocking)
+__device__ __forceinline__ bool tc_test(unsigned long long* bar, uint32_t par) {
+  uint32_t done;
+  asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+               " selp.u32 %0, 1, 0, p;\n}" : "=r"(done) : "r"(smem_addr(bar)), "r"(par)
+               : "memory");
+  return done != 0;
+}
+// Bounded wait for the phase of parity `par`; false (and the CTA's abort
+// flag set) on expiry or when another thread already gave up.
+__device__ __forceinline__ bool tc_wait(unsigned long long* bar, uint32_t par, int* abort_) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}" : "=r"(done) : "r"(smem_addr(bar)), "r"(par)
+                 : "memory");
+    if (done) return true;
+    if (*reinterpret_cast<volatile int*>(abort_) || clock64() - t0 > TC_WAIT) {
+      *reinterpret_cast<volatile int*>(abort_) = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tc_tma_2d(void* dst, const void* tmap, int x, int y,
+                                          unsigned long long* bar) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+               " [%0], [%1, {%2, %3}], [%4];"
+               :: "r"(smem_addr(dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_addr(bar))
+               : "memory");
+}
+#define TC_LD32(r, addr)                                                                        \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,"    \
+               "%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,"  \
+               "%30,%31}, [%32];"                                                               \
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),        \
+                 "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),     \
+                 "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), \
+                 "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), \
+                 "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), \
+                 "=r"(r[30]), "=r"(r[31])                                                      \
+               : "r"(addr) : "memory")
+#define TC_ST32(addr, r)                                                                        \
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,"  \
+               "%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,"  \
+               "%30,%31,%32};"                                                                  \
+               :: "r"(addr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), \
+                 "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]),\
+                 "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),       \
+                 "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),       \
+                 "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]),       \
+                 "r"(r[31]) : "memory")
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// barrier of the four softmax warps
+__device__ __forceinline__ void tc_sbar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ bool tc_sbar_or(bool p) {
+  int r;
+  asm volatile("{\n .reg .pred a, b;\n setp.ne.b32 a, %1, 0;\n"
+               " bar.red.or.pred b, 1, 128, a;\n selp.s32 %0, 1, 0, b;\n}"
+               : "=r"(r) : "r"((int)p) : "memory");
+  return r != 0;
+}
+
+// The CTA's run of tiles as (row, kv head) segments, walked identically by
+// every role.
+struct TcSeg {
+  int b, h, tb, off, tt, t1, nseg, s0, s1;
+};
+__device__ __forceinline__ void tc_seg_init(TcSeg& g, const AttnParams& P, int b0, int t0, int t1) {
+  g.b = b0;
+  g.tb = P.rowpre[b0 + 1] - P.rowpre[b0];
+  g.h = (t0 - P.rowpre[b0] * P.Hkv) / g.tb;
+  g.off = (t0 - P.rowpre[b0] * P.Hkv) % g.tb;
+  g.tt = t0;
+  g.t1 = t1;
+}
+__device__ __forceinline__ void tc_seg_bounds(TcSeg& g, const AttnParams& P) {
+  g.nseg = min(g.tb - g.off, g.t1 - g.tt);
+  g.s0 = g.off * TC_KEYS;
+  g.s1 = min(P.rowkmax[g.b], (g.off + g.nseg) * TC_KEYS);
+}
+// advance past the current segment; false when the run is over
+__device__ __forceinline__ bool tc_seg_next(TcSeg& g, const AttnParams& P) {
+  g.tt += g.nseg;
+  if (g.tt >= g.t1) return false;
+  g.off = 0;
+  if (++g.h == P.Hkv) {
+    g.h = 0;
+    do { ++g.b; } while (P.rowpre[g.b + 1] == P.rowpre[g.b]);
+    g.tb = P.rowpre[g.b + 1] - P.rowpre[g.b];
+  }
+  return true;
+}
+
+template <int NTG>                                    // 8-row groups of real query rows
+__global__ void __launch_bounds__(TC_THREADS, 1)
+attn_tc_kernel(const __grid_constant__ AttnParams P, const __grid_constant__ CUtensorMap tmk,
+               const __grid_constant__ CUtensorMap tmv) {
+  constexpr int RN = 8 * NTG;                          // rows the softmax computes (<= TC_N)
+  extern __shared__ __align__(1024) unsigned char tc_raw[];
+  const uint32_t pad = (1024u - (smem_addr(tc_raw) & 1023u)) & 1023u;  // swizzle atoms: 1024 B
+  TcSmem& S = *reinterpret_cast<TcSmem*>(tc_raw + pad);
+  const int t = threadIdx.x, w = t >> 5, lane = t & 31;
+  const int R = P.R, Hkv = P.Hkv;
+  const int total = P.rowpre[P.B] * Hkv;
+  const int share = max(TC_MIN_SHARE, (total + (int)gridDim.x - 1) / (int)gridDim.x);
+  const int t0 = (int)blockIdx.x * share;
+  if (t0 >= total) return;                             // no work for this CTA (uniform)
+  const int t1 = min(total, t0 + share);
+  for (int b = t; b < P.B; b += TC_THREADS)
+    if (P.rowpre[b] * Hkv <= t0 && t0 < P.rowpre[b + 1] * Hkv) S.seg_b = b;
+  if (t == 0) {
+    for (int i = 0; i < TC_NST; ++i) {
+      tc_bar_init(&S.full[i], 1);
+      tc_bar_init(&S.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc_bar_init(&S.sfull[i], 1);
+      tc_bar_init(&S.sfree[i], 128);
+      tc_bar_init(&S.pfull[i], 128);
+    }
+    tc_bar_init(&S.oready[0], 1);
+    tc_bar_init(&S.oready[1], 1);
+    tc_bar_init(&S.qfull, 128);
+    tc_bar_init(&S.fin, 1);
+    S.abort_ = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (w == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_addr(&S.tmem)), "r"(TC_TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = S.tmem;
+  TcSeg g;
+  tc_seg_init(g, P, S.seg_b, t0, t1);
+
+  if (w == 4) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      uint32_t gi = 0;
+      bool ok = true;
+      do {
+        tc_seg_bounds(g, P);
+        const int row0 = (g.b * Hkv + g.h) * P.C + g.s0;
+        for (int i = 0; i < g.nseg && ok; ++i, ++gi) {
+          const int st = (int)(gi % TC_NST);
+          if (gi >= (uint32_t)TC_NST)
+            ok = tc_wait(&S.empty[st], ((gi / TC_NST) - 1) & 1u, &S.abort_);
+          if (!ok) break;
+          tc_expect_tx(&S.full[st], 4u * TC_KEYS * 128u);
+          const int y = row0 + i * TC_KEYS;
+          tc_tma_2d(S.k[st][0], &tmk, 0, y, &S.full[st]);
+          tc_tma_2d(S.k[st][1], &tmk, 64, y, &S.full[st]);
+          tc_tma_2d(S.v[st][0], &tmv, 0, y, &S.full[st]);
+          tc_tma_2d(S.v[st][1], &tmv, 64, y, &S.full[st]);
+        }
+      } while (ok && tc_seg_next(g, P));
+      if (!ok) {
+        // let the copies already issued land before the CTA leaves
+        for (uint32_t q = gi > (uint32_t)TC_NST ? gi - TC_NST : 0u; q < gi; ++q) {
+          int dummy = 0;
+          tc_wait(&S.full[q % TC_NST], (q / TC_NST) & 1u, &dummy);
+        }
+      }
+    }
+  } else if (w == 5) {
+    // ---------------- MMA issuer: two in-order queues polled together, the
+    // GEMM1s (S^T of tile a: needs its K/V stage loaded, its S buffer read
+    // out, and for a segment's first tile that segment's Q) and the GEMM2s
+    // (O^T += V^T P^T of tile c: needs its P), so that neither waits behind
+    // the other's unrelated dependency
+    if (lane == 0) {
+      constexpr uint32_t ID1 = tc_idesc(128, TC_N, 0, 0);   // S^T = K . Q^T
+      constexpr uint32_t ID2 = tc_idesc(128, TC_N, 1, 1);   // O^T += V^T . P^T
+      const uint32_t ntot = (uint32_t)(t1 - t0);
+      TcSeg ga = g, gc = g;
+      tc_seg_bounds(ga, P);
+      tc_seg_bounds(gc, P);
+      int ia = 0, ic = 0;
+      uint32_t a = 0, c = 0, sa = 0, sc = 0;             // tiles and segments of the two heads
+      long long idle0 = clock64();
+      while (c < ntot) {
+        bool progressed = false;
+        // GEMM1(a) only after GEMM2(a - 2) was issued: its sfull commit then
+        // covers that GEMM2, so the softmax may rewrite P buffer a & 1 and
+        // every oready wait sees at most two phases outstanding
+        if (a < ntot && a < c + 2) {
+          const int st = (int)(a % TC_NST), sb = (int)(a & 1u);
+          const bool ready = tc_test(&S.full[st], (a / TC_NST) & 1u) &&
+                             (a < 2 || tc_test(&S.sfree[sb], ((a >> 1) - 1) & 1u)) &&
+                             (ia != 0 || tc_test(&S.qfull, sa & 1u));
+          if (ready) {
+            tc_fence_after();
+            const uint32_t ka0 = smem_addr(S.k[st][0]), ka1 = smem_addr(S.k[st][1]);
+            const uint32_t qa0 = smem_addr(S.q[sa & 1u][0]), qa1 = smem_addr(S.q[sa & 1u][1]);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const uint32_t ko = (uint32_t)(ks & 3) * 32u;
+              tc_mma(tm + (uint32_t)sb * 32u, tc_desc((ks < 4 ? ka0 : ka1) + ko, 16, 1024, 2),
+                     tc_desc((ks < 4 ? qa0 : qa1) + ko, 16, 1024, 2), ID1, ks > 0 ? 1 : 0);
+            }
+            tc_commit(&S.sfull[sb]);
+            ++a;
+            if (++ia == ga.nseg) {
+              ia = 0;
+              ++sa;
+              if (tc_seg_next(ga, P)) tc_seg_bounds(ga, P);
+            }
+            progressed = true;
+          }
+        }
+        if (c < a) {
+          const int st = (int)(c % TC_NST), pb = (int)(c & 1u);
+          if (tc_test(&S.pfull[pb], (c >> 1) & 1u)) {
+            tc_fence_after();
+            const uint32_t va = smem_addr(S.v[st][0]), pa = smem_addr(S.p[pb]);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+              tc_mma(tm + 64u + 32u * (sc & 1u), tc_desc(va + ks * 2048, 16384, 1024, 2),
+                     tc_desc(pa + ks * 256, 128, 2048, 0), ID2, (ic > 0 || ks > 0) ? 1 : 0);
+            tc_commit(&S.empty[st]);
+            tc_commit(&S.oready[c & 1u]);
+            ++c;
+            if (++ic == gc.nseg) {
+              ic = 0;
+              ++sc;
+              if (tc_seg_next(gc, P)) tc_seg_bounds(gc, P);
+            }
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          idle0 = clock64();
+        } else if (*reinterpret_cast<volatile int*>(&S.abort_) || clock64() - idle0 > TC_WAIT) {
+          *reinterpret_cast<volatile int*>(&S.abort_) = 1;
+          break;
+        }
+      }
+      // every MMA this thread issued has finished before the CTA leaves
+      // (TMEM is released after this)
+      tc_commit(&S.fin);
+      int dummy = 0;
+      tc_wait(&S.fin, 0u, &dummy);
+    }
+  } else {
+    // ---------------- softmax + epilogue warps (thread t: key t of a tile,
+    // head-dim element t of O; TMEM lane quarter = warp)
+    const uint32_t lrow = (uint32_t)(32 * w) << 16;
+    const float sl2 = P.scale * 1.4426950408889634f;
+    const __nv_bfloat16* Qg = reinterpret_cast<const __nv_bfloat16*>(P.q);
+    if (NTG < TC_N / 8) {                              // row groups past RN stay 0 in P^T
+      for (int i = t; i < 2 * 4 * 2048 / 16; i += 128)
+        reinterpret_cast<uint4*>(&S.p[0][0])[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.out);
+    // Q of a (row, kv head) into the swizzled B-operand tile of its segment
+    // parity; rows >= R are 0
+    auto write_q = [&](int qb, int qh, uint32_t qs) {
+      for (int i = t; i < TC_N * 16; i += 128) {
+        const int r = i >> 4, c = i & 15;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < R) {
+          const int j = r / P.group, hq = qh * P.group + r % P.group;
+          v = *reinterpret_cast<const uint4*>(Qg + qb * P.qbs + hq * P.qhs + j * P.qqs + 8 * c);
+        }
+        *reinterpret_cast<uint4*>(S.q[qs & 1u][c >> 3] + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_arrive(&S.qfull);
+    };
+    uint32_t gi = 0, seg = 0;
+    bool run = true;
+    write_q(g.b, g.h, 0u);
+    do {
+      tc_seg_bounds(g, P);
+      const int b = g.b, h = g.h;
+      const uint32_t ocol = 64u + 32u * (seg & 1u);     // this segment's O buffer
+      // per query row: live-key limit within this segment, reference max, partial sum
+      int lim[RN];
+      float m[RN], mc[RN], l[RN];
+      int lim_min = g.s1;
+      // the row's length and cap once (row_limit per query row would repeat
+      // the global loads, serialised, at every segment start)
+      const int64_t lenb = __ldg(P.lengths + b);
+      const int64_t capb = min(P.valid ? __ldg(P.valid + b) : (int64_t)P.C, (int64_t)P.C);
+#pragma unroll
+      for (int r = 0; r < RN; ++r) {
+        const int64_t lj = min(lenb + r / P.group + 1, capb);
+        lim[r] = r < R ? (int)min(max(lj, (int64_t)0), (int64_t)g.s1) : 0;
+        if (r < R) lim_min = min(lim_min, lim[r]);
+        m[r] = -INFINITY;
+        mc[r] = -1e30f;                                // m clamped: 2^(-inf - mc) = 0
+        l[r] = 0.f;
+      }
+      for (int i = 0; i < g.nseg; ++i, ++gi) {
+        const int sb = (int)(gi & 1u);
+        const bool ok = tc_wait(&S.sfull[sb], (gi >> 1) & 1u, &S.abort_);
+        uint32_t sr[TC_N];
+        tc_fence_after();
+        TC_LD32(sr, tm + lrow + (uint32_t)sb * 32u);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        tc_arrive(&S.sfree[sb]);
+        const int key = g.s0 + i * TC_KEYS + t;
+        // every row sees every key of the tile except near a row's limit
+        const bool whole = g.s0 + (i + 1) * TC_KEYS <= lim_min;
+        float sc[RN];
+        bool exceed = false;
+#pragma unroll
+        for (int r = 0; r < RN; ++r) {
+          const float v = __uint_as_float(sr[r]) * sl2;
+          sc[r] = (whole || key < lim[r]) ? v : -INFINITY;
+          exceed |= sc[r] > m[r] + TC_HEADROOM;
+        }
+        if (tc_sbar_or(exceed || !ok)) {
+          if (tc_sbar_or(!ok)) { run = false; break; }   // a wait gave up: all leave together
+          // move the reference max of every row to the tile's maximum
+#pragma unroll
+          for (int r = 0; r < RN; ++r) {
+            float mx = sc[r];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane == 0) S.red[w][r] = mx;
+          }
+          tc_sbar();
+          float alpha[RN];
+#pragma unroll
+          for (int r = 0; r < RN; ++r) {
+            const float mt = fmaxf(fmaxf(S.red[0][r], S.red[1][r]), fmaxf(S.red[2][r], S.red[3][r]));
+            const float mn = fmaxf(m[r], mt);
+            alpha[r] = mn == -INFINITY ? 1.f : (m[r] == -INFINITY ? 0.f : ex2f(m[r] - mn));
+            m[r] = mn;
+            mc[r] = fmaxf(mn, -1e30f);
+            l[r] *= alpha[r];
+          }
+          if (i > 0) {
+            // O holds this segment's earlier tiles: wait for the last GEMM into
+            // it (GEMM2 of tile gi - 1), then rescale every row in TMEM
+            const bool ok2 = tc_wait(&S.oready[(gi - 1) & 1u], ((gi - 1) >> 1) & 1u, &S.abort_);
+            (void)ok2;
+            tc_fence_after();
+            uint32_t o[TC_N];
+            TC_LD32(o, tm + lrow + ocol);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int r = 0; r < RN; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[r]);
+            TC_ST32(tm + lrow + ocol, o);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+          }
+          tc_sbar();                                   // S.red free again; O rescaled by all
+        }
+        // p = 2^(s - m) into P^T (MN-major: 16 B per row group of 8)
+        unsigned char* pb = S.p[sb];
+#pragma unroll
+        for (int gr = 0; gr < NTG; ++gr) {
+          float pv[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int r = 8 * gr + e;
+            pv[e] = ex2f(sc[r] - mc[r]);
+            l[r] += pv[e];
+          }
+          uint4 pk;
+          pk.x = pack_bf16(pv[0], pv[1]); pk.y = pack_bf16(pv[2], pv[3]);
+          pk.z = pack_bf16(pv[4], pv[5]); pk.w = pack_bf16(pv[6], pv[7]);
+          *reinterpret_cast<uint4*>(pb + gr * 2048 + (t >> 3) * 128 + (t & 7) * 16) = pk;
+        }
+        if (key >= g.s1) {
+          // past the live window the tile holds other cache slots (maybe never
+          // written: NaN would survive 0 * x): zero this key's V row
+          const int st = (int)(gi % TC_NST);
+          uint4* v0 = reinterpret_cast<uint4*>(S.v[st][0] + t * 128);
+          uint4* v1 = reinterpret_cast<uint4*>(S.v[st][1] + t * 128);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            v0[c] = make_uint4(0u, 0u, 0u, 0u);
+            v1[c] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc_fence_before();
+        tc_arrive(&S.pfull[sb]);
+      }
+      if (!run) break;
+      {
+        // the next segment's Q now, so its GEMM1s run during this epilogue
+        TcSeg gn = g;
+        if (tc_seg_next(gn, P)) write_q(gn.b, gn.h, seg + 1u);
+      }
+      // ---- segment epilogue: O^T (lane = head-dim element t), row sums, output
+      const bool ok = tc_wait(&S.oready[(gi - 1) & 1u], ((gi - 1) >> 1) & 1u, &S.abort_);
+      if (tc_sbar_or(!ok)) break;
+      tc_fence_after();
+      uint32_t o[TC_N];
+      TC_LD32(o, tm + lrow + ocol);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      tc_fence_before();
+#pragma unroll
+      for (int r = 0; r < RN; ++r) {
+        float sum = l[r];
+#pragma unroll
+        for (int q = 16; q; q >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, q);
+        if (lane == 0) S.red[w][r] = sum;
+      }
+      tc_sbar();
+      const int bh = b * Hkv + h;
+      const int Tb = P.rowpre[b] * Hkv + h * g.tb;     // first tile of this (row, kv head)
+      const int cfirst = Tb / share;
+      const int npieces = (Tb + g.tb - 1) / share - cfirst + 1;
+      const int64_t pbase = ((int64_t)bh * P.npiece + ((int)blockIdx.x - cfirst)) * R;
+      const int d = t;
+#pragma unroll
+      for (int r = 0; r < RN; ++r) {
+        if (r >= R) continue;
+        const float L = (S.red[0][r] + S.red[1][r]) + (S.red[2][r] + S.red[3][r]);
+        const float acc = __uint_as_float(o[r]);
+        if (npieces == 1) {
+          const int j = r / P.group, hq = h * P.group + r % P.group;
+          out[b * P.obs + j * P.oqs + hq * P.ohs + d] = __float2bfloat16(L > 0.f ? acc / L : 0.f);
+        } else {
+          P.part_acc[(pbase + r) * MT_D + d] = acc;
+          if (d == 0) {
+            P.part_ml[(pbase + r) * 2] = m[r] == -INFINITY ? -INFINITY : m[r] * 0.6931471805599453f;
+            P.part_ml[(pbase + r) * 2 + 1] = L;
+          }
+        }
+      }
+      if (npieces > 1) {
+        __threadfence();
+        tc_sbar();
+        if (t == 0) S.last = atomicAdd(&P.split_done[bh], 1) == npieces - 1;
+        tc_sbar();
+        if (S.last) {
+          __threadfence();
+          merge_pieces(P, b, h, npieces, w, lane, out);
+        }
+      }
+      tc_sbar();                                       // S.red and S.last reused next segment
+      ++seg;
+    } while (tc_seg_next(g, P));
+    (void)seg;
+  }
+  // ---------------- teardown: TMEM back once every role is done with it
+  tc_fence_before();
+  __syncthreads();
+  if (w == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                 :: "r"(tm), "r"(TC_TMEM_COLS) : "memory");
+  }
+  if (t == 0 && S.abort_) atomicOr(P.status, 1);
+}
+
 static int nsplit_for(int C, int qlen) {
   const int maxkeys = C + qlen;
   return (maxkeys + SPLIT_KEYS - 1) / SPLIT_KEYS;
@@ -677,6 +1232,75 @@ static int launch_mma(const AttnParams& P, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library)
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::atomic<void*> fn{nullptr};
+  void* f = fn.load();
+  if (f == nullptr) {
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) !=
+            cudaSuccess || qr != cudaDriverEntryPointSuccess || f == nullptr)
+      return nullptr;
+    fn.store(f);
+  }
+  return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+}
+
+// 2D map over a [B, Hkv, C, 128] bf16 cache viewed as [B * Hkv * C, 128]:
+// boxes of 128 rows x 64 columns (128 B), 128-byte swizzle, zero fill
+static bool cache_map(CUtensorMap* map, const void* base, int64_t rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)MT_D, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)MT_D * 2};
+  const cuuint32_t box[2] = {64u, (cuuint32_t)TC_KEYS};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+template <int NTG>
+static int launch_tc_ntg(const AttnParams& P, const CUtensorMap& mk, const CUtensorMap& mv,
+                         int nsm, cudaStream_t st) {
+  const int sm = (int)sizeof(TcSmem) + 1024;         // + room to align to 1024 B
+  if (cudaFuncSetAttribute(attn_tc_kernel<NTG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           sm) != cudaSuccess)
+    return SD_ELAUNCH;
+  attn_tc_kernel<NTG><<<nsm, TC_THREADS, sm, st>>>(P, mk, mv);
+  return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+}
+
+static int launch_tc(const AttnParams& P, cudaStream_t st) {
+  const int64_t rows = (int64_t)P.B * P.Hkv * P.C;
+  if (rows >= (int64_t)1 << 31) return SD_ENOTSUP;
+  CUtensorMap mk, mv;
+  if (!cache_map(&mk, P.k, rows) || !cache_map(&mv, P.v, rows)) return SD_ENOTSUP;
+  int dev = 0, nsm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return SD_ELAUNCH;
+  switch ((P.R + 7) / 8) {
+    case 1: return launch_tc_ntg<1>(P, mk, mv, nsm, st);
+    case 2: return launch_tc_ntg<2>(P, mk, mv, nsm, st);
+    case 3: return launch_tc_ntg<3>(P, mk, mv, nsm, st);
+    default: return launch_tc_ntg<4>(P, mk, mv, nsm, st);
+  }
+}
+
+// Which kernel takes the tensor-core shapes: tcgen05 (default) or the
+// mma.sync kernel (SD_ATTN_KERNEL=mma, kept for comparison).
+static bool use_tcgen05() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("SD_ATTN_KERNEL");
+    mode = (e && e[0] == 'm') ? 0 : 1;
+  }
+  return mode == 1;
+}
+
 }  // namespace sd
 
 using namespace sd;
@@ -688,7 +1312,7 @@ size_t sd_verify_attn_workspace_bytes(int B, int Hq, int Hkv, int D, int C, int 
   const int R = qlen * (Hq / Hkv);
   const size_t np = (size_t)nsplit_for(C, qlen) + 1;   // pieces per (row, kv head), either path
   return (size_t)B * Hkv * np * R * (D + 2) * sizeof(float) +
-         ((size_t)B * Hkv + 2 * (size_t)B + 1) * sizeof(int) + 256;
+         ((size_t)B * Hkv + 2 * (size_t)B + 2) * sizeof(int) + 256;
 }
 
 int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const void* kcache,
@@ -720,6 +1344,8 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
   P.split_done = reinterpret_cast<int*>(P.part_ml + (size_t)B * Hkv * P.npiece * P.R * 2);
   P.rowpre = P.split_done + (size_t)B * Hkv;
   P.rowkmax = P.rowpre + B + 1;
+  P.status = P.rowkmax + B;
+  P.tile_keys = MT_KEYS;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // tensor-core path: bf16, head_dim 128, <= 32 query rows per kv head,
   // 16-byte aligned rows
@@ -728,6 +1354,13 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
                       qhs % 8 == 0 && qqs % 8 == 0 &&
                       (reinterpret_cast<uintptr_t>(kcache) & 15) == 0 &&
                       (reinterpret_cast<uintptr_t>(vcache) & 15) == 0;
+  if (mma_ok && use_tcgen05()) {
+    P.nrc = 1;
+    P.tile_keys = TC_KEYS;
+    attn_plan_kernel<<<1, 1024, 0, st>>>(P);
+    if (cudaGetLastError() != cudaSuccess) return SD_ELAUNCH;
+    return launch_tc(P, st);
+  }
   if (mma_ok) {
     P.nrc = 1;
     attn_plan_kernel<<<1, 1024, 0, st>>>(P);
