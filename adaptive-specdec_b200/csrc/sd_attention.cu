@@ -58,6 +58,7 @@ struct AttnParams {
   int npiece;        // partial slots per (row, kv head) on the tensor-core path
   int out_vec4;      // out is 8-byte aligned and its strides are multiples of 4 elements
   int tile_keys;     // keys per tile of the tensor-core schedule (plan kernel)
+  int seg_ovh;       // schedule cost of a (row, kv head) beyond its tiles, in tiles
   int* status;       // sticky: bit 0 = a bounded wait of the tcgen05 kernel gave up
 };
 
@@ -291,6 +292,64 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
+// Merge with every load issued up front (128 threads; `scratch` holds
+// 2 * R * np floats of shared memory): (max, sum) of every (row, piece) in
+// one pass, per-row weights in shared memory, then each thread (head-dim
+// element t) pulls all its partial O values at once.  About three memory
+// round trips instead of one per row and pass.
+__device__ __noinline__ void merge_pieces_wide(const AttnParams& P, int b, int h, int np, int t,
+                                               float* scratch, __nv_bfloat16* out,
+                                               void (*sync)()) {
+  const int R = P.R;
+  const int64_t base0 = ((int64_t)b * P.Hkv + h) * P.npiece * R;
+  float* ms = scratch;                                 // [R][np] max (natural log units)
+  float* wl = scratch + R * np;                        // [R][np] sum, then weight / L
+  for (int i = t; i < R * np; i += 128) {
+    const int r = i / np, sp = i - r * np;
+    const int64_t o = (base0 + (int64_t)sp * R + r) * 2;
+    ms[i] = __ldcg(&P.part_ml[o]);
+    wl[i] = __ldcg(&P.part_ml[o + 1]);
+  }
+  sync();
+  if (t < R) {
+    float m = -INFINITY;
+    for (int sp = 0; sp < np; ++sp) m = fmaxf(m, ms[t * np + sp]);
+    float L = 0.f;
+    for (int sp = 0; sp < np; ++sp) {
+      const float mv = ms[t * np + sp];
+      const float f = (m == -INFINITY || mv == -INFINITY) ? 0.f : __expf(mv - m);
+      ms[t * np + sp] = f;
+      L += f * wl[t * np + sp];
+    }
+    const float il = L > 0.f ? 1.f / L : 0.f;
+    for (int sp = 0; sp < np; ++sp) wl[t * np + sp] = ms[t * np + sp] * il;
+  }
+  sync();
+  const int d = t;
+  for (int r0 = 0; r0 < R; r0 += 8) {                  // 8 rows x np pieces of loads in flight
+    float acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+    for (int sp = 0; sp < np; ++sp) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int r = r0 + q;
+        if (r < R)
+          acc[q] += wl[r * np + sp] *
+                    __ldcg(&P.part_acc[(base0 + (int64_t)sp * R + r) * MT_D + d]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int r = r0 + q;
+      if (r < R) {
+        const int j = r / P.group, hq = h * P.group + r % P.group;
+        out[b * P.obs + j * P.oqs + hq * P.ohs + d] = __float2bfloat16(acc[q]);
+      }
+    }
+  }
+}
+
 // Merge the partials (max, sum, O) of a (row, kv head)'s pieces into the
 // output: one warp per query row; lanes own pieces for (max, sum), then four
 // head-dim elements each for O (float4), eight pieces' loads in flight.
@@ -382,7 +441,8 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(AttnParams P) {
       km = row_limit(P, b, P.qlen - 1);                // the limit grows with the query index
       P.rowkmax[b] = km;
     }
-    const int tiles = (km + P.tile_keys - 1) / P.tile_keys;
+    int tiles = (km + P.tile_keys - 1) / P.tile_keys;
+    if (tiles > 0) tiles += P.seg_ovh;                 // fixed per-(row, kv head) cost
     int x = tiles;                                     // inclusive scan within the warp
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -682,6 +742,11 @@ constexpr int TC_NST = 3;                // K/V ring stages
 constexpr int TC_THREADS = 192;
 constexpr int TC_MIN_SHARE = SPLIT_KEYS / TC_KEYS;
 constexpr float TC_HEADROOM = 8.f;
+// Schedule cost of starting a (row, kv head) segment, in tiles: its Q,
+// first-tile max, epilogue and barriers take about as long as this many
+// tiles, so CTAs that cover many short rows get fewer tiles.  The schedule
+// lays these virtual tiles in front of each (row, kv head)'s real ones.
+constexpr int TC_OVH = 6;
 constexpr uint32_t TC_TMEM_COLS = 128;   // S0, S1, O0, O1 (32 columns each)
 constexpr long long TC_WAIT = 1LL << 31; // cycles (~1 s) before a wait gives up
 
@@ -810,7 +875,7 @@ __device__ __forceinline__ bool tc_sbar_or(bool p) {
 // The CTA's run of tiles as (row, kv head) segments, walked identically by
 // every role.
 struct TcSeg {
-  int b, h, tb, off, tt, t1, nseg, s0, s1;
+  int b, h, tb, off, tt, t1, ncost, nseg, s0, s1;   // tb, off, ncost: schedule units
 };
 __device__ __forceinline__ void tc_seg_init(TcSeg& g, const AttnParams& P, int b0, int t0, int t1) {
   g.b = b0;
@@ -821,19 +886,31 @@ __device__ __forceinline__ void tc_seg_init(TcSeg& g, const AttnParams& P, int b
   g.t1 = t1;
 }
 __device__ __forceinline__ void tc_seg_bounds(TcSeg& g, const AttnParams& P) {
-  g.nseg = min(g.tb - g.off, g.t1 - g.tt);
-  g.s0 = g.off * TC_KEYS;
-  g.s1 = min(P.rowkmax[g.b], (g.off + g.nseg) * TC_KEYS);
+  g.ncost = min(g.tb - g.off, g.t1 - g.tt);
+  const int r0 = max(g.off, TC_OVH) - TC_OVH;          // real tiles: units past the virtual ones
+  const int r1 = g.off + g.ncost - TC_OVH;
+  g.nseg = max(r1 - r0, 0);
+  g.s0 = r0 * TC_KEYS;
+  g.s1 = min(P.rowkmax[g.b], r1 * TC_KEYS);
 }
 // advance past the current segment; false when the run is over
 __device__ __forceinline__ bool tc_seg_next(TcSeg& g, const AttnParams& P) {
-  g.tt += g.nseg;
+  g.tt += g.ncost;
   if (g.tt >= g.t1) return false;
   g.off = 0;
   if (++g.h == P.Hkv) {
     g.h = 0;
     do { ++g.b; } while (P.rowpre[g.b + 1] == P.rowpre[g.b]);
     g.tb = P.rowpre[g.b + 1] - P.rowpre[g.b];
+  }
+  return true;
+}
+// the current or next segment that holds real tiles; false when none is left
+__device__ __forceinline__ bool tc_seg_real(TcSeg& g, const AttnParams& P) {
+  tc_seg_bounds(g, P);
+  while (g.nseg == 0) {
+    if (!tc_seg_next(g, P)) return false;
+    tc_seg_bounds(g, P);
   }
   return true;
 }
@@ -922,10 +999,18 @@ attn_tc_kernel(const __grid_constant__ AttnParams P, const __grid_constant__ CUt
     if (lane == 0) {
       constexpr uint32_t ID1 = tc_idesc(128, TC_N, 0, 0);   // S^T = K . Q^T
       constexpr uint32_t ID2 = tc_idesc(128, TC_N, 1, 1);   // O^T += V^T . P^T
-      const uint32_t ntot = (uint32_t)(t1 - t0);
+      uint32_t ntot = 0;                               // real tiles of the run
+      {
+        TcSeg gw = g;
+        bool more = tc_seg_real(gw, P);
+        while (more) {
+          ntot += (uint32_t)gw.nseg;
+          more = tc_seg_next(gw, P) && tc_seg_real(gw, P);
+        }
+      }
       TcSeg ga = g, gc = g;
-      tc_seg_bounds(ga, P);
-      tc_seg_bounds(gc, P);
+      tc_seg_real(ga, P);
+      tc_seg_real(gc, P);
       int ia = 0, ic = 0;
       uint32_t a = 0, c = 0, sa = 0, sc = 0;             // tiles and segments of the two heads
       long long idle0 = clock64();
@@ -954,7 +1039,7 @@ attn_tc_kernel(const __grid_constant__ AttnParams P, const __grid_constant__ CUt
             if (++ia == ga.nseg) {
               ia = 0;
               ++sa;
-              if (tc_seg_next(ga, P)) tc_seg_bounds(ga, P);
+              if (tc_seg_next(ga, P)) tc_seg_real(ga, P);
             }
             progressed = true;
           }
@@ -974,7 +1059,7 @@ attn_tc_kernel(const __grid_constant__ AttnParams P, const __grid_constant__ CUt
             if (++ic == gc.nseg) {
               ic = 0;
               ++sc;
-              if (tc_seg_next(gc, P)) tc_seg_bounds(gc, P);
+              if (tc_seg_next(gc, P)) tc_seg_real(gc, P);
             }
             progressed = true;
           }
@@ -1020,9 +1105,9 @@ attn_tc_kernel(const __grid_constant__ AttnParams P, const __grid_constant__ CUt
     };
     uint32_t gi = 0, seg = 0;
     bool run = true;
-    write_q(g.b, g.h, 0u);
-    do {
-      tc_seg_bounds(g, P);
+    bool more = tc_seg_real(g, P);
+    if (more) write_q(g.b, g.h, 0u);
+    while (more) {
       const int b = g.b, h = g.h;
       const uint32_t ocol = 64u + 32u * (seg & 1u);     // this segment's O buffer
       // per query row: live-key limit within this segment, reference max, partial sum
@@ -1131,13 +1216,15 @@ attn_tc_kernel(const __grid_constant__ AttnParams P, const __grid_constant__ CUt
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_before();
         tc_arrive(&S.pfull[sb]);
+        if (i == 0) {
+          // the next segment's Q, early: its buffer's last reader (the previous
+          // segment's GEMM1s) finished before this tile's S arrived, and the
+          // global loads overlap this segment's tiles
+          TcSeg gn = g;
+          if (tc_seg_next(gn, P) && tc_seg_real(gn, P)) write_q(gn.b, gn.h, seg + 1u);
+        }
       }
       if (!run) break;
-      {
-        // the next segment's Q now, so its GEMM1s run during this epilogue
-        TcSeg gn = g;
-        if (tc_seg_next(gn, P)) write_q(gn.b, gn.h, seg + 1u);
-      }
       // ---- segment epilogue: O^T (lane = head-dim element t), row sums, output
       const bool ok = tc_wait(&S.oready[(gi - 1) & 1u], ((gi - 1) >> 1) & 1u, &S.abort_);
       if (tc_sbar_or(!ok)) break;
@@ -1156,7 +1243,7 @@ attn_tc_kernel(const __grid_constant__ AttnParams P, const __grid_constant__ CUt
       tc_sbar();
       const int bh = b * Hkv + h;
       const int Tb = P.rowpre[b] * Hkv + h * g.tb;     // first tile of this (row, kv head)
-      const int cfirst = Tb / share;
+      const int cfirst = (Tb + TC_OVH) / share;         // CTAs holding its real tiles
       const int npieces = (Tb + g.tb - 1) / share - cfirst + 1;
       const int64_t pbase = ((int64_t)bh * P.npiece + ((int)blockIdx.x - cfirst)) * R;
       const int d = t;
@@ -1183,13 +1270,17 @@ attn_tc_kernel(const __grid_constant__ AttnParams P, const __grid_constant__ CUt
         tc_sbar();
         if (S.last) {
           __threadfence();
-          merge_pieces(P, b, h, npieces, w, lane, out);
+          if (2 * R * npieces * (int)sizeof(float) <= (int)sizeof(S.p))
+            merge_pieces_wide(P, b, h, npieces, t, reinterpret_cast<float*>(&S.p[0][0]), out,
+                              tc_sbar);
+          else
+            merge_pieces(P, b, h, npieces, w, lane, out);
         }
       }
       tc_sbar();                                       // S.red and S.last reused next segment
       ++seg;
-    } while (tc_seg_next(g, P));
-    (void)seg;
+      more = tc_seg_next(g, P) && tc_seg_real(g, P);
+    }
   }
   // ---------------- teardown: TMEM back once every role is done with it
   tc_fence_before();
@@ -1346,6 +1437,7 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
   P.rowkmax = P.rowpre + B + 1;
   P.status = P.rowkmax + B;
   P.tile_keys = MT_KEYS;
+  P.seg_ovh = 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // tensor-core path: bf16, head_dim 128, <= 32 query rows per kv head,
   // 16-byte aligned rows
@@ -1357,6 +1449,7 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
   if (mma_ok && use_tcgen05()) {
     P.nrc = 1;
     P.tile_keys = TC_KEYS;
+    P.seg_ovh = TC_OVH;
     attn_plan_kernel<<<1, 1024, 0, st>>>(P);
     if (cudaGetLastError() != cudaSuccess) return SD_ELAUNCH;
     return launch_tc(P, st);
