@@ -84,7 +84,12 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * No counterpart in the reference (added entry point).  The greedy verify
+ * No counterpart in the reference (added entry point), for callers that may
+ * not allocate device memory: a serving framework that reserves nearly all
+ * of the GPU for its own KV-cache pool up front and forbids other
+ * allocations (cudaMalloc can also synchronise the device in the middle of
+ * a decode step), or a host that binds the C ABI and only ever holds
+ * pointers it was handed.  The greedy verify
  * round of sd_verify_sample (temperature <= 0: u_res, draft logits, top-p and
  * top-k unused; same arguments, results and error codes otherwise) with no
  * workspace argument: its scratch is a fixed SD_STATIC_SCRATCH_BYTES device

@@ -1,5 +1,7 @@
 """sd_verify_greedy_static: the greedy verify round on the library's fixed
-device scratch (no workspace, no allocation) against sd_verify_sample.
+device scratch (no workspace, no allocation) against sd_verify_sample.  It
+exists for callers that may not allocate device memory, such as a serving
+framework that owns the whole GPU memory pool.
 
 Kept in its own file, collected last, so it runs both after the rest of the
 suite and alone (`pytest tests/test_zz_no_alloc.py -m gpu`).
