@@ -98,8 +98,8 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
  * allocates no memory.  Returns SD_ENOSPC when the shape needs more scratch
  * than that (about B*(k+1)*(48 + 8*chunks) bytes, chunks <= 64).
  * Calls that overlap on one device (other streams, other host threads) share
- * the scratch and race: serialise them.  Make the first call on each device
- * before capturing it into a CUDA graph (the symbol lookup is not captured).
+ * the scratch and race: serialise them.  The first call on a device does the
+ * one-time set-up (the symbol lookup); make it before any stream capture.
  */
 #define SD_STATIC_SCRATCH_BYTES (1u << 20)
 #define SD_MAX_DEVICES 64
