@@ -726,8 +726,9 @@ __device__ void finalize_histogram(HistSmem& s, const StatsParams& P, int v, con
 struct Stream {
   float Rc2;      // exponent offset of the bulk sum: y(x) = x c2 - Rc2 (-inf until set)
   float m;        // this lane's running max (logit units)
-  float Y;        // y(m - wlist): elements with y(x) >= Y are listed
-  uint32_t pkey;  // largest key this warp has published to the CTA max
+  float xt;       // list threshold: a value of the input type <= m - wlist
+  uint32_t xt2;   // xt twice, packed in the input type
+  float eY;       // 2^y(xt): the bulk term of an element clamped to xt
   double bulk;    // sum of 2^y(x) over the unlisted elements
 };
 
@@ -799,17 +800,55 @@ __device__ __forceinline__ void yof2(float& y0, float& y1, float x0, float x1, f
   fma2(y0, y1, x0, x1, c2h, i0, i1);
 }
 
+// Largest finite value of the input type at or below f (the lowest finite
+// value below that), so that a -inf element is never at or above it.
+template <int DT>
+__device__ __forceinline__ uint32_t round_down16(float f) {
+  if (DT == SD_DTYPE_BF16) {
+    const uint32_t h = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rd(f));
+    return h == 0xFF80u ? 0xFF7Fu : h;
+  }
+  const uint32_t h = (uint32_t)__half_as_ushort(__float2half_rd(f));
+  return h == 0xFC00u ? 0xFBFFu : h;
+}
+template <int DT>
+__device__ __forceinline__ float val16(uint32_t h) {
+  if (DT == SD_DTYPE_BF16) return __uint_as_float(h << 16);
+  return __half2float(__ushort_as_half((unsigned short)h));
+}
+
+// List threshold of a lane from its running max: xt = the largest value of
+// the input type at or below m - wlist, so every element at or above the
+// vector's final M - wlist is at or above it.  The clamped term 2^y(xt) bounds
+// every bulk term; the bulk reference moves up when it would exceed 2^64.
+template <int DT>
+__device__ __forceinline__ void set_thr(Stream& st, float c2h, float c2l, float wlist) {
+  const uint32_t h = round_down16<DT>(st.m - wlist);
+  st.xt2 = h | (h << 16);
+  st.xt = val16<DT>(h);
+  float Y = yof(st.xt, c2h, c2l, st.Rc2);
+  if (Y > 64.f) {
+    const float nr = st.Rc2 + (Y - 32.f);
+    st.bulk *= exp2((double)st.Rc2 - (double)nr);
+    st.Rc2 = nr;
+    Y = yof(st.xt, c2h, c2l, nr);
+  }
+  st.eY = ex2_approx(Y);
+}
+
 // Raise this lane's running max (list threshold follows).
+template <int DT>
 __device__ __forceinline__ void raise_m(Stream& st, float mn, float c2h, float c2l, float wlist) {
   st.m = mn;
-  st.Y = yof(mn - wlist, c2h, c2l, st.Rc2);
+  set_thr<DT>(st, c2h, c2l, wlist);
 }
 
 // Fix the bulk reference of a lane that has none yet (its first finite element).
+template <int DT>
 __device__ __forceinline__ void set_ref(Stream& st, float r, float c2h, float c2l, float wlist) {
   st.Rc2 = r * c2h;
   st.m = fmaxf(st.m, r);
-  st.Y = yof(st.m - wlist, c2h, c2l, st.Rc2);
+  set_thr<DT>(st, c2h, c2l, wlist);
 }
 
 // Lane maximum of 4G packed words.
@@ -826,96 +865,120 @@ __device__ __forceinline__ float lane_max(const uint32_t* w, uint32_t* pm1) {
   return fmaxf(lo16<DT>(pm[0]), hi16<DT>(pm[0]));
 }
 
-// 2^y summed over the elements of 4G packed words with y < Y; the elements
-// with y >= Y are excluded and flagged in lmask (bit 2i + h: word i, low /
-// high half), to be listed instead.
+// element-wise min of two packed pairs
+template <int DT>
+__device__ __forceinline__ uint32_t pmin2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if (DT == SD_DTYPE_BF16) asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else asm("min.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// 2^y summed over the elements of 4G packed words, each first clamped to the
+// list threshold xt (packed pair xt2): an element at or above xt adds exactly
+// 2^y(xt), which the caller takes back out when it lists the element.  No
+// per-element test or select: one packed min per pair.
 template <int DT, int G>
 __device__ __forceinline__ float bulk_words(const uint32_t* w, float c2h, float c2l, float Rc2,
-                                            float Y, uint32_t& lmask) {
+                                            uint32_t xt2) {
   float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-  uint32_t m = 0u;
 #pragma unroll
   for (int i = 0; i < 4 * G; ++i) {
+    const uint32_t c = pmin2<DT>(w[i], xt2);
     float y0, y1;
-    yof2(y0, y1, lo16<DT>(w[i]), hi16<DT>(w[i]), c2h, c2l, Rc2);
-    const bool l0 = y0 >= Y, l1 = y1 >= Y;
-    if (l0) m |= 1u << (2 * i);
-    if (l1) m |= 2u << (2 * i);
-    const float e0 = ex2_approx(l0 ? -INFINITY : y0);
-    const float e1 = ex2_approx(l1 ? -INFINITY : y1);
+    yof2(y0, y1, lo16<DT>(c), hi16<DT>(c), c2h, c2l, Rc2);
+    const float e0 = ex2_approx(y0);
+    const float e1 = ex2_approx(y1);
     if (i & 1) add2(b2, b3, e0, e1); else add2(b0, b1, e0, e1);
   }
-  lmask = m;
   return (b0 + b2) + (b1 + b3);
+}
+
+// Bit mask of the elements of 16 packed words at or above the threshold pair
+// xt2: word i's low element at bit i, its high element at bit 16 + i.
+template <int DT>
+__device__ __forceinline__ uint32_t ge_mask16(const uint32_t* w, uint32_t xt2) {
+  uint32_t m = 0u;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    uint32_t g;                                       // 0xFFFF per half where w >= xt
+    if (DT == SD_DTYPE_BF16) asm("set.ge.u32.bf16x2 %0, %1, %2;" : "=r"(g) : "r"(w[i]), "r"(xt2));
+    else asm("set.ge.u32.f16x2 %0, %1, %2;" : "=r"(g) : "r"(w[i]), "r"(xt2));
+    m |= g & (0x00010001u << i);
+  }
+  return m;
 }
 
 // One pass over 4G packed words per lane; groups without data hold -inf
 // pairs.  Called by whole streaming warps.  RING: the words are streaming
-// thread st's 16-byte units st + q * ST_N of ring slot `slot`, whose first
-// element has vocabulary index jbase; a lane that flagged elements lists them
-// itself, re-reading each from the slot.  Otherwise (the < 16 ragged
-// elements, one per lane in the low half of w[0], index jr) the lane's
-// element is listed the same way.
+// thread st's 16-byte units st + q * ST_N (q < 4) of ring slot `slot`, whose
+// first element has vocabulary index jbase.  A lane whose maximum reaches its
+// threshold lists its elements at or above it (a packed compare per word,
+// then one shared atomic for all of them, each element read again from the
+// slot) and takes their clamped terms back out of its bulk sum.  Otherwise
+// (the < 16 ragged elements, one per lane in the low half of w[0], index jr)
+// the lane's element is listed the same way.
 template <int DT, int G, bool RING>
 __device__ __forceinline__ void stream_words(HistSmem& s, VecHand& H, Stream& st,
                                              const uint32_t* w, int slot, uint32_t jbase,
                                              uint32_t jr, float c2h, float c2l, float wlist) {
-  const int lane = threadIdx.x & 31;
+  static_assert(!RING || G == 4, "16 packed words per lane and slot");
+  // The bulk sum and the lane maximum are independent (straight-line code the
+  // compiler interleaves); a lane without a reference yet discards the sum.
+  const bool had_ref = st.Rc2 != -INFINITY;
+  const float b = bulk_words<DT, G>(w, c2h, c2l, st.Rc2, st.xt2);
   uint32_t pm1[2 * G];
   const float gm = lane_max<DT, G>(w, pm1);
-  if (st.Rc2 == -INFINITY && gm > -INFINITY) set_ref(st, gm, c2h, c2l, wlist);
-  uint32_t lmask = 0u;
-  if (st.Rc2 != -INFINITY) {
-    float b = bulk_words<DT, G>(w, c2h, c2l, st.Rc2, st.Y, lmask);
-    const float ygm = yof(gm, c2h, c2l, st.Rc2);
-    if (ygm > 64.f) {
-      // far above the reference: move it up so that no partial sum overflows
-      // and redo this lane's words (a logit tens of units above everything
-      // seen before in the vector)
-      const float nr = st.Rc2 + (ygm - 32.f);
-      st.bulk *= exp2((double)st.Rc2 - (double)nr);
-      st.Rc2 = nr;
-      st.Y = yof(st.m - wlist, c2h, c2l, nr);
-      b = bulk_words<DT, G>(w, c2h, c2l, nr, st.Y, lmask);
-    }
+  if (had_ref) {
     st.bulk += (double)b;
+  } else if (gm > -INFINITY) {                        // rare: the lane's first finite element
+    set_ref<DT>(st, gm, c2h, c2l, wlist);
+    atomicMax(&H.gkey, fkey(gm));
+    st.bulk += (double)bulk_words<DT, G>(w, c2h, c2l, st.Rc2, st.xt2);
   }
-  // the flagged elements (rare: only near the running maximum), one shared
-  // atomic each
-  if (RING) {
-    if (lmask) {
-      const uint32_t* ring32 = reinterpret_cast<const uint32_t*>(s.ring[slot]);
-      const int tl = (int)threadIdx.x - ST0;
-      do {
-        const int bit = __ffs(lmask) - 1;
-        lmask &= lmask - 1u;
-        const int i = bit >> 1, h = bit & 1;
-        const int unit = tl + (i >> 2) * ST_N;
-        const uint32_t ww = ring32[unit * 4 + (i & 3)];
-        const float xv = h ? hi16<DT>(ww) : lo16<DT>(ww);
+  if (st.Rc2 != -INFINITY) {
+    if (gm >= st.xt) {                                // rare: elements to list
+      if (RING) {
+        uint32_t hm = ge_mask16<DT>(w, st.xt2);
+        const int cnt = __popc(hm);
+        int o = atomicAdd(&H.nkey, cnt);
+        st.bulk -= (double)cnt * (double)st.eY;
+        const uint32_t* ring32 = reinterpret_cast<const uint32_t*>(s.ring[slot]);
+        const int tl = (int)threadIdx.x - ST0;
+        while (hm) {
+          const int bit = __ffs(hm) - 1;
+          hm &= hm - 1u;
+          const int i = bit & 15, h = bit >> 4;
+          const int unit = tl + (i >> 2) * ST_N;
+          const uint32_t ww = ring32[unit * 4 + (i & 3)];
+          const float xv = h ? hi16<DT>(ww) : lo16<DT>(ww);
+          if (o < LIST_CAP)
+            H.key[o] = list_key(xv, jbase + 8u * (uint32_t)unit + 2u * (uint32_t)(i & 3) + (uint32_t)h);
+          ++o;
+        }
+      } else {                                        // the lane's only element
         const int o = atomicAdd(&H.nkey, 1);
-        if (o < LIST_CAP)
-          H.key[o] = list_key(xv, jbase + 8u * (uint32_t)unit + 2u * (uint32_t)(i & 3) + (uint32_t)h);
-      } while (lmask);
+        if (o < LIST_CAP) H.key[o] = list_key(lo16<DT>(w[0]), jr);
+        st.bulk -= (double)st.eY;
+      }
     }
-  } else if (lmask & 1u) {                            // the lane's only element
-    const int o = atomicAdd(&H.nkey, 1);
-    if (o < LIST_CAP) H.key[o] = list_key(lo16<DT>(w[0]), jr);
   }
-  if (gm > st.m) raise_m(st, gm, c2h, c2l, wlist);
-  const uint32_t wk = __reduce_max_sync(0xffffffffu, fkey(gm));
-  if (wk > st.pkey) {                                 // warp-uniform
-    if (lane == 0) atomicMax(&H.gkey, wk);
-    st.pkey = wk;
+  // The lane's running max never exceeds the published vector max: it only
+  // rises from the published value (sync_max), the seed (published), or its
+  // own elements, published here as they raise it.
+  if (gm > st.m) {
+    raise_m<DT>(st, gm, c2h, c2l, wlist);
+    atomicMax(&H.gkey, fkey(gm));
   }
 }
 
 // Start of a ring slot: adopt the vector's running max if it is ahead.
+template <int DT>
 __device__ __forceinline__ void sync_max(VecHand& H, Stream& st, float c2h, float c2l,
                                          float wlist) {
   const uint32_t gk = *reinterpret_cast<volatile uint32_t*>(&H.gkey);
   const float gv = fkey_value(gk);
-  if (st.Rc2 != -INFINITY && gv > st.m) raise_m(st, gv, c2h, c2l, wlist);
+  if (st.Rc2 != -INFINITY && gv > st.m) raise_m<DT>(st, gv, c2h, c2l, wlist);
 }
 
 // Probability of element j of a vector under its stats (the kept predicate
@@ -1580,7 +1643,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
       const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
       const VecGeom gm(x, V);
       Stream st;
-      st.Rc2 = -INFINITY; st.m = -INFINITY; st.Y = INFINITY; st.pkey = 0u;
+      st.Rc2 = -INFINITY; st.m = -INFINITY; st.xt = INFINITY; st.xt2 = 0u; st.eY = 0.f;
       st.bulk = 0.0;
       for (int c = 0; c < gm.nchunk; ++c, ++g) {
         const int sl = g % NSLOT;
@@ -1624,10 +1687,10 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
           if (lane == 0) atomicMax(&H.gkey, wk);
           sbar();
           const float r = fkey_value(*reinterpret_cast<volatile uint32_t*>(&H.gkey));
-          if (r > -INFINITY) set_ref(st, r, c2, c2l, wlist);
+          if (r > -INFINITY) set_ref<DT>(st, r, c2, c2l, wlist);
         }
         if (okw) {
-          sync_max(H, st, c2, c2l, wlist);
+          sync_max<DT>(H, st, c2, c2l, wlist);
           stream_words<DT, GPS, true>(s, H, st, w, sl, (uint32_t)(gm.head + c * (SLOT / 2)), 0u,
                                       c2, c2l, wlist);
         }
