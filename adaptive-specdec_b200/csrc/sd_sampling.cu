@@ -160,14 +160,20 @@ constexpr int SEL_CAP = 1024;            // entries sorted per vector
 constexpr int RANK_MAX = 512;            // row draw by direct prefix sums up to this many kept
 constexpr int NBIN = 49;                 // coarse depth bins: 4 per base-2 unit, + overflow
 constexpr int NBIN_PAD = 64;             // two bins per lane of one warp
+static_assert((unsigned long long)LIST_CAP << 20 <= 0xFFFFFFFFull,
+              "a bin's 20-bit mass parts sum below 2^32");
 
 // Finalize-warp scratch of the list path.
 struct ListBuf {
   float ecache[LIST_CAP];                // exact softmax numerator of each window key
   unsigned long long sel[SEL_CAP];       // entries selected for sorting
   float p[SEL_CAP];
-  unsigned long long binfx[NBIN_PAD];    // depth-bin mass, 2^-40 fixed point
-  int bincnt[NBIN_PAD];
+  // depth-bin mass in 2^-40 fixed point as 2^20 * binhi + binlo (each part
+  // sums at most LIST_CAP terms below 2^20), and count
+  uint32_t binhi[NBIN_PAD];
+  uint32_t binlo[NBIN_PAD];
+  uint32_t bincnt[NBIN_PAD];
+  uint8_t bin8[LIST_CAP];                // depth bin of each window key (NBIN_PAD: outside)
 };
 
 // What the streaming warps hand to the finalize warps for one vector (two
@@ -1054,14 +1060,14 @@ __device__ bool finalize_list(HistSmem& s, VecHand& H, const StatsParams& P, int
   const float M = fkey_value(H.gkey);                   // every element raised gkey
   const float m = scaled_logit(M, P.T);
   const float wlow = M - wlist;
-  if (t < NBIN_PAD) { s.u.l.binfx[t] = 0ull; s.u.l.bincnt[t] = 0; }
+  if (t < NBIN_PAD) { s.u.l.binhi[t] = 0u; s.u.l.binlo[t] = 0u; s.u.l.bincnt[t] = 0u; }
   if (t == 0) { s.nsel = 0; s.npre = 0; }
   cbar();
   // exact softmax numerators of the listed elements of the window (at or
-  // above M - W_LIST), binned by depth below the maximum (4 bins per base-2
-  // unit, mass in 2^-40 fixed point).  The streaming warps' bulk sums are
-  // relative to their offsets wrc2 (terms 2^(x c2 - wrc2)); the listed terms
-  // are exp(x / T - m).
+  // above M - W_LIST) and their depth bins below the maximum (4 bins per
+  // base-2 unit), each bin's mass and count added with 32-bit shared atomics.
+  // The streaming warps' bulk sums are relative to their offsets wrc2 (terms
+  // 2^(x c2 - wrc2)); the listed terms are exp(x / T - m).
   double es = 0.0;
   if (t < NSW && H.wbulk[t] > 0.0 && H.wrc2[t] != -INFINITY)
     es = H.wbulk[t] * exp2((double)H.wrc2[t] - (double)m * 1.4426950408889634);
@@ -1070,20 +1076,24 @@ __device__ bool finalize_list(HistSmem& s, VecHand& H, const StatsParams& P, int
   for (int i = t; i < nl; i += CT) {
     const float xv = list_val(H.key[i]);
     float e;
+    int bin = NBIN_PAD;
     if (!(xv >= wlow)) {
       e = ex2_approx(fmaf(xv, c2, -mc2));
     } else {
       e = softmax_num(xv, P.T, m);                      // <= 1: xv <= M
       s.u.l.ecache[i] = e;
+      bin = depth_bin(M, xv, c2);
       if (!all_kept) {
-        const int bin = depth_bin(M, xv, c2);
-        atomicAdd(&s.u.l.bincnt[bin], 1);
-        atomicAdd(&s.u.l.binfx[bin], (unsigned long long)__float2ull_rn(e * 0x1p40f));
+        const unsigned long long f = __float2ull_rn(e * 0x1p40f);
+        atomicAdd(&s.u.l.binhi[bin], (unsigned)(f >> 20));
+        atomicAdd(&s.u.l.binlo[bin], (unsigned)(f & 0xFFFFFull));
+        atomicAdd(&s.u.l.bincnt[bin], 1u);
       }
     }
+    s.u.l.bin8[i] = (uint8_t)bin;
     es += (double)e;
   }
-  const double S = c_sum<double>(es, s.dred);
+  const double S = c_sum<double>(es, s.dred);            // (its barriers publish bin8, ecache)
   const float inv_s = __double2float_rn(1.0 / S);
   int L = -1;                                            // last kept, sorted-part index
   float kth_x = -INFINITY;
@@ -1097,8 +1107,11 @@ __device__ bool finalize_list(HistSmem& s, VecHand& H, const StatsParams& P, int
       // bin where the top-p or top-k boundary can lie; every element of the
       // bins before it is kept (its exclusive mass is below top_p by the
       // slack and it ranks within top_k), in any order.
-      const unsigned long long f0 = s.u.l.binfx[2 * lane], f1 = s.u.l.binfx[2 * lane + 1];
-      const int c0 = s.u.l.bincnt[2 * lane], c1 = s.u.l.bincnt[2 * lane + 1];
+      const unsigned long long f0 =
+          ((unsigned long long)s.u.l.binhi[2 * lane] << 20) + s.u.l.binlo[2 * lane];
+      const unsigned long long f1 =
+          ((unsigned long long)s.u.l.binhi[2 * lane + 1] << 20) + s.u.l.binlo[2 * lane + 1];
+      const int c0 = (int)s.u.l.bincnt[2 * lane], c1 = (int)s.u.l.bincnt[2 * lane + 1];
       const unsigned long long fi = warp_incl_scan<unsigned long long>(f0 + f1);
       const int ci = warp_incl_scan<int>(c0 + c1);
       const unsigned long long fe = fi - f0 - f1;
@@ -1152,8 +1165,7 @@ __device__ bool finalize_list(HistSmem& s, VecHand& H, const StatsParams& P, int
       const int i = base + t;
       const bool in = i < nl;
       const unsigned long long key = in ? H.key[i] : 0ull;
-      const float xv = in ? list_val(key) : -INFINITY;
-      const int bin = (in && xv >= wlow) ? depth_bin(M, xv, c2) : NBIN_PAD;
+      const int bin = in ? (int)s.u.l.bin8[i] : NBIN_PAD;
       const bool pre = bin < bL;
       if (pre) zp += (double)__fmul_rn(s.u.l.ecache[i], inv_s);
       // kept for sure: straight into the stored kept set (order is free there)
