@@ -133,6 +133,7 @@ constexpr int SLOT = GPS * 16 * ST_N;    // bytes per ring slot (30 KB)
 constexpr int NSLOT = 4;
 constexpr long long WAIT_CYCLES = 1LL << 32;   // ~2 s at 2 GHz: bound on every wait
 constexpr int LIST_CAP = 3072;           // listed elements per vector
+static_assert(LIST_CAP < 65536, "list-path counts pack into 16 bits");
 constexpr int NUC_MAX = 1024;            // kept elements stored per vector for the draw
 constexpr float W_LIST = 12.f;           // list window, base-2 units below the maximum
 
@@ -205,8 +206,8 @@ struct HistSmem {
   uint32_t* gh;        // this CTA's global 65,536-counter histogram (fallback path)
   int ncorr;
   int corr_full;
-  int nsel;
-  int npre;           // kept elements above the sorted part of the list path
+  uint32_t npre_nsel;  // list path: kept elements above the sorted part (low 16 bits) and
+                       // elements selected for sorting (high 16 bits)
   int fb_why;          // FB_* reason of the last hand-over to the histogram path
   int abort_flag;
   int fin_skip;        // finalize warps: skip the work of this vector (after an abort)
@@ -230,10 +231,11 @@ static_assert(sizeof(HistSmem) <= 227 * 1024, "stats kernel shared memory");
 __device__ __forceinline__ int ftid() { return (int)threadIdx.x - FIN0; }
 
 // barrier of the finalize warps
-__device__ __forceinline__ void cbar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 2, %0;" :: "n"(CT) : "memory"); }
 // barrier of the streaming warps
-__device__ __forceinline__ void sbar() { asm volatile("bar.sync 1, 480;" ::: "memory"); }
-static_assert(CT == 128 && ST_N == 480, "named barrier thread counts");
+__device__ __forceinline__ void sbar() { asm volatile("bar.sync 1, %0;" :: "n"(ST_N) : "memory"); }
+static_assert(CT % 32 == 0 && ST_N % 32 == 0, "named barrier thread counts");
+static_assert(NSEG % CT == 0 && RANK_MAX % CT == 0, "finalize loops split evenly over CT threads");
 
 template <typename T>
 __device__ __forceinline__ T c_sum(T v, T* red) {
@@ -956,8 +958,11 @@ __device__ __forceinline__ void stream_words(HistSmem& s, VecHand& H, Stream& st
           hm &= hm - 1u;
           const int i = bit & 15, h = bit >> 4;
           const int unit = tl + (i >> 2) * ST_N;
-          const uint32_t ww = ring32[unit * 4 + (i & 3)];
-          const float xv = h ? hi16<DT>(ww) : lo16<DT>(ww);
+          float xv = gm;                              // the only element at or above xt
+          if (cnt > 1) {
+            const uint32_t ww = ring32[unit * 4 + (i & 3)];
+            xv = h ? hi16<DT>(ww) : lo16<DT>(ww);
+          }
           if (o < LIST_CAP)
             H.key[o] = list_key(xv, jbase + 8u * (uint32_t)unit + 2u * (uint32_t)(i & 3) + (uint32_t)h);
           ++o;
@@ -1061,7 +1066,7 @@ __device__ bool finalize_list(HistSmem& s, VecHand& H, const StatsParams& P, int
   const float m = scaled_logit(M, P.T);
   const float wlow = M - wlist;
   if (t < NBIN_PAD) { s.u.l.binhi[t] = 0u; s.u.l.binlo[t] = 0u; s.u.l.bincnt[t] = 0u; }
-  if (t == 0) { s.nsel = 0; s.npre = 0; }
+  if (t == 0) s.npre_nsel = 0u;
   cbar();
   // exact softmax numerators of the listed elements of the window (at or
   // above M - W_LIST) and their depth bins below the maximum (4 bins per
@@ -1167,21 +1172,33 @@ __device__ bool finalize_list(HistSmem& s, VecHand& H, const StatsParams& P, int
       const unsigned long long key = in ? H.key[i] : 0ull;
       const int bin = in ? (int)s.u.l.bin8[i] : NBIN_PAD;
       const bool pre = bin < bL;
+      const bool sel = bin >= bL && bin <= bstar;
       if (pre) zp += (double)__fmul_rn(s.u.l.ecache[i], inv_s);
-      // kept for sure: straight into the stored kept set (order is free there)
+      // kept for sure: straight into the stored kept set (order is free
+      // there); boundary bins: to be sorted.  One shared atomic per warp for
+      // both counts (each below 2^16: at most LIST_CAP elements).
       const unsigned pm = __ballot_sync(0xffffffffu, pre);
-      if (pm) {
-        const int leader = __ffs(pm) - 1;
-        int b0 = 0;
-        if (lane == leader) b0 = atomicAdd(&s.npre, __popc(pm));
-        const int o = __shfl_sync(0xffffffffu, b0, leader) + __popc(pm & ((1u << lane) - 1u));
-        if (pre && nuc != nullptr && o < NUC_MAX) nuc[o] = key;
+      const unsigned sm = __ballot_sync(0xffffffffu, sel);
+      if (pm | sm) {
+        const int leader = __ffs(pm | sm) - 1;
+        uint32_t b0 = 0u;
+        if (lane == leader)
+          b0 = atomicAdd(&s.npre_nsel, (uint32_t)__popc(pm) | ((uint32_t)__popc(sm) << 16));
+        b0 = __shfl_sync(0xffffffffu, b0, leader);
+        const unsigned lt = (1u << lane) - 1u;
+        if (pre) {
+          const int o = (int)(b0 & 0xFFFFu) + __popc(pm & lt);
+          if (nuc != nullptr && o < NUC_MAX) nuc[o] = key;
+        }
+        if (sel) {
+          const int o = (int)(b0 >> 16) + __popc(sm & lt);
+          if (o < SEL_CAP) s.u.l.sel[o] = key;
+        }
       }
-      warp_append(&s.nsel, s.u.l.sel, SEL_CAP, bin >= bL && bin <= bstar, key);
     }
     const double zpre = c_sum<double>(zp, s.dred);     // (its barriers publish nsel, npre)
-    npre = s.npre;
-    const int nsel = s.nsel;
+    npre = (int)(s.npre_nsel & 0xFFFFu);
+    const int nsel = (int)(s.npre_nsel >> 16);
     if (nsel > SEL_CAP || nsel < 1) return fallback_why(s, FB_SELECT);
     if (nsel <= 32) {
       // one warp: register sort, shuffle scans
