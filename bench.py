@@ -537,6 +537,10 @@ def main():
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_k)]
     with torch.cuda.stream(s):
+        # keep the GPU busy while the host enqueues the calls, so that each
+        # event pair times GPU work only (a call can be shorter than its launch
+        # path on the host); ~100 us of spin per call covers the enqueue
+        torch.cuda._sleep(int(2e5 * n_k))
         for i, (k0, k1) in enumerate(evs):
             k0.record(s)
             call(i)
