@@ -40,6 +40,8 @@ constexpr int SMALLV_MAX = 2048;        // small-vocabulary exact path
 constexpr int ST = 512;                 // threads of the small-V kernel
 constexpr int FT = 512;                 // threads of the finish / probs kernels
 constexpr int NCH_MAX = 64;             // vocabulary chunks per row in finish
+constexpr int AM_UPT = 8;               // argmax: 16-byte units per thread per pass, loaded at once
+constexpr int AM_FT = 256;              // argmax: threads per block (several blocks per SM)
 
 constexpr uint32_t NO_CUT = 0x7FFFFFFFu;
 
@@ -1928,9 +1930,13 @@ struct ArgmaxParams {
   int64_t* n_acc; int64_t* y; float* px; float* qx;
 };
 
+// Argmax key of element j: larger value first, then smaller index.  Every NaN,
+// whatever its sign bit (bf16 conversions of a float NaN give 0xFFFF), takes
+// the largest key: NaN counts as the maximum and the first NaN wins.
 template <int DT>
 __device__ __forceinline__ unsigned long long argmax_key(float x, int j) {
-  return ((unsigned long long)fkey(x) << 32) | (0xFFFFFFFFu - (uint32_t)j);
+  const uint32_t k = x != x ? 0xFFFFFFFFu : fkey(x);
+  return ((unsigned long long)k << 32) | (0xFFFFFFFFu - (uint32_t)j);
 }
 
 // Element-wise max of two packed 16-bit pairs, NaN propagating.
@@ -1945,10 +1951,13 @@ __device__ __forceinline__ uint32_t pmax2_nan(uint32_t a, uint32_t b) {
 // Argmax (first index of the maximum, NaN counting as the largest value) of a
 // vector: block c of the vector reads 16-byte units [c cu, (c+1) cu) of its
 // aligned body with vectorised loads (block 0 also the unaligned head, the
-// last block the tail).  For 16-bit logits a packed max of each unit's eight
-// elements skips the per-element keys unless the unit can hold a new maximum.
+// last block the tail).  Each pass issues a thread's AM_UPT loads at once,
+// keys every unit by its maximum (for 16-bit logits one packed max of its
+// eight elements), takes the warp's largest key once, and builds per-element
+// keys only in the units that reach it (ties included: the first index among
+// equal values is decided by the element keys).
 template <int DT>
-__global__ void __launch_bounds__(FT) argmax_kernel(ArgmaxParams P) {
+__global__ void __launch_bounds__(AM_FT) argmax_kernel(ArgmaxParams P) {
   __shared__ unsigned long long ured[40];
   __shared__ int last;
   constexpr int ESZ = DT == SD_DTYPE_F32 ? 4 : 2;
@@ -1968,46 +1977,51 @@ __global__ void __launch_bounds__(FT) argmax_kernel(ArgmaxParams P) {
     const unsigned long long kk = argmax_key<DT>(load_logit(xb, DT, tail0 + t), tail0 + t);
     best = kk > best ? kk : best;
   }
-  // lanes skip a unit unless it can reach the warp's best value so far
-  // (ties included: the first index among equal values is decided by keys)
-  uint32_t wthr = __reduce_max_sync(0xffffffffu, (uint32_t)(best >> 32));
   const uint4* body = reinterpret_cast<const uint4*>(xb + (size_t)head * ESZ);
   const int u1 = min((c + 1) * P.cu, nunits);
-  const int ub = c * P.cu + (t & ~31);                 // the warp iterates uniformly
-#pragma unroll 4
-  for (int uw = ub; uw < u1; uw += FT) {
-    const int u = uw + (t & 31);
-    uint32_t mk = 0u;                                   // key of the unit's maximum (0: no data)
-    uint4 w = make_uint4(0u, 0u, 0u, 0u);
-    if (u < u1) {
-      w = __ldg(body + u);
-      if (DT == SD_DTYPE_F32) {
-        mk = fkey(fmaxf(fmaxf(__uint_as_float(w.x), __uint_as_float(w.y)),
-                        fmaxf(__uint_as_float(w.z), __uint_as_float(w.w))));
-        const bool nan = __uint_as_float(w.x) != __uint_as_float(w.x) ||
-                         __uint_as_float(w.y) != __uint_as_float(w.y) ||
-                         __uint_as_float(w.z) != __uint_as_float(w.z) ||
-                         __uint_as_float(w.w) != __uint_as_float(w.w);
-        if (nan) mk = 0xFFFFFFFFu;
-      } else {
-        const uint32_t m = pmax2_nan<DT>(pmax2_nan<DT>(w.x, w.y), pmax2_nan<DT>(w.z, w.w));
-        const float lo = lo16<DT>(m), hi = hi16<DT>(m);
-        mk = (lo != lo || hi != hi) ? 0xFFFFFFFFu : fkey(fmaxf(lo, hi));
-      }
-    }
-    if (u < u1 && (mk >= wthr || mk == 0xFFFFFFFFu)) {   // may hold (or tie) the maximum
-      const int j0 = head + u * EPU;
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+  for (int base = c * P.cu; base < u1; base += AM_UPT * AM_FT) {      // block-uniform
+    uint4 w[AM_UPT];
+    uint32_t mk[AM_UPT];
 #pragma unroll
-      for (int e = 0; e < EPU; ++e) {
-        float xv;
-        if (DT == SD_DTYPE_F32) xv = __uint_as_float(ww[e]);
-        else xv = (e & 1) ? hi16<DT>(ww[e >> 1]) : lo16<DT>(ww[e >> 1]);
-        const unsigned long long kk = argmax_key<DT>(xv, j0 + e);
-        best = kk > best ? kk : best;
+    for (int i = 0; i < AM_UPT; ++i) {
+      const int u = base + t + i * AM_FT;
+      w[i] = u < u1 ? __ldg(body + u) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    uint32_t lm = (uint32_t)(best >> 32);
+#pragma unroll
+    for (int i = 0; i < AM_UPT; ++i) {
+      uint32_t k = 0u;                                  // 0: no data
+      if (base + t + i * AM_FT < u1) {
+        if (DT == SD_DTYPE_F32) {
+          const float a = __uint_as_float(w[i].x), b2 = __uint_as_float(w[i].y);
+          const float c2v = __uint_as_float(w[i].z), d = __uint_as_float(w[i].w);
+          const bool nan = a != a || b2 != b2 || c2v != c2v || d != d;
+          k = nan ? 0xFFFFFFFFu : fkey(fmaxf(fmaxf(a, b2), fmaxf(c2v, d)));
+        } else {
+          const uint32_t m = pmax2_nan<DT>(pmax2_nan<DT>(w[i].x, w[i].y), pmax2_nan<DT>(w[i].z, w[i].w));
+          const float lo = lo16<DT>(m), hi = hi16<DT>(m);
+          k = (lo != lo || hi != hi) ? 0xFFFFFFFFu : fkey(fmaxf(lo, hi));
+        }
+      }
+      mk[i] = k;
+      lm = k > lm ? k : lm;
+    }
+    const uint32_t wthr = __reduce_max_sync(0xffffffffu, lm);
+#pragma unroll
+    for (int i = 0; i < AM_UPT; ++i) {
+      if (mk[i] != 0u && mk[i] >= wthr) {              // may hold (or tie) the maximum
+        const int j0 = head + (base + t + i * AM_FT) * EPU;
+        const uint32_t ww[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+        for (int e = 0; e < EPU; ++e) {
+          float xv;
+          if (DT == SD_DTYPE_F32) xv = __uint_as_float(ww[e]);
+          else xv = (e & 1) ? hi16<DT>(ww[e >> 1]) : lo16<DT>(ww[e >> 1]);
+          const unsigned long long kk = argmax_key<DT>(xv, j0 + e);
+          best = kk > best ? kk : best;
+        }
       }
     }
-    wthr = __reduce_max_sync(0xffffffffu, (uint32_t)(best >> 32));
   }
   best = block_max<unsigned long long>(best, ured, 0ull);
   if (t == 0) {
@@ -2341,7 +2355,7 @@ struct WsLayout {
 };
 
 // Argmax geometry: blocks per vector and 16-byte units per block (a multiple
-// of FT, at most NCH_MAX blocks).
+// of AM_FT, at most NCH_MAX blocks).
 struct ArgmaxGeom {
   int nch, cu;
 };
@@ -2349,11 +2363,11 @@ static ArgmaxGeom argmax_geom(int V, int dtype) {
   const int epu = dtype == SD_DTYPE_F32 ? 4 : 8;
   const int units = V / epu + 1;
   ArgmaxGeom g;
-  g.cu = 8 * FT;
+  g.cu = AM_UPT * AM_FT;
   g.nch = (units + g.cu - 1) / g.cu;
   if (g.nch > NCH_MAX) {
     g.nch = NCH_MAX;
-    g.cu = ((units + g.nch - 1) / g.nch + FT - 1) / FT * FT;
+    g.cu = ((units + g.nch - 1) / g.nch + AM_FT - 1) / AM_FT * AM_FT;
   }
   return g;
 }
@@ -2388,9 +2402,9 @@ static int check_launch() {
 }
 
 static int launch_argmax(const ArgmaxParams& P, cudaStream_t st) {
-  if (P.dtype == SD_DTYPE_BF16) argmax_kernel<SD_DTYPE_BF16><<<P.nch * P.nvec, FT, 0, st>>>(P);
-  else if (P.dtype == SD_DTYPE_F16) argmax_kernel<SD_DTYPE_F16><<<P.nch * P.nvec, FT, 0, st>>>(P);
-  else argmax_kernel<SD_DTYPE_F32><<<P.nch * P.nvec, FT, 0, st>>>(P);
+  if (P.dtype == SD_DTYPE_BF16) argmax_kernel<SD_DTYPE_BF16><<<P.nch * P.nvec, AM_FT, 0, st>>>(P);
+  else if (P.dtype == SD_DTYPE_F16) argmax_kernel<SD_DTYPE_F16><<<P.nch * P.nvec, AM_FT, 0, st>>>(P);
+  else argmax_kernel<SD_DTYPE_F32><<<P.nch * P.nvec, AM_FT, 0, st>>>(P);
   return check_launch();
 }
 

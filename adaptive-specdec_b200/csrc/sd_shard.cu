@@ -458,7 +458,8 @@ __global__ void p6_kernel(const sd_shard_args a, Geo g, const int64_t* recv, con
 
 // ---- greedy: per target vector the shard argmax, then the decision ----------
 // key = (fkey(x) << 31) | (0x7FFFFFFF - j): the int64 maximum over shards is
-// the largest value at its first index (NaN above +inf, as the fused argmax)
+// the largest value at its first index (every NaN, whatever its sign bit, takes
+// the largest key, as in the fused argmax)
 __global__ void __launch_bounds__(NT) g1_kernel(const sd_shard_args a, Geo g, int64_t* send) {
   __shared__ unsigned long long red[32];
   const int v = blockIdx.x;                            // b * (k + 1) + i
@@ -467,8 +468,9 @@ __global__ void __launch_bounds__(NT) g1_kernel(const sd_shard_args a, Geo g, in
                   (b * a.tgt_bs + i * a.tgt_ps) * (g.dtype == SD_DTYPE_F32 ? 4 : 2);
   unsigned long long best = 0ull;
   for (int j = threadIdx.x; j < g.Vr; j += NT) {
+    const float xv = load_logit(x, g.dtype, j);
     const unsigned long long kk =
-        ((unsigned long long)fkey(load_logit(x, g.dtype, j)) << 31) |
+        ((unsigned long long)(xv != xv ? 0xFFFFFFFFu : fkey(xv)) << 31) |
         (unsigned long long)(0x7FFFFFFF - (g.v0 + j));
     best = kk > best ? kk : best;
   }

@@ -122,7 +122,9 @@ class NumpyShardBackend:
                 x = self.tgt[b, i].astype(F32)
                 if x.size == 0:
                     continue
-                keys = (_fkey(x).astype(np.uint64) << np.uint64(31)) | (
+                # every NaN (either sign bit) counts as the maximum
+                fk = np.where(np.isnan(x), np.uint32(0xFFFFFFFF), _fkey(x))
+                keys = (fk.astype(np.uint64) << np.uint64(31)) | (
                     np.uint64(0x7FFFFFFF) - (self.v0 + np.arange(x.size)).astype(np.uint64))
                 out[b * (self.k + 1) + i] = np.int64(keys.max())
         return out

@@ -201,6 +201,28 @@ def test_boundary_tie_class_index_order():
     assert others.size > 0 and np.array_equal(others, expect)
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_greedy_argmax_ties_nan_and_alignment(dt):
+    """Greedy (T = 0) picks the first index of the maximum, NaN counting as the
+    maximum and -0 equal to +0, on rows whose starts fall at different 16-byte
+    alignments (unaligned head and tail elements)."""
+    V = 50000
+    g = torch.Generator().manual_seed(9)
+    base = torch.randn(7, V + 5, generator=g) * 3
+    x = base[:, 3:3 + V]                              # row stride V + 5: varied alignment
+    x[1, [40000, 17, 30000]] = 50.0                   # ties in different chunks
+    x[2, 25000] = float("nan"); x[2, 30000] = float("nan"); x[2, 100] = 60.0
+    x[3] = 0.0; x[3, ::3] = -0.0                      # one tie class of zeros
+    x[4] = float("-inf")
+    x[5, 0] = 70.0; x[5, V - 1] = 70.0                # head / tail tie
+    x[6, V - 2] = 80.0                                # maximum in the tail
+    xd = base.to(DEV, dt)[:, 3:3 + V]
+    got = _np(S.to_probs(xd, 0.0)).argmax(-1)
+    want = np.argmax(xd.float().cpu().numpy(), -1)
+    np.testing.assert_array_equal(got, want)
+    assert list(want[1:]) == [17, 25000, 0, 0, 0, V - 2]
+
+
 # ---------------------------------------------------------------------------
 # draft step and the fp32-probability utilities
 # ---------------------------------------------------------------------------
