@@ -32,6 +32,7 @@ namespace sd {
 namespace shard {
 
 constexpr int NT = 256;                   // threads per CTA
+constexpr int PSPLIT = 8;                 // CTAs per row of the per-row phases (P4b, P5)
 constexpr int NB = 128;                   // depth bins
 constexpr float BPU = 8.f;                // bins per base-2 unit (window 16 units)
 constexpr int CAP = SD_SHARD_BOUNDARY_CAP;
@@ -112,15 +113,55 @@ __device__ __forceinline__ float pprime(const Vec& s, float d, int64_t j) {
   return kept ? __fdiv_rn(p, s.zf) : 0.f;
 }
 
+// Calls f(j, x_j) for every element j < n of a logits slice (bf16, fp16 or
+// fp32), a block's threads striding over it: the scalar head up to the first
+// 16-byte boundary, then 16-byte units (8 or 4 elements per load), then the
+// scalar tail.  The order of the calls is unspecified.
+template <typename F>
+__device__ __forceinline__ void slice_for_each(const void* x, int dtype, int n, F&& f) {
+  const int esz = dtype == SD_DTYPE_F32 ? 4 : 2;
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(x);
+  int head = (int)(((16u - (uint32_t)(addr & 15u)) & 15u) / (uint32_t)esz);
+  if ((addr & (uintptr_t)(esz - 1)) != 0 || head > n) head = n;   // (elements are aligned)
+  const int epu = 16 / esz;
+  const int nunits = (n - head) / epu;
+  const int tail0 = head + nunits * epu;
+  for (int j = threadIdx.x; j < head; j += NT) f(j, load_logit(x, dtype, j));
+  const uint4* body = reinterpret_cast<const uint4*>(static_cast<const char*>(x) + (size_t)head * esz);
+  if (esz == 4) {
+    for (int u = threadIdx.x; u < nunits; u += NT) {
+      const uint4 w = __ldg(body + u);
+      const int j0 = head + u * 4;
+      f(j0, __uint_as_float(w.x));
+      f(j0 + 1, __uint_as_float(w.y));
+      f(j0 + 2, __uint_as_float(w.z));
+      f(j0 + 3, __uint_as_float(w.w));
+    }
+  } else {
+#pragma unroll 2
+    for (int u = threadIdx.x; u < nunits; u += NT) {
+      const uint4 w = __ldg(body + u);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+      const int j0 = head + u * 8;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f(j0 + e, bits16_to_float((ww[e >> 1] >> (16 * (e & 1))) & 0xFFFFu, dtype));
+    }
+  }
+  for (int j = tail0 + threadIdx.x; j < n; j += NT) f(j, load_logit(x, dtype, j));
+}
+
 // ---- P1: shard maximum of d and the probe's d ------------------------------
 __global__ void __launch_bounds__(NT) p1_kernel(const sd_shard_args a, Geo g, Msg1* send) {
   __shared__ float red[32];
   const int v = blockIdx.x;
   int b, set, pos;
   const void* x = vec_base(a, g, v, &b, &set, &pos);
+  // max_j fl(x_j / T) = fl(max_j x_j / T): dividing by T > 0 and rounding are
+  // monotone, so one division after the maximum of the logits
   float mx = -INFINITY;
-  for (int j = threadIdx.x; j < g.Vr; j += NT) mx = fmaxf(mx, scaled_logit(load_logit(x, g.dtype, j), g.T));
+  slice_for_each(x, g.dtype, g.Vr, [&](int, float xv) { mx = fmaxf(mx, xv); });
   mx = block_max(mx, red, -INFINITY);
+  mx = scaled_logit(mx, g.T);
   if (threadIdx.x == 0) {
     const int64_t xp = probe_of(a, g, b, pos);
     float dx = __int_as_float(0x7FC00000);             // NaN: not held here
@@ -143,15 +184,15 @@ __global__ void __launch_bounds__(NT) p2_kernel(const sd_shard_args a, Geo g, co
   for (int i = threadIdx.x; i < NB; i += NT) bins[i] = 0.0;
   __syncthreads();
   double s = 0.0;
-  for (int j = threadIdx.x; j < g.Vr; j += NT) {
-    const float t = __fsub_rn(scaled_logit(load_logit(x, g.dtype, j), g.T), m);
+  slice_for_each(x, g.dtype, g.Vr, [&](int, float xv) {
+    const float t = __fsub_rn(scaled_logit(xv, g.T), m);
     const float e = expf(t);
     s += (double)e;
     if (g.truncate) {
       const int bin = depth_bin(t);
       if (bin < NB) atomicAdd(&bins[bin], (double)e);
     }
-  }
+  });
   s = block_sum(s, red);
   __syncthreads();
   double* out = send + (size_t)v * (1 + NB);
@@ -210,8 +251,8 @@ __global__ void __launch_bounds__(NT) p3_kernel(const sd_shard_args a, Geo g, co
   const int lo = lo_s, hi = hi_s;
   Msg3& o = send[v];
   double pre = 0.0;
-  for (int j = threadIdx.x; j < g.Vr; j += NT) {
-    const float t = __fsub_rn(scaled_logit(load_logit(x, g.dtype, j), g.T), m);
+  slice_for_each(x, g.dtype, g.Vr, [&](int j, float xv) {
+    const float t = __fsub_rn(scaled_logit(xv, g.T), m);
     const int bin = depth_bin(t);
     if (bin < lo) {
       pre += (double)__fmul_rn(expf(t), inv_s);
@@ -220,7 +261,7 @@ __global__ void __launch_bounds__(NT) p3_kernel(const sd_shard_args a, Geo g, co
       const int i = atomicAdd(&cnt, 1);
       if (i < CAP) o.e[i] = pkey(p, (int64_t)g.v0 + j);
     }
-  }
+  });
   pre = block_sum(pre, red);
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -310,8 +351,8 @@ __global__ void __launch_bounds__(NT) p4b_kernel(const sd_shard_args a, Geo g, c
                                                  Row* rows, double* send) {
   __shared__ double red[33];
   __shared__ int pick_s, all_s;
-  const int b = blockIdx.x;
-  if (threadIdx.x == 0) {                              // engine.py:286-294
+  const int b = blockIdx.x, part = blockIdx.y;         // part: 1/PSPLIT of the slice
+  if (threadIdx.x == 0) {                              // engine.py:286-294 (every part; part 0 writes)
     bool alive = a.alive ? a.alive[b] != 0 : true;
     int n = 0;
     for (int i = 0; i < g.k; ++i) {
@@ -329,9 +370,11 @@ __global__ void __launch_bounds__(NT) p4b_kernel(const sd_shard_args a, Geo g, c
     }
     const int all_acc = n == g.k;
     const int pick = min(n, g.k - 1);
-    rows[b].n_acc = n;
-    rows[b].pick = pick;
-    rows[b].all_acc = all_acc;
+    if (part == 0) {
+      rows[b].n_acc = n;
+      rows[b].pick = pick;
+      rows[b].all_acc = all_acc;
+    }
     pick_s = pick;
     all_s = all_acc;
   }
@@ -344,7 +387,9 @@ __global__ void __launch_bounds__(NT) p4b_kernel(const sd_shard_args a, Geo g, c
   const void* xq = vec_base(a, g, vq, &bb, &set, &pos);
   const Vec sp = st[vp], sq = st[vq];
   double R = 0.0, Pm = 0.0;
-  for (int j = threadIdx.x; j < g.Vr; j += NT) {
+  const int seg = (g.Vr + PSPLIT - 1) / PSPLIT;
+  const int j1 = min(g.Vr, (part + 1) * seg);
+  for (int j = part * seg + threadIdx.x; j < j1; j += NT) {
     const int64_t gj = (int64_t)g.v0 + j;
     const float pj = pprime(sp, scaled_logit(load_logit(xp, g.dtype, j), g.T), gj);
     float r = pj;
@@ -358,94 +403,140 @@ __global__ void __launch_bounds__(NT) p4b_kernel(const sd_shard_args a, Geo g, c
   R = block_sum(R, red);
   __syncthreads();
   Pm = block_sum(Pm, red);
-  if (threadIdx.x == 0) {
-    send[2 * b] = R;
-    send[2 * b + 1] = Pm;
+  if (threadIdx.x == 0) {                              // send was zeroed before the launch
+    atomicAdd(&send[2 * b], R);
+    atomicAdd(&send[2 * b + 1], Pm);
   }
 }
 
 // ---- P5: per row, the shard that holds the draw walks its slice -------------
-__global__ void __launch_bounds__(NT) p5_kernel(const sd_shard_args a, Geo g, const double* recv,
-                                                const Vec* st, const Row* rows, int64_t* send) {
+// The row's draw state on this shard (every thread computes it): mode 1 when
+// this shard's prefix interval holds t = u * total, 2 when nobody's does (t
+// at or past the total: every shard offers its last nonzero index), 0 when
+// another shard holds it; the offset of this shard's prefix; and the two
+// vectors whose masses are drawn from.
+struct Draw {
+  int mode, all_acc, degen;
+  double base, t;
+  const void* xp;
+  const void* xq;
+  Vec sp, sq;
+};
+__device__ __forceinline__ Draw draw_state(const sd_shard_args& a, const Geo& g, const double* recv,
+                                           const Vec* st, const Row* rows, int b) {
+  Draw d;
+  d.all_acc = rows[b].all_acc;
+  double Rt = 0.0;
+  for (int r = 0; r < g.nranks; ++r) Rt += recv[(size_t)r * 2 * g.B + 2 * b];
+  // engine.py:297-303 / sampling.py:85-89: a residual of (near) zero mass
+  // falls back to p; the bonus draw uses p itself
+  d.degen = !d.all_acc && __double2float_rn(Rt) <= 1e-9f;
+  const int use = (d.all_acc || d.degen) ? 1 : 0;
+  double total = 0.0, before = 0.0;
+  for (int r = 0; r < g.nranks; ++r) {
+    const double w = recv[(size_t)r * 2 * g.B + 2 * b + use];
+    if (r < g.rank) before += w;
+    total += w;
+  }
+  const double mine = recv[(size_t)g.rank * 2 * g.B + 2 * b + use];
+  d.t = (double)a.u_res[b] * total;
+  d.mode = (d.t >= total) ? 2 : ((mine > 0.0 && before <= d.t && d.t < before + mine) ? 1 : 0);
+  d.base = before;
+  const int pick = rows[b].pick;
+  const int vp = b * g.per + (d.all_acc ? g.k : pick);
+  const int vq = b * g.per + g.k + 1 + pick;
+  int bb, set, pos;
+  d.xp = vec_base(a, g, vp, &bb, &set, &pos);
+  d.xq = vec_base(a, g, vq, &bb, &set, &pos);
+  d.sp = st[vp];
+  d.sq = st[vq];
+  return d;
+}
+__device__ __forceinline__ float draw_mass(const Draw& d, const Geo& g, int j) {
+  const int64_t gj = (int64_t)g.v0 + j;
+  const float pj = pprime(d.sp, scaled_logit(load_logit(d.xp, g.dtype, j), g.T), gj);
+  if (d.all_acc || d.degen) return pj;
+  const float qj = pprime(d.sq, scaled_logit(load_logit(d.xq, g.dtype, j), g.T), gj);
+  return fmaxf(__fsub_rn(pj, qj), 0.f);
+}
+
+// P5a: grid (B, PSPLIT).  Part p of the slice: its float64 mass and its last
+// index of nonzero mass (-1: none), for the walk of P5b.
+__global__ void __launch_bounds__(NT) p5a_kernel(const sd_shard_args a, Geo g, const double* recv,
+                                                 const Vec* st, const Row* rows, double* segm,
+                                                 int* segl) {
   __shared__ double red[33];
-  __shared__ double base_s, t_s;
-  __shared__ int mode_s, pick_s, all_s, degen_s;
+  __shared__ int lred[32];
+  const int b = blockIdx.x, part = blockIdx.y;
+  const Draw d = draw_state(a, g, recv, st, rows, b);
+  if (d.mode == 0) return;
+  const int seg = (g.Vr + PSPLIT - 1) / PSPLIT;
+  const int j1 = min(g.Vr, (part + 1) * seg);
+  double m = 0.0;
+  int last = -1;
+  for (int j = part * seg + threadIdx.x; j < j1; j += NT) {
+    const float r = draw_mass(d, g, j);
+    m += (double)r;
+    if (r > 0.f) last = j;
+  }
+  m = block_sum(m, red);
+  last = block_max(last, lred, -1);
+  if (threadIdx.x == 0) {
+    segm[b * PSPLIT + part] = m;
+    segl[b * PSPLIT + part] = last;
+  }
+}
+
+// P5b: grid B.  The parts' masses in order locate the part holding the
+// crossing; within it (and after it, should float64 rounding carry the
+// crossing over) the smallest j with base + sum_{i <= j} r_i > t, a float64
+// prefix in chunks of NT; no crossing: the last element of nonzero mass, as
+// the reference's inverse CDF falls back to.
+__global__ void __launch_bounds__(NT) p5b_kernel(const sd_shard_args a, Geo g, const double* recv,
+                                                 const Vec* st, const Row* rows,
+                                                 const double* segm, const int* segl,
+                                                 int64_t* send) {
+  __shared__ double red[33];
   __shared__ int found;
   const int b = blockIdx.x;
-  if (threadIdx.x == 0) {
-    const int all_acc = rows[b].all_acc;
-    double Rt = 0.0;
-    for (int r = 0; r < g.nranks; ++r) Rt += recv[(size_t)r * 2 * g.B + 2 * b];
-    // engine.py:297-303 / sampling.py:85-89: a residual of (near) zero mass
-    // falls back to p; the bonus draw uses p itself
-    const int degen = !all_acc && __double2float_rn(Rt) <= 1e-9f;
-    const int use = (all_acc || degen) ? 1 : 0;
-    double total = 0.0, before = 0.0;
-    for (int r = 0; r < g.nranks; ++r) {
-      const double w = recv[(size_t)r * 2 * g.B + 2 * b + use];
-      if (r < g.rank) before += w;
-      total += w;
-    }
-    const double mine = recv[(size_t)g.rank * 2 * g.B + 2 * b + use];
-    const double t = (double)a.u_res[b] * total;
-    // 1: this shard holds the crossing; 2: nobody does (t at or past the total):
-    // every shard offers its last nonzero index; 0: another shard holds it
-    mode_s = (t >= total) ? 2 : ((mine > 0.0 && before <= t && t < before + mine) ? 1 : 0);
-    base_s = before;
-    t_s = t;
-    pick_s = rows[b].pick;
-    all_s = all_acc;
-    degen_s = degen;
-    found = 0x7FFFFFFF;
-  }
-  __syncthreads();
-  const int mode = mode_s;
-  if (mode == 0) {
+  const Draw d = draw_state(a, g, recv, st, rows, b);
+  if (d.mode == 0) {
     if (threadIdx.x == 0) send[b] = -1;
     return;
   }
-  const int all_acc = all_s, pick = pick_s, degen = degen_s;
-  const int vp = b * g.per + (all_acc ? g.k : pick);
-  const int vq = b * g.per + g.k + 1 + pick;
-  int bb, set, pos;
-  const void* xp = vec_base(a, g, vp, &bb, &set, &pos);
-  const void* xq = vec_base(a, g, vq, &bb, &set, &pos);
-  const Vec sp = st[vp], sq = st[vq];
-  auto mass = [&](int j) -> float {
-    const int64_t gj = (int64_t)g.v0 + j;
-    const float pj = pprime(sp, scaled_logit(load_logit(xp, g.dtype, j), g.T), gj);
-    if (all_acc || degen) return pj;
-    const float qj = pprime(sq, scaled_logit(load_logit(xq, g.dtype, j), g.T), gj);
-    return fmaxf(__fsub_rn(pj, qj), 0.f);
-  };
-  int best = -1;
-  if (mode == 1) {
-    // smallest j with base + sum_{i <= j} r_i > t, float64 prefix in chunks of NT
-    double run = base_s;
-    const double t = t_s;
-    for (int c0 = 0; c0 < g.Vr; c0 += NT) {
-      const int j = c0 + threadIdx.x;
-      const double r = j < g.Vr ? (double)mass(j) : 0.0;
-      double tot;
-      const double ex = block_excl_scan(r, red, &tot);
-      if (r > 0.0 && run + ex + r > t) atomicMin(&found, j);
-      __syncthreads();
-      if (found != 0x7FFFFFFF) break;
-      run += tot;
+  int best = 0x7FFFFFFF;
+  if (d.mode == 1) {
+    const int seg = (g.Vr + PSPLIT - 1) / PSPLIT;
+    double run = d.base;
+    int p0 = PSPLIT;
+    for (int p = 0; p < PSPLIT; ++p) {                 // same order in every thread
+      const double m = segm[b * PSPLIT + p];
+      if (run + m > d.t) { p0 = p; break; }
+      run += m;
+    }
+    if (threadIdx.x == 0) found = 0x7FFFFFFF;
+    __syncthreads();
+    if (p0 < PSPLIT) {
+      for (int c0 = p0 * seg; c0 < g.Vr; c0 += NT) {
+        const int j = c0 + threadIdx.x;
+        const double r = j < g.Vr ? (double)draw_mass(d, g, j) : 0.0;
+        double tot;
+        const double ex = block_excl_scan(r, red, &tot);
+        if (r > 0.0 && run + ex + r > d.t) atomicMin(&found, j);
+        __syncthreads();
+        if (found != 0x7FFFFFFF) break;
+        run += tot;
+      }
     }
     best = found;
   }
-  if (best == 0x7FFFFFFF || mode == 2) {
-    // no crossing here (t at the total, or float64 rounding): the last
-    // element of nonzero mass, as the reference's inverse CDF falls back to
-    int last = -1;
-    for (int j = threadIdx.x; j < g.Vr; j += NT)
-      if (mass(j) > 0.f) last = j;
-    __shared__ int lred[32];
-    last = block_max(last, lred, -1);
-    best = last;
+  if (threadIdx.x == 0) {
+    if (best == 0x7FFFFFFF) {
+      best = -1;
+      for (int p = 0; p < PSPLIT; ++p) best = max(best, segl[b * PSPLIT + p]);
+    }
+    send[b] = best >= 0 ? (int64_t)g.v0 + best : -1;
   }
-  if (threadIdx.x == 0) send[b] = best >= 0 ? (int64_t)g.v0 + best : -1;
 }
 
 // ---- P6: outputs ------------------------------------------------------------
@@ -467,13 +558,12 @@ __global__ void __launch_bounds__(NT) g1_kernel(const sd_shard_args a, Geo g, in
   const char* x = reinterpret_cast<const char*>(a.tgt) +
                   (b * a.tgt_bs + i * a.tgt_ps) * (g.dtype == SD_DTYPE_F32 ? 4 : 2);
   unsigned long long best = 0ull;
-  for (int j = threadIdx.x; j < g.Vr; j += NT) {
-    const float xv = load_logit(x, g.dtype, j);
+  slice_for_each(x, g.dtype, g.Vr, [&](int j, float xv) {
     const unsigned long long kk =
         ((unsigned long long)(xv != xv ? 0xFFFFFFFFu : fkey(xv)) << 31) |
         (unsigned long long)(0x7FFFFFFF - (g.v0 + j));
     best = kk > best ? kk : best;
-  }
+  });
   best = block_max(best, red, 0ull);
   if (threadIdx.x == 0) send[v] = (int64_t)best;
 }
@@ -510,6 +600,7 @@ constexpr size_t STATUS_BYTES = 256;
 
 size_t vec_bytes(int B, int k) { return (size_t)B * (2 * k + 1) * sizeof(Vec); }
 size_t row_bytes(int B) { return (size_t)B * sizeof(Row); }
+size_t seg_bytes(int B) { return ((size_t)B * PSPLIT * (sizeof(double) + sizeof(int)) + 255) & ~(size_t)255; }
 
 int check_args(const sd_shard_args* a, Geo* g) {
   if (!a) return SD_EINVAL;
@@ -543,7 +634,7 @@ extern "C" {
 
 size_t sd_shard_workspace_bytes(int B, int k, int nranks) {
   if (B <= 0 || k < 1 || nranks < 1) return 0;
-  return STATUS_BYTES + vec_bytes(B, k) + row_bytes(B);
+  return STATUS_BYTES + vec_bytes(B, k) + ((row_bytes(B) + 255) & ~(size_t)255) + seg_bytes(B);
 }
 
 size_t sd_shard_send_bytes(int B, int k, int nranks, int greedy, int phase) {
@@ -571,6 +662,9 @@ int sd_shard_phase(const sd_shard_args* args, int phase, const void* recv, void*
   uint32_t* status = reinterpret_cast<uint32_t*>(ws);
   Vec* vs = reinterpret_cast<Vec*>(ws + STATUS_BYTES);
   Row* rows = reinterpret_cast<Row*>(ws + STATUS_BYTES + vec_bytes(g.B, g.k));
+  char* segw = ws + STATUS_BYTES + vec_bytes(g.B, g.k) + ((row_bytes(g.B) + 255) & ~(size_t)255);
+  double* segm = reinterpret_cast<double*>(segw);                 // [B, PSPLIT]
+  int* segl = reinterpret_cast<int*>(segw + (size_t)g.B * PSPLIT * sizeof(double));
   const bool greedy = !(a.temperature > 0.f);
   if (phase < 1 || phase > 6) return SD_EINVAL;
   if (phase > 1 && !recv) return SD_EINVAL;
@@ -603,11 +697,15 @@ int sd_shard_phase(const sd_shard_args* args, int phase, const void* recv, void*
       break;
     case 4:
       p4a_kernel<<<g.nvec, NT, 0, st>>>(g, reinterpret_cast<const Msg3*>(recv), vs, status);
-      p4b_kernel<<<g.B, NT, 0, st>>>(a, g, vs, rows, reinterpret_cast<double*>(send));
+      if (cudaMemsetAsync(send, 0, (size_t)g.B * 2 * sizeof(double), st) != cudaSuccess)
+        return SD_ELAUNCH;
+      p4b_kernel<<<dim3(g.B, PSPLIT), NT, 0, st>>>(a, g, vs, rows, reinterpret_cast<double*>(send));
       break;
     case 5:
-      p5_kernel<<<g.B, NT, 0, st>>>(a, g, reinterpret_cast<const double*>(recv), vs, rows,
-                                    reinterpret_cast<int64_t*>(send));
+      p5a_kernel<<<dim3(g.B, PSPLIT), NT, 0, st>>>(a, g, reinterpret_cast<const double*>(recv), vs,
+                                                   rows, segm, segl);
+      p5b_kernel<<<g.B, NT, 0, st>>>(a, g, reinterpret_cast<const double*>(recv), vs, rows, segm,
+                                     segl, reinterpret_cast<int64_t*>(send));
       break;
     case 6:
       p6_kernel<<<(g.B + 127) / 128, 128, 0, st>>>(a, g, reinterpret_cast<const int64_t*>(recv),
