@@ -113,41 +113,90 @@ __device__ __forceinline__ float pprime(const Vec& s, float d, int64_t j) {
   return kept ? __fdiv_rn(p, s.zf) : 0.f;
 }
 
-// Calls f(j, x_j) for every element j < n of a logits slice (bf16, fp16 or
-// fp32), a block's threads striding over it: the scalar head up to the first
-// 16-byte boundary, then 16-byte units (8 or 4 elements per load), then the
-// scalar tail.  The order of the calls is unspecified.
+// Calls f(j, x_j) for every element j of [j0, j1) of a logits slice (bf16,
+// fp16 or fp32), a block's threads striding over it: scalar elements up to
+// the first 16-byte boundary, then 16-byte units (8 or 4 elements per load),
+// then the scalar tail.  The order of the calls is unspecified.
 template <typename F>
-__device__ __forceinline__ void slice_for_each(const void* x, int dtype, int n, F&& f) {
+__device__ __forceinline__ void slice_range_for_each(const void* x, int dtype, int j0, int j1,
+                                                     F&& f) {
+  if (j1 <= j0) return;
   const int esz = dtype == SD_DTYPE_F32 ? 4 : 2;
-  const uintptr_t addr = reinterpret_cast<uintptr_t>(x);
-  int head = (int)(((16u - (uint32_t)(addr & 15u)) & 15u) / (uint32_t)esz);
-  if ((addr & (uintptr_t)(esz - 1)) != 0 || head > n) head = n;   // (elements are aligned)
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(x) + (uintptr_t)j0 * esz;
+  int head = (int)(((16u - (uint32_t)(a0 & 15u)) & 15u) / (uint32_t)esz);
+  if ((a0 & (uintptr_t)(esz - 1)) != 0 || head > j1 - j0) head = j1 - j0;   // (elements are aligned)
   const int epu = 16 / esz;
-  const int nunits = (n - head) / epu;
-  const int tail0 = head + nunits * epu;
-  for (int j = threadIdx.x; j < head; j += NT) f(j, load_logit(x, dtype, j));
-  const uint4* body = reinterpret_cast<const uint4*>(static_cast<const char*>(x) + (size_t)head * esz);
+  const int nunits = (j1 - j0 - head) / epu;
+  const int b0 = j0 + head, tail0 = b0 + nunits * epu;
+  for (int j = j0 + threadIdx.x; j < b0; j += NT) f(j, load_logit(x, dtype, j));
+  const uint4* body = reinterpret_cast<const uint4*>(static_cast<const char*>(x) + (size_t)b0 * esz);
   if (esz == 4) {
     for (int u = threadIdx.x; u < nunits; u += NT) {
       const uint4 w = __ldg(body + u);
-      const int j0 = head + u * 4;
-      f(j0, __uint_as_float(w.x));
-      f(j0 + 1, __uint_as_float(w.y));
-      f(j0 + 2, __uint_as_float(w.z));
-      f(j0 + 3, __uint_as_float(w.w));
+      const int j = b0 + u * 4;
+      f(j, __uint_as_float(w.x));
+      f(j + 1, __uint_as_float(w.y));
+      f(j + 2, __uint_as_float(w.z));
+      f(j + 3, __uint_as_float(w.w));
     }
   } else {
-#pragma unroll 2
     for (int u = threadIdx.x; u < nunits; u += NT) {
       const uint4 w = __ldg(body + u);
       const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-      const int j0 = head + u * 8;
+      const int j = b0 + u * 8;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) f(j0 + e, bits16_to_float((ww[e >> 1] >> (16 * (e & 1))) & 0xFFFFu, dtype));
+      for (int e = 0; e < 8; ++e) f(j + e, bits16_to_float((ww[e >> 1] >> (16 * (e & 1))) & 0xFFFFu, dtype));
     }
   }
-  for (int j = tail0 + threadIdx.x; j < n; j += NT) f(j, load_logit(x, dtype, j));
+  for (int j = tail0 + threadIdx.x; j < j1; j += NT) f(j, load_logit(x, dtype, j));
+}
+template <typename F>
+__device__ __forceinline__ void slice_for_each(const void* x, int dtype, int n, F&& f) {
+  slice_range_for_each(x, dtype, 0, n, f);
+}
+
+// The same over [j0, j1) of two slices read in step, f(j, a_j, b_j): 16-byte
+// units when both slices sit at the same offset modulo 16 bytes (contiguous
+// logits tensors do), element by element otherwise.
+template <typename F>
+__device__ __forceinline__ void slice2_range_for_each(const void* xa, const void* xb, int dtype,
+                                                      int j0, int j1, F&& f) {
+  if (j1 <= j0) return;
+  const int esz = dtype == SD_DTYPE_F32 ? 4 : 2;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(xa) + (uintptr_t)j0 * esz;
+  const uintptr_t c0 = reinterpret_cast<uintptr_t>(xb) + (uintptr_t)j0 * esz;
+  if ((a0 & 15u) != (c0 & 15u) || (a0 & (uintptr_t)(esz - 1)) != 0) {
+    for (int j = j0 + threadIdx.x; j < j1; j += NT)
+      f(j, load_logit(xa, dtype, j), load_logit(xb, dtype, j));
+    return;
+  }
+  int head = (int)(((16u - (uint32_t)(a0 & 15u)) & 15u) / (uint32_t)esz);
+  if (head > j1 - j0) head = j1 - j0;
+  const int epu = 16 / esz;
+  const int nunits = (j1 - j0 - head) / epu;
+  const int b0 = j0 + head, tail0 = b0 + nunits * epu;
+  for (int j = j0 + threadIdx.x; j < b0; j += NT)
+    f(j, load_logit(xa, dtype, j), load_logit(xb, dtype, j));
+  const uint4* ba = reinterpret_cast<const uint4*>(static_cast<const char*>(xa) + (size_t)b0 * esz);
+  const uint4* bb = reinterpret_cast<const uint4*>(static_cast<const char*>(xb) + (size_t)b0 * esz);
+  for (int u = threadIdx.x; u < nunits; u += NT) {
+    const uint4 wa = __ldg(ba + u), wb = __ldg(bb + u);
+    const uint32_t va[4] = {wa.x, wa.y, wa.z, wa.w}, vb[4] = {wb.x, wb.y, wb.z, wb.w};
+    const int j = b0 + u * epu;
+    if (esz == 4) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) f(j + e, __uint_as_float(va[e]), __uint_as_float(vb[e]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int sh = 16 * (e & 1);
+        f(j + e, bits16_to_float((va[e >> 1] >> sh) & 0xFFFFu, dtype),
+          bits16_to_float((vb[e >> 1] >> sh) & 0xFFFFu, dtype));
+      }
+    }
+  }
+  for (int j = tail0 + threadIdx.x; j < j1; j += NT)
+    f(j, load_logit(xa, dtype, j), load_logit(xb, dtype, j));
 }
 
 // ---- P1: shard maximum of d and the probe's d ------------------------------
@@ -389,16 +438,20 @@ __global__ void __launch_bounds__(NT) p4b_kernel(const sd_shard_args a, Geo g, c
   double R = 0.0, Pm = 0.0;
   const int seg = (g.Vr + PSPLIT - 1) / PSPLIT;
   const int j1 = min(g.Vr, (part + 1) * seg);
-  for (int j = part * seg + threadIdx.x; j < j1; j += NT) {
-    const int64_t gj = (int64_t)g.v0 + j;
-    const float pj = pprime(sp, scaled_logit(load_logit(xp, g.dtype, j), g.T), gj);
-    float r = pj;
-    if (!all_acc) {
-      const float qj = pprime(sq, scaled_logit(load_logit(xq, g.dtype, j), g.T), gj);
-      r = fmaxf(__fsub_rn(pj, qj), 0.f);
-    }
-    R += (double)r;
-    Pm += (double)pj;
+  if (all_acc) {                                       // the bonus draw: p alone
+    slice_range_for_each(xp, g.dtype, part * seg, j1, [&](int j, float xv) {
+      const float pj = pprime(sp, scaled_logit(xv, g.T), (int64_t)g.v0 + j);
+      R += (double)pj;
+      Pm += (double)pj;
+    });
+  } else {
+    slice2_range_for_each(xp, xq, g.dtype, part * seg, j1, [&](int j, float xpv, float xqv) {
+      const int64_t gj = (int64_t)g.v0 + j;
+      const float pj = pprime(sp, scaled_logit(xpv, g.T), gj);
+      const float qj = pprime(sq, scaled_logit(xqv, g.T), gj);
+      R += (double)fmaxf(__fsub_rn(pj, qj), 0.f);
+      Pm += (double)pj;
+    });
   }
   R = block_sum(R, red);
   __syncthreads();
@@ -474,10 +527,20 @@ __global__ void __launch_bounds__(NT) p5a_kernel(const sd_shard_args a, Geo g, c
   const int j1 = min(g.Vr, (part + 1) * seg);
   double m = 0.0;
   int last = -1;
-  for (int j = part * seg + threadIdx.x; j < j1; j += NT) {
-    const float r = draw_mass(d, g, j);
-    m += (double)r;
-    if (r > 0.f) last = j;
+  if (d.all_acc || d.degen) {                          // p alone
+    slice_range_for_each(d.xp, g.dtype, part * seg, j1, [&](int j, float xv) {
+      const float r = pprime(d.sp, scaled_logit(xv, g.T), (int64_t)g.v0 + j);
+      m += (double)r;
+      if (r > 0.f) last = max(last, j);
+    });
+  } else {
+    slice2_range_for_each(d.xp, d.xq, g.dtype, part * seg, j1, [&](int j, float xpv, float xqv) {
+      const int64_t gj = (int64_t)g.v0 + j;
+      const float r = fmaxf(__fsub_rn(pprime(d.sp, scaled_logit(xpv, g.T), gj),
+                                      pprime(d.sq, scaled_logit(xqv, g.T), gj)), 0.f);
+      m += (double)r;
+      if (r > 0.f) last = max(last, j);
+    });
   }
   m = block_sum(m, red);
   last = block_max(last, lred, -1);
