@@ -122,7 +122,7 @@ __device__ __forceinline__ int64_t vec_probe(const VecSet& vs, int set, int row,
 // accept test and its residual / bonus draw (finalize warps).  Outside the
 // nucleus of p the residual max(p - q, 0) is zero, so the draw only walks p's
 // kept elements in index order (q gathered at those indices).
-constexpr int NSW = 15;                  // streaming warps
+constexpr int NSW = 19;                  // streaming warps
 constexpr int ST_N = NSW * 32;           // streaming threads
 constexpr int ST0 = 32;                  // first streaming thread (warp 0 produces)
 constexpr int NCW = 4;                   // finalize warps
@@ -132,7 +132,7 @@ constexpr int HT = FIN0 + CT;            // threads per CTA
 constexpr int GRID_MAX = 160;            // bound on the persistent grid (fallback buffers)
 constexpr int GPS = 4;                   // 16-byte units per streaming lane per ring slot
 constexpr int SLOT = GPS * 16 * ST_N;    // bytes per ring slot (30 KB)
-constexpr int NSLOT = 4;
+constexpr int NSLOT = 3;
 constexpr long long WAIT_CYCLES = 1LL << 32;   // ~2 s at 2 GHz: bound on every wait
 constexpr int LIST_CAP = 3072;           // listed elements per vector
 static_assert(LIST_CAP < 65536, "list-path counts pack into 16 bits");
