@@ -85,76 +85,126 @@ def _cpu_inputs(rows, seed):
     return tgt, drf, xs, ua, ur
 
 
-def _cpu_rows(args):
-    tgt, drf, xs, ua, ur, T, tp = args
-    from oracle import sampling_oracle as O
-    return O.verify(tgt, drf, xs, ua, ur, T, tp, 0)
+def _load_ref_sampling():
+    """The reference's own specdec/sampling.py, from the offline install in
+    baseline/_ref (loaded under its own module name: the package name
+    `specdec` is also this repository's).  None when it is not installed."""
+    import importlib.util
+    path = ROOT / "baseline" / "_ref" / "specdec" / "sampling.py"
+    if not path.exists():
+        return None
+    spec = importlib.util.spec_from_file_location("_ref_specdec_sampling", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 
-def _cpu_vec(args):
-    x, T, tp = args
-    from oracle import sampling_oracle as O
-    return O.to_probs_row(x, T, tp, 0)
+def _ref_inverse_cdf(probs, u):
+    """Smallest j with float64 cumsum(probs)[j] > u * sum (the uniforms-as-
+    tensors stand-in for torch.multinomial, BASELINE's CPU plan)."""
+    import torch
+    c = probs.double().cumsum(-1)
+    tgt = u.double()[:, None] * c[:, -1:]
+    j = (c <= tgt).sum(-1)
+    return j.clamp(max=probs.shape[-1] - 1)
 
 
-def cpu_baseline(mode, rows=64):
-    """Oracle on `rows` rows, one thread; returns (rows/s, seconds)."""
-    T, tp = (0.0, 1.0) if mode == "greedy" else (T_SAMPLE, TOP_P)
-    tgt, drf, xs, ua, ur = _cpu_inputs(rows, seed=11)
+def ref_verify(ref, tgt, drf, xs, ua, ur, T, tp):
+    """One verify round through the reference's to_probs / gather_prob /
+    residual_probs and its accept loop (reference specdec/engine.py:282-303),
+    uniforms passed in as tensors."""
+    import torch
+    B, k1, _ = tgt.shape
+    k = k1 - 1
+    ps = [ref.to_probs(tgt[:, i, :], T, tp) for i in range(k1)]
+    qs = ps[:k] if drf is None else [ref.to_probs(drf[:, i, :], T, tp) for i in range(k)]
+    n_acc = torch.zeros(B, dtype=torch.long)
+    alive = torch.ones(B, dtype=torch.bool)
+    for i in range(k):
+        ratio = ref.gather_prob(ps[i], xs[:, i]) / ref.gather_prob(qs[i], xs[:, i]).clamp_min(1e-10)
+        ok = (ua[:, i] < ratio.clamp(max=1.0)) & alive & (n_acc == i)
+        n_acc = n_acc + ok.long()
+        alive = alive & ok
+    all_acc = n_acc == k
+    pick = n_acc.clamp(max=k - 1)
+    p_stop = torch.stack(ps[:k], 1)[torch.arange(B), pick]
+    q_stop = torch.stack(qs, 1)[torch.arange(B), pick]
+    y_res = _ref_inverse_cdf(ref.residual_probs(p_stop, q_stop), ur)
+    y_bonus = _ref_inverse_cdf(ps[k], ur)
+    return n_acc, torch.where(all_acc, y_bonus, y_res)
+
+
+def _ref_inputs(rows, seed, greedy):
+    import torch
+    tgt, drf, xs, ua, ur = _cpu_inputs(rows, seed)
+    bf = lambda a: torch.from_numpy(a).bfloat16()
+    return (bf(tgt), None if greedy else bf(drf), torch.from_numpy(xs).long(),
+            torch.from_numpy(ua), torch.from_numpy(ur))
+
+
+def ref_rate(mode, rows, budget_s, max_steps, warmup=1):
+    """rows/s of the reference CPU path on `rows`-row batches, all host threads.
+    Returns (rows/s, timed steps, kind, threads)."""
+    import torch
+    greedy = mode == "greedy"
+    T, tp = (0.0, 1.0) if greedy else (T_SAMPLE, TOP_P)
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    ref = _load_ref_sampling()
+    inp = _ref_inputs(rows, 11, greedy)
+    if ref is None:                    # the port, when the reference is not installed
+        from oracle import sampling_oracle as O
+        args = tuple(None if t is None else t.float().numpy() for t in inp)
+        fn = lambda: O.verify(args[0], args[0][:, :K_DRAFT] if greedy else args[1], args[2],
+                              args[3], args[4], T, tp, 0)
+        kind = "port"
+    else:
+        fn = lambda: ref_verify(ref, *inp, T, tp)
+        kind = "reference"
     t0 = time.perf_counter()
-    _cpu_rows((tgt, drf, xs, ua, ur, T, tp))
+    for _ in range(max(1, warmup)):
+        fn()
+    t_step = (time.perf_counter() - t0) / max(1, warmup)
+    steps = max(1, min(max_steps, int(budget_s / max(t_step, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        fn()
     dt = time.perf_counter() - t0
-    return rows / dt, dt
+    return rows * steps / dt, steps, kind, cores
+
+
+def cpu_baseline(mode, rows=16):
+    """The reference CPU path on a bounded 16-row sample, all host threads."""
+    rate, steps, kind, cores = ref_rate(mode, rows, budget_s=15.0, max_steps=8)
+    return rate, steps, kind, cores, rows
 
 
 def reference_arm(a):
-    """--impl reference: the CPU path on all host cores.
-
-    One step verifies one config-2 row: its 9 to_probs vectors (5 target,
-    4 draft; 5 in greedy mode) run in parallel in a spawn process pool, the
-    accept test and the draw follow in the parent.  That bounds every step to
-    tens of milliseconds, so any --steps finishes within minutes.
+    """--impl reference: the reference's own CPU implementation of the path
+    (its specdec/sampling.py to_probs / gather_prob / residual_probs and the
+    accept loop of engine.py:282-303, installed offline into baseline/_ref) on
+    all host threads, one full config-2 batch (B=64) per step.  The number of
+    timed steps is bounded (at most --steps, about a minute of work) so any
+    --steps finishes within minutes; rank 0 only.
     """
-    import multiprocessing as mp
-    import numpy as np
-    from oracle import sampling_oracle as O
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cores = os.cpu_count() or 1
-    greedy = a.mode == "greedy"
-    T, tp = (0.0, 1.0) if greedy else (T_SAMPLE, TOP_P)
-    nrow = 4
-    tgt, drf, xs, ua, ur = _cpu_inputs(nrow, seed=11)
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(cores) as pool:
-        def step(i):
-            r = i % nrow
-            vecs = [tgt[r, j] for j in range(K_DRAFT + 1)]
-            if not greedy:
-                vecs += [drf[r, j] for j in range(K_DRAFT)]
-            probs = pool.map(_cpu_vec, [(v, T, tp) for v in vecs])
-            P = np.stack(probs[:K_DRAFT + 1])[None]
-            Q = np.stack(probs[K_DRAFT + 1:])[None] if not greedy else P[:, :K_DRAFT]
-            O.verify_from_probs(P, Q, xs[r:r + 1], ua[r:r + 1], ur[r:r + 1])
-        for i in range(max(1, a.warmup)):
-            step(i)
-        t0 = time.perf_counter()
-        for i in range(a.steps):
-            step(i)
-        dt = time.perf_counter() - t0
-    rows_s = a.steps / dt
+    rate, steps, kind, cores = ref_rate(a.mode, B, budget_s=60.0, max_steps=a.steps,
+                                        warmup=min(a.warmup, 1))
+    src = ("specdec/sampling.py of the reference (baseline/_ref), torch CPU"
+           if kind == "reference" else "oracle/sampling_oracle.py (reference not installed)")
     print(json.dumps({
-        "impl": "reference", "metric": metric_name(a.mode), "value": rows_s, "unit": "rows/s",
-        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * dt / a.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded config-2 logits)",
-        "config": dict(workload_config(a.mode, 1), rows_per_step=1),
-        "cpu_baseline": {"value": rows_s, "unit": "rows/s", "cores": cores, "kind": "port",
-                         "sample": "one config-2 row per step, its to_probs vectors spread over "
-                                   f"{cores} processes (the reference path restated in "
-                                   "oracle/sampling_oracle.py)"},
-        "e2e": {"value": rows_s, "unit": "rows/s", "h2d_bytes_per_step": 0,
+        "impl": "reference", "metric": metric_name(a.mode), "value": rate, "unit": "rows/s",
+        "n_gpus": a.gpus, "steps": steps, "warmup": min(a.warmup, 1),
+        "ms_per_step": 1e3 * B / rate, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded config-2 logits, bf16 inputs)",
+        "config": workload_config(a.mode, 1),
+        "cpu_baseline": {"value": rate, "unit": "rows/s", "cores": cores, "kind": kind,
+                         "sample": f"{steps} full B=64 verify rounds through {src}, "
+                                   f"{cores} threads"},
+        "e2e": {"value": rate, "unit": "rows/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0}}))
 
 
@@ -619,9 +669,13 @@ def main():
         "clocks": clk.summary(),
     }
     if cpu_rate is not None:
-        line["cpu_baseline"] = {"value": cpu_rate[0], "unit": "rows/s", "cores": 1, "kind": "port",
-                                "sample": f"64 rows of config 2 through oracle/sampling_oracle.py "
-                                          f"({cpu_rate[1]:.1f} s, numpy, one thread)"}
+        rate, steps, kind, cores, rows = cpu_rate
+        line["cpu_baseline"] = {"value": rate, "unit": "rows/s", "cores": cores, "kind": kind,
+                                "sample": f"{steps} batches of {rows} config-2 rows through the "
+                                          "reference's specdec/sampling.py (baseline/_ref, "
+                                          f"torch CPU, {cores} threads)" if kind == "reference"
+                                          else f"{steps} batches of {rows} rows through "
+                                          "oracle/sampling_oracle.py"}
     if rank == 0:
         print(json.dumps(line))
     for g in graphs.values():
