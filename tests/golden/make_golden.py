@@ -193,6 +193,40 @@ def make_verify(S_stable, S_plain):
     np.savez_compressed(HERE / "verify.npz", names=np.array(list(cases)), **flat)
 
 
+def make_verify_cfg2(S_stable, S_plain):
+    """Config 2 at the full Qwen3 vocabulary (V = 151936), 8 rows: sampling at
+    T = 0.7 / top-p 0.9 and greedy, through the reference's own functions.
+    Inputs are regenerated by tests/golden/cfg2_inputs.py from the seed; only
+    draws, uniforms, outputs and a checksum are stored."""
+    sys.path.insert(0, str(HERE))
+    import cfg2_inputs as CI
+    tgt, drf = CI.cfg2_rows()
+    B, k1, V = tgt.shape
+    k = k1 - 1
+    g = torch.Generator().manual_seed(77)
+    out = {"tgt_sum": np.float64(CI.checksum(tgt)), "drf_sum": np.float64(CI.checksum(drf))}
+    for name, T, tp in (("t07_tp09", 0.7, 0.9), ("greedy", 0.0, 1.0)):
+        q_draw = torch.stack([S_stable.to_probs(drf[:, i], max(T, 0.7), 0.9) for i in range(k)], 1)
+        xs = torch.multinomial(q_draw.reshape(-1, V), 1, generator=g).reshape(B, k)
+        if T == 0.0:                                   # greedy rows: half the drafts are the argmax
+            am = tgt[:, :k].argmax(-1)
+            xs = torch.where(torch.rand(B, k, generator=g) < 0.5, am, xs)
+        u_acc = torch.rand(B, k, generator=g)
+        u_res = torch.rand(B, generator=g)
+        n_acc, y, P, Q = ref_verify(S_stable, tgt, drf, xs, u_acc, u_res, T, tp, 0)
+        n_acc_p, y_p, _, _ = ref_verify(S_plain, tgt, drf, xs, u_acc, u_res, T, tp, 0)
+        bi = torch.arange(B)[:, None]
+        pi = torch.arange(k)[None, :]
+        out.update({f"{name}__xs": xs.numpy(), f"{name}__u_acc": u_acc.numpy(),
+                    f"{name}__u_res": u_res.numpy(), f"{name}__n_acc": n_acc.numpy(),
+                    f"{name}__y": y.numpy(), f"{name}__n_acc_plain": n_acc_p.numpy(),
+                    f"{name}__y_plain": y_p.numpy(),
+                    f"{name}__px": P[bi, pi, xs].numpy(), f"{name}__qx": Q[bi, pi, xs].numpy(),
+                    f"{name}__nkeep_p": (P > 0).sum(-1).numpy(),
+                    f"{name}__nkeep_q": (Q > 0).sum(-1).numpy()})
+    np.savez_compressed(HERE / "verify_cfg2.npz", **out)
+
+
 def make_kvcache(K):
     """RaggedCache length bookkeeping (kvcache.py:165-202) and mask (:138-162)."""
     c = K.RaggedCache(2, 3, 32, torch.device("cpu"))
@@ -274,6 +308,7 @@ def main():
     make_to_probs(stable, sampling)
     make_residual(sampling)
     make_verify(stable, sampling)
+    make_verify_cfg2(stable, sampling)
     make_kvcache(kvcache)
     make_controller(controller)
     for p in sorted(HERE.glob("*.*")):

@@ -106,3 +106,23 @@ def test_bf16_helpers_round_trip():
     y = O.bf16_bits_to_f32(b)
     assert np.all(np.abs(y - x) <= np.abs(x) * 2 ** -8)
     np.testing.assert_array_equal(O.f32_to_bf16_bits(y), b)
+
+
+def test_verify_matches_reference_at_full_vocab():
+    """Config 2 at V = 151936 (8 rows): the oracle against the reference's own
+    to_probs / accept loop outputs (tests/golden/verify_cfg2.npz)."""
+    from tests.golden import cfg2_inputs as CI
+    z = _load("verify_cfg2.npz")
+    tgt, drf = CI.cfg2_rows()
+    assert CI.checksum(tgt) == float(z["tgt_sum"]) and CI.checksum(drf) == float(z["drf_sum"]), \
+        "config-2 input generator changed: regenerate the fixture"
+    tgt, drf = tgt.numpy(), drf.numpy()
+    for name, T, tp in (("t07_tp09", 0.7, 0.9), ("greedy", 0.0, 1.0)):
+        xs, ua, ur = z[name + "__xs"], z[name + "__u_acc"], z[name + "__u_res"]
+        n, y, d = O.verify(tgt, drf, xs, ua, ur, T, tp, 0, return_details=True)
+        ok = (d["acc_margin"] > 1e-6) & (d["cdf_margin"] > 1e-6) & (d["topp_margin"] > 1e-6)
+        assert ok.mean() >= 0.75, name
+        np.testing.assert_array_equal(n[ok], z[name + "__n_acc"][ok], err_msg=name)
+        np.testing.assert_array_equal(y[ok], z[name + "__y"][ok], err_msg=name)
+        np.testing.assert_allclose(d["px"], z[name + "__px"], rtol=REL, atol=1e-30, err_msg=name)
+        np.testing.assert_allclose(d["qx"], z[name + "__qx"], rtol=REL, atol=1e-30, err_msg=name)

@@ -108,6 +108,35 @@ def cfg2():
     return tgt, drf, xs.reshape(64, 4), ua, ur
 
 
+def test_cfg2_reference_golden_full_vocab():
+    """Config 2 at V = 151936 against outputs the reference's own to_probs and
+    accept loop produced (tests/golden/verify_cfg2.npz, 8 rows; sampling at
+    T = 0.7 / top-p 0.9 and greedy).  Rows inside the contract's 1e-6
+    exemption margins (computed by the oracle) may differ."""
+    from tests.golden import cfg2_inputs as CI
+    z = np.load(GOLDEN / "verify_cfg2.npz")
+    tgt, drf = CI.cfg2_rows()
+    assert CI.checksum(tgt) == float(z["tgt_sum"]), "input generator changed"
+    td, dd = tgt.to(DEV, torch.bfloat16), drf.to(DEV, torch.bfloat16)
+    for name, T, tp in (("t07_tp09", 0.7, 0.9), ("greedy", 0.0, 1.0)):
+        xs = torch.from_numpy(z[name + "__xs"]).to(DEV)
+        ua = torch.from_numpy(z[name + "__u_acc"]).to(DEV)
+        ur = torch.from_numpy(z[name + "__u_res"]).to(DEV)
+        n_k, y_k, px_k, qx_k = S.verify_sample(td, dd, xs, ua, ur, T, tp, return_probs=True)
+        _, _, d = O.verify(tgt.numpy(), drf.numpy(), z[name + "__xs"], z[name + "__u_acc"],
+                           z[name + "__u_res"], T, tp, 0, return_details=True)
+        ok = _ok(d)
+        assert ok.mean() >= 0.75, name
+        n_k, y_k = n_k.cpu().numpy(), y_k.cpu().numpy()
+        np.testing.assert_array_equal(n_k[ok], z[name + "__n_acc"][ok], err_msg=name)
+        np.testing.assert_array_equal(y_k[ok], z[name + "__y"][ok], err_msg=name)
+        if T > 0:
+            np.testing.assert_allclose(px_k.cpu().numpy()[ok], z[name + "__px"][ok], rtol=2e-6,
+                                       atol=1e-30, err_msg=name)
+            np.testing.assert_allclose(qx_k.cpu().numpy()[ok], z[name + "__qx"][ok], rtol=2e-6,
+                                       atol=1e-30, err_msg=name)
+
+
 def test_cfg2_sampling_parity(cfg2):
     tgt, drf, xs, ua, ur = cfg2
     n_k, y_k, ok = _check_verify(tgt, drf, xs, ua, ur, 0.7, 0.9, 0, max_exempt=0.05, tag="cfg2")
@@ -265,11 +294,17 @@ def _tv(a, b):
 
 
 def test_rejection_rule_is_lossless():
+    """G1 part A on the kernels (reference tests/test_rejection_sampling.py:82-126):
+    the first emitted token follows p (TV < 0.01 over 200k trials), and the
+    three negative controls are detected (TV > 0.02): skipping the accept
+    test, resampling from p instead of the residual, and drafting with a
+    different top-p than the one the accept test uses."""
     V, N = 16, 200_000
     g = torch.Generator().manual_seed(0)
     lp = torch.randn(1, V, generator=g) * 1.5
     lq = torch.randn(1, V, generator=g) * 1.5
-    for (tp, lq_use) in ((1.0, lq), (0.9, lp + torch.randn(1, V, generator=g) * 0.8)):
+    lq_close = lp + torch.randn(1, V, generator=g) * 0.8     # a plausible draft model
+    for (tp, lq_use) in ((1.0, lq), (0.9, lq_close)):
         p = O.to_probs(lp.numpy(), 1.0, tp)[0]
         tgt = torch.cat([lp, lp]).unsqueeze(0).expand(N, 2, V).contiguous().to(DEV)
         drf = lq_use.unsqueeze(0).expand(N, 1, V).contiguous().to(DEV)
@@ -281,7 +316,53 @@ def test_rejection_rule_is_lossless():
         first = torch.where(n == 1, x, y).cpu().numpy()
         emp = np.bincount(first, minlength=V) / N
         assert _tv(emp, p) < 0.01, f"top_p={tp}: TV={_tv(emp, p):.4f}"
-        # negative control: skipping the accept test emits x ~ q
+        # control 1: skipping the accept test emits x ~ q
         bad = np.bincount(x.cpu().numpy(), minlength=V) / N
-        if tp == 1.0:
-            assert _tv(bad, p) > 0.02
+        assert _tv(bad, p) > 0.02, f"top_p={tp}: skip-accept control TV={_tv(bad, p):.4f}"
+        # control 2: on a rejection, resample from p instead of the residual
+        yp, _ = S.draft_sample(tgt[:, 0], ur, 1.0, tp)
+        bad2 = np.bincount(torch.where(n == 1, x, yp).cpu().numpy(), minlength=V) / N
+        assert _tv(bad2, p) > 0.02, f"top_p={tp}: resample-from-p control TV={_tv(bad2, p):.4f}"
+    # control 3: draft drawn with top-p 0.5, accept test and residual with 0.9
+    p = O.to_probs(lp.numpy(), 1.0, 0.9)[0]
+    q_right = O.to_probs(lq_close.numpy(), 1.0, 0.9)[0]
+    assert np.minimum(p, q_right).sum() > 0.2, "control instance must be non-degenerate"
+    tgt = torch.cat([lp, lp]).unsqueeze(0).expand(N, 2, V).contiguous().to(DEV)
+    drf = lq_close.unsqueeze(0).expand(N, 1, V).contiguous().to(DEV)
+    gd = torch.Generator(device=DEV).manual_seed(11)
+    xm, _ = S.draft_sample(drf[:, 0], torch.rand(N, generator=gd, device=DEV), 1.0, 0.5)
+    ua = torch.rand(N, 1, generator=gd, device=DEV)
+    ur = torch.rand(N, generator=gd, device=DEV)
+    n, y = S.verify_sample(tgt, drf, xm.view(N, 1), ua, ur, 1.0, 0.9)
+    emp = np.bincount(torch.where(n == 1, xm, y).cpu().numpy(), minlength=V) / N
+    assert _tv(emp, p) > 0.02, f"mismatched top-p control TV={_tv(emp, p):.4f}"
+
+
+def _vec_stats(B, nvec, V, dev):
+    """The per-vector stats records the last sampling call on this stream
+    left at the start of its workspace (48-byte records after the 256-byte
+    status word): fb_why is the 11th int32."""
+    from specdec import _lib as L
+    ws = L.workspaces.get(L.lib().sd_sampling_workspace_bytes(B, nvec, V, 2), dev)
+    return ws[256:256 + nvec * 48].cpu().numpy().view(np.int32).reshape(nvec, 12)
+
+
+def test_histogram_fallback_runs_and_is_exact():
+    """Flat distributions (T = 2, top-p 0.9 on N(0, 1) logits, V = 4096) put
+    more elements inside the list window than the list holds, so every vector
+    must take the exact histogram path (VecStats.fb_why != 0); the results
+    stay bit-exact against the oracle.  Inputs come from the CPU generator
+    (an instance checked to have no row inside the exemption margins)."""
+    B, k, V, T, tp = 8, 2, 4096, 2.0, 0.9
+    g = torch.Generator().manual_seed(21)
+    tgt = (torch.randn(B, k + 1, V, generator=g)).bfloat16()
+    drf = (tgt[:, :k].float() + 1.0 * torch.randn(B, k, V, generator=g)).bfloat16()
+    q = O.to_probs(drf.float().reshape(-1, V).numpy(), T, tp)
+    u = np.random.default_rng(3).random(B * k, dtype=np.float32)
+    xs = O.sample_inverse_cdf(q, u).reshape(B, k)
+    ua = torch.from_numpy(np.random.default_rng(5).random((B, k), dtype=np.float32))
+    ur = torch.from_numpy(np.random.default_rng(6).random(B, dtype=np.float32))
+    _check_verify(tgt.to(DEV), drf.to(DEV), torch.from_numpy(xs).to(DEV), ua.to(DEV), ur.to(DEV),
+                  T, tp, 0, max_exempt=0.25, tag="flat")
+    st = _vec_stats(B, B * (2 * k + 1), V, torch.device(DEV, torch.cuda.current_device()))
+    assert (st[:, 10] != 0).all(), f"fallback reasons {st[:, 10].tolist()}"
