@@ -17,6 +17,7 @@ import torch
 from specdec import _lib as L
 
 IMPL = "specdec_b200"
+PREFILL_SDPA_MIN = 64          # prefills longer than this (fresh cache) use torch SDPA
 _ATTN_DTYPES = {torch.bfloat16: 2, torch.float32: 0}
 
 
@@ -72,6 +73,17 @@ def hf_attention(module, query, key, value, attention_mask, dropout=0.0, scaling
     """transformers AttentionInterface function for RaggedCache buffers."""
     cache = getattr(key, "_sd_cache", None)
     if cache is not None:
+        q_len = query.shape[2]
+        if (cache.valid is not None and q_len > PREFILL_SDPA_MIN and cache._host_valid
+                and int(cache._host.max()) == 0):
+            # right-padded prefill of a fresh cache (every row at length 0):
+            # plain causal attention over the q new keys; a real token i < valid[b]
+            # only sees keys s <= i, so the padding never reaches it.  Prefill is
+            # outside the verify round; torch's SDPA (flash / cuDNN) runs it.
+            out = torch.nn.functional.scaled_dot_product_attention(
+                query, key[:, :, :q_len], value[:, :, :q_len], is_causal=True, scale=scaling,
+                enable_gqa=True)
+            return out.transpose(1, 2), None
         out = verify_attention(query, key, value, cache.lengths, valid=cache.valid, scale=scaling)
         return out, None
     # a forward without a RaggedCache: causal self-attention over the given

@@ -243,7 +243,9 @@ class SpecDecodeEngine:
         """Forward `tokens` [B, q] against `cache`.
 
         Returns logits [B, q, V], or [B, V] at per-row positions `rows_last`
-        (the LM head then runs on B hidden states only).
+        (the LM head then runs on B hidden states only).  A model carrying a
+        ``specdec_head(hidden, ids)`` callable gets its logits from it instead
+        of ``lm_head``; ``ids`` are the input tokens at the same positions.
         """
         q = tokens.shape[1]
         mask = cache.attn_mask(q, model.dtype, valid=valid)
@@ -254,7 +256,14 @@ class SpecDecodeEngine:
                              cache_position=cache.cache_position(q),
                              use_cache=True).last_hidden_state
         if rows_last is not None:
-            hidden = hidden[torch.arange(hidden.shape[0], device=hidden.device), rows_last]
+            rows = torch.arange(hidden.shape[0], device=hidden.device)
+            hidden = hidden[rows, rows_last]
+            tokens = tokens[rows, rows_last]
+        head = getattr(model, "specdec_head", None)
+        if head is not None:
+            # a replacement LM head that also sees the token each hidden state
+            # was computed at (the config-5 benchmark's shared-prior drafts)
+            return head(hidden, tokens)
         return model.lm_head(hidden)
 
     def _range(self, name):

@@ -45,8 +45,15 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="sample",
-                    choices=["sample", "greedy", "attn", "vshard", "vshard-greedy", "engine"])
-    ap.add_argument("--new-tokens", type=int, default=256, help="--mode engine: tokens per row")
+                    choices=["sample", "greedy", "attn", "vshard", "vshard-greedy", "engine",
+                             "adaptive"])
+    ap.add_argument("--new-tokens", type=int, default=None,
+                    help="--mode engine / adaptive: tokens per row (256 / 512)")
+    ap.add_argument("--rows", type=int, default=8, help="--mode adaptive: rows per GPU")
+    ap.add_argument("--beta-hi", type=float, default=48.0,
+                    help="--mode adaptive: shared-prior strength of the high-agreement phase")
+    ap.add_argument("--beta-lo", type=float, default=5.0,
+                    help="--mode adaptive: shared-prior strength of the low-agreement phase")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-rows", type=int, default=64, help="--mode attn: rows (config 3: 64)")
     return ap.parse_args()
@@ -291,6 +298,24 @@ def attn_bench(a):
     live = int((lens + ql).sum())
     bytes_call = live * Hkv * D * 2 * 2 + 2 * q.numel() * 2
     flops_call = sum(4 * Hq * ql * (int(n) + (ql + 1) // 2) * D for n in lens)
+    # correctness before timing: eight rows spread over the length range
+    # against the fp32 rule (key s visible to query j of row b iff
+    # s <= len[b] + j); a mismatch aborts the bench
+    A.verify_attention(q, kc, vc, lens_d, out=out)
+    torch.cuda.synchronize(dev)
+    rows = sorted(range(B), key=lambda b: int(lens[b]))[::max(1, B // 8)][:8]
+    worst = 0.0
+    for b in rows:
+        n = int(lens[b]) + ql
+        kf = kc[b, :, :n].float().repeat_interleave(Hq // Hkv, dim=0)
+        vf = vc[b, :, :n].float().repeat_interleave(Hq // Hkv, dim=0)
+        sc = torch.einsum("hqd,hkd->hqk", q[b].float(), kf) * D ** -0.5
+        lim = int(lens[b]) + torch.arange(ql, device=dev).view(1, ql, 1)
+        sc = sc.masked_fill(torch.arange(n, device=dev).view(1, 1, n) > lim, float("-inf"))
+        ref = torch.einsum("hqk,hkd->qhd", torch.softmax(sc, -1), vf)
+        worst = max(worst, float((out[b].float() - ref).abs().max()))
+    if not worst < 3e-2:
+        raise SystemExit(f"verify attention differs from the fp32 rule: max abs error {worst}")
     s = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(s):
         for _ in range(max(3, a.warmup)):
@@ -317,6 +342,8 @@ def attn_bench(a):
         "config": {"workload": "config 3 verify attention, one layer" + ("" if B == 64 else
                    f" ({B} rows)"), "rows": B, "Hq": Hq,
                    "Hkv": Hkv, "head_dim": D, "queries": ql, "live_keys": live,
+                   "checked": f"8 rows vs the fp32 mask rule before timing, max abs error "
+                              f"{worst:.2e}",
                    "l2": "one layer reads >1 GB of K/V (> 126 MB L2)"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                      "frac": gbs / peak, "tflops": flops_call / (ms * 1e-3) / 1e12,
@@ -409,6 +436,186 @@ def vshard_bench(a):
         dist.destroy_process_group()
 
 
+class _NoTok:
+    """Tokenizer stand-in: random-init models have no end-of-sequence token."""
+    eos_token_id = None
+
+
+def _qwen_pair(dev):
+    """Random-init bf16 models (N(0, 0.02), no checkpoints offline): the
+    Qwen3-8B target shape (36 layers, 4096 hidden, 32/8 heads x 128, FFN 12288,
+    V 151936, RMSNorm, rope theta 1e6) and the Qwen3-0.6B draft shape (28
+    layers, 1024 hidden, 16/8 heads x 128, FFN 3072, tied embeddings)."""
+    import torch
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    common = dict(vocab_size=VOCAB, head_dim=128, num_key_value_heads=8, rope_theta=1e6,
+                  max_position_embeddings=16384, rms_norm_eps=1e-6, initializer_range=0.02)
+    tcfg = Qwen3Config(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
+                       num_attention_heads=32, tie_word_embeddings=False, **common)
+    dcfg = Qwen3Config(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                       num_attention_heads=16, tie_word_embeddings=True, **common)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        target = Qwen3ForCausalLM(tcfg).to(torch.bfloat16).eval()
+        draft = Qwen3ForCausalLM(dcfg).to(torch.bfloat16).eval()
+    return target, draft
+
+
+class _SharedPrior:
+    """The config-5 agreement knob.  Target logits for the draft positions do
+    not exist when the draft runs, so "mixing the draft toward the target" is
+    realised by a component both models share: each model's logits at a
+    position get beta * z(x) added, where x is the token at that position and
+    z(x) = U[x] @ W is a fixed pseudo-bigram prior (rank 16, N(0, 1) entries).
+    beta = 0 leaves two unrelated random models (acceptance ~0.05); a larger
+    beta makes both distributions follow z, so the draft agrees with the
+    target more often.  beta is a device scalar, read inside the engine's CUDA
+    graphs, and switched between rounds."""
+
+    def __init__(self, dev, r=16, seed=7):
+        import torch
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.U = (torch.randn(VOCAB, r, generator=g, device=dev) / r ** 0.5).to(torch.bfloat16)
+        self.W = torch.randn(r, VOCAB, generator=g, device=dev).to(torch.bfloat16)
+        self.beta = torch.zeros(1, dtype=torch.bfloat16, device=dev)
+
+    def head(self, lm_head):
+        def f(hidden, ids):
+            return lm_head(hidden) + self.beta * (self.U[ids] @ self.W)
+        return f
+
+
+class _AlphaSchedule:
+    """Controller proxy for config 5: delegates k to the wrapped controller and
+    switches the shared-prior strength every `period` emitted tokens per row
+    (high agreement first), keeping per-phase acceptance counts."""
+
+    def __init__(self, ctrl, prior, betas, period=64):
+        self.ctrl, self.prior, self.betas, self.period = ctrl, prior, betas, period
+        self.tokens = 0.0
+        self.phase = 0
+        self.acc = [0, 0]
+        self.prop = [0, 0]
+        self.offered = [0, 0]
+        self.k_hist = {}
+        prior.beta.fill_(betas[0])
+
+    def propose_k(self):
+        k = self.ctrl.propose_k()
+        self.k_hist[k] = self.k_hist.get(k, 0) + 1
+        return k
+
+    def should_stop_drafting(self, i, conf):
+        return self.ctrl.should_stop_drafting(i, conf)
+
+    def update(self, k, n_accepted, dt, **kw):
+        self.ctrl.update(k, n_accepted, dt, **kw)
+        self.acc[self.phase] += sum(n_accepted)
+        self.prop[self.phase] += k * len(n_accepted)
+        self.offered[self.phase] += sum(min(k, a + 1) for a in n_accepted)
+        self.tokens += (sum(n_accepted) + len(n_accepted)) / len(n_accepted)
+        phase = int(self.tokens // self.period) % 2
+        if phase != self.phase:
+            self.phase = phase
+            self.prior.beta.fill_(self.betas[phase])
+
+
+def adaptive_bench(a):
+    """--mode adaptive: config 5, the adaptive-k serving sweep, rows sharded by
+    GPU (weak scaling: every rank runs its own --rows rows; no collective on
+    the data path, one all-reduce of the results after the timed region).
+
+    Per rank: the config-4 model shapes (random init), --rows rows with prompt
+    lengths uniform in [128, 4096] (random ids, rank-seeded), --new-tokens new
+    tokens per row (default 512 here), T = 0.7 / top-p 0.9, the "ewma"
+    controller choosing k in [1, 8] from its online alpha and cost ratio.  The
+    draft-target agreement alternates every 64 tokens between a high and a
+    low setting of the shared prior (_SharedPrior; --beta-hi / --beta-lo,
+    calibrated for alpha near 0.9 and 0.45).  value = tokens emitted by all
+    ranks / the slowest rank's generate time (CUDA events around generate,
+    max over ranks).  256 rows per GPU do not fit the capacity-padded cache
+    with 4096-token prompts (about 330 GB of K/V); the mode runs any --rows
+    that fits.
+    """
+    import torch
+    import torch.distributed as dist
+    from specdec.controller import make_controller
+    from specdec.engine import SamplingConfig, SpecDecodeEngine
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    target, draft = _qwen_pair(dev)
+    prior = _SharedPrior(dev)
+    target.specdec_head = prior.head(target.lm_head)
+    draft.specdec_head = prior.head(draft.lm_head)
+    rows, new, kmax, pmin, pmax = a.rows, a.new_tokens, 8, 128, 4096
+    eng = SpecDecodeEngine(target, draft, _NoTok(), device=dev,
+                           capacity=pmax + 2 * new + 2 * kmax + 8)
+    g = torch.Generator().manual_seed(1000 + rank)
+    plen = torch.randint(pmin, pmax + 1, (rows,), generator=g)
+    ids = torch.randint(0, VOCAB, (rows, int(plen.max())), generator=g)
+    sp = SamplingConfig(temperature=T_SAMPLE, top_p=TOP_P)
+    betas = (a.beta_hi, a.beta_lo)
+    warm = _AlphaSchedule(make_controller("ewma", k_max=kmax), prior, betas)
+    eng.generate(ids[:, :256], plen.clamp(max=256), 24, sampling=sp, seed=0, controller=warm)
+    ctrl = _AlphaSchedule(make_controller("ewma", k_max=kmax), prior, betas)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index or 0) as clk:
+        e0.record()
+        _, st = eng.generate(ids, plen, new, sampling=sp, seed=1 + rank, controller=ctrl)
+        e1.record()
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    res = torch.tensor([ms, float(st.emitted), float(ctrl.acc[0]), float(ctrl.prop[0]),
+                        float(ctrl.acc[1]), float(ctrl.prop[1]), float(ctrl.offered[0]),
+                        float(ctrl.offered[1])], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = res[:1].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(res, op=dist.ReduceOp.SUM)
+        res[0] = mx[0]
+    ms, emitted = float(res[0]), float(res[1])
+    # alpha as the reference's RunStats.alpha_conditional (accepted / offered
+    # positions) and the acceptance rate (accepted / proposed), per phase
+    alpha_hi = float(res[2] / max(res[6], 1.0))
+    alpha_lo = float(res[4] / max(res[7], 1.0))
+    rate_hi = float(res[2] / max(res[3], 1.0))
+    rate_lo = float(res[4] / max(res[5], 1.0))
+    d = st.to_dict()
+    line = {
+        "metric": "accepted tok/s (config 5: adaptive k, Qwen3-8B / Qwen3-0.6B shapes, "
+                  "rows sharded by GPU)",
+        "value": emitted / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": 1,
+        "warmup": 1, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0,0.02), random prompt ids)",
+        "config": {"workload": "config 5 adaptive-k serving sweep", "rows_per_gpu": rows,
+                   "prompt": f"U[{pmin},{pmax}]", "new_tokens": new, "k_range": [1, kmax],
+                   "controller": "ewma", "temperature": T_SAMPLE, "top_p": TOP_P,
+                   "alpha_switch_tokens": 64, "beta_hi_lo": list(betas),
+                   "parallelism": f"row-sharded x{world}, no collective on the data path"},
+        "alpha_conditional": {"high_phase": alpha_hi, "low_phase": alpha_lo},
+        "acceptance_rate": {"high_phase": rate_hi, "low_phase": rate_lo},
+        "engine_rank0": {key: d[key] for key in ("rounds", "emitted", "acceptance_rate",
+                                                 "mean_accepted_len", "draft_forwards",
+                                                 "target_forwards")},
+        "k_histogram_rank0": {str(kk): v for kk, v in sorted(ctrl.k_hist.items())},
+        "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def engine_bench(a):
     """--mode engine: config 4, the whole speculative round through the engine.
 
@@ -423,32 +630,19 @@ def engine_bench(a):
     events around it (one step = one generate call).
     """
     import torch
-    from transformers import Qwen3Config, Qwen3ForCausalLM
     from specdec.engine import SamplingConfig, SpecDecodeEngine
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    common = dict(vocab_size=VOCAB, head_dim=128, num_key_value_heads=8, rope_theta=1e6,
-                  max_position_embeddings=8192, rms_norm_eps=1e-6, initializer_range=0.02)
-    tcfg = Qwen3Config(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
-                       num_attention_heads=32, tie_word_embeddings=False, **common)
-    dcfg = Qwen3Config(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
-                       num_attention_heads=16, tie_word_embeddings=True, **common)
-    torch.manual_seed(0)
-    with torch.device(dev):
-        target = Qwen3ForCausalLM(tcfg).to(torch.bfloat16).eval()
-        draft = Qwen3ForCausalLM(dcfg).to(torch.bfloat16).eval()
-
-    class _Tok:
-        eos_token_id = None
+    target, draft = _qwen_pair(dev)
 
     Bq, P, k = 32, 512, 4
     new = max(8, a.new_tokens)
     # rows that finish early keep one cache slot per round until the slowest row
     # ends (the reference's rollback leaves k - n_acc with n_acc = 0 for them),
     # so a row can reach P + 2 * new
-    eng = SpecDecodeEngine(target, draft, _Tok(), device=dev, capacity=P + 2 * new + 2 * k + 8,
-                           time_phases=True)
+    eng = SpecDecodeEngine(target, draft, _NoTok(), device=dev,
+                           capacity=P + 2 * new + 2 * k + 8, time_phases=True)
     g = torch.Generator().manual_seed(1)
     ids = torch.randint(0, VOCAB, (Bq, P), generator=g)
     plen = torch.full((Bq,), P, dtype=torch.long)
@@ -503,7 +697,13 @@ def main():
     if a.mode.startswith("vshard"):
         return vshard_bench(a)
     if a.mode == "engine":
+        if a.new_tokens is None:
+            a.new_tokens = 256
         return engine_bench(a)
+    if a.mode == "adaptive":
+        if a.new_tokens is None:
+            a.new_tokens = 512
+        return adaptive_bench(a)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -16,6 +16,7 @@ import pytest
 import torch
 
 from specdec import attention as A
+from specdec import workloads as W
 from specdec.kvcache import RaggedCache
 from tests.golden import GOLDEN
 
@@ -152,6 +153,47 @@ def test_verify_attention_tensor_core_splits_and_caps():
         vc2[b, :, n:] = float("nan")
     out2 = A.verify_attention(q, kc2, vc2, lens, valid=valid, scale=D ** -0.5)
     assert torch.equal(out2, out)
+
+
+def _ref_rows(q, kc, vc, lens, scale, rows):
+    """fp32 attention of the reference's mask rule (key s visible to query j
+    of row b iff s <= lens[b] + j), one row at a time (config-3 sized caches
+    do not fit a dense [B, Hq, q, C] score tensor comfortably)."""
+    B, Hq, ql, D = q.shape
+    g = Hq // kc.shape[1]
+    out = {}
+    for b in rows:
+        n = int(lens[b]) + ql
+        kf = kc[b, :, :n].float().repeat_interleave(g, dim=0)
+        vf = vc[b, :, :n].float().repeat_interleave(g, dim=0)
+        s = torch.einsum("hqd,hkd->hqk", q[b].float(), kf) * scale
+        pos = torch.arange(n, device=q.device).view(1, 1, n)
+        lim = int(lens[b]) + torch.arange(ql, device=q.device).view(1, ql, 1)
+        s = s.masked_fill(pos > lim, float("-inf"))
+        out[b] = torch.einsum("hqk,hkd->qhd", torch.softmax(s, -1), vf)
+    return out
+
+
+def test_verify_attention_config3_shape():
+    """The headline shape of config 3: B = 64 rows, 32 query / 8 kv heads x
+    128, 5 queries, context lengths uniform in [512, 8192] (the bench's
+    seeded lengths), one layer, every row checked against the fp32 rule.
+    This is the stream-K schedule, piece merge and cost-aware split at the
+    size they are timed at."""
+    B, Hq, Hkv, D, ql = 64, 32, 8, 128, 5
+    lens = W.attn_lengths(B, seed=0).to(DEV)
+    C = int(lens.max()) + ql + 3
+    g = torch.Generator(device=DEV).manual_seed(0)
+    q = torch.randn(B, Hq, ql, D, generator=g, device=DEV).to(torch.bfloat16)
+    kc = torch.randn(B, Hkv, C, D, generator=g, device=DEV).to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, C, D, generator=g, device=DEV).to(torch.bfloat16)
+    out = A.verify_attention(q, kc, vc, lens, scale=D ** -0.5)
+    ref = _ref_rows(q, kc, vc, lens, D ** -0.5, range(B))
+    for b in range(B):
+        torch.testing.assert_close(out[b].float(), ref[b], atol=2e-2, rtol=2e-2,
+                                   msg=lambda m: f"row {b} (len {int(lens[b])}): {m}")
+    again = A.verify_attention(q, kc, vc, lens, scale=D ** -0.5)
+    assert torch.equal(again, out)
 
 
 def test_prefill_valid_cap():
