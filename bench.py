@@ -50,6 +50,12 @@ def parse():
     ap.add_argument("--new-tokens", type=int, default=None,
                     help="--mode engine / adaptive: tokens per row (256 / 512)")
     ap.add_argument("--rows", type=int, default=8, help="--mode adaptive: rows per GPU")
+    ap.add_argument("--temperature", type=float, default=T_SAMPLE,
+                    help="--mode sample: temperature (config 2: 0.7)")
+    ap.add_argument("--top-p", type=float, default=TOP_P, help="--mode sample: top-p (config 2: 0.9)")
+    ap.add_argument("--flat", action="store_true",
+                    help="--mode sample: N(0, 1) logits (random-model-like flat rows) instead of "
+                         "config 2's peaked ones")
     ap.add_argument("--beta-hi", type=float, default=48.0,
                     help="--mode adaptive: shared-prior strength of the high-agreement phase")
     ap.add_argument("--beta-lo", type=float, default=5.0,
@@ -59,14 +65,17 @@ def parse():
     return ap.parse_args()
 
 
-def metric_name(mode):
+def metric_name(mode, T=T_SAMPLE, tp=TOP_P, flat=False):
     if mode == "greedy":
         return "verify rows/s (B=64,k=4,V=151936 bf16, greedy)"
-    return "verify rows/s (B=64,k=4,V=151936 bf16, T=0.7 top-p 0.9)"
+    return (f"verify rows/s (B=64,k=4,V=151936 bf16, T={T:g} top-p {tp:g}"
+            + (", flat N(0,1) logits)" if flat else ")"))
 
 
-def workload_config(mode, n):
-    return {"workload": f"config 2 fused verify round, {'greedy' if mode == 'greedy' else 'T=0.7 top-p 0.9'}",
+def workload_config(mode, n, T=T_SAMPLE, tp=TOP_P, flat=False):
+    knobs = "greedy" if mode == "greedy" else f"T={T:g} top-p {tp:g}"
+    return {"workload": f"config 2 fused verify round, {knobs}"
+                        + (", flat N(0,1) logits" if flat else ""),
             "rows_per_gpu": B, "k": K_DRAFT, "vocab": VOCAB, "logits": "bf16",
             "parallelism": f"row-sharded x{n}, no collective",
             "l2": "2 input sets of 175 MB alternate (> 126 MB L2)"}
@@ -720,11 +729,16 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     greedy = a.mode == "greedy"
-    T, tp = (0.0, 1.0) if greedy else (T_SAMPLE, TOP_P)
+    T, tp = (0.0, 1.0) if greedy else (a.temperature, a.top_p)
 
     bufs = []
     for i in range(NBUF):
         tgt, drf = W.cfg2_logits(B, K_DRAFT, VOCAB, seed=100 * rank + i, device=dev)
+        if a.flat:
+            g = torch.Generator(device=dev).manual_seed(100 * rank + i)
+            tgt = torch.randn(tgt.shape, generator=g, device=dev).to(torch.bfloat16)
+            drf = (tgt[:, :K_DRAFT].float() + 0.3 * torch.randn(drf.shape, generator=g,
+                                                                 device=dev)).to(torch.bfloat16)
         xs, _ = S.draft_sample(drf.reshape(-1, VOCAB), torch.rand(B * K_DRAFT, device=dev), T, tp)
         ua, ur = W.uniforms(B, K_DRAFT, seed=100 * rank + i, device=dev)
         bufs.append((tgt, drf, xs.view(B, K_DRAFT), ua, ur))
@@ -851,11 +865,12 @@ def main():
         traffic = json.loads(prof.read_text()).get("bytes_per_call")
     launches_per_step = 1             # our kernels per verify call (the stats or argmax kernel)
     line = {
-        "metric": metric_name(a.mode), "value": value, "unit": "rows/s", "n_gpus": world,
+        "metric": metric_name(a.mode, T, tp, a.flat), "value": value, "unit": "rows/s",
+        "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded config-2 logits, see specdec/workloads.py)",
-        "config": workload_config(a.mode, world),
+        "config": workload_config(a.mode, world, T, tp, a.flat),
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                      "frac": gbs / peak, "traffic": traffic,
                      "peak_source": peak_src,
