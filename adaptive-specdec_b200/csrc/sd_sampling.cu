@@ -33,8 +33,7 @@
 
 namespace sd {
 
-constexpr int HIST_WORDS = 32768;       // 65536 16-bit counters
-constexpr int NGROUP = 8192;            // key groups of 8 keys
+constexpr int HIST_WORDS = 32768;       // 65536 16-bit counters (exact fallback)
 constexpr int NCORR_MAX = 96;           // counter-wrap corrections per vector
 constexpr int SMALLV_MAX = 2048;        // small-vocabulary exact path
 constexpr int ST = 512;                 // threads of the small-V kernel
@@ -149,15 +148,8 @@ constexpr int FB_BOUNDARY = 4;           // top-p / top-k boundary outside the s
 constexpr int F_INEXACT = 2;             // that path's correction table overflowed
 constexpr int F_LISTED = 4;              // kept elements stored in the workspace
 constexpr int F_ALLKEPT = 8;             // no truncation: every element kept
+constexpr int F_DEFER = 16;              // handed to the fallback kernel (not yet computed)
 
-constexpr int NSEG = 512;                // 128-key segments of the 16-bit key space
-
-// Shared-memory part of the exact full-histogram path; the 65,536 counters
-// themselves live in a per-CTA global buffer (the path is rare).
-struct HistBuf {
-  uint16_t list[NGROUP];                 // populated key groups, descending key order
-  uint16_t occ[NSEG];                    // populated-group mask per 128-key segment
-};
 
 constexpr int SEL_CAP = 1024;            // entries sorted per vector
 constexpr int RANK_MAX = 512;            // row draw by direct prefix sums up to this many kept
@@ -189,15 +181,25 @@ struct VecHand {
   int nkey;                              // listed elements
 };
 
+// The exact fallback's counters reuse the ring and hand-over memory once the
+// CTA has streamed all its vectors.
+struct FbScratch {
+  uint32_t hist[HIST_WORDS];             // 65,536 16-bit counters, indexed by raw value
+  uint32_t corr_raw[NCORR_MAX];          // counters that wrapped: +65536 per entry
+  int32_t corr_add[NCORR_MAX];
+};
+
 struct HistSmem {
-  alignas(128) unsigned char ring[NSLOT][SLOT];
-  VecHand hand[2];
   union {
-    HistBuf h;
+    struct {
+      alignas(128) unsigned char ring[NSLOT][SLOT];
+      VecHand hand[2];
+    } st;
+    FbScratch fb;
+  } w;
+  union {
     ListBuf l;
   } u;
-  uint32_t corr_raw[NCORR_MAX];
-  int32_t corr_add[NCORR_MAX];
   double dred[40];
   uint32_t ured[40];
   float fred[40];
@@ -205,7 +207,6 @@ struct HistSmem {
   alignas(8) unsigned long long empty[NSLOT];
   alignas(8) unsigned long long streamed[2];   // the streaming warps finished a vector
   alignas(8) unsigned long long freed[2];      // the finalize warps released its hand-over
-  uint32_t* gh;        // this CTA's global 65,536-counter histogram (fallback path)
   int ncorr;
   int corr_full;
   uint32_t npre_nsel;  // list path: kept elements above the sorted part (low 16 bits) and
@@ -237,7 +238,7 @@ __device__ __forceinline__ void cbar() { asm volatile("bar.sync 2, %0;" :: "n"(C
 // barrier of the streaming warps
 __device__ __forceinline__ void sbar() { asm volatile("bar.sync 1, %0;" :: "n"(ST_N) : "memory"); }
 static_assert(CT % 32 == 0 && ST_N % 32 == 0, "named barrier thread counts");
-static_assert(NSEG % CT == 0 && RANK_MAX % CT == 0, "finalize loops split evenly over CT threads");
+static_assert(RANK_MAX % CT == 0, "finalize loops split evenly over CT threads");
 
 template <typename T>
 __device__ __forceinline__ T c_sum(T v, T* red) {
@@ -377,92 +378,6 @@ __device__ void bitonic_sort(unsigned long long* key, int N, bool descending) {
 }
 
 // ---- exact full-histogram path (fallback) ---------------------------------
-__device__ __forceinline__ uint32_t hist_field(const HistSmem& s, uint32_t raw) {
-  return (__ldcg(&s.gh[raw >> 1]) >> ((raw & 1u) << 4)) & 0xFFFFu;
-}
-
-__device__ __forceinline__ uint32_t hist_count(const HistSmem& s, uint32_t raw) {
-  uint32_t c = hist_field(s, raw);
-  const int n = min(s.ncorr, NCORR_MAX);
-  for (int i = 0; i < n; ++i)
-    if (s.corr_raw[i] == raw) c += s.corr_add[i];
-  return c;
-}
-
-__device__ __forceinline__ void corr_log(HistSmem& s, uint32_t raw, int add) {
-  int i = atomicAdd(&s.ncorr, 1);
-  if (i < NCORR_MAX) { s.corr_raw[i] = raw; s.corr_add[i] = add; }
-  else s.corr_full = 1;
-}
-
-// -0 (raw 0x8000) joins +0 (raw 0x0000): its counter and any wrap corrections
-// logged against it move to +0, so equal values form one tie class.
-__device__ void merge_signed_zero(HistSmem& s) {
-  const uint32_t fneg0 = hist_field(s, 0x8000u);
-  if (fneg0) {
-    s.gh[0x4000] &= 0xFFFF0000u;
-    corr_log(s, 0u, (int)fneg0);
-  }
-  const int n = min(s.ncorr, NCORR_MAX);
-  for (int i = 0; i < n; ++i)
-    if (s.corr_raw[i] == 0x8000u) s.corr_raw[i] = 0u;
-}
-
-// Count one 16-bit pattern; a wrap of its 16-bit counter is logged in the
-// correction table (the returned old word shows it).
-__device__ __forceinline__ void hist_add_checked(HistSmem& s, uint32_t raw) {
-  const uint32_t inc = 1u << ((raw & 1u) << 4);
-  const uint32_t old = atomicAdd(&s.gh[raw >> 1], inc);
-  if ((raw & 1u) == 0u) {
-    if ((old & 0xFFFFu) == 0xFFFFu) {        // low counter wrapped, carried into high
-      corr_log(s, raw, 65536);
-      corr_log(s, raw + 1, -1);
-      if ((old >> 16) == 0xFFFFu) corr_log(s, raw + 1, 65536);
-    }
-  } else if ((old >> 16) == 0xFFFFu) {      // high counter wrapped out of the word
-    corr_log(s, raw, 65536);
-  }
-}
-
-__device__ void hist_clear_all(HistSmem& s) {
-  uint4* h = reinterpret_cast<uint4*>(s.gh);
-  for (int i = ftid(); i < HIST_WORDS / 4; i += CT) h[i] = make_uint4(0, 0, 0, 0);
-  if (ftid() == 0) { s.ncorr = 0; s.corr_full = 0; }
-  __threadfence_block();
-}
-
-// Pass A: segments seg = t, t + CT, ... (segment = key groups [16 seg, 16 seg + 16)).
-__device__ void hist_pass_a(HistSmem& s, uint32_t* maxkey_out) {
-  uint32_t kmax = 0;
-  bool any = false;
-  for (int seg = ftid(); seg < NSEG; seg += CT) {
-    uint32_t occ = 0;
-    for (int j = 0; j < 16; ++j) {
-      const uint32_t G = 16u * seg + j;
-      const bool pos = G >= 4096u;
-      const uint32_t wo = pos ? 4u * (G - 4096u) : 0x7FFCu - 4u * G;
-      const uint4 w = __ldcg(reinterpret_cast<const uint4*>(&s.gh[wo]));
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-      int hi_idx = -1, lo_idx = 8;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t f0 = ws[q] & 0xFFFFu, f1 = ws[q] >> 16;
-        if (f0) { hi_idx = max(hi_idx, 2 * q); lo_idx = min(lo_idx, 2 * q); }
-        if (f1) { hi_idx = max(hi_idx, 2 * q + 1); lo_idx = min(lo_idx, 2 * q + 1); }
-      }
-      if (hi_idx >= 0) {
-        occ |= 1u << j;
-        const uint32_t raw = 2u * wo + (pos ? (uint32_t)hi_idx : (uint32_t)lo_idx);
-        const uint32_t key = key16(raw);
-        kmax = any ? max(kmax, key) : key;
-        any = true;
-      }
-    }
-    s.u.h.occ[seg] = (uint16_t)occ;
-  }
-  *maxkey_out = c_max<uint32_t>(any ? kmax : 0u, s.ured, 0u);
-}
-
 struct StatsParams {
   VecSet vs;
   int dtype, V, nvec;
@@ -470,7 +385,6 @@ struct StatsParams {
   int top_k;
   VecStats* stats;
   unsigned long long* nuc;   // [nvec, NUC_MAX] kept elements (list keys)
-  uint32_t* ghist;           // [grid, 32768] counters for the exact fallback path
   int* row_ctr;              // [rows] vectors finished per row (zeroed before launch)
   int* status;               // device status word: bit0 = a bounded wait timed out
   // fused row finish (top-p / top-k modes)
@@ -480,256 +394,6 @@ struct StatsParams {
   const uint8_t* alive;
   int64_t* n_acc; int64_t* y; float* px; float* qx; float* y_prob;
 };
-
-// Exact per-class computation over the full histogram of vector x (every
-// element counted).  Writes the stats record; the kept set is not listed.
-__device__ void finalize_histogram(HistSmem& s, const StatsParams& P, int v, const uint16_t* x,
-                                   int64_t probe) {
-  const int t = ftid();
-  const int V = P.V;
-  const bool topk_on = P.top_k > 0 && P.top_k < V;
-  const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
-  const float tp32 = P.top_p;
-  int flags = F_FALLBACK;
-
-  hist_clear_all(s);
-  cbar();
-  for (int j = t; j < V; j += CT) hist_add_checked(s, __ldg(x + j));
-  cbar();
-  if (t == 0) merge_signed_zero(s);
-  cbar();
-  uint32_t maxkey;
-  hist_pass_a(s, &maxkey);
-  if (s.corr_full) flags |= F_INEXACT;
-  cbar();
-  if (t == 0) {
-    const int n = min(s.ncorr, NCORR_MAX);
-    for (int i = 0; i < n; ++i) {
-      const uint32_t key = key16(s.corr_raw[i]);
-      const uint32_t G = key >> 3;
-      s.u.h.occ[G >> 4] |= (uint16_t)(1u << (G & 15u));
-      if (s.corr_add[i] > 0 && key > maxkey) maxkey = key;
-    }
-    s.ured[34] = maxkey;
-  }
-  cbar();
-  maxkey = s.ured[34];
-  const float m = scaled_logit(bits16_to_float(raw16(maxkey), P.dtype), P.T);
-
-  {   // populated groups in descending key order: thread t handles segments
-      // NSEG-1-(2t), NSEG-2-(2t) (two consecutive segments, descending)
-    constexpr int SPT = NSEG / CT;
-    uint32_t o[SPT];
-    uint32_t cnt = 0;
-    for (int q = 0; q < SPT; ++q) {
-      o[q] = s.u.h.occ[NSEG - 1 - (SPT * t + q)];
-      cnt += __popc(o[q]);
-    }
-    uint32_t tot;
-    uint32_t off = c_excl_scan<uint32_t>(cnt, s.ured, &tot);
-    for (int q = 0; q < SPT; ++q) {
-      const int seg = NSEG - 1 - (SPT * t + q);
-      for (int j = 15; j >= 0; --j)
-        if (o[q] & (1u << j)) s.u.h.list[off++] = (uint16_t)(16 * seg + j);
-    }
-    cbar();
-    if (t == 0) s.ured[35] = tot;
-    cbar();
-  }
-  const int nlist = (int)s.ured[35];
-  const int per = (nlist + CT - 1) / CT;
-  const int l0 = min(nlist, t * per), l1 = min(nlist, l0 + per);
-
-  uint32_t keyk = 0;
-  if (topk_on) {
-    uint32_t c = 0;
-    for (int l = l0; l < l1; ++l) {
-      const uint32_t G = s.u.h.list[l];
-      for (int q = 7; q >= 0; --q) c += hist_count(s, raw16(8 * G + q));
-    }
-    uint32_t tot;
-    const uint32_t pre = c_excl_scan<uint32_t>(c, s.ured, &tot);
-    if (t == 0) s.keyk16 = 0;
-    cbar();
-    if (pre < (uint32_t)P.top_k && pre + c >= (uint32_t)P.top_k) {
-      uint32_t run = pre;
-      for (int l = l0; l < l1 && run < (uint32_t)P.top_k; ++l) {
-        const uint32_t G = s.u.h.list[l];
-        for (int q = 7; q >= 0; --q) {
-          const uint32_t key = 8 * G + q;
-          run += hist_count(s, raw16(key));
-          if (run >= (uint32_t)P.top_k) { s.keyk16 = key; break; }
-        }
-      }
-    }
-    cbar();
-    keyk = s.keyk16;
-  }
-
-  double es = 0.0;
-  for (int l = l0; l < l1; ++l) {
-    const uint32_t G = s.u.h.list[l];
-    for (int q = 7; q >= 0; --q) {
-      const uint32_t raw = raw16(8 * G + q);
-      const uint32_t c = hist_count(s, raw);
-      if (c) es += (double)c * (double)softmax_num(bits16_to_float(raw, P.dtype), P.T, m);
-    }
-  }
-  const double S = c_sum<double>(es, s.dred);
-  const float inv_s = __double2float_rn(1.0 / S);
-
-  double pm = 0.0;
-  for (int l = l0; l < l1; ++l) {
-    const uint32_t G = s.u.h.list[l];
-    for (int q = 7; q >= 0; --q) {
-      const uint32_t key = 8 * G + q;
-      if (key < keyk) continue;
-      const uint32_t raw = raw16(key);
-      const uint32_t c = hist_count(s, raw);
-      if (c) pm += (double)c * (double)prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
-    }
-  }
-  double z;
-  if (!topp_on) {
-    z = c_sum<double>(pm, s.dred);
-    if (t == 0) { s.vstar16 = 0xFFFFFFFFu; s.n_keep = 0; }
-  } else {
-    double ptot;
-    const double pre = c_excl_scan<double>(pm, s.dred, &ptot);
-    if (t == 0) { s.vstar16 = 0xFFFFFFFFu; s.ured[36] = 0; }
-    cbar();
-    if (l0 < l1 && pre + pm >= (double)tp32 - 1e-9) {
-      double C = pre;
-      bool done = false;
-      for (int l = l0; l < l1 && !done; ++l) {
-        const uint32_t G = s.u.h.list[l];
-        for (int q = 7; q >= 0; --q) {
-          const uint32_t key = 8 * G + q;
-          if (key < keyk) { done = true; break; }
-          const uint32_t raw = raw16(key);
-          const uint32_t c = hist_count(s, raw);
-          if (!c) continue;
-          const float p = prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
-          const float cl = __fsub_rn(__double2float_rn(C + (double)c * (double)p), p);
-          if (!(cl < tp32)) { atomicMax(&s.ured[36], key + 1u); done = true; break; }
-          C += (double)c * (double)p;
-        }
-      }
-    }
-    cbar();
-    const uint32_t vk1 = s.ured[36];
-    if (vk1 != 0u && l0 < l1) {
-      const uint32_t vkey = vk1 - 1u;
-      const uint32_t Gv = vkey >> 3;
-      bool mine = false;
-      for (int l = l0; l < l1; ++l) mine |= (s.u.h.list[l] == Gv);
-      if (mine) {
-        double C = pre;
-        for (int l = l0; l < l1; ++l) {
-          const uint32_t G = s.u.h.list[l];
-          for (int q = 7; q >= 0; --q) {
-            const uint32_t key = 8 * G + q;
-            const uint32_t raw = raw16(key);
-            const uint32_t c = key >= keyk ? hist_count(s, raw) : 0u;
-            if (!c) continue;
-            const float p = prob_of(bits16_to_float(raw, P.dtype), P.T, m, inv_s);
-            if (key == vkey) {
-              int lo = 0, hi = (int)c;   // largest n with keep(j) for all j < n
-              while (lo < hi) {
-                const int mid = (lo + hi) >> 1;
-                const float cl = __fsub_rn(
-                    __double2float_rn(C + (double)(mid + 1) * (double)p), p);
-                if (cl < tp32) lo = mid + 1; else hi = mid;
-              }
-              int nk = lo;
-              if (nk == 0 && key == maxkey) nk = 1;   // the first sorted entry is always kept
-              s.vstar16 = vkey;
-              s.n_keep = nk;
-              s.vcount = (int)c;
-              s.z = C + (double)nk * (double)p;
-            }
-            C += (double)c * (double)p;
-          }
-        }
-      }
-    }
-    cbar();
-    z = (s.vstar16 == 0xFFFFFFFFu) ? ptot : s.z;
-  }
-  cbar();
-  const uint32_t vstar16 = s.vstar16;
-  const float zf = fmaxf(__double2float_rn(z), 1e-12f);
-
-  // index of the n_keep-th member (ascending index) of the boundary class
-  int32_t idx_cut = (int32_t)NO_CUT;
-  if (vstar16 != 0xFFFFFFFFu) {
-    const int nk = s.n_keep;
-    if (nk == 0) idx_cut = -1;
-    else if (nk < s.vcount) {
-      const uint32_t r0 = raw16(vstar16);
-      const bool zero_cls = (r0 == 0u);
-      if (t == 0) s.found_cut = 0;
-      cbar();
-      uint32_t run = 0;
-      constexpr int PT = 32;
-      for (int base = 0; base < V; base += CT * PT) {
-        const int j0 = base + t * PT;
-        uint32_t c = 0;
-        for (int e = 0; e < PT; ++e) {
-          const int j = j0 + e;
-          if (j < V) {
-            const uint32_t r = __ldg(x + j);
-            c += (r == r0) || (zero_cls && r == 0x8000u);
-          }
-        }
-        uint32_t tot;
-        const uint32_t pre = c_excl_scan<uint32_t>(c, s.ured, &tot);
-        if (run + pre < (uint32_t)nk && run + pre + c >= (uint32_t)nk) {
-          uint32_t rr = run + pre;
-          for (int e = 0; e < PT; ++e) {
-            const int j = j0 + e;
-            if (j < V) {
-              const uint32_t r = __ldg(x + j);
-              if ((r == r0) || (zero_cls && r == 0x8000u)) {
-                if (++rr == (uint32_t)nk) { s.idx_cut = j; s.found_cut = 1; break; }
-              }
-            }
-          }
-        }
-        run += tot;
-        cbar();
-        if (s.found_cut) break;
-      }
-      idx_cut = s.idx_cut;
-    }
-  }
-
-  if (t == 0) {
-    VecStats o;
-    o.m = m;
-    o.inv_s = inv_s;
-    o.zf = zf;
-    o.kth = topk_on ? fkey(bits16_to_float(raw16(keyk), P.dtype)) : 0u;
-    o.vstar = vstar16 == 0xFFFFFFFFu ? 0u : fkey(bits16_to_float(raw16(vstar16), P.dtype));
-    o.idx_cut = vstar16 == 0xFFFFFFFFu ? (int32_t)NO_CUT : idx_cut;
-    o.argmax = -1;
-    o.flags = flags | ((!topp_on && !topk_on) ? F_ALLKEPT : 0);
-    o.n_keep = -1;
-    o.fb_why = s.fb_why;
-    o.pad = 0;
-    float pp = 0.f;
-    if (probe >= 0 && probe < V) {
-      const float xv = bits16_to_float(__ldg(x + probe), P.dtype);
-      const uint32_t kx = fkey(xv);
-      const bool kept = kx >= o.kth &&
-                        (kx > o.vstar || (kx == o.vstar && probe <= (int64_t)o.idx_cut));
-      if (kept) pp = __fdiv_rn(prob_of(xv, P.T, m, inv_s), zf);
-    }
-    o.probe_p = pp;
-    P.stats[v] = o;
-  }
-  cbar();
-}
 
 // ---- streaming ---------------------------------------------------------------
 
@@ -953,7 +617,7 @@ __device__ __forceinline__ void stream_words(HistSmem& s, VecHand& H, Stream& st
         const int cnt = __popc(hm);
         int o = atomicAdd(&H.nkey, cnt);
         st.bulk -= (double)cnt * (double)st.eY;
-        const uint32_t* ring32 = reinterpret_cast<const uint32_t*>(s.ring[slot]);
+        const uint32_t* ring32 = reinterpret_cast<const uint32_t*>(s.w.st.ring[slot]);
         const int tl = (int)threadIdx.x - ST0;
         while (hm) {
           const int bit = __ffs(hm) - 1;
@@ -1592,6 +1256,387 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
   cbar();
 }
 
+// ---------------------------------------------------------------------------
+// exact fallback (bf16 / fp16): vectors the list path cannot decide
+// ---------------------------------------------------------------------------
+// The finalize warps defer a vector (VecStats.flags F_DEFER) when its list
+// overflows or the top-k / top-p boundary lies below the list window: flat
+// distributions, high temperatures, top-p near 1.  Once the CTA has streamed
+// all its vectors, all its threads take its deferred vectors one at a time
+// and compute them exactly from a 65,536-bin count histogram of the vector's
+// 16-bit values in shared memory (the ring's memory)
+// (two 16-bit counters per word, a counter that wraps is logged as a +65536
+// correction): every element of one value has the same probability, so the
+// normaliser, the top-k value and the top-p boundary follow from per-value
+// counts, walked in descending value order with each thread owning 64
+// consecutive values and one block scan carrying the mass across threads.
+// Within the boundary value, the kept members are the first ones in
+// vocabulary order (the stable-sort tie policy): the n-th is found by one
+// counting pass over the vector.  The CTA that completes a row then performs
+// the row's accept test and draw with all its threads: two ordered passes
+// over the pick vector's vocabulary (each thread a contiguous slice, block
+// scans in between).
+
+
+__device__ __forceinline__ void fb_corr(HistSmem& s, FbScratch& h, uint32_t raw, int add) {
+  const int i = atomicAdd(&s.ncorr, 1);
+  if (i < NCORR_MAX) { h.corr_raw[i] = raw; h.corr_add[i] = add; }
+  else s.corr_full = 1;
+}
+
+// Count one 16-bit pattern; a wrap of its 16-bit counter (the returned old
+// word shows it) is logged as a correction.
+__device__ __forceinline__ void fb_count(HistSmem& s, FbScratch& h, uint32_t raw) {
+  const uint32_t inc = 1u << ((raw & 1u) << 4);
+  const uint32_t old = atomicAdd(&h.hist[raw >> 1], inc);
+  if ((raw & 1u) == 0u) {
+    if ((old & 0xFFFFu) == 0xFFFFu) {        // low counter wrapped, carried into high
+      fb_corr(s, h, raw, 65536);
+      fb_corr(s, h, raw + 1, -1);
+      if ((old >> 16) == 0xFFFFu) fb_corr(s, h, raw + 1, 65536);
+    }
+  } else if ((old >> 16) == 0xFFFFu) {      // high counter wrapped out of the word
+    fb_corr(s, h, raw, 65536);
+  }
+}
+
+// Elements of 16-bit value `raw` (-0 counted with +0, its key being +0's).
+__device__ __forceinline__ uint32_t fb_get(const FbScratch& h, uint32_t raw, int ncorr) {
+  uint32_t c = (h.hist[raw >> 1] >> ((raw & 1u) << 4)) & 0xFFFFu;
+  for (int i = 0; i < ncorr; ++i)
+    if (h.corr_raw[i] == raw) c += (uint32_t)h.corr_add[i];
+  if (raw == 0u) {
+    c += (h.hist[0x8000u >> 1] >> ((0x8000u & 1u) << 4)) & 0xFFFFu;
+    for (int i = 0; i < ncorr; ++i)
+      if (h.corr_raw[i] == 0x8000u) c += (uint32_t)h.corr_add[i];
+  }
+  return c;
+}
+__device__ __forceinline__ uint32_t fb_count_key(const FbScratch& h, uint32_t key, int ncorr) {
+  const uint32_t raw = raw16(key);
+  return raw == 0x8000u ? 0u : fb_get(h, raw, ncorr);   // -0 lives in +0's class
+}
+
+// Keys are visited in chunks of NT consecutive keys, descending: in chunk c
+// thread t holds key 65535 - NT c - t (none past the last key), so
+// neighbouring threads read neighbouring counters (no bank conflicts) and
+// thread order is descending key order within a chunk.
+template <int NT>
+__device__ __forceinline__ uint32_t fb_chunk_count(const FbScratch& h, int c, int t, int ncorr,
+                                                   uint32_t* key) {
+  const int i = NT * c + t;
+  *key = 65535u - (uint32_t)i;
+  return i < 65536 ? fb_count_key(h, *key, ncorr) : 0u;
+}
+
+// Exact stats of vector v (all NT threads of the CTA).
+template <int NT>
+__device__ void fb_vector(HistSmem& s, FbScratch& h, const StatsParams& P, int v,
+                          const uint16_t* x, int64_t probe, int fb_why) {
+  const int t = threadIdx.x;
+  const int V = P.V;
+  const bool topk_on = P.top_k > 0 && P.top_k < V;
+  const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
+  const float tp32 = P.top_p;
+  // A: the histogram (16-byte loads, neighbouring threads on neighbouring units)
+  uint4* h4 = reinterpret_cast<uint4*>(h.hist);
+  for (int i = t; i < HIST_WORDS / 4; i += NT) h4[i] = make_uint4(0, 0, 0, 0);
+  if (t == 0) { s.ncorr = 0; s.corr_full = 0; }
+  __syncthreads();
+  const VecGeom gm(x, V);
+  const uint4* body = reinterpret_cast<const uint4*>(x + gm.head);
+  for (int u = t; u < gm.nunits; u += NT) {
+    const uint4 q = __ldg(body + u);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      fb_count(s, h, w[i] & 0xFFFFu);
+      fb_count(s, h, w[i] >> 16);
+    }
+  }
+  if (t < gm.head) fb_count(s, h, __ldg(x + t));
+  else if (t < gm.head + V - gm.tail0) fb_count(s, h, __ldg(x + gm.tail0 + (t - gm.head)));
+  __syncthreads();
+  const int ncorr = min(s.ncorr, NCORR_MAX);
+  const int flags = F_FALLBACK | (s.corr_full ? F_INEXACT : 0);
+  // B: populated chunks, the maximum
+  constexpr int NCH = (65536 + NT - 1) / NT;
+  static_assert(NCH <= 128, "chunk mask");
+  unsigned long long occ[2] = {0ull, 0ull};
+  uint32_t kmax = 0u;
+  for (int c = 0; c < NCH; ++c) {
+    uint32_t key;
+    const uint32_t n = fb_chunk_count<NT>(h, c, t, ncorr, &key);
+    if (n && kmax == 0u) kmax = key;                  // this thread's largest populated key
+    if (__syncthreads_or(n != 0u)) occ[c >> 6] |= 1ull << (c & 63);
+  }
+  const uint32_t maxkey = block_max<uint32_t>(kmax, s.ured, 0u);
+  const float m = scaled_logit(bits16_to_float(raw16(maxkey), P.dtype), P.T);
+  // C: the normaliser
+  double es = 0.0;
+  for (int c = 0; c < NCH; ++c) {
+    if (!(occ[c >> 6] >> (c & 63) & 1ull)) continue;
+    uint32_t key;
+    const uint32_t n = fb_chunk_count<NT>(h, c, t, ncorr, &key);
+    if (n) es += (double)n * (double)softmax_num(bits16_to_float(raw16(key), P.dtype), P.T, m);
+  }
+  const double S = block_sum<double>(es, s.dred);
+  const float inv_s = __double2float_rn(1.0 / S);
+  // D: top-k: the key of the top_k-th element in descending order
+  uint32_t keyk = 0u;
+  if (topk_on) {
+    uint32_t carry = 0u;
+    for (int c = 0; c < NCH; ++c) {
+      if (!(occ[c >> 6] >> (c & 63) & 1ull)) continue;
+      uint32_t key;
+      const uint32_t n = fb_chunk_count<NT>(h, c, t, ncorr, &key);
+      uint32_t tot;
+      const uint32_t pre = carry + block_excl_scan<uint32_t>(n, s.ured, &tot);
+      if (t == 0) s.ured[37] = 0u;
+      __syncthreads();
+      if (n && pre < (uint32_t)P.top_k && pre + n >= (uint32_t)P.top_k) s.ured[37] = key;
+      __syncthreads();
+      keyk = s.ured[37];
+      carry += tot;
+      if (keyk != 0u || carry >= (uint32_t)P.top_k) break;   // (uniform)
+    }
+  }
+  // E: top-p: walk the kept candidates (keys >= keyk) in descending order
+  // with the float64 running mass; the boundary class is the first whose
+  // last member is dropped (keep while fl32(cum - p) < top_p)
+  uint32_t vstar = 0xFFFFFFFFu;
+  int nkeep = 0, vcount = 0;
+  double z = 0.0;
+  {
+    double carry = 0.0;
+    if (t == 0) s.ured[38] = 0xFFFFFFFFu;
+    __syncthreads();
+    for (int c = 0; c < NCH; ++c) {
+      if (!(occ[c >> 6] >> (c & 63) & 1ull)) continue;
+      uint32_t key;
+      uint32_t n = fb_chunk_count<NT>(h, c, t, ncorr, &key);
+      if (key < keyk) n = 0u;
+      const float p = n ? prob_of(bits16_to_float(raw16(key), P.dtype), P.T, m, inv_s) : 0.f;
+      const double mine = (double)n * (double)p;
+      double tot;
+      const double pre = carry + block_excl_scan<double>(mine, s.dred, &tot);
+      bool cand = false;
+      if (topp_on && n) {
+        const float cl = __fsub_rn(__double2float_rn(pre + mine), p);
+        cand = !(cl < tp32);
+      }
+      if (cand) atomicMin(&s.ured[38], (uint32_t)t);   // lowest thread = highest key
+      __syncthreads();
+      if (s.ured[38] != 0xFFFFFFFFu) {                  // (uniform) the boundary is here
+        if ((uint32_t)t == s.ured[38]) {
+          int lo = 0, hi = (int)n;                      // largest k with keep(j) for all j < k
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            const float cl = __fsub_rn(__double2float_rn(pre + (double)(mid + 1) * (double)p), p);
+            if (cl < tp32) lo = mid + 1; else hi = mid;
+          }
+          int nk = lo;
+          if (nk == 0 && key == maxkey) nk = 1;         // the first sorted entry is always kept
+          s.ured[39] = key;
+          s.ured[36] = (uint32_t)nk;
+          s.sc_n = (int)n;
+          s.dred[39] = pre + (double)nk * (double)p;
+        }
+        __syncthreads();
+        vstar = s.ured[39];
+        nkeep = (int)s.ured[36];
+        vcount = s.sc_n;
+        z = s.dred[39];
+        break;
+      }
+      carry += tot;
+    }
+    if (vstar == 0xFFFFFFFFu) z = carry;
+    __syncthreads();
+  }
+  const float zf = fmaxf(__double2float_rn(z), 1e-12f);
+  // F: the nkeep-th member (vocabulary order) of the boundary class, tile by
+  // tile (NT groups of 8 consecutive elements per tile)
+  int32_t idx_cut = (int32_t)NO_CUT;
+  if (vstar != 0xFFFFFFFFu) {
+    if (nkeep == 0) {
+      idx_cut = -1;
+    } else if (nkeep < vcount) {
+      const uint32_t r0 = raw16(vstar);
+      const bool zero_cls = r0 == 0u;
+      if (t == 0) s.ured[37] = (uint32_t)NO_CUT;
+      uint32_t carry = 0u;
+      for (int base = 0; base < V; base += 8 * NT) {
+        const int j0 = base + 8 * t;
+        uint32_t c = 0u;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int j = j0 + e;
+          if (j < V) {
+            const uint32_t r = __ldg(x + j);
+            c += (r == r0) || (zero_cls && r == 0x8000u);
+          }
+        }
+        uint32_t tot;
+        const uint32_t pc = carry + block_excl_scan<uint32_t>(c, s.ured, &tot);
+        if (pc < (uint32_t)nkeep && pc + c >= (uint32_t)nkeep) {
+          uint32_t rr = pc;
+          for (int e = 0; e < 8; ++e) {
+            const int j = j0 + e;
+            if (j < V) {
+              const uint32_t r = __ldg(x + j);
+              if ((r == r0) || (zero_cls && r == 0x8000u)) {
+                if (++rr == (uint32_t)nkeep) { s.ured[37] = (uint32_t)j; break; }
+              }
+            }
+          }
+        }
+        carry += tot;
+        __syncthreads();
+        if (carry >= (uint32_t)nkeep) break;            // (uniform)
+      }
+      idx_cut = (int32_t)s.ured[37];
+    }
+  }
+  if (t == 0) {
+    VecStats o;
+    o.m = m;
+    o.inv_s = inv_s;
+    o.zf = zf;
+    o.kth = topk_on ? fkey(bits16_to_float(raw16(keyk), P.dtype)) : 0u;
+    o.vstar = vstar == 0xFFFFFFFFu ? 0u : fkey(bits16_to_float(raw16(vstar), P.dtype));
+    o.idx_cut = vstar == 0xFFFFFFFFu ? (int32_t)NO_CUT : idx_cut;
+    o.argmax = -1;
+    o.flags = flags | ((!topp_on && !topk_on) ? F_ALLKEPT : 0);
+    o.n_keep = -1;
+    o.fb_why = fb_why;
+    o.pad = 0;
+    float pp = 0.f;
+    if (probe >= 0 && probe < V) {
+      const float xv = bits16_to_float(__ldg(x + probe), P.dtype);
+      const uint32_t kx = fkey(xv);
+      const bool kept = kx >= o.kth &&
+                        (kx > o.vstar || (kx == o.vstar && probe <= (int64_t)o.idx_cut));
+      if (kept) pp = __fdiv_rn(prob_of(xv, P.T, m, inv_s), zf);
+    }
+    o.probe_p = pp;
+    P.stats[v] = o;
+  }
+  __syncthreads();
+}
+
+// The row's accept test and its residual / bonus draw by inverse CDF over the
+// whole vocabulary, in vocabulary order (all NT threads; reference
+// engine.py:282-303).  Tiles of NT groups of 8 consecutive elements:
+// neighbouring threads read neighbouring logits, one block scan per tile
+// carries the running mass.  Valid for any pair of stats records.
+template <int NT>
+__device__ void fb_finish_row(HistSmem& s, const StatsParams& P, int row) {
+  const int t = threadIdx.x;
+  const int npos0 = P.vs.npos[0], npos = P.vs.npos[0] + P.vs.npos[1];
+  const int vrow = row * npos;
+  const int k = P.k;
+  const int V = P.V;
+  if (t < 32) {
+    // accepted prefix: one lane per draft position
+    const int lane = t;
+    int n = k;
+    for (int base = 0; base < k; base += 32) {
+      const int i = base + lane;
+      bool acc = false;
+      if (i < k) {
+        const float pxi = __ldcg(&P.stats[vrow + i].probe_p);
+        const float qxi = __ldcg(&P.stats[vrow + npos0 + i].probe_p);
+        const float thr = fminf(__fdiv_rn(pxi, fmaxf(qxi, 1e-10f)), 1.0f);
+        if (P.px) P.px[row * k + i] = pxi;
+        if (P.qx) P.qx[row * k + i] = qxi;
+        acc = P.u_acc[row * P.u_bs + i] < thr;
+      }
+      const unsigned rm = __ballot_sync(0xffffffffu, i < k && !acc);
+      if (rm && n == k) n = base + __ffs(rm) - 1;
+    }
+    if (P.alive && P.alive[row] == 0) n = 0;
+    if (lane == 0) { s.sc_n = n; s.sc_y = -1; }
+  }
+  __syncthreads();
+  const int n = s.sc_n;
+  const bool resid = n < k;
+  const int ppos = resid ? n : k;
+  const VecStats stp = load_stats_cg(P.stats + vrow + ppos);
+  VecStats stq = stp;
+  const void* xp = vec_ptr(P.vs, 0, row, ppos, P.dtype);
+  const void* xq = xp;
+  if (resid) {
+    stq = load_stats_cg(P.stats + vrow + npos0 + n);
+    xq = vec_ptr(P.vs, 1, row, n, P.dtype);
+  }
+  // pass 1: the residual mass R and the kept mass of p, and the last index
+  // with mass of each
+  double rs = 0.0, ps = 0.0;
+  int last_r = -1, last_p = -1;
+  for (int base = 0; base < V; base += 8 * NT) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int j = base + 8 * t + e;
+      if (j < V) {
+        const float pj = stats_prob(stp, xp, P.dtype, P.T, j);
+        ps += (double)pj;
+        if (pj > 0.f) last_p = j;
+        if (resid && pj != 0.f) {
+          const float r = fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+          rs += (double)r;
+          if (r > 0.f) last_r = j;
+        }
+      }
+    }
+  }
+  const double R = block_sum<double>(rs, s.dred);
+  const double Pm = block_sum<double>(ps, s.dred);
+  const bool use_p = !resid || __double2float_rn(R) <= 1e-9f;   // sampling.py:86-89
+  const double tgt = (double)P.u_res[row] * (use_p ? Pm : R);
+  const int lastv = block_max<int>(use_p ? last_p : last_r, reinterpret_cast<int*>(s.ured), -1);
+  // pass 2: tiles in vocabulary order until the one holding the crossing
+  double carry = 0.0;
+  for (int base = 0; base < V; base += 8 * NT) {
+    float vals[8];
+    double ls = 0.0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int j = base + 8 * t + e;
+      float val = 0.f;
+      if (j < V) {
+        val = stats_prob(stp, xp, P.dtype, P.T, j);
+        if (!use_p && val != 0.f)
+          val = fmaxf(__fsub_rn(val, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+      }
+      vals[e] = val;
+      ls += (double)val;
+    }
+    double tot;
+    const double pre = carry + block_excl_scan<double>(ls, s.dred, &tot);
+    if (pre <= tgt && pre + ls > tgt) {
+      double run = pre;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        run += (double)vals[e];
+        if (run > tgt) { s.sc_y = base + 8 * t + e; break; }
+      }
+    }
+    carry += tot;
+    __syncthreads();
+    if (s.sc_y >= 0) break;                           // (uniform)
+  }
+  if (t == 0) {
+    long long yy = s.sc_y;
+    if (yy < 0) yy = lastv >= 0 ? lastv : 0;         // rounding put the crossing past the end
+    if (P.n_acc) P.n_acc[row] = n;
+    P.y[row] = yy;
+    if (P.y_prob) P.y_prob[row] = stats_prob(stp, xp, P.dtype, P.T, yy);
+    P.row_ctr[row] = 0;
+  }
+  __syncthreads();
+}
+
 template <int DT>
 __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -1613,10 +1658,9 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.streamed[i], NSW);
       mbar_init(&s.freed[i], 1);
-      s.hand[i].nkey = 0;
-      s.hand[i].gkey = 0u;
+      s.w.st.hand[i].nkey = 0;
+      s.w.st.hand[i].gkey = 0u;
     }
-    s.gh = P.ghist + (size_t)blockIdx.x * HIST_WORDS;
     s.abort_flag = 0;
     s.fb_why = 0;
     s.ncorr = 0;
@@ -1625,9 +1669,8 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
   }
   __syncthreads();
 
-  if (threadIdx.x < ST0) {
+  if (threadIdx.x == 0) {
     // ---------------- producer warp (lane 0): ring refills
-    if (threadIdx.x != 0) return;
     bool ok = true;
     uint32_t g = 0, issued = 0;
     for (int v = blockIdx.x; v < P.nvec; v += gridDim.x) {
@@ -1643,7 +1686,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
         if (ok) {
           const uint32_t bytes = (uint32_t)min(SLOT, gm.nunits * 16 - c * SLOT);
           mbar_expect_tx(&s.full[sl], bytes);
-          bulk_g2s(s.ring[sl], body + (size_t)c * SLOT, bytes, &s.full[sl]);
+          bulk_g2s(s.w.st.ring[sl], body + (size_t)c * SLOT, bytes, &s.full[sl]);
           issued = g + 1;
         }
       }
@@ -1656,17 +1699,18 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
       }
       atomicOr(P.status, 1);
     }
-    return;
+  } else if (threadIdx.x < ST0) {
+    // producer warp, lanes 1-31: nothing to do until the fallback phase
   }
 
-  if (threadIdx.x < FIN0) {
+  else if (threadIdx.x < FIN0) {
     // ---------------- streaming warps
     const int t = threadIdx.x - ST0;
     const int lane = t & 31, wl = t >> 5;
     uint32_t g = 0;
     int vl = 0;
     for (int v = blockIdx.x; v < P.nvec; v += gridDim.x, ++vl) {
-      VecHand& H = s.hand[vl & 1];
+      VecHand& H = s.w.st.hand[vl & 1];
       if (vl >= 2)                                   // wait until the finalize warps release it
         __all_sync(0xffffffffu, mbar_wait(&s.freed[vl & 1], ((vl >> 1) - 1) & 1, &s.abort_flag));
       int set, row, pos;
@@ -1680,7 +1724,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
         const int sl = g % NSLOT;
         const bool okw = __all_sync(0xffffffffu, mbar_wait(&s.full[sl], (g / NSLOT) & 1u, &s.abort_flag));
         const int units = okw ? min(SLOT, gm.nunits * 16 - c * SLOT) >> 4 : 0;
-        const uint4* u4 = reinterpret_cast<const uint4*>(s.ring[sl]);
+        const uint4* u4 = reinterpret_cast<const uint4*>(s.w.st.ring[sl]);
         uint32_t w[4 * GPS];
 #pragma unroll
         for (int q = 0; q < GPS; ++q) {
@@ -1702,7 +1746,7 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
             const bool oki = __all_sync(0xffffffffu, mbar_test(&s.full[gi % NSLOT], (gi / NSLOT) & 1u));
             if (oki) {
               const int ui = min(SLOT, gm.nunits * 16 - i * SLOT) >> 4;
-              const uint4* wi4 = reinterpret_cast<const uint4*>(s.ring[gi % NSLOT]);
+              const uint4* wi4 = reinterpret_cast<const uint4*>(s.w.st.ring[gi % NSLOT]);
               uint32_t wi[4 * GPS];
 #pragma unroll
               for (int q = 0; q < GPS; ++q) {
@@ -1751,15 +1795,14 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
         mbar_arrive(&s.streamed[vl & 1]);
       }
     }
-    return;
-  }
+  } else {
 
   // ---------------- finalize warps: list -> stats -> row draw, one vector
   // behind the streaming warps
   const int t = ftid();
   int vl = 0;
   for (int v = blockIdx.x; v < P.nvec; v += gridDim.x, ++vl) {
-    VecHand& H = s.hand[vl & 1];
+    VecHand& H = s.w.st.hand[vl & 1];
     const uint32_t par = (vl >> 1) & 1;
     if (!mbar_wait(&s.streamed[vl & 1], par, &s.abort_flag)) s.abort_flag = 1;
     cbar();
@@ -1770,9 +1813,17 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
       vec_locate(P.vs, v, &set, &row, &pos);
       const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
       const int64_t probe = vec_probe(P.vs, set, row, pos);
-      if (finalize_list(s, H, P, v, x, probe, c2, wlist)) finalize_histogram(s, P, v, x, probe);
+      // a vector the list cannot decide is deferred to this CTA's fallback
+      // phase, which also counts it toward its row
+      const bool deferred = finalize_list(s, H, P, v, x, probe, c2, wlist);
+      if (deferred && t == 0) {
+        VecStats o = {};
+        o.flags = F_DEFER;
+        o.fb_why = s.fb_why;
+        P.stats[v] = o;
+      }
       // row bookkeeping: the CTA that completes a row draws for it
-      if (P.fused) {
+      if (P.fused && !deferred) {
         __threadfence();
         cbar();
         if (t == 0) s.last_row = atomicAdd(&P.row_ctr[row], 1) == npos - 1;
@@ -1787,7 +1838,30 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
       mbar_arrive(&s.freed[vl & 1]);
     }
   }
-  if (t == 0 && s.abort_flag) atomicOr(P.status, 1);
+    if (t == 0 && s.abort_flag) atomicOr(P.status, 1);
+  }
+
+  // ---------------- fallback phase: every warp of the CTA, after all its
+  // vectors streamed (the ring and hand-over memory is free now)
+  __syncthreads();
+  if (!*reinterpret_cast<volatile int*>(&s.abort_flag)) {
+    for (int v = blockIdx.x; v < P.nvec; v += gridDim.x) {
+      const VecStats* sv = P.stats + v;
+      if (!(*reinterpret_cast<const volatile int*>(&sv->flags) & F_DEFER)) continue;
+      int set, row, pos;
+      vec_locate(P.vs, v, &set, &row, &pos);
+      const uint16_t* x = reinterpret_cast<const uint16_t*>(vec_ptr(P.vs, set, row, pos, P.dtype));
+      fb_vector<HT>(s, s.w.fb, P, v, x, vec_probe(P.vs, set, row, pos),
+                    *reinterpret_cast<const volatile int*>(&sv->fb_why));
+      if (P.fused) {
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s.last_row = atomicAdd(&P.row_ctr[row], 1) == npos - 1;
+        __syncthreads();
+        if (s.last_row) fb_finish_row<HT>(s, P, row);
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -2351,7 +2425,7 @@ static int device_sms() {
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct WsLayout {
-  size_t status, stats, partial, counter, vcounter, rcounter, apartial, mat, nuc, ghist, total;
+  size_t status, stats, partial, counter, vcounter, rcounter, apartial, mat, nuc, total;
 };
 
 // Argmax geometry: blocks per vector and 16-byte units per block (a multiple
@@ -2391,8 +2465,6 @@ static WsLayout ws_layout(int n_rows, int n_vec, int V, bool small) {
   L.apartial = off; off = align256(off + (size_t)n_vec * NCH_MAX * sizeof(unsigned long long));
   L.mat = off; off = align256(off + (small ? (size_t)n_vec * V * sizeof(float) : 0));
   L.nuc = off; off = align256(off + (small ? 0 : (size_t)n_vec * NUC_MAX * sizeof(unsigned long long)));
-  L.ghist = off;
-  off = align256(off + (small ? 0 : (size_t)GRID_MAX * HIST_WORDS * sizeof(uint32_t)));
   L.total = off;
   return L;
 }
@@ -2450,10 +2522,9 @@ static int run_sampling(const VecSet& vs, int nvec, int dtype, int V, float T, f
       P.k = draw->k; P.u_acc = draw->u_acc; P.u_bs = draw->u_bs; P.u_res = draw->u_res;
       P.alive = draw->alive; P.n_acc = draw->n_acc; P.y = draw->y; P.px = draw->px;
       P.qx = draw->qx; P.y_prob = draw->y_prob;
-      if (cudaMemsetAsync(ws + L.rcounter, 0, (size_t)rows * sizeof(int), st) != cudaSuccess)
-        return SD_ELAUNCH;
     }
-    P.ghist = reinterpret_cast<uint32_t*>(ws + L.ghist);
+    if (fused && cudaMemsetAsync(ws + L.rcounter, 0, (size_t)rows * sizeof(int), st) != cudaSuccess)
+      return SD_ELAUNCH;
     const int nsm = device_sms();
     int grid = nsm;
     if (grid > GRID_MAX) grid = GRID_MAX;
@@ -2463,6 +2534,7 @@ static int run_sampling(const VecSet& vs, int nvec, int dtype, int V, float T, f
     else
       hist_stats_kernel<SD_DTYPE_F16><<<grid, HT, sizeof(HistSmem), st>>>(P);
     if (int rc = check_launch()) return rc;
+
     need_finish = draw != nullptr && !fused;
     if (need_finish &&
         cudaMemsetAsync(ws + L.counter, 0, (size_t)rows * sizeof(int), st) != cudaSuccess)
