@@ -1300,6 +1300,12 @@ __device__ __forceinline__ void fb_count(HistSmem& s, FbScratch& h, uint32_t raw
   }
 }
 
+// Count one 16-bit pattern without reading the counter back (a reduction,
+// no round trip); a wrap shows up afterwards as a total below V.
+__device__ __forceinline__ void fb_count_fast(FbScratch& h, uint32_t raw) {
+  atomicAdd(&h.hist[raw >> 1], 1u << ((raw & 1u) << 4));
+}
+
 // Elements of 16-bit value `raw` (-0 counted with +0, its key being +0's).
 __device__ __forceinline__ uint32_t fb_get(const FbScratch& h, uint32_t raw, int ncorr) {
   uint32_t c = (h.hist[raw >> 1] >> ((raw & 1u) << 4)) & 0xFFFFu;
@@ -1338,44 +1344,72 @@ __device__ void fb_vector(HistSmem& s, FbScratch& h, const StatsParams& P, int v
   const bool topk_on = P.top_k > 0 && P.top_k < V;
   const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
   const float tp32 = P.top_p;
-  // A: the histogram (16-byte loads, neighbouring threads on neighbouring units)
-  uint4* h4 = reinterpret_cast<uint4*>(h.hist);
-  for (int i = t; i < HIST_WORDS / 4; i += NT) h4[i] = make_uint4(0, 0, 0, 0);
-  if (t == 0) { s.ncorr = 0; s.corr_full = 0; }
-  __syncthreads();
-  const VecGeom gm(x, V);
-  const uint4* body = reinterpret_cast<const uint4*>(x + gm.head);
-  for (int u = t; u < gm.nunits; u += NT) {
-    const uint4 q = __ldg(body + u);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      fb_count(s, h, w[i] & 0xFFFFu);
-      fb_count(s, h, w[i] >> 16);
-    }
-  }
-  if (t < gm.head) fb_count(s, h, __ldg(x + t));
-  else if (t < gm.head + V - gm.tail0) fb_count(s, h, __ldg(x + gm.tail0 + (t - gm.head)));
-  __syncthreads();
-  const int ncorr = min(s.ncorr, NCORR_MAX);
-  const int flags = F_FALLBACK | (s.corr_full ? F_INEXACT : 0);
-  // B: populated chunks, the maximum
+  // A: the histogram (16-byte loads, neighbouring threads on neighbouring
+  // units, two loads in flight per thread); counters are incremented without
+  // reading them back, and a wrap (more than 65,535 equal values) is caught
+  // by the total and recounted with checked increments
   constexpr int NCH = (65536 + NT - 1) / NT;
   static_assert(NCH <= 128, "chunk mask");
-  unsigned long long occ[2] = {0ull, 0ull};
+  const VecGeom gm(x, V);
+  const uint4* body = reinterpret_cast<const uint4*>(x + gm.head);
+  uint4* h4 = reinterpret_cast<uint4*>(h.hist);
+  uint32_t occ[4];
   uint32_t kmax = 0u;
-  for (int c = 0; c < NCH; ++c) {
-    uint32_t key;
-    const uint32_t n = fb_chunk_count<NT>(h, c, t, ncorr, &key);
-    if (n && kmax == 0u) kmax = key;                  // this thread's largest populated key
-    if (__syncthreads_or(n != 0u)) occ[c >> 6] |= 1ull << (c & 63);
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int i = t; i < HIST_WORDS / 4; i += NT) h4[i] = make_uint4(0, 0, 0, 0);
+    if (t == 0) { s.ncorr = 0; s.corr_full = 0; }
+    __syncthreads();
+    for (int u = t; u < gm.nunits; u += 2 * NT) {
+      const uint4 q0 = __ldg(body + u);
+      const bool two = u + NT < gm.nunits;
+      const uint4 q1 = two ? __ldg(body + u + NT) : make_uint4(0, 0, 0, 0);
+      const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < 4 || two) {
+          if (pass == 0) { fb_count_fast(h, w[i] & 0xFFFFu); fb_count_fast(h, w[i] >> 16); }
+          else { fb_count(s, h, w[i] & 0xFFFFu); fb_count(s, h, w[i] >> 16); }
+        }
+      }
+    }
+    uint32_t rr = 0xFFFFFFFFu;
+    if (t < gm.head) rr = __ldg(x + t);
+    else if (t < gm.head + V - gm.tail0) rr = __ldg(x + gm.tail0 + (t - gm.head));
+    if (rr != 0xFFFFFFFFu) { if (pass == 0) fb_count_fast(h, rr); else fb_count(s, h, rr); }
+    if (t < 4) s.ured[34 + t] = 0u;
+    __syncthreads();
+    // B: populated chunks (one OR reduction), the maximum, the total
+    const int ncorr = min(s.ncorr, NCORR_MAX);
+    uint32_t lmask[4] = {0u, 0u, 0u, 0u};
+    uint32_t cnt = 0u;
+    kmax = 0u;
+    for (int c = 0; c < NCH; ++c) {
+      uint32_t key;
+      const uint32_t n = fb_chunk_count<NT>(h, c, t, ncorr, &key);
+      if (n) {
+        if (kmax == 0u) kmax = key;                   // this thread's largest populated key
+        lmask[c >> 5] |= 1u << (c & 31);
+        cnt += n;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t m4 = __reduce_or_sync(0xffffffffu, lmask[i]);
+      if ((t & 31) == 0 && m4) atomicOr(&s.ured[34 + i], m4);
+    }
+    const uint32_t total = block_sum<uint32_t>(cnt, s.ured);   // (its barriers publish the mask)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) occ[i] = s.ured[34 + i];
+    if (total == (uint32_t)V) break;                  // (uniform) no counter wrapped
   }
+  const int ncorr = min(s.ncorr, NCORR_MAX);
+  const int flags = F_FALLBACK | (s.corr_full ? F_INEXACT : 0);
   const uint32_t maxkey = block_max<uint32_t>(kmax, s.ured, 0u);
   const float m = scaled_logit(bits16_to_float(raw16(maxkey), P.dtype), P.T);
   // C: the normaliser
   double es = 0.0;
   for (int c = 0; c < NCH; ++c) {
-    if (!(occ[c >> 6] >> (c & 63) & 1ull)) continue;
+    if (!(occ[c >> 5] >> (c & 31) & 1u)) continue;
     uint32_t key;
     const uint32_t n = fb_chunk_count<NT>(h, c, t, ncorr, &key);
     if (n) es += (double)n * (double)softmax_num(bits16_to_float(raw16(key), P.dtype), P.T, m);
@@ -1387,7 +1421,7 @@ __device__ void fb_vector(HistSmem& s, FbScratch& h, const StatsParams& P, int v
   if (topk_on) {
     uint32_t carry = 0u;
     for (int c = 0; c < NCH; ++c) {
-      if (!(occ[c >> 6] >> (c & 63) & 1ull)) continue;
+      if (!(occ[c >> 5] >> (c & 31) & 1u)) continue;
       uint32_t key;
       const uint32_t n = fb_chunk_count<NT>(h, c, t, ncorr, &key);
       uint32_t tot;
@@ -1412,7 +1446,7 @@ __device__ void fb_vector(HistSmem& s, FbScratch& h, const StatsParams& P, int v
     if (t == 0) s.ured[38] = 0xFFFFFFFFu;
     __syncthreads();
     for (int c = 0; c < NCH; ++c) {
-      if (!(occ[c >> 6] >> (c & 63) & 1ull)) continue;
+      if (!(occ[c >> 5] >> (c & 31) & 1u)) continue;
       uint32_t key;
       uint32_t n = fb_chunk_count<NT>(h, c, t, ncorr, &key);
       if (key < keyk) n = 0u;
@@ -1456,7 +1490,7 @@ __device__ void fb_vector(HistSmem& s, FbScratch& h, const StatsParams& P, int v
   }
   const float zf = fmaxf(__double2float_rn(z), 1e-12f);
   // F: the nkeep-th member (vocabulary order) of the boundary class, tile by
-  // tile (NT groups of 8 consecutive elements per tile)
+  // tile (NT groups of 32 consecutive elements per tile)
   int32_t idx_cut = (int32_t)NO_CUT;
   if (vstar != 0xFFFFFFFFu) {
     if (nkeep == 0) {
@@ -1466,11 +1500,11 @@ __device__ void fb_vector(HistSmem& s, FbScratch& h, const StatsParams& P, int v
       const bool zero_cls = r0 == 0u;
       if (t == 0) s.ured[37] = (uint32_t)NO_CUT;
       uint32_t carry = 0u;
-      for (int base = 0; base < V; base += 8 * NT) {
-        const int j0 = base + 8 * t;
+      for (int base = 0; base < V; base += 32 * NT) {
+        const int j0 = base + 32 * t;
         uint32_t c = 0u;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
+#pragma unroll 8
+        for (int e = 0; e < 32; ++e) {
           const int j = j0 + e;
           if (j < V) {
             const uint32_t r = __ldg(x + j);
@@ -1481,7 +1515,7 @@ __device__ void fb_vector(HistSmem& s, FbScratch& h, const StatsParams& P, int v
         const uint32_t pc = carry + block_excl_scan<uint32_t>(c, s.ured, &tot);
         if (pc < (uint32_t)nkeep && pc + c >= (uint32_t)nkeep) {
           uint32_t rr = pc;
-          for (int e = 0; e < 8; ++e) {
+          for (int e = 0; e < 32; ++e) {
             const int j = j0 + e;
             if (j < V) {
               const uint32_t r = __ldg(x + j);
@@ -1570,34 +1604,67 @@ __device__ void fb_finish_row(HistSmem& s, const StatsParams& P, int row) {
     stq = load_stats_cg(P.stats + vrow + npos0 + n);
     xq = vec_ptr(P.vs, 1, row, n, P.dtype);
   }
-  // pass 1: the residual mass R and the kept mass of p, and the last index
-  // with mass of each
+  // pass 1: per tile (NT groups of 8 consecutive elements) the residual mass
+  // and the kept mass of p, summed per warp into shared memory (the
+  // histogram's memory), and the last index with mass of each
+  constexpr int NW = NT / 32;
+  double* tsum = reinterpret_cast<double*>(&s.w);          // [tiles][NW][2]
+  static_assert(((1 << 21) / (8 * NT) + 1) * NW * 2 * sizeof(double) <= sizeof(s.w),
+                "tile sums of the largest vocabulary fit the ring's memory");
+  const int ntile = (V + 8 * NT - 1) / (8 * NT);
   double rs = 0.0, ps = 0.0;
   int last_r = -1, last_p = -1;
-  for (int base = 0; base < V; base += 8 * NT) {
+  for (int ti = 0; ti < ntile; ++ti) {
+    const int base = ti * 8 * NT;
+    double tr = 0.0, tpm = 0.0;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int j = base + 8 * t + e;
       if (j < V) {
         const float pj = stats_prob(stp, xp, P.dtype, P.T, j);
-        ps += (double)pj;
+        tpm += (double)pj;
         if (pj > 0.f) last_p = j;
         if (resid && pj != 0.f) {
           const float r = fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
-          rs += (double)r;
+          tr += (double)r;
           if (r > 0.f) last_r = j;
         }
       }
     }
+    rs += tr;
+    ps += tpm;
+    tr = warp_sum(tr);
+    tpm = warp_sum(tpm);
+    if ((t & 31) == 0) {
+      tsum[(ti * NW + (t >> 5)) * 2] = tr;
+      tsum[(ti * NW + (t >> 5)) * 2 + 1] = tpm;
+    }
   }
   const double R = block_sum<double>(rs, s.dred);
-  const double Pm = block_sum<double>(ps, s.dred);
+  const double Pm = block_sum<double>(ps, s.dred);     // (its barriers publish tsum)
   const bool use_p = !resid || __double2float_rn(R) <= 1e-9f;   // sampling.py:86-89
   const double tgt = (double)P.u_res[row] * (use_p ? Pm : R);
   const int lastv = block_max<int>(use_p ? last_p : last_r, reinterpret_cast<int*>(s.ured), -1);
-  // pass 2: tiles in vocabulary order until the one holding the crossing
-  double carry = 0.0;
-  for (int base = 0; base < V; base += 8 * NT) {
+  // pass 2: the tile holding the crossing from the tile sums (thread 0, in
+  // tile order), then that tile alone, recomputed
+  if (t == 0) {
+    double carry = 0.0;
+    int hit = -1;
+    double hit_carry = 0.0;
+    for (int ti = 0; ti < ntile && hit < 0; ++ti) {
+      double tt = 0.0;
+      for (int w = 0; w < NW; ++w) tt += tsum[(ti * NW + w) * 2 + (use_p ? 1 : 0)];
+      if (carry <= tgt && carry + tt > tgt) { hit = ti; hit_carry = carry; }
+      carry += tt;
+    }
+    s.ured[38] = (uint32_t)hit;
+    s.dred[39] = hit_carry;
+  }
+  __syncthreads();
+  const int hit = (int)s.ured[38];
+  const double hit_carry = s.dred[39];
+  if (hit >= 0) {                                     // (uniform)
+    const int base = hit * 8 * NT;
     float vals[8];
     double ls = 0.0;
 #pragma unroll
@@ -1613,7 +1680,7 @@ __device__ void fb_finish_row(HistSmem& s, const StatsParams& P, int row) {
       ls += (double)val;
     }
     double tot;
-    const double pre = carry + block_excl_scan<double>(ls, s.dred, &tot);
+    const double pre = hit_carry + block_excl_scan<double>(ls, s.dred, &tot);
     if (pre <= tgt && pre + ls > tgt) {
       double run = pre;
 #pragma unroll
@@ -1622,9 +1689,7 @@ __device__ void fb_finish_row(HistSmem& s, const StatsParams& P, int row) {
         if (run > tgt) { s.sc_y = base + 8 * t + e; break; }
       }
     }
-    carry += tot;
     __syncthreads();
-    if (s.sc_y >= 0) break;                           // (uniform)
   }
   if (t == 0) {
     long long yy = s.sc_y;
