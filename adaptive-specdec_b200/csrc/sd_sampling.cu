@@ -27,6 +27,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "sd_common.cuh"
@@ -2056,10 +2057,13 @@ __global__ void __launch_bounds__(ST) small_stats_kernel(SmallParams P) {
 // ---------------------------------------------------------------------------
 struct ArgmaxParams {
   VecSet vs;           // set 0 only
-  int dtype, V, nvec, nch, cu;   // nch blocks per vector, cu 16-byte units per block
-  unsigned long long* partial;   // [nvec, nch]
-  int* vec_counter;              // [nvec]
-  int* row_counter;              // [rows]
+  int dtype, V, nvec, nch, cu;   // f32: nch blocks per vector, cu 16-byte units per block
+  // 16-bit: chunk units, chunks (key slots) per vector, launched warps
+  int ch;
+  uint32_t cpv, nwarps;
+  unsigned long long* partial;   // f32: [nvec, nch] block keys; 16-bit: [nvec, cpv] chunk keys
+  int* vec_counter;              // f32: [nvec], zeroed by the launch
+  int* row_counter;              // f32: [rows], zeroed by the launch
   VecStats* stats;
   // row decision (verify mode: k >= 1; draft mode: k == 0)
   int k;
@@ -2068,6 +2072,42 @@ struct ArgmaxParams {
   const uint8_t* alive;
   int64_t* n_acc; int64_t* y; float* px; float* qx;
 };
+
+// One thread, once vector v's argmax `am` is known: its stats entry, then, if
+// it completes its row (and the call decides rows: k >= 0), the row's accept
+// count and emitted token.
+__device__ __forceinline__ void argmax_vector_done(const ArgmaxParams& P, int v, int row, int am) {
+  VecStats st;
+  st.m = 0.f; st.inv_s = 1.f; st.zf = 1.f; st.probe_p = 0.f;
+  st.kth = 0; st.vstar = 0; st.idx_cut = (int32_t)NO_CUT; st.argmax = am;
+  st.flags = 0; st.n_keep = -1; st.fb_why = 0; st.pad = 0;
+  P.stats[v] = st;
+  __threadfence();
+  const int per = P.vs.npos[0];
+  if (P.k < 0 || atomicAdd(&P.row_counter[row], 1) != per - 1) return;
+  __threadfence();
+  P.row_counter[row] = 0;
+  const volatile VecStats* vst = P.stats + (int64_t)row * per;
+  if (P.k == 0) {
+    P.y[row] = vst[0].argmax;
+    if (P.qx) P.qx[row] = 1.0f;
+    return;
+  }
+  // p_i(x_i) is 1 iff x_i is the target argmax; the ratio is then >= 1
+  // whatever q is, so the test is u < 1 (engine.py:290-292 with one-hot p).
+  int n = 0;
+  bool alive = P.alive ? P.alive[row] != 0 : true;
+  for (int i = 0; i < P.k; ++i) {
+    const int64_t xi = P.xs[row * P.xs_bs + i];
+    const float pxi = (xi == (int64_t)vst[i].argmax) ? 1.f : 0.f;
+    if (P.px) P.px[row * P.k + i] = pxi;
+    if (P.qx) P.qx[row * P.k + i] = nanf("");
+    const float thr = pxi > 0.f ? 1.f : 0.f;
+    if (alive && n == i && P.u_acc[row * P.u_bs + i] < thr) ++n; else alive = false;
+  }
+  P.n_acc[row] = n;
+  P.y[row] = vst[n].argmax;     // residual and bonus are both one-hot at argmax p_n
+}
 
 // Argmax key of element j: larger value first, then smaller index.  Every NaN,
 // whatever its sign bit (bf16 conversions of a float NaN give 0xFFFF), takes
@@ -2177,40 +2217,247 @@ __global__ void __launch_bounds__(AM_FT) argmax_kernel(ArgmaxParams P) {
       const unsigned long long w = *((volatile unsigned long long*)&P.partial[(int64_t)v * P.nch + i]);
       b = w > b ? w : b;
     }
-    const int am = (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFu));
     P.vec_counter[v] = 0;
-    VecStats st;
-    st.m = 0.f; st.inv_s = 1.f; st.zf = 1.f; st.probe_p = 0.f;
-    st.kth = 0; st.vstar = 0; st.idx_cut = (int32_t)NO_CUT; st.argmax = am;
-    st.flags = 0; st.n_keep = -1; st.fb_why = 0; st.pad = 0;
-    P.stats[v] = st;
-    __threadfence();
-    const int per = P.vs.npos[0];
-    if (P.k >= 0 && atomicAdd(&P.row_counter[row], 1) == per - 1) {
-      __threadfence();
-      P.row_counter[row] = 0;
-      const volatile VecStats* vst = P.stats + (int64_t)row * per;
-      if (P.k == 0) {
-        P.y[row] = vst[0].argmax;
-        if (P.qx) P.qx[row] = 1.0f;
-      } else {
-        // p_i(x_i) is 1 iff x_i is the target argmax; the ratio is then >= 1
-        // whatever q is, so the test is u < 1 (engine.py:290-292 with one-hot p).
-        int n = 0;
-        bool alive = P.alive ? P.alive[row] != 0 : true;
-        for (int i = 0; i < P.k; ++i) {
-          const int64_t xi = P.xs[row * P.xs_bs + i];
-          const float pxi = (xi == (int64_t)vst[i].argmax) ? 1.f : 0.f;
-          if (P.px) P.px[row * P.k + i] = pxi;
-          if (P.qx) P.qx[row * P.k + i] = nanf("");
-          const float thr = pxi > 0.f ? 1.f : 0.f;
-          if (alive && n == i && P.u_acc[row * P.u_bs + i] < thr) ++n; else alive = false;
-        }
-        P.n_acc[row] = n;
-        P.y[row] = vst[n].argmax;     // residual and bonus are both one-hot at argmax p_n
-      }
+    argmax_vector_done(P, v, row, (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFu)));
+  }
+}
+
+// Order-preserving 16-bit key of one bf16 / fp16 element: every NaN, whatever
+// its sign, is the largest key (0xFFFF) and -0 keys as +0.  Keys are >= 1.
+template <int DT>
+__device__ __forceinline__ uint32_t elem_key16(uint32_t h) {
+  constexpr uint32_t INF = DT == SD_DTYPE_BF16 ? 0x7F80u : 0x7C00u;
+  h &= 0xFFFFu;
+  if ((h & 0x7FFFu) > INF) return 0xFFFFu;
+  if (h == 0x8000u) h = 0u;
+  return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
+}
+
+// 16-byte streaming load, not kept in L1 (every byte is read once).
+__device__ __forceinline__ uint4 ld_stream16(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+constexpr int AM16_WARPS = AM_FT / 32;     // warps per block
+constexpr int AM16_BLOCKS_PER_SM = 2;      // 16 resident warps per SM
+constexpr int AM16_UPT = 16;               // 16-byte loads per lane per chunk (one pass)
+constexpr int AM16_PER_MAX = 65;           // vectors per row (k + 1 <= 65)
+constexpr int AM16_SLOTS_MAX = 512;        // chunks per vector (V <= 2^21 at 512 units)
+constexpr int AM16_CHUNK_COST = 128;       // a chunk's fixed cost, in units of streaming
+
+// One warp per row: per vector the largest key over its chunks' slots, its
+// stats entry, and (k >= 0) the row's accept count and emitted token.  The decision's inputs are loaded first, so their latency overlaps
+// the keys' loads.  Every lane takes part.
+__device__ __forceinline__ void argmax16_row_done(const ArgmaxParams& P, int row, int lane,
+                                                  unsigned long long* red) {
+  const int per = P.vs.npos[0];
+  const int k = P.k;
+  int64_t xq[3];
+  float uq[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int i = lane + 32 * j;
+    xq[j] = (k > 0 && i < k) ? P.xs[row * P.xs_bs + i] : -1;
+    uq[j] = (k > 0 && i < k) ? P.u_acc[row * P.u_bs + i] : 2.f;
+  }
+  const bool alive_row = (k > 0 && P.alive) ? P.alive[row] != 0 : true;
+  // the inputs above are the caller's; the keys below come from pass 1
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const uint32_t cpv = P.cpv;
+  const uint32_t v0 = (uint32_t)row * per;
+  for (int p = lane; p < per; p += 32) red[p] = 0ull;
+  __syncwarp();
+  // the row's keys are contiguous: 8 loads per lane in flight at once
+  const unsigned long long* keys = P.partial + (size_t)v0 * cpv;
+  const uint32_t nk = (uint32_t)per * cpv;
+  for (uint32_t f0 = 0; f0 < nk; f0 += 32 * 8) {
+    unsigned long long kk[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t f = f0 + lane + 32 * i;
+      kk[i] = f < nk ? __ldcg(keys + f) : 0ull;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t f = f0 + lane + 32 * i;
+      if (f < nk) atomicMax(red + f / cpv, kk[i]);
     }
   }
+  __syncwarp();
+  for (int p = lane; p < per; p += 32) {
+    VecStats st;
+    st.m = 0.f; st.inv_s = 1.f; st.zf = 1.f; st.probe_p = 0.f;
+    st.kth = 0; st.vstar = 0; st.idx_cut = (int32_t)NO_CUT;
+    st.argmax = (int32_t)(0xFFFFFFFFu - (uint32_t)red[p]);
+    st.flags = 0; st.n_keep = -1; st.fb_why = 0; st.pad = 0;
+    P.stats[v0 + p] = st;
+  }
+  if (k < 0) return;
+  if (k == 0) {
+    if (lane == 0) {
+      P.y[row] = (int64_t)(0xFFFFFFFFu - (uint32_t)red[0]);
+      if (P.qx) P.qx[row] = 1.0f;
+    }
+    return;
+  }
+  // p_i(x_i) is 1 iff x_i is the target argmax; the ratio is then >= 1
+  // whatever q is, so the test is u < 1 (engine.py:290-292 with one-hot p).
+  int n = 0;
+  bool run = alive_row;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int i0 = 32 * j, i = i0 + lane;
+    if (i0 >= k) break;                                     // warp-uniform
+    bool ok = false;
+    if (i < k) {
+      const int64_t am = (int64_t)(0xFFFFFFFFu - (uint32_t)red[i]);
+      const float pxi = xq[j] == am ? 1.f : 0.f;
+      if (P.px) P.px[row * k + i] = pxi;
+      if (P.qx) P.qx[row * k + i] = nanf("");
+      ok = uq[j] < (pxi > 0.f ? 1.f : 0.f);
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, ok);
+    if (run) {
+      const int lim = min(32, k - i0);
+      const unsigned full = lim == 32 ? 0xffffffffu : ((1u << lim) - 1u);
+      if ((m & full) == full) n += lim;
+      else { n += __ffs(~m) - 1; run = false; }
+    }
+  }
+  if (lane == 0) {
+    P.n_acc[row] = n;
+    P.y[row] = (int64_t)(0xFFFFFFFFu - (uint32_t)red[n]);   // residual and bonus: argmax p_n
+  }
+}
+
+// Where chunk c lies: vector v = c / cpv, chunk j = c mod cpv covering
+// vector-local 16-byte units [a, b) of the vector's aligned body (b clipped
+// to the body), and for the vector's first chunk the head / tail elements.
+struct Am16Chunk {
+  const char* xb;                  // the vector's first element
+  const uint4* body;               // its 16-byte-aligned body
+  int a, b;                        // units of this chunk
+  int head, tail0;                 // unaligned head [0, head), tail [tail0, V)
+  uint32_t v, j;
+  int row;
+};
+
+template <int DT>
+__device__ __forceinline__ Am16Chunk am16_chunk(const ArgmaxParams& P, uint32_t c) {
+  Am16Chunk q;
+  q.v = c / P.cpv;
+  q.j = c - q.v * P.cpv;
+  int set, pos;
+  vec_locate(P.vs, (int)q.v, &set, &q.row, &pos);
+  q.xb = reinterpret_cast<const char*>(vec_ptr(P.vs, set, q.row, pos, DT));
+  const int V = P.V;
+  int head = (int)(((16u - (uint32_t)(reinterpret_cast<uintptr_t>(q.xb) & 15u)) & 15u) >> 1);
+  if (head > V) head = V;
+  const int nunits = (V - head) >> 3;
+  q.head = head;
+  q.tail0 = head + nunits * 8;
+  q.body = reinterpret_cast<const uint4*>(q.xb + (size_t)head * 2);
+  q.a = (int)q.j * P.ch;
+  q.b = min(q.a + P.ch, nunits);
+  return q;
+}
+
+// Issues a chunk's loads: AM16_UPT 16-byte units per lane, and (first chunk
+// of a vector) lane l < 8 the head element l, lane 8 + t the tail element t.
+__device__ __forceinline__ void am16_issue(const Am16Chunk& q, int V, int lane,
+                                           uint4 (&w)[AM16_UPT], uint32_t& ends) {
+#pragma unroll
+  for (int i = 0; i < AM16_UPT; ++i) {
+    const int u = q.a + lane + 32 * i;
+    w[i] = u < q.b ? ld_stream16(q.body + u) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  ends = 0xFFFFFFFFu;                                       // no element
+  if (q.j == 0) {
+    const uint16_t* x16 = reinterpret_cast<const uint16_t*>(q.xb);
+    if (lane < q.head) ends = x16[lane];
+    else if (lane >= 8 && lane - 8 < V - q.tail0) ends = x16[q.tail0 + lane - 8];
+  }
+}
+
+// Argmax of bf16 / fp16 vectors, pass 1 of 2 (first index of the maximum,
+// NaN counting as the largest value, -0 equal to +0): persistent and
+// warp-granular.  Each vector is cut into cpv chunks of ch 16-byte units
+// (ch <= 32 * AM16_UPT: one load per lane and unit group, all issued at
+// once); chunk c goes to warp c mod nwarps, so the warps sweep memory
+// together, round after round, and a warp's next loads go out right after
+// its current chunk's key is stored.  Per unit a lane takes one packed
+// NaN-propagating maximum of its eight elements (a NaN comes out as the
+// canonical positive NaN), keys it with -0 merged into +0, and keeps the
+// first of its units reaching its best key with that unit's data; the
+// chunk's key (value key, then the complement of the index) is resolved
+// inside the lanes' winning units from registers and stored to slot j of the
+// vector.  No fences, counters or atomics: pass 2 (argmax16_rows_kernel)
+// reads the keys after this kernel ends.
+template <int DT>
+__global__ void __launch_bounds__(AM_FT, AM16_BLOCKS_PER_SM) argmax16_kernel(ArgmaxParams P) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t gw = blockIdx.x * AM16_WARPS + (threadIdx.x >> 5);
+  const uint32_t nchunks = (uint32_t)P.nvec * P.cpv;
+  // pass 2 may launch now: its blocks load their own inputs, then wait for
+  // this grid to finish (griddepcontrol.wait) before reading the keys
+  asm volatile("griddepcontrol.launch_dependents;");
+  uint32_t c = gw;
+  if (c >= nchunks) return;
+  uint4 w[AM16_UPT];
+  uint32_t ends;
+  Am16Chunk q = am16_chunk<DT>(P, c);
+  am16_issue(q, P.V, lane, w, ends);
+  for (;;) {
+    uint32_t bk = 0u;                                       // 0: no unit yet
+    int bu = -1;
+    uint4 bw = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int i = 0; i < AM16_UPT; ++i) {
+      const int u = q.a + lane + 32 * i;
+      const uint32_t m = pmax2_nan<DT>(pmax2_nan<DT>(w[i].x, w[i].y),
+                                       pmax2_nan<DT>(w[i].z, w[i].w));
+      const uint32_t k2 = m ^ (((m >> 15) & 0x00010001u) * 0x7FFFu) ^ 0x80008000u;
+      uint32_t k = max(k2 & 0xFFFFu, k2 >> 16);
+      k += (k == 0x7FFFu);                                  // -0 -> +0
+      if (u < q.b && k > bk) { bk = k; bu = u; bw = w[i]; }
+    }
+    unsigned long long best = 0ull;
+    if (bu >= 0) {
+      const uint32_t ww[4] = {bw.x, bw.y, bw.z, bw.w};
+      int e = 7;
+#pragma unroll
+      for (int i = 7; i >= 0; --i)
+        if (elem_key16<DT>((i & 1) ? ww[i >> 1] >> 16 : ww[i >> 1]) == bk) e = i;
+      best = ((unsigned long long)bk << 32) | (0xFFFFFFFFu - (uint32_t)(q.head + bu * 8 + e));
+    }
+    if (ends != 0xFFFFFFFFu) {
+      const int jx = lane < 8 ? lane : q.tail0 + lane - 8;
+      const unsigned long long kk = ((unsigned long long)elem_key16<DT>(ends) << 32) |
+                                    (0xFFFFFFFFu - (uint32_t)jx);
+      best = kk > best ? kk : best;
+    }
+    const uint32_t hi = (uint32_t)(best >> 32);
+    const uint32_t mh = __reduce_max_sync(0xffffffffu, hi);
+    const uint32_t ml = __reduce_max_sync(0xffffffffu, hi == mh ? (uint32_t)best : 0u);
+    if (lane == 0) P.partial[(size_t)q.v * P.cpv + q.j] = ((unsigned long long)mh << 32) | ml;
+    c += P.nwarps;
+    if (c >= nchunks) break;
+    q = am16_chunk<DT>(P, c);
+    am16_issue(q, P.V, lane, w, ends);
+  }
+}
+
+// Pass 2: one warp per row reduces its vectors' chunk keys and finishes the
+// row (argmax16_row_done).  Launched as a programmatic dependent of pass 1:
+// it may start while pass 1 runs and waits for it before reading the keys.
+__global__ void __launch_bounds__(AM_FT) argmax16_rows_kernel(ArgmaxParams P) {
+  __shared__ unsigned long long red_all[AM16_WARPS][AM16_PER_MAX];
+  const int row = blockIdx.x * AM16_WARPS + (threadIdx.x >> 5);
+  if (row >= P.vs.nrows) return;
+  argmax16_row_done(P, row, threadIdx.x & 31, red_all[threadIdx.x >> 5]);
 }
 
 // ---------------------------------------------------------------------------
@@ -2527,7 +2774,9 @@ static WsLayout ws_layout(int n_rows, int n_vec, int V, bool small) {
   L.counter = off; off = align256(off + (size_t)n_rows * sizeof(int));
   L.vcounter = off; off = align256(off + (size_t)n_vec * sizeof(int));
   L.rcounter = off; off = align256(off + (size_t)n_rows * sizeof(int));
-  L.apartial = off; off = align256(off + (size_t)n_vec * NCH_MAX * sizeof(unsigned long long));
+  // keys: f32, NCH_MAX blocks per vector; 16-bit, one per chunk of >= 256 units
+  const size_t nkey = std::max<size_t>(NCH_MAX, ((size_t)V / 8 + 255) / 256);
+  L.apartial = off; off = align256(off + (size_t)n_vec * nkey * sizeof(unsigned long long));
   L.mat = off; off = align256(off + (small ? (size_t)n_vec * V * sizeof(float) : 0));
   L.nuc = off; off = align256(off + (small ? 0 : (size_t)n_vec * NUC_MAX * sizeof(unsigned long long)));
   L.total = off;
@@ -2538,10 +2787,68 @@ static int check_launch() {
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
 }
 
-static int launch_argmax(const ArgmaxParams& P, cudaStream_t st) {
-  if (P.dtype == SD_DTYPE_BF16) argmax_kernel<SD_DTYPE_BF16><<<P.nch * P.nvec, AM_FT, 0, st>>>(P);
-  else if (P.dtype == SD_DTYPE_F16) argmax_kernel<SD_DTYPE_F16><<<P.nch * P.nvec, AM_FT, 0, st>>>(P);
-  else argmax_kernel<SD_DTYPE_F32><<<P.nch * P.nvec, AM_FT, 0, st>>>(P);
+// argmax16_kernel geometry: the grid fills every SM (fewer warps for small
+// inputs); the chunk size ch (a multiple of 32 units, at most 32 * AM16_UPT,
+// at least 32 * AM16_UPT / 2 unless a vector is shorter, at most
+// AM16_SLOTS_MAX chunks per vector) minimises rounds * (ch + AM16_CHUNK_COST),
+// the time of the round-robin sweep with each chunk's fixed cost (its load
+// latency and key publishing) counted as AM16_CHUNK_COST units; the larger
+// chunk wins ties.
+struct Am16Geom {
+  int ch, cpv, grid;
+};
+static int am16_geom(int V, int nvec, Am16Geom* g) {
+  const int64_t nu = V / 8 > 0 ? V / 8 : 1;
+  if ((int64_t)nvec * nu > INT32_MAX / 2) return SD_ENOTSUP;
+  const int64_t full = (int64_t)device_sms() * AM16_BLOCKS_PER_SM * AM16_WARPS;
+  const int64_t cmax = 32 * AM16_UPT;
+  int64_t best_t = -1, best_ch = cmax;
+  for (int64_t ch = cmax; ch >= cmax / 2; ch -= 32) {
+    const int64_t cpv = (nu + ch - 1) / ch;
+    if (cpv > AM16_SLOTS_MAX) break;
+    const int64_t nch = (int64_t)nvec * cpv;
+    const int64_t t = (nch + full - 1) / full * (std::min(ch, nu) + AM16_CHUNK_COST);
+    if (best_t < 0 || t < best_t) { best_t = t; best_ch = ch; }
+  }
+  if (best_t < 0) return SD_ENOTSUP;        // V above 8 * AM16_SLOTS_MAX * 32 * AM16_UPT
+  const int64_t cpv = (nu + best_ch - 1) / best_ch;
+  const int64_t nwarps = std::min<int64_t>(full, (int64_t)nvec * cpv);
+  g->ch = (int)best_ch;
+  g->cpv = (int)cpv;
+  g->grid = (int)((nwarps + AM16_WARPS - 1) / AM16_WARPS);
+  return SD_OK;
+}
+
+// f32 logits: zero the two counter arrays, then argmax_kernel over (vector,
+// chunk) blocks.  16-bit logits: argmax16_kernel (chunk keys into P.partial,
+// nvec * cpv of them), then argmax16_rows_kernel.
+static int launch_argmax(ArgmaxParams P, cudaStream_t st) {
+  if (P.dtype == SD_DTYPE_F32) {
+    if (cudaMemsetAsync(P.vec_counter, 0, (size_t)P.nvec * sizeof(int), st) != cudaSuccess ||
+        cudaMemsetAsync(P.row_counter, 0, (size_t)P.vs.nrows * sizeof(int), st) != cudaSuccess)
+      return SD_ELAUNCH;
+    argmax_kernel<SD_DTYPE_F32><<<P.nch * P.nvec, AM_FT, 0, st>>>(P);
+    return check_launch();
+  }
+  if (P.vs.npos[0] > AM16_PER_MAX) return SD_EINVAL;
+  Am16Geom g;
+  if (int rc = am16_geom(P.V, P.nvec, &g)) return rc;
+  P.ch = g.ch;
+  P.cpv = (uint32_t)g.cpv;
+  P.nwarps = (uint32_t)g.grid * AM16_WARPS;
+  if (P.dtype == SD_DTYPE_BF16) argmax16_kernel<SD_DTYPE_BF16><<<g.grid, AM_FT, 0, st>>>(P);
+  else argmax16_kernel<SD_DTYPE_F16><<<g.grid, AM_FT, 0, st>>>(P);
+  if (int rc = check_launch()) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((P.vs.nrows + AM16_WARPS - 1) / AM16_WARPS));
+  cfg.blockDim = dim3(AM_FT);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, argmax16_rows_kernel, P) != cudaSuccess) return SD_ELAUNCH;
   return check_launch();
 }
 
@@ -2620,17 +2927,8 @@ static int run_sampling(const VecSet& vs, int nvec, int dtype, int V, float T, f
   return check_launch();
 }
 
-// Completion counters live at shape-dependent offsets, so every call zeroes
-// the ones it uses before its first kernel increments them.
-static int zero_argmax_counters(const WsLayout& L, int nvec, int nrows, char* ws, cudaStream_t st) {
-  if (cudaMemsetAsync(ws + L.vcounter, 0, (size_t)nvec * sizeof(int), st) != cudaSuccess) return 1;
-  if (cudaMemsetAsync(ws + L.rcounter, 0, (size_t)nrows * sizeof(int), st) != cudaSuccess) return 1;
-  return 0;
-}
-
 // Greedy verify round over caller-provided buffers: argmax of every target
-// vector, then per row the accepted prefix and the emitted token.  The two
-// counter arrays must hold zeros on entry (zeroed here on the stream).
+// vector, then per row the accepted prefix and the emitted token.
 static int launch_greedy_verify(const void* tgt, int64_t tgt_bs, int64_t tgt_ps, int dtype,
                                 const int64_t* xs, int64_t xs_bs, const float* u_acc,
                                 int64_t u_bs, const uint8_t* alive, int B, int k, int V,
@@ -2651,25 +2949,23 @@ static int launch_greedy_verify(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
   P.stats = stats;
   P.k = k; P.xs = xs; P.xs_bs = xs_bs; P.u_acc = u_acc; P.u_bs = u_bs; P.alive = alive;
   P.n_acc = n_acc; P.y = y; P.px = px; P.qx = qx;
-  if (cudaMemsetAsync(vcounter, 0, (size_t)nvec * sizeof(int), st) != cudaSuccess) return SD_ELAUNCH;
-  if (cudaMemsetAsync(rcounter, 0, (size_t)B * sizeof(int), st) != cudaSuccess) return SD_ELAUNCH;
   return launch_argmax(P, st);
 }
 
 // Fixed device scratch of sd_verify_greedy_static (one copy per device, in
-// this library's module): stats, chunk maxima and the two counter arrays.
+// this library's module): stats, the counters and the per-vector keys.
 static __device__ __align__(256) unsigned char g_static_scratch[SD_STATIC_SCRATCH_BYTES];
 
 struct StaticLayout {
-  size_t stats, partial, vcounter, rcounter, total;
+  size_t stats, vcounter, rcounter, partial, total;
 };
-static StaticLayout static_layout(int B, int nvec, int nch) {
+static StaticLayout static_layout(int B, int nvec, int nslot) {
   StaticLayout L;
   size_t off = 0;
   L.stats = off; off = align256(off + (size_t)nvec * sizeof(VecStats));
-  L.partial = off; off = align256(off + (size_t)nvec * nch * sizeof(unsigned long long));
   L.vcounter = off; off = align256(off + (size_t)nvec * sizeof(int));
   L.rcounter = off; off = align256(off + (size_t)B * sizeof(int));
+  L.partial = off; off = align256(off + (size_t)nvec * nslot * sizeof(unsigned long long));
   L.total = off;
   return L;
 }
@@ -2754,7 +3050,16 @@ int sd_verify_greedy_static(const void* tgt, int64_t tgt_bs, int64_t tgt_ps, int
   int rc = validate_common(dtype, V, 0.0f);
   if (rc) return rc;
   if (B <= 0 || k < 1 || k > 64 || !tgt || !xs || !u_acc || !n_acc || !y) return SD_EINVAL;
-  const StaticLayout L = static_layout(B, B * (k + 1), argmax_geom(V, dtype).nch);
+  // per vector: f32, one key per chunk block; 16-bit, one per warp slot
+  int nslot = 0;
+  if (dtype == SD_DTYPE_F32) {
+    nslot = argmax_geom(V, dtype).nch;
+  } else {
+    Am16Geom g;
+    if ((rc = am16_geom(V, B * (k + 1), &g))) return rc;
+    nslot = g.cpv;
+  }
+  const StaticLayout L = static_layout(B, B * (k + 1), nslot);
   if (L.total > SD_STATIC_SCRATCH_BYTES) return SD_ENOSPC;
   char* ws = nullptr;
   if ((rc = static_scratch(&ws))) return rc;
@@ -2791,7 +3096,6 @@ int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, in
     P.stats = reinterpret_cast<VecStats*>(ws + L.stats);
     P.k = 0; P.xs = nullptr; P.xs_bs = 0; P.u_acc = nullptr; P.u_bs = 0; P.alive = nullptr;
     P.n_acc = nullptr; P.y = x; P.px = nullptr; P.qx = qx;
-    if (zero_argmax_counters(L, B, B, ws, st)) return SD_ELAUNCH;
     return launch_argmax(P, st);
   }
   WsLayout L = ws_layout(B, B, V, use_small(V, dtype));
@@ -2834,7 +3138,6 @@ int sd_to_probs(const void* logits, int64_t row_stride, int dtype, int n_rows, i
     A.k = -1;   // stats only: no per-row decision
     A.xs = nullptr; A.xs_bs = 0; A.u_acc = nullptr; A.u_bs = 0; A.alive = nullptr;
     A.n_acc = nullptr; A.y = nullptr; A.px = nullptr; A.qx = nullptr;
-    if (zero_argmax_counters(L, n_rows, n_rows, ws, st)) return SD_ELAUNCH;
     if ((rc = launch_argmax(A, st))) return rc;
   } else {
     rc = run_sampling(vs, n_rows, dtype, V, temperature, top_p, top_k, L, ws, st, nullptr);

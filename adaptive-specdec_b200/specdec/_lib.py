@@ -127,9 +127,10 @@ def dtype_code(dt):
 class _Workspaces:
     """Per (device, stream) scratch, grown on demand.
 
-    Each call zeroes the completion counters it uses, so a workspace is
-    reusable by any later call on the same stream; one per stream keeps calls
-    on different streams from overlapping in the same scratch.
+    Each call zeroes the completion counters it uses (the greedy calls use
+    none), so a workspace is reusable by any later call on the same stream;
+    one per stream keeps calls on different streams from overlapping in the
+    same scratch.
     """
 
     def __init__(self):

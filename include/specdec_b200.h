@@ -43,9 +43,9 @@ int sd_version(void);
 
 /* Workspace bytes needed by sd_verify_sample / sd_draft_sample / sd_to_probs
  * for n_vec logits vectors of width V split over n_rows rows.  A workspace
- * needs no initialisation (each call zeroes the counters it uses) and may be
- * reused by later calls on the same stream; calls that overlap on the GPU
- * need separate workspaces. */
+ * needs no initialisation (each call zeroes the counters it uses; the greedy
+ * calls use none) and may be reused by later calls of any shape on the same
+ * stream; calls that overlap on the GPU need separate workspaces. */
 size_t sd_sampling_workspace_bytes(int n_rows, int n_vec, int V, int dtype);
 
 /* The first 4 bytes of a sampling workspace hold a sticky device status word:
@@ -96,7 +96,8 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
  * array inside this library, one per device, whose address is looked up once
  * per device (cudaGetSymbolAddress) on the first call there.  The call
  * allocates no memory.  Returns SD_ENOSPC when the shape needs more scratch
- * than that (about B*(k+1)*(48 + 8*chunks) bytes, chunks <= 64).
+ * than that (about B*(k+1)*(52 + 8*chunks) bytes; chunks = the vector's
+ * 16-byte units / 256..512, 43 at V = 151936).
  * Calls that overlap on one device (other streams, other host threads) share
  * the scratch and race: serialise them.  The first call on a device does the
  * one-time set-up (the symbol lookup); make it before any stream capture.

@@ -252,6 +252,106 @@ def test_greedy_argmax_ties_nan_and_alignment(dt):
     assert list(want[1:]) == [17, 25000, 0, 0, 0, V - 2]
 
 
+def _greedy_ref(tgt, xs, ua, alive=None):
+    """Greedy verify on torch: first-index argmax per vector, accepted prefix
+    (x_i equal to the argmax and u_i < 1, while alive), emitted token."""
+    am = tgt.float().argmax(-1)
+    k = xs.shape[1]
+    ok = (xs == am[:, :k]) & (ua < 1.0)
+    if alive is not None:
+        ok &= alive[:, None]
+    n = torch.where(ok.all(-1), torch.full_like(xs[:, 0], k), (~ok).int().argmax(-1).long())
+    return n, am.gather(1, n[:, None])[:, 0]
+
+
+def _greedy_inputs(B, k, V, g, p_match=0.7):
+    tgt = (torch.randn(B, k + 1, V, generator=g, device=DEV) * 3).to(torch.bfloat16)
+    am = tgt.float().argmax(-1)
+    xs = torch.where(torch.rand(B, k, generator=g, device=DEV) < p_match, am[:, :k],
+                     torch.randint(0, V, (B, k), generator=g, device=DEV)).contiguous()
+    return tgt, xs, torch.rand(B, k, generator=g, device=DEV), torch.rand(B, generator=g, device=DEV)
+
+
+def _verify_ws(tgt, drf, xs, ua, ur, T, ws):
+    """sd_verify_sample through the C ABI on a caller-given workspace."""
+    from specdec import _lib as L
+    B, k1, V = tgt.shape
+    n = torch.full((B,), -1, dtype=torch.long, device=DEV)
+    y = torch.full((B,), -1, dtype=torch.long, device=DEV)
+    rc = L.lib().sd_verify_sample(
+        L.ptr(tgt), tgt.stride(0), tgt.stride(1), L.ptr(drf), 0 if drf is None else drf.stride(0),
+        0 if drf is None else drf.stride(1), L.dtype_code(tgt.dtype), L.ptr(xs), xs.stride(0),
+        L.ptr(ua), ua.stride(0), L.ptr(ur), None, B, k1 - 1, V, T, 0.9, 0, L.ptr(n), L.ptr(y),
+        None, None, L.ptr(ws), ws.numel(), L.stream_ptr(tgt.device))
+    assert rc == 0
+    return n, y
+
+
+def test_greedy_workspace_needs_no_initialisation():
+    """The greedy calls keep no counters: a workspace full of random bytes,
+    shared by greedy calls of several shapes with sampling calls (which write
+    stats, lists and their own counters there) in between, gives the results
+    of a fresh one."""
+    from specdec import _lib as L
+    g = torch.Generator(device=DEV).manual_seed(11)
+    shapes = [(64, 4, 151936), (7, 2, 32003), (3, 64, 4096), (33, 8, 4096), (64, 4, 151936)]
+    nbytes = max(L.lib().sd_sampling_workspace_bytes(B, B * (2 * k + 1), V, 2) for B, k, V in shapes)
+    ws = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, generator=torch.Generator(
+        device=DEV).manual_seed(5), device=DEV)
+    for i, (B, k, V) in enumerate(shapes):
+        tgt, xs, ua, ur = _greedy_inputs(B, k, V, g, p_match=0.97 if k > 32 else 0.7)
+        for _ in range(2):                             # the same shape twice in a row
+            n, y = _verify_ws(tgt, None, xs, ua, ur, 0.0, ws)
+            n_r, y_r = _greedy_ref(tgt, xs, ua)
+            assert torch.equal(n, n_r) and torch.equal(y, y_r), (i, B, k, V)
+        drf = (tgt[:, :k].float() + torch.randn(B, k, V, generator=g, device=DEV)).to(tgt.dtype)
+        _verify_ws(tgt, drf, xs, ua, ur, 0.7, ws)     # a sampling call in between
+    torch.cuda.synchronize()
+
+
+def test_greedy_long_rows():
+    """k = 64 (65 vectors per row): accepted prefixes across the 32-lane groups
+    of the row decision."""
+    g = torch.Generator(device=DEV).manual_seed(13)
+    B, k, V = 6, 64, 2048
+    tgt, xs, ua, ur = _greedy_inputs(B, k, V, g, p_match=1.0)
+    ua[:, :] = 0.5
+    xs[1, 40] = (xs[1, 40] + 1) % V                    # rejected at 40
+    xs[2, 31] = (xs[2, 31] + 1) % V                    # at 31, the first group's last lane
+    xs[3, 32] = (xs[3, 32] + 1) % V                    # at 32, the second group's first lane
+    ua[4, 0] = 1.0                                     # u = 1 rejects even a match
+    alive = torch.ones(B, dtype=torch.bool, device=DEV)
+    alive[5] = False
+    n, y = S.verify_sample(tgt, None, xs, ua, ur, 0.0, alive=alive)
+    n_r, y_r = _greedy_ref(tgt, xs, ua, alive)
+    assert n.tolist() == [64, 40, 31, 32, 0, 0] and torch.equal(n, n_r)
+    assert torch.equal(y, y_r)
+
+
+def test_greedy_graph_replay():
+    """A captured greedy call (two kernels, no memset) replays on new inputs."""
+    B, k, V = 16, 4, 151936
+    g = torch.Generator(device=DEV).manual_seed(12)
+    bufs = _greedy_inputs(B, k, V, g)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        S.verify_sample(bufs[0], None, *bufs[1:], 0.0)  # the stream's workspace exists before capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        n, y = S.verify_sample(bufs[0], None, *bufs[1:], 0.0)
+    for rep in range(4):
+        new = _greedy_inputs(B, k, V, g)
+        for dst, src in zip(bufs, new):
+            dst.copy_(src)
+        graph.replay()
+        torch.cuda.synchronize()
+        n_r, y_r = _greedy_ref(bufs[0], bufs[1], bufs[2])
+        assert torch.equal(n, n_r) and torch.equal(y, y_r), rep
+    del graph
+
+
 # ---------------------------------------------------------------------------
 # draft step and the fp32-probability utilities
 # ---------------------------------------------------------------------------
