@@ -2128,12 +2128,13 @@ __device__ __forceinline__ uint32_t pmax2_nan(uint32_t a, uint32_t b) {
 }
 
 // Argmax (first index of the maximum, NaN counting as the largest value) of a
-// vector: block c of the vector reads 16-byte units [c cu, (c+1) cu) of its
-// aligned body with vectorised loads (block 0 also the unaligned head, the
-// last block the tail).  Each pass issues a thread's AM_UPT loads at once,
-// keys every unit by its maximum (for 16-bit logits one packed max of its
-// eight elements), takes the warp's largest key once, and builds per-element
-// keys only in the units that reach it (ties included: the first index among
+// vector, used for fp32 logits (bf16 / fp16 go through argmax16_kernel):
+// block c of the vector reads 16-byte units [c cu, (c+1) cu) of its aligned
+// body with vectorised loads (block 0 also the unaligned head, the last block
+// the tail).  Each pass issues a thread's AM_UPT loads at once, keys every
+// unit by its maximum (the 16-bit branch keys one packed max of its eight
+// elements), takes the warp's largest key once, and builds per-element keys
+// only in the units that reach it (ties included: the first index among
 // equal values is decided by the element keys).
 template <int DT>
 __global__ void __launch_bounds__(AM_FT) argmax_kernel(ArgmaxParams P) {
@@ -2248,8 +2249,9 @@ constexpr int AM16_PER_MAX = 65;           // vectors per row (k + 1 <= 65)
 constexpr int AM16_SLOTS_MAX = 512;        // chunks per vector (V <= 2^21 at 512 units)
 constexpr int AM16_CHUNK_COST = 128;       // a chunk's fixed cost, in units of streaming
 
-// One warp per row: per vector the largest key over its chunks' slots, its
-// stats entry, and (k >= 0) the row's accept count and emitted token.  The decision's inputs are loaded first, so their latency overlaps
+// One warp per row: per vector the largest key over its chunks' slots, then
+// either its stats entry (k < 0, to_probs) or the row's accept count and
+// emitted token (k >= 0).  The decision's inputs are loaded first, so their latency overlaps
 // the keys' loads.  Every lane takes part.
 __device__ __forceinline__ void argmax16_row_done(const ArgmaxParams& P, int row, int lane,
                                                   unsigned long long* red) {
@@ -2287,15 +2289,17 @@ __device__ __forceinline__ void argmax16_row_done(const ArgmaxParams& P, int row
     }
   }
   __syncwarp();
-  for (int p = lane; p < per; p += 32) {
-    VecStats st;
-    st.m = 0.f; st.inv_s = 1.f; st.zf = 1.f; st.probe_p = 0.f;
-    st.kth = 0; st.vstar = 0; st.idx_cut = (int32_t)NO_CUT;
-    st.argmax = (int32_t)(0xFFFFFFFFu - (uint32_t)red[p]);
-    st.flags = 0; st.n_keep = -1; st.fb_why = 0; st.pad = 0;
-    P.stats[v0 + p] = st;
+  if (k < 0) {                         // to_probs: the stats records are the output
+    for (int p = lane; p < per; p += 32) {
+      VecStats st;
+      st.m = 0.f; st.inv_s = 1.f; st.zf = 1.f; st.probe_p = 0.f;
+      st.kth = 0; st.vstar = 0; st.idx_cut = (int32_t)NO_CUT;
+      st.argmax = (int32_t)(0xFFFFFFFFu - (uint32_t)red[p]);
+      st.flags = 0; st.n_keep = -1; st.fb_why = 0; st.pad = 0;
+      P.stats[v0 + p] = st;
+    }
+    return;
   }
-  if (k < 0) return;
   if (k == 0) {
     if (lane == 0) {
       P.y[row] = (int64_t)(0xFFFFFFFFu - (uint32_t)red[0]);
