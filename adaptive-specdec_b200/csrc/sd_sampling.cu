@@ -1707,6 +1707,10 @@ template <int DT>
 __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   HistSmem& s = *reinterpret_cast<HistSmem*>(smem_raw);
+  // a row-draw pass launched as this grid's programmatic dependent may start
+  // its blocks as CTAs of this grid exit; it waits for the whole grid before
+  // it reads any stats
+  asm volatile("griddepcontrol.launch_dependents;");
   const int V = P.V;
   // log2(e) / T as c2 + c2l, c2 rounded down so that c2l > 0: y(x) is then
   // monotone and y(-inf) = -inf (a negative c2l would give -inf + inf)
@@ -1928,6 +1932,29 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
       }
     }
   }
+}
+
+// Row draws of a truncated sampling call, after the stats kernel: one CTA per
+// row (the stats kernel's thread layout and shared memory), launched as its
+// programmatic dependent so the launch overlaps the stats kernel's tail.  A
+// row whose vectors all took the list path draws on the finalize warps
+// (finish_row); a row with a vector from the exact fallback draws on all
+// threads over the whole vocabulary (fb_finish_row).
+__global__ void __launch_bounds__(HT, 1) row_draw_kernel(StatsParams P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  HistSmem& s = *reinterpret_cast<HistSmem*>(smem_raw);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int row = blockIdx.x;
+  const int npos = P.vs.npos[0] + P.vs.npos[1];
+  if (threadIdx.x == 0) {
+    int fb = 0;
+    for (int i = 0; i < npos; ++i)
+      fb |= __ldcg(&P.stats[(int64_t)row * npos + i].flags) & F_FALLBACK;
+    s.last_row = fb;
+  }
+  __syncthreads();
+  if (s.last_row) fb_finish_row<HT>(s, P, row);
+  else if (threadIdx.x >= FIN0) finish_row(s, P, row);
 }
 
 // ---------------------------------------------------------------------------
@@ -2733,6 +2760,8 @@ static int device_sms() {
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(HistSmem));
     cudaFuncSetAttribute(hist_stats_kernel<SD_DTYPE_F16>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(HistSmem));
+    cudaFuncSetAttribute(row_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(HistSmem));
     g_attr_set[dev] = true;
   }
   return g_num_sms[dev];
@@ -2886,21 +2915,19 @@ static int run_sampling(const VecSet& vs, int nvec, int dtype, int V, float T, f
     if (int rc = check_launch()) return rc;
   } else {
     const bool truncated = (top_p > 0.0f && top_p < 1.0f) || (top_k > 0 && top_k < V);
-    const bool fused = draw != nullptr && truncated;
+    const bool rowpass = draw != nullptr && truncated;   // rows drawn by row_draw_kernel
     StatsParams P = {};
     P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec; P.T = T; P.top_p = top_p;
     P.top_k = top_k; P.stats = stats;
     P.nuc = draw ? reinterpret_cast<unsigned long long*>(ws + L.nuc) : nullptr;
     P.row_ctr = reinterpret_cast<int*>(ws + L.rcounter);
     P.status = reinterpret_cast<int*>(ws + L.status);
-    P.fused = fused;
-    if (fused) {
+    P.fused = false;
+    if (rowpass) {
       P.k = draw->k; P.u_acc = draw->u_acc; P.u_bs = draw->u_bs; P.u_res = draw->u_res;
       P.alive = draw->alive; P.n_acc = draw->n_acc; P.y = draw->y; P.px = draw->px;
       P.qx = draw->qx; P.y_prob = draw->y_prob;
     }
-    if (fused && cudaMemsetAsync(ws + L.rcounter, 0, (size_t)rows * sizeof(int), st) != cudaSuccess)
-      return SD_ELAUNCH;
     const int nsm = device_sms();
     int grid = nsm;
     if (grid > GRID_MAX) grid = GRID_MAX;
@@ -2910,8 +2937,22 @@ static int run_sampling(const VecSet& vs, int nvec, int dtype, int V, float T, f
     else
       hist_stats_kernel<SD_DTYPE_F16><<<grid, HT, sizeof(HistSmem), st>>>(P);
     if (int rc = check_launch()) return rc;
+    if (rowpass) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)rows);
+      cfg.blockDim = dim3(HT);
+      cfg.dynamicSmemBytes = sizeof(HistSmem);
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, row_draw_kernel, P) != cudaSuccess) return SD_ELAUNCH;
+      if (int rc = check_launch()) return rc;
+    }
 
-    need_finish = draw != nullptr && !fused;
+    need_finish = draw != nullptr && !rowpass;
     if (need_finish &&
         cudaMemsetAsync(ws + L.counter, 0, (size_t)rows * sizeof(int), st) != cudaSuccess)
       return SD_ELAUNCH;
