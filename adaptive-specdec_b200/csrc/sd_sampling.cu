@@ -1934,27 +1934,159 @@ __global__ void __launch_bounds__(HT, 1) hist_stats_kernel(StatsParams P) {
   }
 }
 
+// Inverse-CDF draw over p's kept entries when they are listed (up to NUC_MAX
+// of them), on all NT threads: each entry's weight (r = (p - q)+ for a
+// residual draw, p for the bonus draw, and p again when the residual mass is
+// <= 1e-9, sampling.py:86-89), the entries put in vocabulary order by a
+// bitonic sort of (index, position) pairs, one block scan of the weights in
+// that order, and the entry whose [prefix, prefix + w) holds u * R.  When
+// rounding leaves no such entry: the last one with a positive weight, else the
+// first (reference engine.py:294-303).
+template <int NT>
+__device__ void row_draw_listed(HistSmem& s, const StatsParams& P, int row, int n, int ppos,
+                                bool resid, const VecStats& stp, const VecStats& stq,
+                                const void* xp, const void* xq) {
+  const int t = threadIdx.x;
+  const int npos = P.vs.npos[0] + P.vs.npos[1];
+  const int cnt = stp.n_keep;
+  int N = 1;
+  while (N < cnt) N <<= 1;                              // <= NUC_MAX <= SEL_CAP
+  const unsigned long long* src = P.nuc + (int64_t)(row * npos + ppos) * NUC_MAX;
+  float* rr = s.u.l.p;                                  // weight r of entry i
+  float* pv = s.u.l.ecache;                             // p of entry i
+  double rs = 0.0, ps = 0.0;
+  for (int i = t; i < N; i += NT) {
+    unsigned long long sk = ~0ull;
+    if (i < cnt) {
+      const unsigned long long key = __ldcg(src + i);
+      const uint32_t j = list_idx(key);
+      const float pj = __fdiv_rn(prob_of(list_val(key), P.T, stp.m, stp.inv_s), stp.zf);
+      float r = pj;
+      if (resid && pj != 0.f)
+        r = fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, (int64_t)j)), 0.f);
+      rr[i] = r;
+      pv[i] = pj;
+      rs += (double)r;
+      ps += (double)pj;
+      sk = ((unsigned long long)j << 32) | (uint32_t)i;
+    }
+    s.u.l.sel[i] = sk;
+  }
+  const double R0 = block_sum<double>(rs, s.dred);
+  const double Pm = block_sum<double>(ps, s.dred);
+  const bool use_p = !resid || __double2float_rn(R0) <= 1e-9f;
+  const float* wv = use_p ? pv : rr;
+  const double tgt = (double)P.u_res[row] * (use_p ? Pm : R0);
+  // ascending (index, position): vocabulary order
+  for (int k2 = 2; k2 <= N; k2 <<= 1) {
+    for (int j2 = k2 >> 1; j2 > 0; j2 >>= 1) {
+      for (int i = t; i < N; i += NT) {
+        const int ixj = i ^ j2;
+        if (ixj > i) {
+          const unsigned long long a = s.u.l.sel[i], b = s.u.l.sel[ixj];
+          if (((i & k2) == 0) ? (a > b) : (a < b)) { s.u.l.sel[i] = b; s.u.l.sel[ixj] = a; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // each thread E consecutive entries; block scan of their sums
+  const int E = (N + NT - 1) / NT;
+  double loc = 0.0;
+  for (int e = 0; e < E; ++e) {
+    const int i = t * E + e;
+    if (i < cnt) loc += (double)wv[(uint32_t)s.u.l.sel[i]];
+  }
+  // (index << 32 | position) of the crossing entry and of the last entry
+  // with a positive weight
+  unsigned long long* pick = reinterpret_cast<unsigned long long*>(&s.sc_pre);
+  unsigned long long* last = reinterpret_cast<unsigned long long*>(&s.sc_y);   // + 1; 0: none
+  if (t == 0) { pick[0] = ~0ull; *last = 0ull; }
+  double tot;
+  double run = block_excl_scan<double>(loc, s.dred, &tot);
+  for (int e = 0; e < E; ++e) {
+    const int i = t * E + e;
+    if (i < cnt) {
+      const unsigned long long sk = s.u.l.sel[i];
+      const float w = wv[(uint32_t)sk];
+      if (run <= tgt && run + (double)w > tgt) atomicMin(pick, sk);
+      if (w > 0.f) atomicMax(last, sk + 1ull);
+      run += (double)w;
+    }
+  }
+  __syncthreads();
+  if (t == 0) {
+    const unsigned long long sk = pick[0] != ~0ull ? pick[0]
+                                  : *last > 0ull ? *last - 1ull : s.u.l.sel[0];
+    if (P.n_acc) P.n_acc[row] = n;
+    P.y[row] = (int64_t)(sk >> 32);
+    if (P.y_prob) P.y_prob[row] = pv[(uint32_t)sk];   // = p at the drawn index
+  }
+}
+
 // Row draws of a truncated sampling call, after the stats kernel: one CTA per
 // row (the stats kernel's thread layout and shared memory), launched as its
-// programmatic dependent so the launch overlaps the stats kernel's tail.  A
-// row whose vectors all took the list path draws on the finalize warps
-// (finish_row); a row with a vector from the exact fallback draws on all
-// threads over the whole vocabulary (fb_finish_row).
+// programmatic dependent so the launch overlaps the stats kernel's tail.
+// Warp 0 takes the accept test (the accepted prefix n, and p(x_i), q(x_i));
+// the draw then follows the kept set of the pick vector: at most 32 listed
+// entries, one warp (finish_row); more listed entries, all threads
+// (row_draw_listed); a kept set that is not listed (the exact fallback's
+// vectors), all threads over the whole vocabulary (fb_finish_row).
 __global__ void __launch_bounds__(HT, 1) row_draw_kernel(StatsParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   HistSmem& s = *reinterpret_cast<HistSmem*>(smem_raw);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int row = blockIdx.x;
-  const int npos = P.vs.npos[0] + P.vs.npos[1];
-  if (threadIdx.x == 0) {
-    int fb = 0;
-    for (int i = 0; i < npos; ++i)
-      fb |= __ldcg(&P.stats[(int64_t)row * npos + i].flags) & F_FALLBACK;
-    s.last_row = fb;
+  const int npos0 = P.vs.npos[0], npos = P.vs.npos[0] + P.vs.npos[1];
+  const int vrow = row * npos;
+  const int k = P.k;
+  // the row's stats records, all in one round trip (npos * 48 bytes)
+  VecStats* rst = reinterpret_cast<VecStats*>(s.u.l.ecache);
+  {
+    const int* src = reinterpret_cast<const int*>(P.stats + vrow);
+    int* dst = reinterpret_cast<int*>(rst);
+    for (int i = threadIdx.x; i < npos * 12; i += HT) dst[i] = __ldcg(src + i);
   }
   __syncthreads();
-  if (s.last_row) fb_finish_row<HT>(s, P, row);
-  else if (threadIdx.x >= FIN0) finish_row(s, P, row);
+  if (threadIdx.x < 32) {
+    // accepted prefix: one lane per draft position (engine.py:286-293)
+    const int lane = threadIdx.x;
+    int n = k;
+    for (int base = 0; base < k; base += 32) {
+      const int i = base + lane;
+      bool acc = false;
+      if (i < k) {
+        const float pxi = rst[i].probe_p;
+        const float qxi = rst[npos0 + i].probe_p;
+        const float thr = fminf(__fdiv_rn(pxi, fmaxf(qxi, 1e-10f)), 1.0f);
+        if (P.px) P.px[row * k + i] = pxi;
+        if (P.qx) P.qx[row * k + i] = qxi;
+        acc = P.u_acc[row * P.u_bs + i] < thr;
+      }
+      const unsigned rm = __ballot_sync(0xffffffffu, i < k && !acc);
+      if (rm && n == k) n = base + __ffs(rm) - 1;
+    }
+    if (P.alive && P.alive[row] == 0) n = 0;
+    if (lane == 0) s.sc_n = n;
+  }
+  __syncthreads();
+  const int n = s.sc_n;
+  const bool resid = n < k;
+  const int ppos = resid ? n : k;
+  const VecStats stp = rst[ppos];
+  const VecStats stq = resid ? rst[npos0 + n] : stp;
+  __syncthreads();                                    // rst is overwritten below
+  if (!(stp.flags & F_LISTED)) {
+    fb_finish_row<HT>(s, P, row);
+    return;
+  }
+  if (stp.n_keep <= 32) {
+    if (threadIdx.x >= FIN0) finish_row(s, P, row);
+    return;
+  }
+  const void* xp = vec_ptr(P.vs, 0, row, ppos, P.dtype);
+  const void* xq = resid ? vec_ptr(P.vs, 1, row, n, P.dtype) : xp;
+  row_draw_listed<HT>(s, P, row, n, ppos, resid, stp, stq, xp, xq);
 }
 
 // ---------------------------------------------------------------------------
