@@ -394,7 +394,25 @@ struct StatsParams {
   const float* u_res;
   const uint8_t* alive;
   int64_t* n_acc; int64_t* y; float* px; float* qx; float* y_prob;
+  // draft distributions given as probabilities (null: computed from the draft
+  // logits of set 1): row b, position i at qprob + b q_bs + i q_ps, [V] fp32
+  const float* qprob; int64_t q_bs, q_ps;
 };
+
+// q at element j of the draft distribution of row `row`, position `n`: the
+// caller's probability row when given, else from the draft vector's stats.
+__device__ __forceinline__ float q_at(const StatsParams& P, const VecStats& stq, const void* xq,
+                                      int row, int n, int64_t j);
+
+// q(x_i) of the accept test of row `row`, position i.
+__device__ __forceinline__ float q_probe(const StatsParams& P, int row, int i) {
+  const int npos0 = P.vs.npos[0], npos = P.vs.npos[0] + P.vs.npos[1];
+  if (P.qprob) {
+    const int64_t x = P.vs.probe[row * P.vs.probe_bs + i];
+    return __ldg(P.qprob + row * P.q_bs + i * P.q_ps + x);
+  }
+  return __ldcg(&P.stats[(int64_t)row * npos + npos0 + i].probe_p);
+}
 
 // ---- streaming ---------------------------------------------------------------
 
@@ -668,6 +686,12 @@ __device__ __forceinline__ float stats_prob(const VecStats& st, const void* x, i
   const bool kept = kx >= st.kth && (kx > st.vstar || (kx == st.vstar && j <= (int64_t)st.idx_cut));
   if (!kept) return 0.f;
   return __fdiv_rn(prob_of(xv, T, st.m, st.inv_s), st.zf);
+}
+
+__device__ __forceinline__ float q_at(const StatsParams& P, const VecStats& stq, const void* xq,
+                                      int row, int n, int64_t j) {
+  if (P.qprob) return __ldg(P.qprob + row * P.q_bs + n * P.q_ps + j);
+  return stats_prob(stq, xq, P.dtype, P.T, j);
 }
 
 __device__ __forceinline__ VecStats load_stats_cg(const VecStats* p) {
@@ -1005,7 +1029,7 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
       bool acc = false;
       if (i < k) {
         const float pxi = __ldcg(&P.stats[vrow + i].probe_p);
-        const float qxi = __ldcg(&P.stats[vrow + npos0 + i].probe_p);
+        const float qxi = q_probe(P, row, i);
         const float thr = fminf(__fdiv_rn(pxi, fmaxf(qxi, 1e-10f)), 1.0f);
         if (P.px) P.px[row * k + i] = pxi;
         if (P.qx) P.qx[row * k + i] = qxi;
@@ -1025,7 +1049,7 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
   VecStats stq = stp;
   const void* xp = vec_ptr(P.vs, 0, row, ppos, P.dtype);
   const void* xq = xp;
-  if (resid) {
+  if (resid && !P.qprob) {
     stq = load_stats_cg(P.stats + vrow + npos0 + n);
     xq = vec_ptr(P.vs, 1, row, n, P.dtype);
   }
@@ -1043,7 +1067,7 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
       float pp = valid ? __fdiv_rn(prob_of(list_val(key), P.T, stp.m, stp.inv_s), stp.zf) : 0.f;
       float rr = pp;
       if (resid && valid && pp != 0.f)
-        rr = fmaxf(__fsub_rn(pp, stats_prob(stq, xq, P.dtype, P.T, jj)), 0.f);
+        rr = fmaxf(__fsub_rn(pp, q_at(P, stq, xq, row, n, jj)), 0.f);
 #pragma unroll
       for (int k2 = 2; k2 <= 32; k2 <<= 1) {
 #pragma unroll
@@ -1106,7 +1130,7 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
         const float pj = __fdiv_rn(prob_of(list_val(key), P.T, stp.m, stp.inv_s), stp.zf);
         float r = pj;
         if (resid && pj != 0.f)
-          r = fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, (int64_t)j)), 0.f);
+          r = fmaxf(__fsub_rn(pj, q_at(P, stq, xq, row, n, (int64_t)j)), 0.f);
         s.u.l.sel[i] = j;
         ra[i] = r;
         ra[RANK_MAX + i] = pj;
@@ -1161,7 +1185,7 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
       const int64_t j = (int64_t)s.u.l.sel[i];
       const float pj = stats_prob(stp, xp, P.dtype, P.T, j);
       float r = pj;
-      if (resid && pj != 0.f) r = fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+      if (resid && pj != 0.f) r = fmaxf(__fsub_rn(pj, q_at(P, stq, xq, row, n, j)), 0.f);
       s.u.l.p[i] = r;
       rs += (double)r;
     }
@@ -1200,7 +1224,7 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
     for (int j = t; j < P.V; j += CT) {
       const float pj = stats_prob(stp, xp, P.dtype, P.T, j);
       ps += (double)pj;
-      if (resid && pj != 0.f) rs += (double)fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+      if (resid && pj != 0.f) rs += (double)fmaxf(__fsub_rn(pj, q_at(P, stq, xq, row, n, j)), 0.f);
     }
     double R = c_sum<double>(rs, s.dred);
     const double Pm = c_sum<double>(ps, s.dred);
@@ -1218,7 +1242,7 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
         float v = 0.f;
         if (j < P.V) {
           v = stats_prob(stp, xp, P.dtype, P.T, j);
-          if (!use_p && v != 0.f) v = fmaxf(__fsub_rn(v, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+          if (!use_p && v != 0.f) v = fmaxf(__fsub_rn(v, q_at(P, stq, xq, row, n, j)), 0.f);
         }
         r[e] = v;
         ls += (double)v;
@@ -1240,7 +1264,7 @@ __device__ void finish_row(HistSmem& s, const StatsParams& P, int row) {
     if (t == 0 && s.sc_y < 0) {
       for (int j = P.V - 1; j >= 0; --j) {
         float v = stats_prob(stp, xp, P.dtype, P.T, j);
-        if (!use_p && v != 0.f) v = fmaxf(__fsub_rn(v, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+        if (!use_p && v != 0.f) v = fmaxf(__fsub_rn(v, q_at(P, stq, xq, row, n, j)), 0.f);
         if (v > 0.f) { s.sc_y = j; break; }
       }
       if (s.sc_y < 0) s.sc_y = 0;
@@ -1581,7 +1605,7 @@ __device__ void fb_finish_row(HistSmem& s, const StatsParams& P, int row) {
       bool acc = false;
       if (i < k) {
         const float pxi = __ldcg(&P.stats[vrow + i].probe_p);
-        const float qxi = __ldcg(&P.stats[vrow + npos0 + i].probe_p);
+        const float qxi = q_probe(P, row, i);
         const float thr = fminf(__fdiv_rn(pxi, fmaxf(qxi, 1e-10f)), 1.0f);
         if (P.px) P.px[row * k + i] = pxi;
         if (P.qx) P.qx[row * k + i] = qxi;
@@ -1601,7 +1625,7 @@ __device__ void fb_finish_row(HistSmem& s, const StatsParams& P, int row) {
   VecStats stq = stp;
   const void* xp = vec_ptr(P.vs, 0, row, ppos, P.dtype);
   const void* xq = xp;
-  if (resid) {
+  if (resid && !P.qprob) {
     stq = load_stats_cg(P.stats + vrow + npos0 + n);
     xq = vec_ptr(P.vs, 1, row, n, P.dtype);
   }
@@ -1626,7 +1650,7 @@ __device__ void fb_finish_row(HistSmem& s, const StatsParams& P, int row) {
         tpm += (double)pj;
         if (pj > 0.f) last_p = j;
         if (resid && pj != 0.f) {
-          const float r = fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+          const float r = fmaxf(__fsub_rn(pj, q_at(P, stq, xq, row, n, j)), 0.f);
           tr += (double)r;
           if (r > 0.f) last_r = j;
         }
@@ -1675,7 +1699,7 @@ __device__ void fb_finish_row(HistSmem& s, const StatsParams& P, int row) {
       if (j < V) {
         val = stats_prob(stp, xp, P.dtype, P.T, j);
         if (!use_p && val != 0.f)
-          val = fmaxf(__fsub_rn(val, stats_prob(stq, xq, P.dtype, P.T, j)), 0.f);
+          val = fmaxf(__fsub_rn(val, q_at(P, stq, xq, row, n, j)), 0.f);
       }
       vals[e] = val;
       ls += (double)val;
@@ -1963,7 +1987,7 @@ __device__ void row_draw_listed(HistSmem& s, const StatsParams& P, int row, int 
       const float pj = __fdiv_rn(prob_of(list_val(key), P.T, stp.m, stp.inv_s), stp.zf);
       float r = pj;
       if (resid && pj != 0.f)
-        r = fmaxf(__fsub_rn(pj, stats_prob(stq, xq, P.dtype, P.T, (int64_t)j)), 0.f);
+        r = fmaxf(__fsub_rn(pj, q_at(P, stq, xq, row, n, (int64_t)j)), 0.f);
       rr[i] = r;
       pv[i] = pj;
       rs += (double)r;
@@ -2057,7 +2081,7 @@ __global__ void __launch_bounds__(HT, 1) row_draw_kernel(StatsParams P) {
       bool acc = false;
       if (i < k) {
         const float pxi = rst[i].probe_p;
-        const float qxi = rst[npos0 + i].probe_p;
+        const float qxi = P.qprob ? q_probe(P, row, i) : rst[npos0 + i].probe_p;
         const float thr = fminf(__fdiv_rn(pxi, fmaxf(qxi, 1e-10f)), 1.0f);
         if (P.px) P.px[row * k + i] = pxi;
         if (P.qx) P.qx[row * k + i] = qxi;
@@ -2074,7 +2098,7 @@ __global__ void __launch_bounds__(HT, 1) row_draw_kernel(StatsParams P) {
   const bool resid = n < k;
   const int ppos = resid ? n : k;
   const VecStats stp = rst[ppos];
-  const VecStats stq = resid ? rst[npos0 + n] : stp;
+  const VecStats stq = resid && !P.qprob ? rst[npos0 + n] : stp;
   __syncthreads();                                    // rst is overwritten below
   if (!(stp.flags & F_LISTED)) {
     fb_finish_row<HT>(s, P, row);
@@ -2085,7 +2109,7 @@ __global__ void __launch_bounds__(HT, 1) row_draw_kernel(StatsParams P) {
     return;
   }
   const void* xp = vec_ptr(P.vs, 0, row, ppos, P.dtype);
-  const void* xq = resid ? vec_ptr(P.vs, 1, row, n, P.dtype) : xp;
+  const void* xq = resid && !P.qprob ? vec_ptr(P.vs, 1, row, n, P.dtype) : xp;
   row_draw_listed<HT>(s, P, row, n, ppos, resid, stp, stq, xp, xq);
 }
 
@@ -3025,6 +3049,7 @@ struct DrawSpec {
   const float* u_res;
   const uint8_t* alive;
   int64_t* n_acc; int64_t* y; float* px; float* qx; float* y_prob;
+  const float* qprob; int64_t q_bs, q_ps;     // draft distributions as probabilities, or null
 };
 
 // Non-greedy path: stats for every vector of `vs`, then (if `draw`) each
@@ -3047,7 +3072,9 @@ static int run_sampling(const VecSet& vs, int nvec, int dtype, int V, float T, f
     if (int rc = check_launch()) return rc;
   } else {
     const bool truncated = (top_p > 0.0f && top_p < 1.0f) || (top_k > 0 && top_k < V);
-    const bool rowpass = draw != nullptr && truncated;   // rows drawn by row_draw_kernel
+    // rows drawn by row_draw_kernel (always when the draft distributions come
+    // as probabilities: finish_kernel reads them from draft stats)
+    const bool rowpass = draw != nullptr && (truncated || draw->qprob != nullptr);
     StatsParams P = {};
     P.vs = vs; P.dtype = dtype; P.V = V; P.nvec = nvec; P.T = T; P.top_p = top_p;
     P.top_k = top_k; P.stats = stats;
@@ -3059,6 +3086,7 @@ static int run_sampling(const VecSet& vs, int nvec, int dtype, int V, float T, f
       P.k = draw->k; P.u_acc = draw->u_acc; P.u_bs = draw->u_bs; P.u_res = draw->u_res;
       P.alive = draw->alive; P.n_acc = draw->n_acc; P.y = draw->y; P.px = draw->px;
       P.qx = draw->qx; P.y_prob = draw->y_prob;
+      P.qprob = draw->qprob; P.q_bs = draw->q_bs; P.q_ps = draw->q_ps;
     }
     const int nsm = device_sms();
     int grid = nsm;
@@ -3216,7 +3244,38 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
   vs.base[1] = drf; vs.bs[1] = drf_bs; vs.ps[1] = drf_ps; vs.npos[1] = k;
   vs.probe = xs; vs.probe_bs = xs_bs; vs.probe_npos[0] = k; vs.probe_npos[1] = k;
   vs.nrows = B;
-  DrawSpec d = {k, u_acc, u_bs, u_res, alive, n_acc, y, px, qx, nullptr};
+  DrawSpec d = {k, u_acc, u_bs, u_res, alive, n_acc, y, px, qx, nullptr, nullptr, 0, 0};
+  return run_sampling(vs, nvec, dtype, V, temperature, top_p, top_k, L, ws, st, &d);
+}
+
+int sd_verify_sample_qprobs(const void* tgt, int64_t tgt_bs, int64_t tgt_ps, int dtype,
+                            const float* qprobs, int64_t q_bs, int64_t q_ps,
+                            const int64_t* xs, int64_t xs_bs, const float* u_acc, int64_t u_bs,
+                            const float* u_res, const uint8_t* alive,
+                            int B, int k, int V, float temperature, float top_p, int top_k,
+                            int64_t* n_acc, int64_t* y, float* px, float* qx,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = validate_common(dtype, V, temperature);
+  if (rc) return rc;
+  if (B <= 0 || k < 1 || k > 64 || !tgt || !xs || !u_acc || !u_res || !n_acc || !y || !workspace)
+    return SD_EINVAL;
+  const bool greedy = !(temperature > 0.0f);
+  if (greedy)                       // one-hot p: q plays no part (sd_verify_sample's greedy path)
+    return sd_verify_sample(tgt, tgt_bs, tgt_ps, nullptr, 0, 0, dtype, xs, xs_bs, u_acc, u_bs,
+                            u_res, alive, B, k, V, temperature, top_p, top_k, n_acc, y, px, qx,
+                            workspace, workspace_bytes, stream);
+  if (!qprobs) return SD_EINVAL;
+  if (use_small(V, dtype)) return SD_ENOTSUP;       // the list kernels: bf16 / fp16, V > 2048
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = reinterpret_cast<char*>(workspace);
+  const int nvec = B * (k + 1);
+  WsLayout L = ws_layout(B, nvec, V, false);
+  if (workspace_bytes < L.total) return SD_ENOSPC;
+  VecSet vs = {};
+  vs.base[0] = tgt; vs.bs[0] = tgt_bs; vs.ps[0] = tgt_ps; vs.npos[0] = k + 1; vs.npos[1] = 0;
+  vs.probe = xs; vs.probe_bs = xs_bs; vs.probe_npos[0] = k; vs.probe_npos[1] = 0;
+  vs.nrows = B;
+  DrawSpec d = {k, u_acc, u_bs, u_res, alive, n_acc, y, px, qx, nullptr, qprobs, q_bs, q_ps};
   return run_sampling(vs, nvec, dtype, V, temperature, top_p, top_k, L, ws, st, &d);
 }
 
@@ -3277,7 +3336,7 @@ int sd_draft_sample(const void* logits, int64_t row_stride, int dtype, int B, in
   }
   WsLayout L = ws_layout(B, B, V, use_small(V, dtype));
   if (workspace_bytes < L.total) return SD_ENOSPC;
-  DrawSpec d = {0, nullptr, 0, u, nullptr, nullptr, x, nullptr, nullptr, qx};
+  DrawSpec d = {0, nullptr, 0, u, nullptr, nullptr, x, nullptr, nullptr, qx, nullptr, 0, 0};
   return run_sampling(vs, B, dtype, V, temperature, top_p, top_k, L, ws, st, &d);
 }
 

@@ -24,6 +24,9 @@ _SIGNATURES = {
     "sd_verify_sample": ([_vp, _i64, _i64, _vp, _i64, _i64, _i32, _vp, _i64, _vp, _i64, _vp, _vp,
                           _i32, _i32, _i32, _f32, _f32, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp],
                          _i32),
+    "sd_verify_sample_qprobs": ([_vp, _i64, _i64, _i32, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp,
+                                 _vp, _i32, _i32, _i32, _f32, _f32, _i32, _vp, _vp, _vp, _vp, _vp,
+                                 _sz, _vp], _i32),
     "sd_verify_greedy_static": ([_vp, _i64, _i64, _i32, _vp, _i64, _vp, _i64, _vp, _i32, _i32,
                                  _i32, _vp, _vp, _vp, _vp, _vp], _i32),
     "sd_draft_sample": ([_vp, _i64, _i32, _i32, _i32, _vp, _f32, _f32, _i32, _vp, _vp, _vp, _sz,

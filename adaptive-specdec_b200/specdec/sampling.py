@@ -22,7 +22,7 @@ import torch
 from specdec import _lib as L
 
 __all__ = ["to_probs", "sample_from_probs", "residual_probs", "gather_prob",
-           "verify_sample", "draft_sample"]
+           "verify_sample", "verify_sample_probs", "draft_sample"]
 
 
 def _knobs(temperature, top_p, top_k):
@@ -161,6 +161,56 @@ def verify_sample(target_logits, draft_logits, draft_ids, u_acc, u_res, temperat
                                      L.ptr(ur), L.ptr(al), B, k, V, T, tp, tk, L.ptr(n_acc),
                                      L.ptr(y), L.ptr(px), L.ptr(qx), L.ptr(ws), ws.numel(),
                                      L.stream_ptr(dev)), "verify_sample")
+    if return_probs:
+        return n_acc, y, px, qx
+    return n_acc, y
+
+
+def verify_sample_probs(target_logits, draft_probs, draft_ids, u_acc, u_res, temperature=1.0,
+                        top_p=1.0, top_k=0, alive=None, return_probs=False):
+    """The fused verify round with the draft distributions given as
+    probabilities: q_i = draft_probs[:, i] (fp32 [B, k, V], used as given),
+    as a serving engine's rejection sampler holds them.  Otherwise as
+    ``verify_sample``: to_probs (temperature, top-p, top-k) on the target
+    logits [B, k+1, V], the accept test u < min(1, p(x)/max(q(x), 1e-10)), the
+    residual draw from norm((p - q)+) at the first rejection or the bonus draw
+    from p_k (reference engine.py:282-303).  Returns (n_acc, y) int64, plus
+    (p_i(x_i), q_i(x_i)) when return_probs.
+    """
+    L.require_cuda(target_logits, draft_ids, u_acc, u_res)
+    B, k1, V = target_logits.shape
+    k = k1 - 1
+    T, tp, tk = _knobs(temperature, top_p, top_k)
+    tgt = _vocab_rows(target_logits, "target_logits")
+    q = None
+    if T > 0.0:
+        L.require_cuda(draft_probs)
+        if draft_probs.shape != (B, k, V) or draft_probs.dtype != torch.float32:
+            raise L.SpecdecError("draft_probs must be float32 [B, k, V]")
+        q = _vocab_rows(draft_probs, "draft_probs")
+    xs = draft_ids.long()
+    if xs.stride(-1) != 1:
+        xs = xs.contiguous()
+    ua = u_acc.float()
+    if ua.stride(-1) != 1:
+        ua = ua.contiguous()
+    ur = u_res.float().contiguous()
+    al = None if alive is None else alive.to(torch.uint8).contiguous()
+    dev = tgt.device
+    n_acc = torch.empty(B, dtype=torch.long, device=dev)
+    y = torch.empty(B, dtype=torch.long, device=dev)
+    px = torch.empty(B, k, dtype=torch.float32, device=dev) if return_probs else None
+    qx = torch.empty(B, k, dtype=torch.float32, device=dev) if return_probs else None
+    code = L.dtype_code(tgt.dtype)
+    lib = L.lib()
+    with torch.cuda.device(dev):
+        ws = L.workspaces.get(lib.sd_sampling_workspace_bytes(B, B * (k + 1), V, code), dev)
+        L.check(lib.sd_verify_sample_qprobs(
+            L.ptr(tgt), tgt.stride(0), tgt.stride(1), code, L.ptr(q),
+            0 if q is None else q.stride(0), 0 if q is None else q.stride(1), L.ptr(xs),
+            xs.stride(0), L.ptr(ua), ua.stride(0), L.ptr(ur), L.ptr(al), B, k, V, T, tp, tk,
+            L.ptr(n_acc), L.ptr(y), L.ptr(px), L.ptr(qx), L.ptr(ws), ws.numel(),
+            L.stream_ptr(dev)), "verify_sample_probs")
     if return_probs:
         return n_acc, y, px, qx
     return n_acc, y

@@ -10,6 +10,10 @@ package adds on top of vLLM's own draft-model proposer is:
 
 * the adaptive-k controller (``SPECDEC_CONTROLLER=ewma|ewma+exit|ucb|fixed``),
   fed with the accepted counts and the measured draft / target step costs;
+* the verify round on this package's fused kernel: ``B200RejectionSampler``
+  replaces vLLM's rejection sampler (``SPECDEC_B200_REJECTION=0`` keeps
+  vLLM's) and runs the accept test and the residual / bonus draw of a uniform
+  batch in one call, from vLLM's draft probabilities;
 * the draft draw on this package's kernels when vLLM samples drafts
   probabilistically (``draft_sample_method="probabilistic"``): the draft
   distribution is the reference's full ``to_probs`` (temperature, top-p,
@@ -33,6 +37,9 @@ def register():
     import os
     if os.environ.get("SPECDEC_PLUGIN", "").strip().lower() not in ("1", "true", "yes", "on"):
         return False
-    from vllm_draft_spec.proposer import install
-    install()
+    from vllm_draft_spec import proposer, rejection
+    proposer.install()
+    if os.environ.get("SPECDEC_B200_REJECTION", "1").strip().lower() not in ("0", "false", "no",
+                                                                           "off"):
+        rejection.install()
     return True

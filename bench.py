@@ -46,7 +46,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="sample",
                     choices=["sample", "greedy", "attn", "vshard", "vshard-greedy", "engine",
-                             "adaptive"])
+                             "adaptive", "rejection"])
     ap.add_argument("--new-tokens", type=int, default=None,
                     help="--mode engine / adaptive: tokens per row (256 / 512)")
     ap.add_argument("--rows", type=int, default=8, help="--mode adaptive: rows per GPU")
@@ -697,6 +697,74 @@ class _SelfComm:
         return t
 
 
+def rejection_bench(a):
+    """--mode rejection: vLLM's rejection-sampler step at config 2 (64 requests,
+    4 draft tokens each, V=151936, bf16 target logits, fp32 draft probabilities,
+    T=0.7, top-p 0.9), through ``vllm_draft_spec.rejection.B200RejectionSampler``
+    (the fused kernel) and through vLLM 0.22's own ``RejectionSampler``, on the
+    same inputs.  A step is one ``forward`` call, host work included (both
+    make small host copies); time per step = wall clock over the timed steps
+    with the device synchronised at both ends."""
+    import time
+    import torch
+    from vllm.v1.sample.logits_processor import LogitsProcessors
+    from vllm.v1.sample.metadata import SamplingMetadata
+    from vllm.v1.sample.rejection_sampler import RejectionSampler
+    from vllm.v1.sample.sampler import Sampler
+    from vllm.v1.spec_decode.metadata import SpecDecodeMetadata
+    from specdec import sampling as S
+    from specdec import workloads as W
+    from vllm_draft_spec.rejection import B200RejectionSampler
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    B, k, V, T, tp = 64, K_DRAFT, VOCAB, 0.7, 0.9
+    tgt, drf = W.cfg2_logits(B, k, V, seed=0, device=dev)
+    q = S.to_probs(drf, T, tp).reshape(B * k, V)
+    xs, _ = S.draft_sample(drf.reshape(-1, V), torch.rand(B * k, device=dev), T, tp)
+    logits = tgt.reshape(B * (k + 1), V)
+    md = SpecDecodeMetadata.make_dummy(xs.view(B, k).tolist(), dev)
+    blk = torch.arange(B, device=dev, dtype=torch.int32) * (k + 1)
+    md.target_logits_indices = (blk[:, None] + torch.arange(k, device=dev, dtype=torch.int32)).reshape(-1)
+    md.bonus_logits_indices = blk + k
+    zeros = torch.zeros(B, device=dev)
+    smd = SamplingMetadata(
+        temperature=torch.full((B,), T, device=dev), all_greedy=False, all_random=True,
+        top_p=torch.full((B,), tp, device=dev), top_k=None, generators={}, max_num_logprobs=None,
+        no_penalties=True, prompt_token_ids=None, frequency_penalties=zeros,
+        presence_penalties=zeros, repetition_penalties=torch.ones(B, device=dev),
+        output_token_ids=[[] for _ in range(B)], allowed_token_ids_mask=None,
+        bad_words_token_ids={}, logitsprocs=LogitsProcessors())
+    ours = B200RejectionSampler(Sampler(), None, dev)
+    stock = RejectionSampler(Sampler(), None, dev)
+    steps = max(5, min(a.steps, 200))
+    res = {}
+    for name, rs in (("b200", ours), ("vllm", stock)):
+        for _ in range(max(3, a.warmup)):
+            out = rs.forward(md, q, logits, smd)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            out = rs.forward(md, q, logits, smd)
+        torch.cuda.synchronize(dev)
+        res[name] = (time.perf_counter() - t0) / steps * 1e3
+        res[name + "_tokens"] = float((out.sampled_token_ids >= 0).sum()) / B
+        if name == "b200":
+            assert ours.calls["vllm"] == 0, "the batch must take the fused path"
+    print(json.dumps({
+        "metric": "vLLM rejection-sampler steps/s (config 2: 64 requests x 4 drafts, V=151936, "
+                  "T=0.7 top-p 0.9)", "value": 1e3 / res["b200"], "unit": "steps/s",
+        "n_gpus": 1, "steps": steps, "warmup": a.warmup, "ms_per_step": res["b200"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded config-2 logits, see specdec/workloads.py)",
+        "config": {"workload": "vLLM RejectionSampler.forward, fused kernel vs vLLM 0.22's own",
+                   "vllm_stock_ms_per_step": res["vllm"],
+                   "speedup_vs_vllm": res["vllm"] / res["b200"],
+                   "tokens_per_request_last_step": {"b200": res["b200_tokens"],
+                                                     "vllm": res["vllm_tokens"]},
+                   "timing": "wall clock per forward() call, host work included"},
+        "gpu_launches": 2 * steps}))
+
+
 def main():
     a = parse()
     if a.impl == "reference":
@@ -713,6 +781,8 @@ def main():
         if a.new_tokens is None:
             a.new_tokens = 512
         return adaptive_bench(a)
+    if a.mode == "rejection":
+        return rejection_bench(a)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -84,6 +84,30 @@ int sd_verify_sample(const void* tgt, int64_t tgt_bs, int64_t tgt_ps,
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The verify round of sd_verify_sample with the draft distributions given as
+ * probabilities instead of draft logits: what a serving engine's rejection
+ * sampler holds (vLLM's RejectionSampler.forward receives draft_probs
+ * [num_tokens, V] fp32, vllm/v1/sample/rejection_sampler.py:87-95, built
+ * from the draws its drafter made).  Same accept test, residual and bonus
+ * draws as sd_verify_sample (reference specdec/engine.py:282-303), with
+ * q_i = qprobs[b, i, :] used as given (no temperature, top-p or top-k on it);
+ * to_probs (temperature, top-p, top-k) applies to the target logits only.
+ *
+ *   qprobs [B, k, V] fp32, element strides (q_bs, q_ps, 1)
+ *   other arguments as sd_verify_sample (drf is not taken)
+ *
+ * temperature <= 0 is the greedy round (qprobs unused).  Sampling needs
+ * bf16 / fp16 target logits with V > 2048 (SD_ENOTSUP otherwise).
+ */
+int sd_verify_sample_qprobs(const void* tgt, int64_t tgt_bs, int64_t tgt_ps, int dtype,
+                            const float* qprobs, int64_t q_bs, int64_t q_ps,
+                            const int64_t* xs, int64_t xs_bs, const float* u_acc, int64_t u_bs,
+                            const float* u_res, const uint8_t* alive,
+                            int B, int k, int V, float temperature, float top_p, int top_k,
+                            int64_t* n_acc, int64_t* y, float* px, float* qx,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * No counterpart in the reference (added entry point), for callers that may
  * not allocate device memory: a serving framework that reserves nearly all
  * of the GPU for its own KV-cache pool up front and forbids other

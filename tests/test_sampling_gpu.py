@@ -150,6 +150,64 @@ def test_cfg2_greedy_parity(cfg2):
     _check_verify(tgt, drf, xs_g, ua, ur, 0.0, 1.0, 0, max_exempt=0.0, tag="greedy")
 
 
+def _check_verify_probs(tgt, drf, xs, ua, ur, T, tp, tk, max_exempt=0.1, tag=""):
+    """verify_sample_probs with q = to_probs(draft logits) on the kernels vs the
+    oracle's verify from the draft logits: the same q, so the same results."""
+    B, k, V = drf.shape
+    q = S.to_probs(drf, T, tp, tk).reshape(B, k, V)
+    n_k, y_k, px_k, qx_k = S.verify_sample_probs(tgt, q, xs, ua, ur, T, tp, tk, return_probs=True)
+    n_o, y_o, d = O.verify(_np(tgt), _np(drf), xs.cpu().numpy(), _np(ua), _np(ur), T, tp, tk,
+                           return_details=True)
+    ok = _ok(d)
+    assert ok.mean() >= 1.0 - max_exempt, f"{tag}: too many boundary rows {(~ok).sum()}"
+    n_k, y_k = n_k.cpu().numpy(), y_k.cpu().numpy()
+    bad = np.nonzero(ok & ((n_k != n_o) | (y_k != y_o)))[0]
+    assert bad.size == 0, (f"{tag}: rows {bad[:8]} differ: kernel n/y "
+                           f"{n_k[bad[:8]]}/{y_k[bad[:8]]} oracle {n_o[bad[:8]]}/{y_o[bad[:8]]}")
+    px_k, qx_k = px_k.cpu().numpy(), qx_k.cpu().numpy()
+    sel = ok[:, None] & np.ones_like(px_k, dtype=bool)
+    np.testing.assert_allclose(px_k[sel], d["px"][sel], rtol=2e-6, atol=1e-30, err_msg=tag)
+    np.testing.assert_allclose(qx_k[sel], d["qx"][sel], rtol=2e-6, atol=1e-30, err_msg=tag)
+    return n_k, y_k, ok
+
+
+def test_cfg2_verify_with_draft_probabilities(cfg2):
+    """The draft distributions given as probabilities (as a serving engine's
+    rejection sampler holds them): config 2 at T = 0.7 / top-p 0.9."""
+    tgt, drf, xs, ua, ur = cfg2
+    n_k, _, _ = _check_verify_probs(tgt, drf, xs, ua, ur, 0.7, 0.9, 0, max_exempt=0.05,
+                                    tag="cfg2 probs")
+    assert len(set(n_k.tolist())) >= 3
+
+
+@pytest.mark.parametrize("T,tp,tk,V", [(1.0, 1.0, 0, 32000), (1.2, 0.95, 50, 32000),
+                                       (0.8, 1.0, 0, 151936)])
+def test_verify_with_draft_probabilities_modes(T, tp, tk, V):
+    """No truncation (every element kept), top-k with top-p, and the full
+    vocabulary untruncated: each draws through the row pass from q as given."""
+    g = torch.Generator().manual_seed(17)
+    B, k = 12, 4
+    tgt = W.zipf_logits(B * (k + 1), V, g).reshape(B, k + 1, V)
+    drf = tgt[:, :k] + torch.randn(B, k, V, generator=g)
+    tgt, drf = tgt.to(DEV, torch.bfloat16), drf.to(DEV, torch.bfloat16)
+    am = tgt.float().argmax(-1)
+    xs = torch.where(torch.rand(B, k, generator=g).to(DEV) < 0.5, am[:, :k],
+                     torch.randint(0, V, (B, k), generator=g).to(DEV)).contiguous()
+    ua = torch.rand(B, k, generator=g).to(DEV)
+    ur = torch.rand(B, generator=g).to(DEV)
+    _check_verify_probs(tgt, drf, xs, ua, ur, T, tp, tk, max_exempt=0.25, tag=f"probs {T} {tp} {tk}")
+
+
+def test_verify_with_draft_probabilities_greedy(cfg2):
+    """T = 0: the greedy round, the draft probabilities unused."""
+    tgt, drf, xs, ua, ur = cfg2
+    am = tgt.float().argmax(-1)
+    xs_g = torch.where(torch.rand(64, 4, device=DEV) < 0.7, am[:, :4], xs)
+    n_p, y_p = S.verify_sample_probs(tgt, None, xs_g, ua, ur, 0.0)
+    n_l, y_l = S.verify_sample(tgt, None, xs_g, ua, ur, 0.0)
+    assert torch.equal(n_p, n_l) and torch.equal(y_p, y_l)
+
+
 def test_cfg2_topk_and_topp(cfg2):
     tgt, drf, xs, ua, ur = cfg2
     _check_verify(tgt[:16], drf[:16], xs[:16], ua[:16], ur[:16], 1.0, 0.8, 40, tag="topk40+topp")
