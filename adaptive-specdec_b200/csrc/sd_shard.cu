@@ -156,8 +156,10 @@ __device__ __forceinline__ void slice_for_each(const void* x, int dtype, int n, 
 }
 
 // The same over [j0, j1) of two slices read in step, f(j, a_j, b_j): 16-byte
-// units when both slices sit at the same offset modulo 16 bytes (contiguous
-// logits tensors do), element by element otherwise.
+// units when both slices sit at the same offset modulo 16 bytes (rows of a
+// contiguous slice tensor do when the slice width times the element size is a
+// multiple of 16: even_split's default boundaries give that), element by
+// element otherwise.
 template <typename F>
 __device__ __forceinline__ void slice2_range_for_each(const void* xa, const void* xb, int dtype,
                                                       int j0, int j1, F&& f) {
@@ -397,7 +399,7 @@ __global__ void __launch_bounds__(NT) p4a_kernel(Geo g, const Msg3* recv, Vec* s
 
 // ---- P4b: per row, the accept test and the shard's residual mass ------------
 __global__ void __launch_bounds__(NT) p4b_kernel(const sd_shard_args a, Geo g, const Vec* st,
-                                                 Row* rows, double* send) {
+                                                 Row* rows, double* psum) {
   __shared__ double red[33];
   __shared__ int pick_s, all_s;
   const int b = blockIdx.x, part = blockIdx.y;         // part: 1/PSPLIT of the slice
@@ -456,10 +458,25 @@ __global__ void __launch_bounds__(NT) p4b_kernel(const sd_shard_args a, Geo g, c
   R = block_sum(R, red);
   __syncthreads();
   Pm = block_sum(Pm, red);
-  if (threadIdx.x == 0) {                              // send was zeroed before the launch
-    atomicAdd(&send[2 * b], R);
-    atomicAdd(&send[2 * b + 1], Pm);
+  if (threadIdx.x == 0) {                              // this part's sums, in its own slot
+    psum[((size_t)b * PSPLIT + part) * 2] = R;
+    psum[((size_t)b * PSPLIT + part) * 2 + 1] = Pm;
   }
+}
+
+// P4c: per row, the shard's (R, Pm) as the parts' sums added in part order,
+// so the totals every rank agrees on are reproducible from run to run (and
+// are the sums of the part masses that P5 walks).
+__global__ void p4c_kernel(Geo g, const double* psum, double* send) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= g.B) return;
+  double R = 0.0, Pm = 0.0;
+  for (int p = 0; p < PSPLIT; ++p) {
+    R += psum[((size_t)b * PSPLIT + p) * 2];
+    Pm += psum[((size_t)b * PSPLIT + p) * 2 + 1];
+  }
+  send[2 * b] = R;
+  send[2 * b + 1] = Pm;
 }
 
 // ---- P5: per row, the shard that holds the draw walks its slice -------------
@@ -663,7 +680,12 @@ constexpr size_t STATUS_BYTES = 256;
 
 size_t vec_bytes(int B, int k) { return (size_t)B * (2 * k + 1) * sizeof(Vec); }
 size_t row_bytes(int B) { return (size_t)B * sizeof(Row); }
-size_t seg_bytes(int B) { return ((size_t)B * PSPLIT * (sizeof(double) + sizeof(int)) + 255) & ~(size_t)255; }
+// P5's part masses [B, PSPLIT] and last indices [B, PSPLIT], then P4's part
+// sums [B, PSPLIT, 2] (offset B * PSPLIT * 12 bytes: a multiple of 8)
+size_t seg_bytes(int B) {
+  return ((size_t)B * PSPLIT * (sizeof(double) + sizeof(int) + 2 * sizeof(double)) + 255) &
+         ~(size_t)255;
+}
 
 int check_args(const sd_shard_args* a, Geo* g) {
   if (!a) return SD_EINVAL;
@@ -728,6 +750,7 @@ int sd_shard_phase(const sd_shard_args* args, int phase, const void* recv, void*
   char* segw = ws + STATUS_BYTES + vec_bytes(g.B, g.k) + ((row_bytes(g.B) + 255) & ~(size_t)255);
   double* segm = reinterpret_cast<double*>(segw);                 // [B, PSPLIT]
   int* segl = reinterpret_cast<int*>(segw + (size_t)g.B * PSPLIT * sizeof(double));
+  double* psum = reinterpret_cast<double*>(segw + (size_t)g.B * PSPLIT * (sizeof(double) + sizeof(int)));
   const bool greedy = !(a.temperature > 0.f);
   if (phase < 1 || phase > 6) return SD_EINVAL;
   if (phase > 1 && !recv) return SD_EINVAL;
@@ -760,9 +783,8 @@ int sd_shard_phase(const sd_shard_args* args, int phase, const void* recv, void*
       break;
     case 4:
       p4a_kernel<<<g.nvec, NT, 0, st>>>(g, reinterpret_cast<const Msg3*>(recv), vs, status);
-      if (cudaMemsetAsync(send, 0, (size_t)g.B * 2 * sizeof(double), st) != cudaSuccess)
-        return SD_ELAUNCH;
-      p4b_kernel<<<dim3(g.B, PSPLIT), NT, 0, st>>>(a, g, vs, rows, reinterpret_cast<double*>(send));
+      p4b_kernel<<<dim3(g.B, PSPLIT), NT, 0, st>>>(a, g, vs, rows, psum);
+      p4c_kernel<<<(g.B + 127) / 128, 128, 0, st>>>(g, psum, reinterpret_cast<double*>(send));
       break;
     case 5:
       p5a_kernel<<<dim3(g.B, PSPLIT), NT, 0, st>>>(a, g, reinterpret_cast<const double*>(recv), vs,

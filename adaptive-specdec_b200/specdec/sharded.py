@@ -27,12 +27,26 @@ __all__ = ["ProcessGroupCollectives", "CudaShardBackend", "run_round", "run_roun
            "verify_sharded", "verify_sharded_local", "even_split"]
 
 
-def even_split(V, nranks):
-    """v_start for nranks near-equal contiguous slices of a vocabulary of V."""
-    base, extra = divmod(V, nranks)
+def even_split(V, nranks, align=8):
+    """v_start for nranks near-equal contiguous slices of a vocabulary of V.
+
+    Every boundary but the last is a multiple of `align` columns (8 bf16 /
+    fp16 columns = 16 bytes), so every slice except possibly the last has a
+    width that keeps its rows 16-byte aligned and the phase kernels on their
+    16-byte loads for any rank count; a vocabulary narrower than `align`
+    columns per rank is split column by column."""
+    units, tail = divmod(V, align)
+    if units < nranks:
+        base, extra = divmod(V, nranks)
+        out = [0]
+        for r in range(nranks):
+            out.append(out[-1] + base + (1 if r < extra else 0))
+        return out
+    base, extra = divmod(units, nranks)
     out = [0]
     for r in range(nranks):
-        out.append(out[-1] + base + (1 if r < extra else 0))
+        out.append(out[-1] + (base + (1 if r < extra else 0)) * align)
+    out[-1] += tail
     return out
 
 

@@ -97,6 +97,35 @@ def test_cuda_phases_agree_with_numpy_restatement():
         assert np.array_equal(n.cpu().numpy()[sel], n_o[sel])
 
 
+def test_draw_crossing_on_a_part_boundary():
+    """P5 walks the slice in PSPLIT = 8 parts.  Here the residual (p - q)+ of
+    the first three parts (columns 0-23 of a 64-column vector) is zero and
+    u_res = 0, so the inverse-CDF crossing falls exactly on the boundary of
+    part 3: the draw must be column 24 (the first with residual mass), on 1
+    and 2 shards alike, as in the numpy restatement and the oracle."""
+    V = 64
+    tgt = torch.zeros(2, 2, V)
+    drf = torch.zeros(2, 1, V)
+    tgt[:, 0, 24:32] = 3.0                    # p puts its mass on columns 24-31
+    drf[:, 0, :24] = 3.0                      # q on columns 0-23
+    tgt[1, 1] = torch.linspace(-1, 1, V)
+    tgt, drf = tgt.to(DEV, torch.bfloat16), drf.to(DEV, torch.bfloat16)
+    xs = torch.zeros(2, 1, dtype=torch.long, device=DEV)       # q(0) >> p(0): rejected
+    ua = torch.full((2, 1), 0.5, device=DEV)
+    ur = torch.tensor([0.0, 0.37], device=DEV)
+    n_o, y_o, _ = O.verify(_np(tgt), _np(drf), xs.cpu().numpy(), _np(ua), _np(ur), 1.0, 1.0, 0,
+                           return_details=True)
+    assert list(n_o) == [0, 0] and y_o[0] == 24
+    for vs in ([0, V], [0, 32, V]):
+        outs_c, st_c = SH.verify_sharded_local(tgt, drf, xs, ua, ur, vs, 1.0, 1.0)
+        outs_n, st_n = SH.verify_sharded_local(tgt.cpu(), drf.cpu(), xs.cpu(), ua.cpu(), ur.cpu(),
+                                               vs, 1.0, 1.0, backend_factory=NumpyShardBackend)
+        assert st_c == st_n == [0] * (len(vs) - 1)
+        for (n, y), (nn, yn) in zip(outs_c, outs_n):
+            assert n.cpu().tolist() == nn.tolist() == [0, 0], vs
+            assert y.cpu().tolist() == yn.tolist() == [int(y_o[0]), int(y_o[1])], vs
+
+
 def test_fallback_status_matches_restatement():
     g = torch.Generator(device=DEV).manual_seed(0)
     B, k, V = 4, 2, 3000
