@@ -866,8 +866,8 @@ def main():
 
     # roofline time: one verify call's share of the timed region (graph replays
     # of back-to-back calls, events on the launching stream).  A call is the
-    # stats kernel (plus a few-hundred-byte memset of its row counters), or
-    # for greedy the argmax streaming kernel and its small per-row pass; the
+    # stats kernel and its row pass, or for greedy the argmax streaming kernel
+    # and its small per-row pass; the
     # whole call is charged to the dominant kernel, so `achieved` is a lower
     # bound for it.  The same call timed alone between its own event pair
     # (launch gaps included) is reported beside it.
@@ -938,9 +938,9 @@ def main():
     prof = ROOT / "profiles" / ("verify_greedy_traffic.json" if greedy else "verify_sample_traffic.json")
     if prof.exists():
         traffic = json.loads(prof.read_text()).get("bytes_per_call")
-    # our kernels per verify call: the stats kernel; greedy, the argmax
-    # streaming kernel and its per-row pass
-    launches_per_step = 2 if greedy else 1
+    # our kernels per verify call: the stats kernel and the row pass, or for
+    # greedy the argmax streaming kernel and its per-row pass
+    launches_per_step = 2
     line = {
         "metric": metric_name(a.mode, T, tp, a.flat), "value": value, "unit": "rows/s",
         "n_gpus": world,
