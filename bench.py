@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--beta-lo", type=float, default=5.0,
                     help="--mode adaptive: shared-prior strength of the low-agreement phase")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="default run: skip the greedy / attention / rejection-sampler lines "
+                         "reported under 'also'")
     ap.add_argument("--attn-rows", type=int, default=64, help="--mode attn: rows (config 3: 64)")
     return ap.parse_args()
 
@@ -765,6 +768,34 @@ def rejection_bench(a):
         "gpu_launches": 2 * steps}))
 
 
+def extra_measurements():
+    """The other verify-round rows, each from its own bench mode in a child
+    process on this GPU (its own clock samples, timing and checks), so that the
+    default run's record carries them: the greedy round (config 2), the verify
+    attention (config 3, checked against fp32 before timing) and the vLLM
+    rejection-sampler step against vLLM's own.  A mode that fails is recorded
+    with its error; the main line is unaffected."""
+    import subprocess
+    runs = {"greedy": ["--mode", "greedy", "--steps", "1000", "--warmup", "10", "--no-cpu-baseline"],
+            "attn": ["--mode", "attn", "--steps", "100", "--warmup", "5"],
+            "rejection": ["--mode", "rejection", "--steps", "50", "--warmup", "5"]}
+    keep = ("metric", "value", "unit", "ms_per_step", "roofline", "clocks", "config", "e2e")
+    out = {}
+    for name, argv in runs.items():
+        try:
+            r = subprocess.run([sys.executable, str(ROOT / "bench.py"), *argv], capture_output=True,
+                               text=True, timeout=600, cwd=str(ROOT))
+            last = [x for x in r.stdout.splitlines() if x.startswith("{")]
+            if r.returncode != 0 or not last:
+                out[name] = {"error": f"exit {r.returncode}: {r.stderr.strip()[-300:]}"}
+                continue
+            d = json.loads(last[-1])
+            out[name] = {k: d[k] for k in keep if k in d}
+        except Exception as e:                          # noqa: BLE001 - recorded, not raised
+            out[name] = {"error": repr(e)[-300:]}
+    return out
+
+
 def main():
     a = parse()
     if a.impl == "reference":
@@ -970,6 +1001,9 @@ def main():
                                           f"torch CPU, {cores} threads)" if kind == "reference"
                                           else f"{steps} batches of {rows} rows through "
                                           "oracle/sampling_oracle.py"}
+    if (rank == 0 and world == 1 and a.mode == "sample" and not a.flat and not a.no_extras
+            and T == T_SAMPLE and tp == TOP_P):
+        line["also"] = extra_measurements()
     if rank == 0:
         print(json.dumps(line))
     for g in graphs.values():
