@@ -7,12 +7,112 @@
 // advance, rollback and the verify-round commit are one tiny kernel each (O(1)
 // per row, no data movement, no host synchronisation), and the append writes
 // each row's new tokens at its own offset with 16-byte copies.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "specdec_b200.h"
 
 namespace sd {
+
+// ---- fused post-projection step of an attention layer ------------------------
+// Per (row b, position l, head) vector of D elements, one warp: the head's
+// RMSNorm (q and k, when a weight is given), the rotary embedding with that
+// position's (cos, sin) (q and k), then q to q_out [B, Hq, L, D] and k, v
+// into the ragged cache at slot lengths[b] + l.  It does in one launch what
+// transformers' Qwen3Attention.forward does between the projections and the
+// attention (modeling_qwen3.py: q_norm / k_norm, apply_rotary_pos_emb, and the
+// cache update, specdec/kvcache.py:61-74 in the reference), with the same
+// bf16 tensor arithmetic: the sum of squares in float32 (in a warp reduction
+// order, where torch's differs: a normalised value can land one bf16 ulp
+// apart), x * rsqrt(mean + eps) in float32 rounded to bf16, times the weight
+// rounded to bf16; rope = rn(rn(x * cos) + rn(rotate_half(x) * sin)).
+struct QkvArgs {
+  const __nv_bfloat16* q; int64_t q_rs;      // [B * L rows, Hq * D], row stride
+  const __nv_bfloat16* k; int64_t k_rs;      // [B * L rows, Hkv * D]
+  const __nv_bfloat16* v; int64_t v_rs;
+  const __nv_bfloat16* qw;                   // [D] or null: no norm
+  const __nv_bfloat16* kw;
+  float eps;
+  const __nv_bfloat16* cos; const __nv_bfloat16* sin;   // [B, L, D], strides (cs_bs, cs_ls, 1)
+  int64_t cs_bs, cs_ls;
+  __nv_bfloat16* kc; __nv_bfloat16* vc;      // [B, Hkv, C, D]
+  const int64_t* lengths;
+  __nv_bfloat16* q_out;                      // [B, Hq, L, D]
+  int B, L, Hq, Hkv, D, C;
+  int* err;
+};
+
+constexpr int QKV_WARPS = 8;
+constexpr int QKV_DMAX = 256;
+
+__device__ __forceinline__ float bf16_rn(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__global__ void __launch_bounds__(QKV_WARPS * 32) qkv_rope_append_kernel(QkvArgs a) {
+  __shared__ float buf[QKV_WARPS][QKV_DMAX];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int nh = a.Hq + 2 * a.Hkv;
+  const int64_t w = (int64_t)blockIdx.x * QKV_WARPS + wl;
+  if (w >= (int64_t)a.B * a.L * nh) return;
+  const int hv = (int)(w % nh);
+  const int64_t r = w / nh;                  // b * L + l
+  const int l = (int)(r % a.L), b = (int)(r / a.L);
+  const int D = a.D;
+  const __nv_bfloat16* src;
+  const __nv_bfloat16* nw = nullptr;
+  __nv_bfloat16* dst;
+  bool rope = true;
+  if (hv < a.Hq) {
+    src = a.q + r * a.q_rs + (int64_t)hv * D;
+    nw = a.qw;
+    dst = a.q_out + (((int64_t)b * a.Hq + hv) * a.L + l) * D;
+  } else {
+    const int64_t len = a.lengths[b];
+    if (len < 0 || len + a.L > a.C) {        // the row's slots would pass the capacity
+      if (lane == 0 && l == 0 && hv == a.Hq && a.err) atomicOr(a.err, 1);
+      return;
+    }
+    const int h = hv < a.Hq + a.Hkv ? hv - a.Hq : hv - a.Hq - a.Hkv;
+    const int64_t slot = (((int64_t)b * a.Hkv + h) * a.C + len + l) * D;
+    if (hv < a.Hq + a.Hkv) {
+      src = a.k + r * a.k_rs + (int64_t)h * D;
+      nw = a.kw;
+      dst = a.kc + slot;
+    } else {
+      src = a.v + r * a.v_rs + (int64_t)h * D;
+      rope = false;
+      dst = a.vc + slot;
+    }
+  }
+  float* x = buf[wl];
+  float ss = 0.f;
+  for (int i = lane; i < D; i += 32) {
+    const float xv = __bfloat162float(src[i]);
+    x[i] = xv;
+    ss = fmaf(xv, xv, ss);
+  }
+  if (nw != nullptr) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rs = rsqrtf(__fdiv_rn(ss, (float)D) + a.eps);
+    for (int i = lane; i < D; i += 32)
+      x[i] = bf16_rn(__bfloat162float(nw[i]) * bf16_rn(x[i] * rs));
+  }
+  __syncwarp();
+  const int half = D >> 1;
+  const __nv_bfloat16* cp = a.cos + (int64_t)b * a.cs_bs + (int64_t)l * a.cs_ls;
+  const __nv_bfloat16* sp = a.sin + (int64_t)b * a.cs_bs + (int64_t)l * a.cs_ls;
+  for (int i = lane; i < D; i += 32) {
+    float o = x[i];
+    if (rope) {
+      const float rot = i < half ? -x[i + half] : x[i - half];
+      o = bf16_rn(bf16_rn(x[i] * __bfloat162float(cp[i])) + bf16_rn(rot * __bfloat162float(sp[i])));
+    }
+    dst[i] = __float2bfloat16_rn(o);
+  }
+}
 
 __global__ void lengths_update_kernel(int64_t* lengths, const int64_t* delta, int64_t q, int sign,
                                       int B, int64_t capacity, int* err) {
@@ -107,6 +207,39 @@ int sd_kv_commit(int64_t* lengths, const int64_t* n_acc, int k, int B, int* err,
   if (B == 0) return SD_OK;
   commit_kernel<<<(B + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       lengths, n_acc, k, B, err);
+  return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+}
+
+int sd_qkv_norm_rope_append(const void* q, int64_t q_rs, const void* k, int64_t k_rs,
+                            const void* v, int64_t v_rs, const void* q_norm_w,
+                            const void* k_norm_w, float eps, const void* cos, const void* sin,
+                            int64_t cs_bs, int64_t cs_ls, void* kcache, void* vcache,
+                            const int64_t* lengths, int B, int L, int Hq, int Hkv, int D, int C,
+                            void* q_out, int* err, void* stream) {
+  if (!q || !k || !v || !cos || !sin || !kcache || !vcache || !lengths || !q_out) return SD_EINVAL;
+  if (B < 0 || L < 0 || Hq <= 0 || Hkv <= 0 || C <= 0 || D <= 0) return SD_EINVAL;
+  if (D % 2 || D > sd::QKV_DMAX) return SD_ENOTSUP;
+  if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return SD_EINVAL;
+  if (B == 0 || L == 0) return SD_OK;
+  sd::QkvArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q); a.q_rs = q_rs;
+  a.k = static_cast<const __nv_bfloat16*>(k); a.k_rs = k_rs;
+  a.v = static_cast<const __nv_bfloat16*>(v); a.v_rs = v_rs;
+  a.qw = static_cast<const __nv_bfloat16*>(q_norm_w);
+  a.kw = static_cast<const __nv_bfloat16*>(k_norm_w);
+  a.eps = eps;
+  a.cos = static_cast<const __nv_bfloat16*>(cos); a.sin = static_cast<const __nv_bfloat16*>(sin);
+  a.cs_bs = cs_bs; a.cs_ls = cs_ls;
+  a.kc = static_cast<__nv_bfloat16*>(kcache); a.vc = static_cast<__nv_bfloat16*>(vcache);
+  a.lengths = lengths;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.B = B; a.L = L; a.Hq = Hq; a.Hkv = Hkv; a.D = D; a.C = C;
+  a.err = err;
+  const int64_t nwarp = (int64_t)B * L * (Hq + 2 * Hkv);
+  const int64_t grid = (nwarp + sd::QKV_WARPS - 1) / sd::QKV_WARPS;
+  if (grid > 0x7FFFFFFF) return SD_ENOTSUP;
+  sd::qkv_rope_append_kernel<<<(unsigned)grid, sd::QKV_WARPS * 32, 0,
+                               reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
 }
 

@@ -201,7 +201,7 @@ class SpecDecodeEngine:
     """Speculative decoding for a (target, draft) pair sharing a tokenizer."""
 
     def __init__(self, target, draft, tokenizer, device=None, capacity=4096, nvtx=False,
-                 time_phases=False, cuda_graphs=True):
+                 time_phases=False, cuda_graphs=True, fused_qkv=False):
         self.target = target.eval()
         self.draft = draft.eval()
         self.tok = tokenizer
@@ -223,6 +223,13 @@ class SpecDecodeEngine:
         A.register()
         for m in (self.target, self.draft):
             m.set_attn_implementation(A.IMPL)
+        # fused_qkv: one QKV GEMM and one norm + RoPE + KV-append kernel per
+        # attention layer (bf16 models; specdec.fused_attention)
+        self.fused_qkv = bool(fused_qkv)
+        if self.fused_qkv:
+            from specdec import fused_attention as FA
+            for m in (self.target, self.draft):
+                FA.install(m)
 
     @staticmethod
     def _eos_ids(tok, cfg):

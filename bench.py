@@ -60,6 +60,9 @@ def parse():
                     help="--mode adaptive: shared-prior strength of the high-agreement phase")
     ap.add_argument("--beta-lo", type=float, default=5.0,
                     help="--mode adaptive: shared-prior strength of the low-agreement phase")
+    ap.add_argument("--fused-qkv", action="store_true",
+                    help="--mode engine / adaptive: one QKV GEMM + the fused norm / RoPE / "
+                         "KV-append kernel per attention layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="default run: skip the greedy / attention / rejection-sampler lines "
@@ -567,7 +570,7 @@ def adaptive_bench(a):
     draft.specdec_head = prior.head(draft.lm_head)
     rows, new, kmax, pmin, pmax = a.rows, a.new_tokens, 8, 128, 4096
     eng = SpecDecodeEngine(target, draft, _NoTok(), device=dev,
-                           capacity=pmax + 2 * new + 2 * kmax + 8)
+                           capacity=pmax + 2 * new + 2 * kmax + 8, fused_qkv=a.fused_qkv)
     g = torch.Generator().manual_seed(1000 + rank)
     plen = torch.randint(pmin, pmax + 1, (rows,), generator=g)
     ids = torch.randint(0, VOCAB, (rows, int(plen.max())), generator=g)
@@ -613,6 +616,7 @@ def adaptive_bench(a):
                    "prompt": f"U[{pmin},{pmax}]", "new_tokens": new, "k_range": [1, kmax],
                    "controller": "ewma", "temperature": T_SAMPLE, "top_p": TOP_P,
                    "alpha_switch_tokens": 64, "beta_hi_lo": list(betas),
+                   "fused_qkv": a.fused_qkv,
                    "parallelism": f"row-sharded x{world}, no collective on the data path"},
         "alpha_conditional": {"high_phase": alpha_hi, "low_phase": alpha_lo},
         "acceptance_rate": {"high_phase": rate_hi, "low_phase": rate_lo},
@@ -654,7 +658,8 @@ def engine_bench(a):
     # ends (the reference's rollback leaves k - n_acc with n_acc = 0 for them),
     # so a row can reach P + 2 * new
     eng = SpecDecodeEngine(target, draft, _NoTok(), device=dev,
-                           capacity=P + 2 * new + 2 * k + 8, time_phases=True)
+                           capacity=P + 2 * new + 2 * k + 8, time_phases=True,
+                           fused_qkv=a.fused_qkv)
     g = torch.Generator().manual_seed(1)
     ids = torch.randint(0, VOCAB, (Bq, P), generator=g)
     plen = torch.full((Bq,), P, dtype=torch.long)
@@ -678,7 +683,7 @@ def engine_bench(a):
         "config": {"workload": "config 4 full speculative round", "rows": Bq, "prompt": P,
                    "new_tokens": new, "k": k, "temperature": T_SAMPLE, "top_p": TOP_P,
                    "target": "Qwen3-8B shape (random init)",
-                   "draft": "Qwen3-0.6B shape (random init)"},
+                   "draft": "Qwen3-0.6B shape (random init)", "fused_qkv": a.fused_qkv},
         "engine": {key: d[key] for key in ("rounds", "emitted", "acceptance_rate",
                                            "mean_accepted_len", "draft_forwards",
                                            "target_forwards", "t_draft", "t_target",

@@ -198,6 +198,30 @@ int sd_kv_append(void* kcache, void* vcache, const void* new_k, const void* new_
                  int B, int H, int C, int D, int q, int dtype, int* err, void* stream);
 
 /*
+ * The fused step between an attention layer's QKV projections and its
+ * attention, for bf16 Qwen3 / Llama-style layers: per row b, position
+ * l < L and head, the head's RMSNorm on q and k (weights q_norm_w / k_norm_w
+ * [D], eps; both null: no norm), the rotary embedding with (cos, sin)
+ * [B, L, D] (element strides (cs_bs, cs_ls, 1)) on q and k, then
+ *   q_out[b, h, l, :]             = q'      ([B, Hq, L, D] contiguous)
+ *   kcache[b, h, lengths[b] + l]  = k',  vcache[...] = v
+ * (caches [B, Hkv, C, D]).  q, k, v are the projections' outputs, rows
+ * b * L + l with element strides q_rs / k_rs / v_rs and heads of D contiguous
+ * elements.  Replaces transformers' q_norm / k_norm and apply_rotary_pos_emb
+ * in Qwen3Attention.forward and the cache update of _RaggedLayer.update
+ * (reference specdec/kvcache.py:61-74): one launch instead of a dozen
+ * elementwise kernels and the append.  Same arithmetic on bf16 tensors, but
+ * for the float32 sum of squares' order (a normalised value may differ by one
+ * bf16 ulp).  Rows whose slots would pass C are not written and set *err.
+ */
+int sd_qkv_norm_rope_append(const void* q, int64_t q_rs, const void* k, int64_t k_rs,
+                            const void* v, int64_t v_rs, const void* q_norm_w,
+                            const void* k_norm_w, float eps, const void* cos, const void* sin,
+                            int64_t cs_bs, int64_t cs_ls, void* kcache, void* vcache,
+                            const int64_t* lengths, int B, int L, int Hq, int Hkv, int D, int C,
+                            void* q_out, int* err, void* stream);
+
+/*
  * Verify attention over the ragged cache (after the append of this forward):
  * query j of row b (position lengths[b] + j) attends to cache slots
  * s <= lengths[b] + j, i.e. the reference mask s <= len[b] + j
