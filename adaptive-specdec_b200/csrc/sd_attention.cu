@@ -60,7 +60,22 @@ struct AttnParams {
   int tile_keys;     // keys per tile of the tensor-core schedule (plan kernel)
   int seg_ovh;       // schedule cost of a (row, kv head) beyond its tiles, in tiles
   int* status;       // sticky: bit 0 = a bounded wait of the tcgen05 kernel gave up
+  // paged caches: k / v are pools [npages, Hkv, SD_KV_PAGE, D] and row b's key
+  // s sits in page bt[b * bt_stride + s / SD_KV_PAGE]; bt == nullptr: the
+  // contiguous [B, Hkv, C, D] layout
+  const int32_t* bt;
+  int bt_stride, npages;
 };
+
+// Offset, in rows of D elements, of key s of row b and kv head h.  A page
+// index outside the pool reads page 0 (the caller's block table is wrong, but
+// nothing is read out of bounds).
+__device__ __forceinline__ int64_t kv_row(const AttnParams& P, int b, int h, int s) {
+  if (P.bt == nullptr) return ((int64_t)b * P.Hkv + h) * P.C + s;
+  int pg = __ldg(P.bt + (int64_t)b * P.bt_stride + (s / SD_KV_PAGE));
+  if ((unsigned)pg >= (unsigned)P.npages) pg = 0;
+  return ((int64_t)pg * P.Hkv + h) * SD_KV_PAGE + (s % SD_KV_PAGE);
+}
 
 __device__ __forceinline__ int row_limit(const AttnParams& P, int b, int j) {
   int64_t lim = P.lengths[b] + j + 1;
@@ -112,15 +127,16 @@ __global__ void __launch_bounds__(AT) attn_split_kernel(AttnParams P) {
 #pragma unroll
   for (int i = 0; i < NA; ++i) acc[i] = 0.f;
   __syncthreads();
-  const T* kb = reinterpret_cast<const T*>(P.k) + ((int64_t)b * P.Hkv + h) * P.C * D;
-  const T* vb = reinterpret_cast<const T*>(P.v) + ((int64_t)b * P.Hkv + h) * P.C * D;
+  const T* kb = reinterpret_cast<const T*>(P.k);
+  const T* vb = reinterpret_cast<const T*>(P.v);
   for (int kt = s0; kt < s1; kt += KT) {
     const int nk = min(KT, s1 - kt);
     for (int i = t; i < KT * D; i += AT) {
       const int kk = i / D, d = i % D;
       const bool in = kk < nk;
-      ks[kk][d] = in ? kb[(int64_t)(kt + kk) * D + d] : from_f<T>(0.f);
-      vs[kk][d] = in ? vb[(int64_t)(kt + kk) * D + d] : from_f<T>(0.f);
+      const int64_t e = in ? kv_row(P, b, h, kt + kk) * D + d : 0;
+      ks[kk][d] = in ? kb[e] : from_f<T>(0.f);
+      vs[kk][d] = in ? vb[e] : from_f<T>(0.f);
     }
     __syncthreads();
     for (int i = t; i < R * KT; i += AT) {
@@ -515,17 +531,15 @@ attn_mma_kernel(const __grid_constant__ AttnParams P) {
   while (true) {
     const int nseg = min(tb - off, t1 - tt);           // tiles of this segment
     const int s0 = off * MT_KEYS, s1 = min(P.rowkmax[b], (off + nseg) * MT_KEYS);
-    const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(P.k) +
-                              ((int64_t)b * Hkv + h) * P.C * MT_D;
-    const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(P.v) +
-                              ((int64_t)b * Hkv + h) * P.C * MT_D;
+    const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(P.k);
+    const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(P.v);
     auto load_tile = [&](int tile, int buf) {
       const int key0 = s0 + tile * MT_KEYS;
       const uint32_t kd = smem_addr(S.u.kv.k[buf]), vd = smem_addr(S.u.kv.v[buf]);
       for (int i = t; i < MT_KEYS * 16; i += MT_THREADS) {
         const int kk = i >> 4, c = i & 15;
         const bool in = key0 + kk < s1;
-        const int64_t row = in ? key0 + kk : s0;       // a valid address when nothing is read
+        const int64_t row = kv_row(P, b, h, in ? key0 + kk : s0);   // valid when nothing is read
         cp_async16(kd + sw_off(kk, c), kb + row * MT_D + 8 * c, in);
         cp_async16(vd + sw_off(kk, c), vb + row * MT_D + 8 * c, in);
       }
@@ -737,6 +751,7 @@ attn_mma_kernel(const __grid_constant__ AttnParams P) {
 // wait is bounded; on expiry the CTA records SD attention error bit 0 and
 // drains.
 constexpr int TC_KEYS = 128;             // keys per tile
+static_assert(TC_KEYS == SD_KV_PAGE, "a K/V tile of the tcgen05 kernel is one cache page");
 constexpr int TC_N = 32;                 // query rows per kv head (padded)
 constexpr int TC_NST = 3;                // K/V ring stages
 constexpr int TC_THREADS = 192;
@@ -968,14 +983,15 @@ attn_tc_kernel(const __grid_constant__ AttnParams P, const __grid_constant__ CUt
       bool ok = true;
       do {
         tc_seg_bounds(g, P);
-        const int row0 = (g.b * Hkv + g.h) * P.C + g.s0;
+        const int row0 = P.bt ? 0 : (g.b * Hkv + g.h) * P.C + g.s0;
         for (int i = 0; i < g.nseg && ok; ++i, ++gi) {
           const int st = (int)(gi % TC_NST);
           if (gi >= (uint32_t)TC_NST)
             ok = tc_wait(&S.empty[st], ((gi / TC_NST) - 1) & 1u, &S.abort_);
           if (!ok) break;
           tc_expect_tx(&S.full[st], 4u * TC_KEYS * 128u);
-          const int y = row0 + i * TC_KEYS;
+          // a tile is one page of a paged cache (segments start on tile bounds)
+          const int y = P.bt ? (int)kv_row(P, g.b, g.h, g.s0 + i * TC_KEYS) : row0 + i * TC_KEYS;
           tc_tma_2d(S.k[st][0], &tmk, 0, y, &S.full[st]);
           tc_tma_2d(S.k[st][1], &tmk, 64, y, &S.full[st]);
           tc_tma_2d(S.v[st][0], &tmv, 0, y, &S.full[st]);
@@ -1365,7 +1381,7 @@ static int launch_tc_ntg(const AttnParams& P, const CUtensorMap& mk, const CUten
 }
 
 static int launch_tc(const AttnParams& P, cudaStream_t st) {
-  const int64_t rows = (int64_t)P.B * P.Hkv * P.C;
+  const int64_t rows = P.bt ? (int64_t)P.npages * P.Hkv * SD_KV_PAGE : (int64_t)P.B * P.Hkv * P.C;
   if (rows >= (int64_t)1 << 31) return SD_ENOTSUP;
   CUtensorMap mk, mv;
   if (!cache_map(&mk, P.k, rows) || !cache_map(&mv, P.v, rows)) return SD_ENOTSUP;
@@ -1406,11 +1422,15 @@ size_t sd_verify_attn_workspace_bytes(int B, int Hq, int Hkv, int D, int C, int 
          ((size_t)B * Hkv + 2 * (size_t)B + 2) * sizeof(int) + 256;
 }
 
-int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const void* kcache,
-                   const void* vcache, const int64_t* lengths, const int64_t* valid, int B, int Hq,
-                   int Hkv, int D, int C, int qlen, float scale, void* out, int64_t obs,
-                   int64_t oqs, int64_t ohs, int dtype, void* workspace, size_t workspace_bytes,
-                   void* stream) {
+}  // extern "C"
+
+namespace sd {
+static int verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const void* kcache,
+                       const void* vcache, const int32_t* bt, int bt_stride, int npages,
+                       const int64_t* lengths, const int64_t* valid, int B, int Hq, int Hkv, int D,
+                       int C, int qlen, float scale, void* out, int64_t obs, int64_t oqs,
+                       int64_t ohs, int dtype, void* workspace, size_t workspace_bytes,
+                       void* stream) {
   if (dtype != SD_DTYPE_BF16 && dtype != SD_DTYPE_F32) return SD_ENOTSUP;
   if (!q || !kcache || !vcache || !lengths || !out) return SD_EINVAL;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || qlen <= 0 || C <= 0) return SD_EINVAL;
@@ -1438,6 +1458,7 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
   P.status = P.rowkmax + B;
   P.tile_keys = MT_KEYS;
   P.seg_ovh = 0;
+  P.bt = bt; P.bt_stride = bt_stride; P.npages = npages;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // tensor-core path: bf16, head_dim 128, <= 32 query rows per kv head,
   // 16-byte aligned rows
@@ -1479,6 +1500,32 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const v
     attn_combine_kernel<float><<<B * Hkv * P.R, D, 0, st>>>(P);
   }
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+}
+}  // namespace sd
+
+extern "C" {
+
+int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const void* kcache,
+                   const void* vcache, const int64_t* lengths, const int64_t* valid, int B, int Hq,
+                   int Hkv, int D, int C, int qlen, float scale, void* out, int64_t obs,
+                   int64_t oqs, int64_t ohs, int dtype, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  return sd::verify_attn(q, qbs, qhs, qqs, kcache, vcache, nullptr, 0, 0, lengths, valid, B, Hq,
+                         Hkv, D, C, qlen, scale, out, obs, oqs, ohs, dtype, workspace,
+                         workspace_bytes, stream);
+}
+
+int sd_verify_attn_paged(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, const void* kpool,
+                         const void* vpool, const int32_t* block_table, int bt_stride, int npages,
+                         const int64_t* lengths, const int64_t* valid, int B, int Hq, int Hkv,
+                         int D, int qlen, float scale, void* out, int64_t obs, int64_t oqs,
+                         int64_t ohs, int dtype, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (!block_table || bt_stride <= 0 || npages <= 0) return SD_EINVAL;
+  if ((int64_t)bt_stride * SD_KV_PAGE > 0x7FFFFFFF) return SD_ENOTSUP;
+  return sd::verify_attn(q, qbs, qhs, qqs, kpool, vpool, block_table, bt_stride, npages, lengths,
+                         valid, B, Hq, Hkv, D, bt_stride * SD_KV_PAGE, qlen, scale, out, obs, oqs,
+                         ohs, dtype, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

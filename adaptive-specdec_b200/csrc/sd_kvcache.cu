@@ -15,6 +15,24 @@
 
 namespace sd {
 
+// Where a layer's K / V rows live: the contiguous [B, H, C, D] cache
+// (bt == nullptr) or a pool of pages [npages, H, SD_KV_PAGE, D] with row b's
+// slot s in page bt[b * bt_stride + s / SD_KV_PAGE] (-1: no page assigned).
+struct KvLayout {
+  const int32_t* bt;
+  int bt_stride, npages;
+};
+
+// Row index (in rows of D elements) of slot s of row b, head h; -1 when a
+// paged row has no page there (the write is skipped and *err gets bit 1).
+__device__ __forceinline__ int64_t kv_slot(const KvLayout& lay, int b, int h, int H, int C,
+                                           int64_t s) {
+  if (lay.bt == nullptr) return ((int64_t)b * H + h) * C + s;
+  const int pg = lay.bt[(int64_t)b * lay.bt_stride + (s / SD_KV_PAGE)];
+  if (pg < 0 || pg >= lay.npages) return -1;
+  return ((int64_t)pg * H + h) * SD_KV_PAGE + (s % SD_KV_PAGE);
+}
+
 // ---- fused post-projection step of an attention layer ------------------------
 // Per (row b, position l, head) vector of D elements, one warp: the head's
 // RMSNorm (q and k, when a weight is given), the rotary embedding with that
@@ -41,6 +59,7 @@ struct QkvArgs {
   __nv_bfloat16* q_out;                      // [B, Hq, L, D]
   int B, L, Hq, Hkv, D, C;
   int* err;
+  KvLayout lay;
 };
 
 constexpr int QKV_WARPS = 8;
@@ -75,7 +94,12 @@ __global__ void __launch_bounds__(QKV_WARPS * 32) qkv_rope_append_kernel(QkvArgs
       return;
     }
     const int h = hv < a.Hq + a.Hkv ? hv - a.Hq : hv - a.Hq - a.Hkv;
-    const int64_t slot = (((int64_t)b * a.Hkv + h) * a.C + len + l) * D;
+    const int64_t row = kv_slot(a.lay, b, h, a.Hkv, a.C, len + l);
+    if (row < 0) {
+      if (lane == 0 && a.err) atomicOr(a.err, 2);
+      return;
+    }
+    const int64_t slot = row * D;
     if (hv < a.Hq + a.Hkv) {
       src = a.k + r * a.k_rs + (int64_t)h * D;
       nw = a.kw;
@@ -144,7 +168,7 @@ __global__ void append_vec_kernel(uint4* __restrict__ kc, uint4* __restrict__ vc
                                   const char* __restrict__ nk, const char* __restrict__ nv,
                                   int64_t nbs, int64_t nhs, int64_t nqs, int esz,
                                   const int64_t* __restrict__ lengths, int B, int H, int C, int q,
-                                  int upr, int64_t total, int* err) {
+                                  int upr, int64_t total, int* err, KvLayout lay) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
   const int u = (int)(i % upr);
@@ -157,8 +181,13 @@ __global__ void append_vec_kernel(uint4* __restrict__ kc, uint4* __restrict__ vc
     if (u == 0 && j == 0 && h == 0 && err) atomicOr(err, 1);
     return;
   }
+  const int64_t row = kv_slot(lay, b, h, H, C, L + j);
+  if (row < 0) {
+    if (u == 0 && err) atomicOr(err, 2);
+    return;
+  }
   const int64_t src = (b * nbs + h * nhs + j * nqs) * esz;        // bytes
-  const int64_t dst = (((int64_t)b * H + h) * C + (L + j)) * upr;  // uint4 units
+  const int64_t dst = row * upr;                                   // uint4 units
   kc[dst + u] = *reinterpret_cast<const uint4*>(nk + src + 16 * (int64_t)u);
   vc[dst + u] = *reinterpret_cast<const uint4*>(nv + src + 16 * (int64_t)u);
 }
@@ -166,7 +195,8 @@ __global__ void append_vec_kernel(uint4* __restrict__ kc, uint4* __restrict__ vc
 // Element-wise fallback for rows that are not 16-byte aligned.
 __global__ void append_elem_kernel(char* kc, char* vc, const char* nk, const char* nv, int64_t nbs,
                                    int64_t nhs, int64_t nqs, int esz, const int64_t* lengths, int B,
-                                   int H, int C, int D, int q, int64_t total, int* err) {
+                                   int H, int C, int D, int q, int64_t total, int* err,
+                                   KvLayout lay) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
   const int d = (int)(i % D);
@@ -179,8 +209,13 @@ __global__ void append_elem_kernel(char* kc, char* vc, const char* nk, const cha
     if (d == 0 && j == 0 && h == 0 && err) atomicOr(err, 1);
     return;
   }
+  const int64_t row = kv_slot(lay, b, h, H, C, L + j);
+  if (row < 0) {
+    if (d == 0 && err) atomicOr(err, 2);
+    return;
+  }
   const int64_t src = (b * nbs + h * nhs + j * nqs + d) * esz;
-  const int64_t dst = ((((int64_t)b * H + h) * C + (L + j)) * D + d) * esz;
+  const int64_t dst = (row * D + d) * esz;
   for (int e = 0; e < esz; ++e) {
     kc[dst + e] = nk[src + e];
     vc[dst + e] = nv[src + e];
@@ -214,9 +249,12 @@ int sd_qkv_norm_rope_append(const void* q, int64_t q_rs, const void* k, int64_t 
                             const void* v, int64_t v_rs, const void* q_norm_w,
                             const void* k_norm_w, float eps, const void* cos, const void* sin,
                             int64_t cs_bs, int64_t cs_ls, void* kcache, void* vcache,
+                            const int32_t* block_table, int bt_stride, int npages,
                             const int64_t* lengths, int B, int L, int Hq, int Hkv, int D, int C,
                             void* q_out, int* err, void* stream) {
   if (!q || !k || !v || !cos || !sin || !kcache || !vcache || !lengths || !q_out) return SD_EINVAL;
+  if (block_table && (bt_stride <= 0 || npages <= 0 || (int64_t)bt_stride * SD_KV_PAGE < C))
+    return SD_EINVAL;
   if (B < 0 || L < 0 || Hq <= 0 || Hkv <= 0 || C <= 0 || D <= 0) return SD_EINVAL;
   if (D % 2 || D > sd::QKV_DMAX) return SD_ENOTSUP;
   if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return SD_EINVAL;
@@ -235,6 +273,7 @@ int sd_qkv_norm_rope_append(const void* q, int64_t q_rs, const void* k, int64_t 
   a.q_out = static_cast<__nv_bfloat16*>(q_out);
   a.B = B; a.L = L; a.Hq = Hq; a.Hkv = Hkv; a.D = D; a.C = C;
   a.err = err;
+  a.lay = sd::KvLayout{block_table, bt_stride, npages};
   const int64_t nwarp = (int64_t)B * L * (Hq + 2 * Hkv);
   const int64_t grid = (nwarp + sd::QKV_WARPS - 1) / sd::QKV_WARPS;
   if (grid > 0x7FFFFFFF) return SD_ENOTSUP;
@@ -243,9 +282,12 @@ int sd_qkv_norm_rope_append(const void* q, int64_t q_rs, const void* k, int64_t 
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
 }
 
-int sd_kv_append(void* kcache, void* vcache, const void* new_k, const void* new_v, int64_t nbs,
-                 int64_t nhs, int64_t nqs, const int64_t* lengths, int B, int H, int C, int D,
-                 int q, int dtype, int* err, void* stream) {
+}  // extern "C"
+
+namespace sd {
+static int kv_append(void* kcache, void* vcache, const void* new_k, const void* new_v, int64_t nbs,
+                     int64_t nhs, int64_t nqs, const int64_t* lengths, int B, int H, int C, int D,
+                     int q, int dtype, int* err, KvLayout lay, void* stream) {
   if (!kcache || !vcache || !new_k || !new_v || !lengths) return SD_EINVAL;
   if (B < 0 || H <= 0 || C <= 0 || D <= 0 || q < 0) return SD_EINVAL;
   if (dtype != SD_DTYPE_F32 && dtype != SD_DTYPE_F16 && dtype != SD_DTYPE_BF16) return SD_EINVAL;
@@ -263,15 +305,36 @@ int sd_kv_append(void* kcache, void* vcache, const void* new_k, const void* new_
     append_vec_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
         reinterpret_cast<uint4*>(kcache), reinterpret_cast<uint4*>(vcache),
         reinterpret_cast<const char*>(new_k), reinterpret_cast<const char*>(new_v), nbs, nhs, nqs,
-        esz, lengths, B, H, C, q, upr, total, err);
+        esz, lengths, B, H, C, q, upr, total, err, lay);
   } else {
     const int64_t total = (int64_t)B * H * q * D;
     append_elem_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
         reinterpret_cast<char*>(kcache), reinterpret_cast<char*>(vcache),
         reinterpret_cast<const char*>(new_k), reinterpret_cast<const char*>(new_v), nbs, nhs, nqs,
-        esz, lengths, B, H, C, D, q, total, err);
+        esz, lengths, B, H, C, D, q, total, err, lay);
   }
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+}
+}  // namespace sd
+
+extern "C" {
+
+int sd_kv_append(void* kcache, void* vcache, const void* new_k, const void* new_v, int64_t nbs,
+                 int64_t nhs, int64_t nqs, const int64_t* lengths, int B, int H, int C, int D,
+                 int q, int dtype, int* err, void* stream) {
+  return sd::kv_append(kcache, vcache, new_k, new_v, nbs, nhs, nqs, lengths, B, H, C, D, q, dtype,
+                       err, sd::KvLayout{nullptr, 0, 0}, stream);
+}
+
+int sd_kv_append_paged(void* kpool, void* vpool, const void* new_k, const void* new_v,
+                       int64_t nbs, int64_t nhs, int64_t nqs, const int32_t* block_table,
+                       int bt_stride, int npages, const int64_t* lengths, int B, int H, int D,
+                       int q, int dtype, int* err, void* stream) {
+  if (!block_table || bt_stride <= 0 || npages <= 0) return SD_EINVAL;
+  if ((int64_t)bt_stride * SD_KV_PAGE > 0x7FFFFFFF) return SD_ENOTSUP;
+  return sd::kv_append(kpool, vpool, new_k, new_v, nbs, nhs, nqs, lengths, B, H,
+                       bt_stride * SD_KV_PAGE, D, q, dtype, err,
+                       sd::KvLayout{block_table, bt_stride, npages}, stream);
 }
 
 }  // extern "C"

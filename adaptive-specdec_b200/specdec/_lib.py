@@ -38,8 +38,13 @@ _SIGNATURES = {
     "sd_gather_prob": ([_vp, _i32, _i32, _vp, _vp, _vp], _i32),
     "sd_kv_lengths_update": ([_vp, _vp, _i64, _i32, _i32, _i64, _vp, _vp], _i32),
     "sd_qkv_norm_rope_append": ([_vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _f32, _vp, _vp, _i64,
-                                 _i64, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
-                                 _vp], _i32),
+                                 _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i32, _i32, _i32,
+                                 _i32, _i32, _vp, _vp, _vp], _i32),
+    "sd_kv_append_paged": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i32,
+                            _i32, _i32, _i32, _i32, _vp, _vp], _i32),
+    "sd_verify_attn_paged": ([_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp, _vp, _i32,
+                              _i32, _i32, _i32, _i32, _f32, _vp, _i64, _i64, _i64, _i32, _vp,
+                              _sz, _vp], _i32),
     "sd_kv_commit": ([_vp, _vp, _i32, _i32, _vp, _vp], _i32),
     "sd_kv_append": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i32, _i32, _i32, _i32, _i32,
                       _i32, _vp, _vp], _i32),

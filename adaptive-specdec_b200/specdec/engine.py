@@ -39,7 +39,7 @@ from dataclasses import dataclass, field
 import torch
 
 from specdec import attention as A
-from specdec.kvcache import RaggedCache
+from specdec.kvcache import PAGE, PagedRaggedCache, RaggedCache
 from specdec.sampling import draft_sample, to_probs, verify_sample
 
 __all__ = ["SamplingConfig", "RunStats", "SpecDecodeEngine"]
@@ -201,7 +201,8 @@ class SpecDecodeEngine:
     """Speculative decoding for a (target, draft) pair sharing a tokenizer."""
 
     def __init__(self, target, draft, tokenizer, device=None, capacity=4096, nvtx=False,
-                 time_phases=False, cuda_graphs=True, fused_qkv=False):
+                 time_phases=False, cuda_graphs=True, fused_qkv=True, paged_kv=False,
+                 kv_pages=None):
         self.target = target.eval()
         self.draft = draft.eval()
         self.tok = tokenizer
@@ -223,9 +224,14 @@ class SpecDecodeEngine:
         A.register()
         for m in (self.target, self.draft):
             m.set_attn_implementation(A.IMPL)
-        # fused_qkv: one QKV GEMM and one norm + RoPE + KV-append kernel per
-        # attention layer (bf16 models; specdec.fused_attention)
+        # fused_qkv (default): one QKV GEMM and one norm + RoPE + KV-append
+        # kernel per attention layer of a bf16 model (specdec.fused_attention;
+        # layers of other dtypes keep their own forward)
         self.fused_qkv = bool(fused_qkv)
+        # paged_kv: both caches are PagedRaggedCache pools sized from the
+        # prompts' own lengths (kv_pages: pages per pool instead)
+        self.paged_kv = bool(paged_kv)
+        self.kv_pages = kv_pages
         if self.fused_qkv:
             from specdec import fused_attention as FA
             for m in (self.target, self.draft):
@@ -242,9 +248,20 @@ class SpecDecodeEngine:
         return ids
 
     # ---- plumbing ----------------------------------------------------------
-    def _mk_cache(self, model, batch):
-        return RaggedCache(model.config.num_hidden_layers, batch, self.capacity, self.device,
-                           attn_impl=A.IMPL)
+    def _mk_cache(self, model, batch, plen=None, max_new=0, k_max=16):
+        n_layers = model.config.num_hidden_layers
+        if not self.paged_kv:
+            return RaggedCache(n_layers, batch, self.capacity, self.device, attn_impl=A.IMPL)
+        n_pages = self.kv_pages
+        if n_pages is None:
+            # a row ends within plen + max_new + k_max + 1 tokens of its own
+            # and grows by one per round after that (at most max_new rounds);
+            # a round holds up to k_max + 1 more before its commit
+            pl = plen.to("cpu", torch.long)
+            per = (pl + 2 * int(max_new) + 2 * (int(k_max) + 1)).clamp(max=self.capacity)
+            n_pages = int(((per + PAGE - 1) // PAGE).sum()) + 1
+        return PagedRaggedCache(n_layers, batch, self.capacity, self.device, attn_impl=A.IMPL,
+                                n_pages=n_pages)
 
     def _forward(self, model, cache, tokens, valid=None, rows_last=None):
         """Forward `tokens` [B, q] against `cache`.
@@ -278,6 +295,8 @@ class SpecDecodeEngine:
 
     def _prefill(self, model, cache, input_ids, plen):
         """Right-padded prefill; logits [B, V] at each row's last real token."""
+        if isinstance(cache, PagedRaggedCache):
+            cache.reserve_prefill(input_ids.shape[1], plen)
         logits = self._forward(model, cache, input_ids, valid=plen, rows_last=plen - 1)
         cache.set_lengths(plen)
         return logits
@@ -302,8 +321,10 @@ class SpecDecodeEngine:
         B = input_ids.shape[0]
         input_ids = input_ids.to(dev)
         plen = plen.to(dev)
-        tcache = self._mk_cache(self.target, B)
-        dcache = self._mk_cache(self.draft, B)
+        k_cap = int(k_fixed) if k_fixed is not None else int(getattr(controller, "k_max", 16))
+        tcache = self._mk_cache(self.target, B, plen, max_new_tokens, k_cap)
+        dcache = self._mk_cache(self.draft, B, plen, max_new_tokens, k_cap)
+        paged = self.paged_kv
         st = RunStats(batch=B)
         t0 = time.perf_counter()
 
@@ -337,6 +358,11 @@ class SpecDecodeEngine:
                 graphs = _RoundGraphs(self, B, drf_buf.shape[1], dcache, tcache, drf_buf,
                                       T, tp, tk)
                 use_g = True
+            if paged:
+                # pages for this round's k + 1 tokens per cache, from the
+                # lengths read back at the end of the last round (no sync)
+                dcache.reserve(k + 1)
+                tcache.reserve(k + 1)
             conf = torch.ones(B, device=dev)
             u_draft = torch.rand(k, B, generator=gen, device=dev)
             d0 = time.perf_counter()
@@ -407,8 +433,15 @@ class SpecDecodeEngine:
                                          alive=alive)
                 tcache.commit(n_acc, k_eff)
                 dcache.commit(n_acc, k_eff)
-                # the one designed host sync of the round
-                host = torch.cat([n_acc.view(B, 1), y.view(B, 1), xs], dim=1).tolist()
+                # the one designed host sync of the round (with the paged
+                # caches' lengths, for the next round's page reservation)
+                cols = [n_acc.view(B, 1), y.view(B, 1), xs]
+                if paged:
+                    cols += [tcache.lengths.view(B, 1), dcache.lengths.view(B, 1)]
+                host = torch.cat(cols, dim=1).tolist()
+                if paged:
+                    tcache.set_host_lengths([r[-2] for r in host])
+                    dcache.set_host_lengths([r[-1] for r in host])
             n_acc_l = [r[0] for r in host]
 
             st.rounds += 1
@@ -455,7 +488,7 @@ class SpecDecodeEngine:
         gen.manual_seed(int(seed) if seed is not None else int(torch.seed() % (2 ** 63)))
         B = input_ids.shape[0]
         input_ids, plen = input_ids.to(dev), plen.to(dev)
-        cache = self._mk_cache(self.target, B)
+        cache = self._mk_cache(self.target, B, plen, max_new_tokens, 1)
         st = RunStats(batch=B)
         t0 = time.perf_counter()
         logits = self._prefill(self.target, cache, input_ids, plen)
@@ -466,6 +499,8 @@ class SpecDecodeEngine:
         done_l = [int(nl[b]) in self.eos_ids for b in range(B)]
         st.emitted += B
         while not all(done_l):
+            if isinstance(cache, PagedRaggedCache):
+                cache.reserve(1)
             logits = self._forward(self.target, cache, nxt.view(B, 1),
                                    rows_last=torch.zeros(B, dtype=torch.long, device=dev))
             cache.advance(1)

@@ -49,15 +49,17 @@ def _row_stride(x, name):
 
 
 def qkv_norm_rope_append(q, k, v, q_norm_w, k_norm_w, eps, cos, sin, k_cache, v_cache, lengths,
-                         head_dim, q_out=None, err=None):
+                         head_dim, q_out=None, err=None, block_table=None):
     """q [B, L, Hq*D], k / v [B, L, Hkv*D] (bf16 projection outputs) ->
     q_out [B, Hq, L, D]; k and v are written to k_cache / v_cache
-    [B, Hkv, C, D] at slots lengths[b] + l.
+    [B, Hkv, C, D] at slots lengths[b] + l, or, with ``block_table`` [B, W]
+    int32, to the page pools [n_pages, Hkv, PAGE, D] of a PagedRaggedCache
+    (C = W * PAGE).
 
     q_norm_w / k_norm_w [D] (or both None: no norm) and eps are the heads'
     RMSNorm; cos / sin [B or 1, L, D] the rotary tables of the positions.
-    ``err`` ([1] int32) gets bit 0 when a row's slots would pass C (those rows'
-    k / v are not written)."""
+    ``err`` ([1] int32) gets bit 0 when a row's slots would pass C and bit 1
+    when a paged slot has no page (those k / v are not written)."""
     L.require_cuda(q, k, v, cos, sin, k_cache, v_cache, lengths)
     ts = [q, k, v, cos, sin, k_cache, v_cache] + [w for w in (q_norm_w, k_norm_w) if w is not None]
     if any(t.dtype != torch.bfloat16 for t in ts):
@@ -67,6 +69,13 @@ def qkv_norm_rope_append(q, k, v, q_norm_w, k_norm_w, eps, cos, sin, k_cache, v_
     D = int(head_dim)
     B, Lq, nq = q.shape
     Bc, Hkv, C, Dc = k_cache.shape
+    bts = npages = 0
+    if block_table is not None:
+        if block_table.dtype != torch.int32 or block_table.dim() != 2 or \
+                block_table.shape[0] != B or not block_table.is_contiguous():
+            raise L.SpecdecError("block_table must be a contiguous [B, W] int32 tensor")
+        npages, bts = Bc, block_table.shape[1]
+        Bc, C = B, bts * C
     if Dc != D or nq % D or k.shape != (B, Lq, Hkv * D) or v.shape != k.shape or Bc != B:
         raise L.SpecdecError(f"shape mismatch: q {tuple(q.shape)}, k {tuple(k.shape)}, "
                              f"cache {tuple(k_cache.shape)}, head_dim {D}")
@@ -92,8 +101,9 @@ def qkv_norm_rope_append(q, k, v, q_norm_w, k_norm_w, eps, cos, sin, k_cache, v_
         L.check(L.lib().sd_qkv_norm_rope_append(
             L.ptr(q), _row_stride(q, "q"), L.ptr(k), _row_stride(k, "k"), L.ptr(v),
             _row_stride(v, "v"), L.ptr(q_norm_w), L.ptr(k_norm_w), float(eps), L.ptr(cos),
-            L.ptr(sin), cs_bs, cs_ls, L.ptr(k_cache), L.ptr(v_cache), L.ptr(lens), B, Lq, Hq, Hkv,
-            D, C, L.ptr(q_out), L.ptr(err), L.stream_ptr(q.device)), "qkv_norm_rope_append")
+            L.ptr(sin), cs_bs, cs_ls, L.ptr(k_cache), L.ptr(v_cache), L.ptr(block_table), bts,
+            npages, L.ptr(lens), B, Lq, Hq, Hkv, D, C, L.ptr(q_out), L.ptr(err),
+            L.stream_ptr(q.device)), "qkv_norm_rope_append")
     return q_out
 
 
@@ -156,7 +166,8 @@ def _fused_forward(self, hidden_states, position_embeddings=None, attention_mask
     kw, _ = _norm_of(self, "k_norm")
     cos, sin = position_embeddings
     q_out = qkv_norm_rope_append(q, k, v, qw, kw, eps if eps is not None else 0.0, cos, sin,
-                                 layer.keys, layer.values, cache.lengths, D, err=cache._err)
+                                 layer.keys, layer.values, cache.lengths, D, err=cache._err,
+                                 block_table=getattr(cache, "block_table", None))
     cache._last_q = Lq
     out, w = A.hf_attention(self, q_out, layer.keys, layer.values, attention_mask,
                             scaling=self.scaling)

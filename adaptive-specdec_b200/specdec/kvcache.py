@@ -24,13 +24,21 @@ Two attention modes:
 
 Invariant (the reference's, kvcache.py:17-21): after a rollback the cache is
 indistinguishable from one that only ever processed the accepted prefix.
+
+``PagedRaggedCache`` keeps the same interface over pages of PAGE tokens
+drawn from one pool per layer, so that memory follows each row's own length
+rather than the widest row's (the reference pads every row to the capacity,
+kvcache.py:98-116).
 """
+import numpy as np
 import torch
 from transformers.cache_utils import Cache, CacheLayerMixin
 
 from specdec import _lib as L
 
-__all__ = ["RaggedCache"]
+__all__ = ["RaggedCache", "PagedRaggedCache", "PAGE"]
+
+PAGE = 128            # tokens per page (SD_KV_PAGE): one K/V tile of the verify attention
 
 
 class _RaggedLayer(CacheLayerMixin):
@@ -103,6 +111,8 @@ class RaggedCache(Cache):
         cache.advance(q)                           # exactly once per forward
     """
 
+    _layer_cls = _RaggedLayer
+
     def __init__(self, n_layers, batch_size, capacity, device, attn_impl=None):
         self.capacity = int(capacity)
         self.batch_size = int(batch_size)
@@ -116,7 +126,7 @@ class RaggedCache(Cache):
         self._host_valid = True
         self.valid = None           # optional [B] cap for right-padded prefill
         self._last_q = 0
-        super().__init__(layers=[_RaggedLayer(self) for _ in range(n_layers)])
+        super().__init__(layers=[self._layer_cls(self) for _ in range(n_layers)])
 
     # ---- host mirror -----------------------------------------------------
     def _mirror(self):
@@ -213,6 +223,13 @@ class RaggedCache(Cache):
             self._host_valid = True
             self.lengths.copy_(t, non_blocking=False)
 
+    def set_host_lengths(self, lengths):
+        """Tell the cache its device lengths, as the caller read them back
+        (no device work): host-side geometry and page reservations then need
+        no sync of their own."""
+        self._host = torch.as_tensor(lengths, dtype=torch.long).reshape(-1).clone()
+        self._host_valid = True
+
     def rollback(self, n):
         """Drop the last n[b] tokens of row b.  O(1): no copy, no allocation.
 
@@ -280,3 +297,212 @@ class RaggedCache(Cache):
             if layer.is_initialized:
                 layer.keys.zero_()
                 layer.values.zero_()
+
+
+class _PagedLayer(_RaggedLayer):
+    """One layer's K and V page pools [n_pages, Hkv, PAGE, D]."""
+
+    def lazy_initialization(self, key_states, value_states=None):
+        p = self.parent
+        _, h, _, d = key_states.shape
+        self.dtype, self.device = key_states.dtype, key_states.device
+        self.keys = torch.zeros(p.n_pages, h, PAGE, d, dtype=self.dtype, device=self.device)
+        self.values = torch.zeros(p.n_pages, h, PAGE, d, dtype=self.dtype, device=self.device)
+        self.keys._sd_cache = p
+        self.values._sd_cache = p
+        self.is_initialized = True
+
+    def update(self, key_states, value_states, *args, **kwargs):
+        if not self.is_initialized:
+            self.lazy_initialization(key_states, value_states)
+        p = self.parent
+        b, h, q, d = key_states.shape
+        L.require_cuda(key_states, value_states, p.lengths)
+        ks, vs = key_states, value_states
+        if ks.stride(-1) != 1:
+            ks = ks.contiguous()
+        if vs.stride() != ks.stride():
+            vs, ks = vs.contiguous(), ks.contiguous()
+        with torch.cuda.device(ks.device):
+            L.check(L.lib().sd_kv_append_paged(
+                L.ptr(self.keys), L.ptr(self.values), L.ptr(ks), L.ptr(vs), ks.stride(0),
+                ks.stride(1), ks.stride(2), L.ptr(p.block_table), p.pages_per_row, p.n_pages,
+                L.ptr(p.lengths), b, h, d, q, L.dtype_code(ks.dtype), L.ptr(p._err),
+                L.stream_ptr(ks.device)), "kv_append_paged")
+        p._last_q = q
+        return self.keys, self.values
+
+
+class PageTable:
+    """Host-side page bookkeeping of a PagedRaggedCache (no device state).
+
+    ``bt`` [B, pages_per_row] int32 holds row b's pages in slot order (-1 =
+    none); pages [0, n_pages - 1) are handed out from a free stack, page
+    n_pages - 1 is the sink that a right-padded prefill writes its padding
+    to.  Every method returns True when ``bt`` changed.
+    """
+
+    def __init__(self, batch_size, pages_per_row, n_pages):
+        if n_pages < 2:
+            raise L.SpecdecError("a page pool needs at least two pages (one is the sink)")
+        self.B, self.W, self.n_pages = int(batch_size), int(pages_per_row), int(n_pages)
+        self.sink = self.n_pages - 1
+        self.bt = np.full((self.B, self.W), -1, dtype=np.int32)
+        self.owned = np.zeros(self.B, dtype=np.int64)              # real pages per row
+        self.free = list(range(self.sink - 1, -1, -1))             # stack, page 0 on top
+
+    def grow(self, need):
+        """Give row b pages until it owns need[b] (slots [0, need[b] * PAGE))."""
+        need = np.asarray(need, dtype=np.int64)
+        if int(need.max(initial=0)) > self.W:
+            raise RuntimeError("KV pages beyond the row capacity")
+        short = np.maximum(need - self.owned, 0)
+        total = int(short.sum())
+        if total == 0:
+            return False
+        if total > len(self.free):
+            raise L.SpecdecError(f"KV page pool exhausted: {total} pages wanted, "
+                                 f"{len(self.free)} free of {self.n_pages - 1}")
+        for b in np.nonzero(short)[0]:
+            o = int(self.owned[b])
+            for j in range(o, o + int(short[b])):
+                self.bt[b, j] = self.free.pop()
+            self.owned[b] = o + int(short[b])
+        return True
+
+    def reserve(self, lengths, q):
+        """Pages for slots [0, lengths[b] + q) of every row."""
+        lens = np.asarray(lengths, dtype=np.int64)
+        return self.grow(-(-(lens + int(q)) // PAGE))
+
+    def reserve_prefill(self, lengths, P, plen):
+        """Real pages for [0, lengths[b] + plen[b]), the sink for the rest of
+        [0, lengths[b] + P)."""
+        lens = np.asarray(lengths, dtype=np.int64)
+        pl = np.asarray(plen, dtype=np.int64)
+        top = -(-(lens + int(P)) // PAGE)
+        if int(top.max(initial=0)) > self.W:
+            raise RuntimeError("KV pages beyond the row capacity")
+        self.grow(-(-(lens + np.minimum(pl, int(P))) // PAGE))
+        for b in range(self.B):
+            o = int(self.owned[b])
+            if top[b] > o:
+                self.bt[b, o:top[b]] = self.sink
+        return True
+
+    def unsink(self):
+        hit = self.bt == self.sink
+        if not hit.any():
+            return False
+        self.bt[hit] = -1
+        return True
+
+    def release(self, rows):
+        """Return the pages of the given rows to the free stack."""
+        changed = False
+        for b in (int(r) for r in rows):
+            o = int(self.owned[b])
+            self.free.extend(int(x) for x in self.bt[b, :o][::-1])
+            changed = changed or o > 0 or bool((self.bt[b] >= 0).any())
+            self.bt[b, :] = -1
+            self.owned[b] = 0
+        return changed
+
+    def reset(self):
+        self.bt[:] = -1
+        self.owned[:] = 0
+        self.free = list(range(self.sink - 1, -1, -1))
+        return True
+
+    def check(self):
+        """Invariant: every handed-out page belongs to exactly one row slot."""
+        used = self.bt[(self.bt >= 0) & (self.bt != self.sink)]
+        assert len(set(used.tolist())) == used.size, "a page is owned twice"
+        assert used.size + len(self.free) == self.n_pages - 1, "pages lost"
+        for b in range(self.B):
+            o = int(self.owned[b])
+            assert (self.bt[b, :o] >= 0).all() and (self.bt[b, :o] != self.sink).all()
+
+
+class PagedRaggedCache(RaggedCache):
+    """RaggedCache whose rows own pages of PAGE tokens from a shared pool.
+
+    Row b's slot s lives in page ``block_table[b, s // PAGE]`` of every
+    layer's pool.  Pages are handed out on the host, before the forwards that
+    need them: ``reserve(q)`` gives each row the pages for its next q tokens
+    (one small host-to-device copy of the table when anything changed; no
+    host sync while the host mirror of the lengths is valid), and
+    ``reserve_prefill(P, plen)`` does the same for a right-padded prefill,
+    pointing the padding past each row's own prompt at a shared sink page
+    that nothing reads.  Pages stay with their row after a rollback (the row
+    grows back into them); ``release(rows)`` and ``reset()`` return them.
+    A slot written without a page sets the device error flag (bit 1).
+
+    Only the kernel attention path (attn_impl "specdec_b200") reads paged
+    layers.
+    """
+
+    _layer_cls = _PagedLayer
+
+    def __init__(self, n_layers, batch_size, capacity, device, attn_impl="specdec_b200",
+                 n_pages=None):
+        if attn_impl != "specdec_b200":
+            raise L.SpecdecError("PagedRaggedCache is read by the specdec_b200 attention only")
+        self.pages_per_row = -(-int(capacity) // PAGE)
+        super().__init__(n_layers, batch_size, self.pages_per_row * PAGE, device, attn_impl)
+        self.n_pages = int(n_pages) if n_pages is not None else \
+            self.batch_size * self.pages_per_row + 1
+        self.pages = PageTable(self.batch_size, self.pages_per_row, self.n_pages)
+        self.block_table = torch.full((self.batch_size, self.pages_per_row), -1,
+                                      dtype=torch.int32, device=self.device)
+
+    # ---- pages -------------------------------------------------------------
+    @property
+    def free_pages(self):
+        return len(self.pages.free)
+
+    def _push(self, changed=True):
+        if changed:
+            self.block_table.copy_(torch.from_numpy(self.pages.bt))
+
+    def reserve(self, q):
+        """Pages for the next q tokens of every row (call before the forward)."""
+        self._push(self.pages.reserve(self._mirror().numpy(), q))
+
+    def reserve_prefill(self, P, plen):
+        """Pages for a right-padded prefill of P tokens with prompt lengths
+        plen (real pages for each row's prompt, the sink for its padding)."""
+        pl = torch.as_tensor(plen).to("cpu", torch.long).reshape(-1).numpy()
+        self._push(self.pages.reserve_prefill(self._mirror().numpy(), P, pl))
+
+    def release(self, rows):
+        """Return the pages of the given rows to the pool (their lengths go to 0)."""
+        rows = [int(r) for r in rows]
+        h = self._mirror().clone()
+        h[rows] = 0
+        self.pages.release(rows)
+        self.set_lengths(h)
+        self._push()
+
+    def set_lengths(self, lengths):
+        super().set_lengths(lengths)
+        self._push(self.pages.unsink())
+
+    def reset(self):
+        super().reset()
+        self._push(self.pages.reset())
+
+    def check_errors(self):
+        e = int(self._err.item())
+        if e:
+            self._err.zero_()
+            if e & 2:
+                raise RuntimeError("PagedRaggedCache: a slot was written without a page "
+                                   "(reserve() before the forward)")
+            raise RuntimeError("RaggedCache: a length update left [0, capacity]")
+
+    @property
+    def kv_bytes(self):
+        """Bytes held by the K and V pools of the initialised layers."""
+        return sum(2 * l.keys.numel() * l.keys.element_size() for l in self.layers
+                   if l.is_initialized)

@@ -60,9 +60,13 @@ def parse():
                     help="--mode adaptive: shared-prior strength of the high-agreement phase")
     ap.add_argument("--beta-lo", type=float, default=5.0,
                     help="--mode adaptive: shared-prior strength of the low-agreement phase")
-    ap.add_argument("--fused-qkv", action="store_true",
-                    help="--mode engine / adaptive: one QKV GEMM + the fused norm / RoPE / "
-                         "KV-append kernel per attention layer")
+    ap.add_argument("--no-fused-qkv", dest="fused_qkv", action="store_false",
+                    help="--mode engine / adaptive: the layers' own forwards instead of one QKV "
+                         "GEMM + the fused norm / RoPE / KV-append kernel per attention layer")
+    ap.add_argument("--paged", action="store_true",
+                    help="--mode attn: time the paged-cache kernel (the same K/V scattered over "
+                         "128-token pages in a random order); --mode engine / adaptive: paged "
+                         "caches")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="default run: skip the greedy / attention / rejection-sampler lines "
@@ -304,6 +308,9 @@ def attn_bench(a):
     B, Hq, Hkv, D, ql = a.attn_rows, 32, 8, 128, 5
     lens = W.attn_lengths(B, seed=0)
     C = int(lens.max()) + ql + 3
+    if a.paged:
+        from specdec.kvcache import PAGE
+        C = -(-C // PAGE) * PAGE
     g = torch.Generator(device=dev).manual_seed(0)
     q = torch.randn(B, Hq, ql, D, generator=g, device=dev).to(torch.bfloat16)
     kc = torch.randn(B, Hkv, C, D, generator=g, device=dev).to(torch.bfloat16)
@@ -331,10 +338,30 @@ def attn_bench(a):
         worst = max(worst, float((out[b].float() - ref).abs().max()))
     if not worst < 3e-2:
         raise SystemExit(f"verify attention differs from the fp32 rule: max abs error {worst}")
+    bt = None
+    if a.paged:
+        # the same K / V over pages of one pool in a random page order; the
+        # paged call must reproduce the contiguous output bit for bit
+        Wp = C // PAGE
+        perm = torch.randperm(B * Wp, generator=torch.Generator().manual_seed(0)).to(dev)
+
+        def to_pool(c):
+            pages = c.view(B, Hkv, Wp, PAGE, D).permute(0, 2, 1, 3, 4).reshape(B * Wp, Hkv,
+                                                                                 PAGE, D)
+            pool = torch.empty_like(pages)
+            pool[perm] = pages
+            return pool
+        kc, vc = to_pool(kc), to_pool(vc)
+        bt = perm.view(B, Wp).to(torch.int32).contiguous()
+        out_c = out.clone()
+        A.verify_attention(q, kc, vc, lens_d, out=out, block_table=bt)
+        torch.cuda.synchronize(dev)
+        if not torch.equal(out, out_c):
+            raise SystemExit("paged verify attention differs from the contiguous cache")
     s = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(s):
         for _ in range(max(3, a.warmup)):
-            A.verify_attention(q, kc, vc, lens_d, out=out)
+            A.verify_attention(q, kc, vc, lens_d, out=out, block_table=bt)
         torch.cuda.synchronize(dev)
         steps = max(5, min(a.steps, 200))
         e0 = torch.cuda.Event(enable_timing=True)
@@ -342,7 +369,7 @@ def attn_bench(a):
         with ClockSampler(dev.index or 0) as clk:
             e0.record(s)
             for _ in range(steps):
-                A.verify_attention(q, kc, vc, lens_d, out=out)
+                A.verify_attention(q, kc, vc, lens_d, out=out, block_table=bt)
             e1.record(s)
             torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / steps
@@ -355,7 +382,8 @@ def attn_bench(a):
         "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q / k / v)",
         "config": {"workload": "config 3 verify attention, one layer" + ("" if B == 64 else
-                   f" ({B} rows)"), "rows": B, "Hq": Hq,
+                   f" ({B} rows)") + (", paged cache (128-token pages, random order)"
+                                      if a.paged else ""), "rows": B, "Hq": Hq,
                    "Hkv": Hkv, "head_dim": D, "queries": ql, "live_keys": live,
                    "checked": f"8 rows vs the fp32 mask rule before timing, max abs error "
                               f"{worst:.2e}",
@@ -570,7 +598,8 @@ def adaptive_bench(a):
     draft.specdec_head = prior.head(draft.lm_head)
     rows, new, kmax, pmin, pmax = a.rows, a.new_tokens, 8, 128, 4096
     eng = SpecDecodeEngine(target, draft, _NoTok(), device=dev,
-                           capacity=pmax + 2 * new + 2 * kmax + 8, fused_qkv=a.fused_qkv)
+                           capacity=pmax + 2 * new + 2 * kmax + 8, fused_qkv=a.fused_qkv,
+                           paged_kv=a.paged)
     g = torch.Generator().manual_seed(1000 + rank)
     plen = torch.randint(pmin, pmax + 1, (rows,), generator=g)
     ids = torch.randint(0, VOCAB, (rows, int(plen.max())), generator=g)
@@ -616,7 +645,7 @@ def adaptive_bench(a):
                    "prompt": f"U[{pmin},{pmax}]", "new_tokens": new, "k_range": [1, kmax],
                    "controller": "ewma", "temperature": T_SAMPLE, "top_p": TOP_P,
                    "alpha_switch_tokens": 64, "beta_hi_lo": list(betas),
-                   "fused_qkv": a.fused_qkv,
+                   "fused_qkv": a.fused_qkv, "paged_kv": a.paged,
                    "parallelism": f"row-sharded x{world}, no collective on the data path"},
         "alpha_conditional": {"high_phase": alpha_hi, "low_phase": alpha_lo},
         "acceptance_rate": {"high_phase": rate_hi, "low_phase": rate_lo},
@@ -659,7 +688,7 @@ def engine_bench(a):
     # so a row can reach P + 2 * new
     eng = SpecDecodeEngine(target, draft, _NoTok(), device=dev,
                            capacity=P + 2 * new + 2 * k + 8, time_phases=True,
-                           fused_qkv=a.fused_qkv)
+                           fused_qkv=a.fused_qkv, paged_kv=a.paged)
     g = torch.Generator().manual_seed(1)
     ids = torch.randint(0, VOCAB, (Bq, P), generator=g)
     plen = torch.full((Bq,), P, dtype=torch.long)
@@ -683,7 +712,8 @@ def engine_bench(a):
         "config": {"workload": "config 4 full speculative round", "rows": Bq, "prompt": P,
                    "new_tokens": new, "k": k, "temperature": T_SAMPLE, "top_p": TOP_P,
                    "target": "Qwen3-8B shape (random init)",
-                   "draft": "Qwen3-0.6B shape (random init)", "fused_qkv": a.fused_qkv},
+                   "draft": "Qwen3-0.6B shape (random init)", "fused_qkv": a.fused_qkv,
+                   "paged_kv": a.paged},
         "engine": {key: d[key] for key in ("rounds", "emitted", "acceptance_rate",
                                            "mean_accepted_len", "draft_forwards",
                                            "target_forwards", "t_draft", "t_target",

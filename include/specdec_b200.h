@@ -38,6 +38,13 @@ extern "C" {
 #define SD_DTYPE_F16 1
 #define SD_DTYPE_BF16 2
 
+/* Tokens per page of a paged KV cache (one K/V tile of the tcgen05 verify
+ * attention).  A paged layer is a pool [npages, H, SD_KV_PAGE, D] per K and
+ * V; row b's slot s lives in page block_table[b * bt_stride + s / SD_KV_PAGE]
+ * (int32, -1 = no page assigned), so a row's capacity is
+ * bt_stride * SD_KV_PAGE. */
+#define SD_KV_PAGE 128
+
 /* Library version and build information, for the loaders' sanity checks. */
 int sd_version(void);
 
@@ -198,6 +205,16 @@ int sd_kv_append(void* kcache, void* vcache, const void* new_k, const void* new_
                  int B, int H, int C, int D, int q, int dtype, int* err, void* stream);
 
 /*
+ * sd_kv_append into a paged layer (pools and block table as SD_KV_PAGE
+ * describes).  A slot whose page is not assigned (-1) is not written and
+ * sets bit 1 of *err; rows past bt_stride * SD_KV_PAGE set bit 0.
+ */
+int sd_kv_append_paged(void* kpool, void* vpool, const void* new_k, const void* new_v,
+                       int64_t nbs, int64_t nhs, int64_t nqs, const int32_t* block_table,
+                       int bt_stride, int npages, const int64_t* lengths, int B, int H, int D,
+                       int q, int dtype, int* err, void* stream);
+
+/*
  * The fused step between an attention layer's QKV projections and its
  * attention, for bf16 Qwen3 / Llama-style layers: per row b, position
  * l < L and head, the head's RMSNorm on q and k (weights q_norm_w / k_norm_w
@@ -212,12 +229,16 @@ int sd_kv_append(void* kcache, void* vcache, const void* new_k, const void* new_
  * (reference specdec/kvcache.py:61-74): one launch instead of a dozen
  * elementwise kernels and the append.  Same arithmetic on bf16 tensors, but
  * for the float32 sum of squares' order (a normalised value may differ by one
- * bf16 ulp).  Rows whose slots would pass C are not written and set *err.
+ * bf16 ulp).  Rows whose slots would pass C are not written and set bit 0
+ * of *err.  block_table non-NULL: kcache / vcache are page pools
+ * (SD_KV_PAGE), C <= bt_stride * SD_KV_PAGE, and a slot without a page is
+ * not written and sets bit 1.
  */
 int sd_qkv_norm_rope_append(const void* q, int64_t q_rs, const void* k, int64_t k_rs,
                             const void* v, int64_t v_rs, const void* q_norm_w,
                             const void* k_norm_w, float eps, const void* cos, const void* sin,
                             int64_t cs_bs, int64_t cs_ls, void* kcache, void* vcache,
+                            const int32_t* block_table, int bt_stride, int npages,
                             const int64_t* lengths, int B, int L, int Hq, int Hkv, int D, int C,
                             void* q_out, int* err, void* stream);
 
@@ -241,6 +262,22 @@ int sd_verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs,
                    void* workspace, size_t workspace_bytes, void* stream);
 
 size_t sd_verify_attn_workspace_bytes(int B, int Hq, int Hkv, int D, int C, int qlen);
+
+/*
+ * sd_verify_attn over a paged cache: kpool / vpool [npages, Hkv, SD_KV_PAGE,
+ * D] and the rows' block table [B, bt_stride] (SD_KV_PAGE above).  Same
+ * masking and arithmetic; the row capacity C is bt_stride * SD_KV_PAGE (size
+ * the workspace with it).  A page index outside [0, npages) reads page 0.
+ * The reference keeps one capacity-padded buffer per layer
+ * (specdec/kvcache.py:98-116); pages let rows of very different lengths
+ * share one pool.
+ */
+int sd_verify_attn_paged(const void* q, int64_t qbs, int64_t qhs, int64_t qqs,
+                         const void* kpool, const void* vpool, const int32_t* block_table,
+                         int bt_stride, int npages, const int64_t* lengths, const int64_t* valid,
+                         int B, int Hq, int Hkv, int D, int qlen, float scale, void* out,
+                         int64_t obs, int64_t oqs, int64_t ohs, int dtype, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /*
  * Vocabulary-sharded verify round: the SPMD form of sd_verify_sample for a
