@@ -17,7 +17,7 @@ CSRC = HERE / "csrc"
 INCLUDE = ROOT / "include"
 LIB = HERE / "libspecdec_b200.so"
 
-SOURCES = ["sd_sampling.cu", "sd_kvcache.cu", "sd_attention.cu", "sd_shard.cu"]
+SOURCES = ["sd_sampling.cu", "sd_kvcache.cu", "sd_attention.cu", "sd_shard.cu", "sd_layers.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-Xptxas", "-warn-spills"]

@@ -1,0 +1,100 @@
+// The decoder layers' RMSNorm and gated-MLP activation around the verify
+// round's forwards (sm_100a, bf16).
+//
+// transformers' Qwen3RMSNorm / LlamaRMSNorm.forward is about eight small
+// kernels per call (cast, square, mean, add, rsqrt, multiply, cast, weight);
+// Qwen3MLP / LlamaMLP.forward runs the gate and up GEMMs, the SiLU and the
+// product.  Both appear twice per decoder layer in every draft and verify
+// forward of the reference's engine (specdec/engine.py:245-274 call the HF
+// models), where launches, not bytes, set their cost.  Here each is one
+// launch with transformers' bf16 arithmetic in the same order:
+//   rmsnorm:  y = rn(w * rn(x * rsqrt(mean(x^2) + eps)))   (x^2 summed in f32)
+//   silu_mul: y = rn(rn(g / (1 + exp(-g))) * u)
+// The float32 sum of squares is reduced in another order than torch's, so a
+// normalised value can land one bf16 ulp apart.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "specdec_b200.h"
+
+namespace sd {
+
+constexpr int NORM_THREADS = 256;
+
+__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// One CTA per row of H elements; the row is read twice (the second time from
+// L1 / L2).  Rows are `x_rs` / `out_rs` elements apart.
+__global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(
+    const __nv_bfloat16* x, int64_t x_rs, const __nv_bfloat16* __restrict__ w, float eps,
+    __nv_bfloat16* out, int64_t out_rs, int H) {     // out may be x: each element has one owner
+  __shared__ float red[NORM_THREADS / 32];
+  const int64_t r = blockIdx.x;
+  const __nv_bfloat16* xr = x + r * x_rs;
+  __nv_bfloat16* yr = out + r * out_rs;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += NORM_THREADS) {
+    const float v = __bfloat162float(xr[i]);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) red[wid] = ss;
+  __syncthreads();
+  if (wid == 0) {
+    ss = lane < NORM_THREADS / 32 ? red[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[0] = ss;
+  }
+  __syncthreads();
+  const float rs = rsqrtf(__fdiv_rn(red[0], (float)H) + eps);
+  for (int i = threadIdx.x; i < H; i += NORM_THREADS)
+    yr[i] = __float2bfloat16_rn(__bfloat162float(w[i]) * bfr(__bfloat162float(xr[i]) * rs));
+}
+
+// out[r, i] = silu(gu[r, i]) * gu[r, I + i], one thread per output element
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t gu_rs,
+                                __nv_bfloat16* __restrict__ out, int64_t out_rs, int I,
+                                int64_t total) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= total) return;
+  const int64_t r = e / I;
+  const int i = (int)(e - r * I);
+  const float g = __bfloat162float(gu[r * gu_rs + i]);
+  const float u = __bfloat162float(gu[r * gu_rs + I + i]);
+  const float s = bfr(g / (1.0f + expf(-g)));
+  out[r * out_rs + i] = __float2bfloat16_rn(s * u);
+}
+
+}  // namespace sd
+
+extern "C" {
+
+int sd_rmsnorm(const void* x, int64_t x_rs, const void* w, float eps, void* out, int64_t out_rs,
+               int rows, int H, void* stream) {
+  if (!x || !w || !out || rows < 0 || H <= 0) return SD_EINVAL;
+  if (rows == 0) return SD_OK;
+  sd::rmsnorm_kernel<<<(unsigned)rows, sd::NORM_THREADS, 0,
+                       reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), x_rs, static_cast<const __nv_bfloat16*>(w), eps,
+      static_cast<__nv_bfloat16*>(out), out_rs, H);
+  return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+}
+
+int sd_silu_mul(const void* gu, int64_t gu_rs, void* out, int64_t out_rs, int rows, int I,
+                void* stream) {
+  if (!gu || !out || rows < 0 || I <= 0) return SD_EINVAL;
+  const int64_t total = (int64_t)rows * I;
+  if (total == 0) return SD_OK;
+  const int64_t grid = (total + 255) / 256;
+  if (grid > 0x7FFFFFFF) return SD_ENOTSUP;
+  sd::silu_mul_kernel<<<(unsigned)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gu), gu_rs, static_cast<__nv_bfloat16*>(out), out_rs, I,
+      total);
+  return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+}
+
+}  // extern "C"

@@ -201,8 +201,8 @@ class SpecDecodeEngine:
     """Speculative decoding for a (target, draft) pair sharing a tokenizer."""
 
     def __init__(self, target, draft, tokenizer, device=None, capacity=4096, nvtx=False,
-                 time_phases=False, cuda_graphs=True, fused_qkv=True, paged_kv=False,
-                 kv_pages=None):
+                 time_phases=False, cuda_graphs=True, fused_qkv=True, fused_norm_mlp=True,
+                 paged_kv=False, kv_pages=None):
         self.target = target.eval()
         self.draft = draft.eval()
         self.tok = tokenizer
@@ -228,6 +228,13 @@ class SpecDecodeEngine:
         # kernel per attention layer of a bf16 model (specdec.fused_attention;
         # layers of other dtypes keep their own forward)
         self.fused_qkv = bool(fused_qkv)
+        # fused_norm_mlp (default): every RMSNorm one launch, every SiLU-gated
+        # MLP one gate / up GEMM + one activation launch (specdec.fused_layers)
+        self.fused_norm_mlp = bool(fused_norm_mlp)
+        if self.fused_norm_mlp:
+            from specdec import fused_layers as FL
+            for m in (self.target, self.draft):
+                FL.install(m)
         # paged_kv: both caches are PagedRaggedCache pools sized from the
         # prompts' own lengths (kv_pages: pages per pool instead)
         self.paged_kv = bool(paged_kv)

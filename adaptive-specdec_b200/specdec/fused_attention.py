@@ -201,13 +201,17 @@ def install(model, fuse_qkv_gemm=True):
     return n
 
 
+def _installed(m):
+    return getattr(m.forward, "__func__", None) is _fused_forward
+
+
 def uninstall(model):
     """Restore the original forwards (the projections keep their views)."""
     for m in model.modules():
-        if hasattr(m, "_sd_orig_forward"):
+        if _installed(m):
             m.forward = m._sd_orig_forward
             del m._sd_orig_forward, m._sd_qkv_w, m._sd_qkv_b
 
 
 def installed_layers(model):
-    return sum(1 for m in model.modules() if hasattr(m, "_sd_orig_forward"))
+    return sum(1 for m in model.modules() if _installed(m))

@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--no-fused-qkv", dest="fused_qkv", action="store_false",
                     help="--mode engine / adaptive: the layers' own forwards instead of one QKV "
                          "GEMM + the fused norm / RoPE / KV-append kernel per attention layer")
+    ap.add_argument("--no-fused-norm-mlp", dest="fused_norm_mlp", action="store_false",
+                    help="--mode engine / adaptive: the RMSNorm and MLP modules' own forwards "
+                         "instead of one launch per norm and a fused gate / up GEMM + activation")
     ap.add_argument("--paged", action="store_true",
                     help="--mode attn: time the paged-cache kernel (the same K/V scattered over "
                          "128-token pages in a random order); --mode engine / adaptive: paged "
@@ -599,7 +602,7 @@ def adaptive_bench(a):
     rows, new, kmax, pmin, pmax = a.rows, a.new_tokens, 8, 128, 4096
     eng = SpecDecodeEngine(target, draft, _NoTok(), device=dev,
                            capacity=pmax + 2 * new + 2 * kmax + 8, fused_qkv=a.fused_qkv,
-                           paged_kv=a.paged)
+                           fused_norm_mlp=a.fused_norm_mlp, paged_kv=a.paged)
     g = torch.Generator().manual_seed(1000 + rank)
     plen = torch.randint(pmin, pmax + 1, (rows,), generator=g)
     ids = torch.randint(0, VOCAB, (rows, int(plen.max())), generator=g)
@@ -645,7 +648,8 @@ def adaptive_bench(a):
                    "prompt": f"U[{pmin},{pmax}]", "new_tokens": new, "k_range": [1, kmax],
                    "controller": "ewma", "temperature": T_SAMPLE, "top_p": TOP_P,
                    "alpha_switch_tokens": 64, "beta_hi_lo": list(betas),
-                   "fused_qkv": a.fused_qkv, "paged_kv": a.paged,
+                   "fused_qkv": a.fused_qkv, "fused_norm_mlp": a.fused_norm_mlp,
+                   "paged_kv": a.paged,
                    "parallelism": f"row-sharded x{world}, no collective on the data path"},
         "alpha_conditional": {"high_phase": alpha_hi, "low_phase": alpha_lo},
         "acceptance_rate": {"high_phase": rate_hi, "low_phase": rate_lo},
@@ -688,7 +692,8 @@ def engine_bench(a):
     # so a row can reach P + 2 * new
     eng = SpecDecodeEngine(target, draft, _NoTok(), device=dev,
                            capacity=P + 2 * new + 2 * k + 8, time_phases=True,
-                           fused_qkv=a.fused_qkv, paged_kv=a.paged)
+                           fused_qkv=a.fused_qkv, fused_norm_mlp=a.fused_norm_mlp,
+                           paged_kv=a.paged)
     g = torch.Generator().manual_seed(1)
     ids = torch.randint(0, VOCAB, (Bq, P), generator=g)
     plen = torch.full((Bq,), P, dtype=torch.long)
@@ -713,7 +718,7 @@ def engine_bench(a):
                    "new_tokens": new, "k": k, "temperature": T_SAMPLE, "top_p": TOP_P,
                    "target": "Qwen3-8B shape (random init)",
                    "draft": "Qwen3-0.6B shape (random init)", "fused_qkv": a.fused_qkv,
-                   "paged_kv": a.paged},
+                   "fused_norm_mlp": a.fused_norm_mlp, "paged_kv": a.paged},
         "engine": {key: d[key] for key in ("rounds", "emitted", "acceptance_rate",
                                            "mean_accepted_len", "draft_forwards",
                                            "target_forwards", "t_draft", "t_target",

@@ -243,6 +243,26 @@ int sd_qkv_norm_rope_append(const void* q, int64_t q_rs, const void* k, int64_t 
                             void* q_out, int* err, void* stream);
 
 /*
+ * The decoder layers' RMSNorm as one launch (bf16): for each of `rows` rows
+ * of H elements (x rows x_rs elements apart, out rows out_rs apart)
+ *   out = rn(w * rn(x * rsqrt(mean(x^2) + eps)))
+ * transformers' Qwen3RMSNorm / LlamaRMSNorm arithmetic (the float32 sum of
+ * squares in another order: a value may differ by one bf16 ulp).  In place
+ * (out == x) is allowed.
+ */
+int sd_rmsnorm(const void* x, int64_t x_rs, const void* w, float eps, void* out, int64_t out_rs,
+               int rows, int H, void* stream);
+
+/*
+ * The gated MLP's activation as one launch (bf16): gu rows hold [gate | up]
+ * (2 I elements, rows gu_rs apart);
+ *   out[r, i] = rn(rn(silu(gate[r, i])) * up[r, i])
+ * as transformers' act_fn(gate_proj(x)) * up_proj(x) with SiLU.
+ */
+int sd_silu_mul(const void* gu, int64_t gu_rs, void* out, int64_t out_rs, int rows, int I,
+                void* stream);
+
+/*
  * Verify attention over the ragged cache (after the append of this forward):
  * query j of row b (position lengths[b] + j) attends to cache slots
  * s <= lengths[b] + j, i.e. the reference mask s <= len[b] + j
