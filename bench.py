@@ -66,6 +66,9 @@ def parse():
     ap.add_argument("--no-fused-norm-mlp", dest="fused_norm_mlp", action="store_false",
                     help="--mode engine / adaptive: the RMSNorm and MLP modules' own forwards "
                          "instead of one launch per norm and a fused gate / up GEMM + activation")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="--mode engine: cudaProfilerStart / Stop around the timed generate "
+                         "(for ncu --profile-from-start off)")
     ap.add_argument("--paged", action="store_true",
                     help="--mode attn: time the paged-cache kernel (the same K/V scattered over "
                          "128-token pages in a random order); --mode engine / adaptive: paged "
@@ -702,10 +705,14 @@ def engine_bench(a):
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index or 0) as clk:
+        if a.profile_range:
+            torch.cuda.profiler.start()
         e0.record()
         _, st = eng.generate(ids, plen, new, sampling=sp, seed=1, k_fixed=k)
         e1.record()
         torch.cuda.synchronize(dev)
+        if a.profile_range:
+            torch.cuda.profiler.stop()
     ms = e0.elapsed_time(e1)
     d = st.to_dict()
     print(json.dumps({
