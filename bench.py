@@ -78,6 +78,13 @@ def parse():
                     help="default run: skip the greedy / attention / rejection-sampler lines "
                          "reported under 'also'")
     ap.add_argument("--attn-rows", type=int, default=64, help="--mode attn: rows (config 3: 64)")
+    ap.add_argument("--attn-ctx", default="512:8192",
+                    help="--mode attn: context lengths uniform in LO:HI (config 3: 512:8192; "
+                         "the engine's config-4 rounds: about 512:640)")
+    ap.add_argument("--attn-queries", type=int, default=5,
+                    help="--mode attn: queries per row (verify: k + 1 = 5; a draft step: 1)")
+    ap.add_argument("--attn-heads", default="32:8",
+                    help="--mode attn: query:kv heads (Qwen3-8B 32:8, Qwen3-0.6B 16:8)")
     return ap.parse_args()
 
 
@@ -311,8 +318,11 @@ def attn_bench(a):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    B, Hq, Hkv, D, ql = a.attn_rows, 32, 8, 128, 5
-    lens = W.attn_lengths(B, seed=0)
+    B, D, ql = a.attn_rows, 128, a.attn_queries
+    Hq, Hkv = (int(x) for x in a.attn_heads.split(":"))
+    lo, hi = (int(x) for x in a.attn_ctx.split(":"))
+    lens = W.attn_lengths(B, lo, hi, seed=0)
+    cfg3 = (lo, hi, ql, Hq, Hkv) == (512, 8192, 5, 32, 8)
     C = int(lens.max()) + ql + 3
     if a.paged:
         from specdec.kvcache import PAGE
@@ -364,18 +374,23 @@ def attn_bench(a):
         torch.cuda.synchronize(dev)
         if not torch.equal(out, out_c):
             raise SystemExit("paged verify attention differs from the contiguous cache")
+    # caches smaller than L2 (short contexts): rotate over copies holding
+    # more than 2x L2 between them, as a forward's layers would
+    kv_bytes = 2 * kc.numel() * kc.element_size()
+    nrep = max(1, -(-(2 * 126 * 2 ** 20) // kv_bytes)) if kv_bytes < 2 * 126 * 2 ** 20 else 1
+    sets = [(kc, vc)] + [(kc.clone(), vc.clone()) for _ in range(nrep - 1)]
     s = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(s):
-        for _ in range(max(3, a.warmup)):
-            A.verify_attention(q, kc, vc, lens_d, out=out, block_table=bt)
+        for i in range(max(3, a.warmup)):
+            A.verify_attention(q, *sets[i % nrep], lens_d, out=out, block_table=bt)
         torch.cuda.synchronize(dev)
         steps = max(5, min(a.steps, 200))
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         with ClockSampler(dev.index or 0) as clk:
             e0.record(s)
-            for _ in range(steps):
-                A.verify_attention(q, kc, vc, lens_d, out=out, block_table=bt)
+            for i in range(steps):
+                A.verify_attention(q, *sets[i % nrep], lens_d, out=out, block_table=bt)
             e1.record(s)
             torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / steps
@@ -387,13 +402,18 @@ def attn_bench(a):
                   "len U[512,8192])", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": steps,
         "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q / k / v)",
-        "config": {"workload": "config 3 verify attention, one layer" + ("" if B == 64 else
-                   f" ({B} rows)") + (", paged cache (128-token pages, random order)"
-                                      if a.paged else ""), "rows": B, "Hq": Hq,
+        "config": {"workload": ("config 3 verify attention, one layer" if cfg3 else
+                                f"verify attention, one layer, len U[{lo},{hi}]") +
+                   ("" if B == 64 else f" ({B} rows)") +
+                   (", paged cache (128-token pages, random order)" if a.paged else "") +
+                   (", mma.sync kernel" if os.environ.get("SD_ATTN_KERNEL", "")[:1] == "m"
+                    else ""), "rows": B, "Hq": Hq,
                    "Hkv": Hkv, "head_dim": D, "queries": ql, "live_keys": live,
                    "checked": f"8 rows vs the fp32 mask rule before timing, max abs error "
                               f"{worst:.2e}",
-                   "l2": "one layer reads >1 GB of K/V (> 126 MB L2)"},
+                   "l2": ("one layer reads >1 GB of K/V (> 126 MB L2)" if nrep == 1 else
+                          f"{nrep} cache copies rotated ({nrep * kv_bytes / 1e6:.0f} MB of K/V "
+                          f"> 126 MB L2)")},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                      "frac": gbs / peak, "tflops": flops_call / (ms * 1e-3) / 1e12,
                      "scope": f"{bytes_call} algorithmic bytes per call / event-timed call"},
