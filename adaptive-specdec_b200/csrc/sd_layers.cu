@@ -55,6 +55,52 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(
     yr[i] = __float2bfloat16_rn(__bfloat162float(w[i]) * bfr(__bfloat162float(xr[i]) * rs));
 }
 
+// The residual add fused in front of the norm (a decoder layer's
+// "residual = residual + h; h = norm(residual)"):
+//   s = rn(x + res) -> res_out,  out = rn(w * rn(s * rsqrt(mean(s^2) + eps)))
+// The sum is kept in registers between the passes (up to ADD_NORM_PER
+// elements per thread).
+constexpr int ADD_NORM_PER = 32;
+__global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(
+    const __nv_bfloat16* x, int64_t x_rs, const __nv_bfloat16* res, int64_t res_rs,
+    const __nv_bfloat16* __restrict__ w, float eps, __nv_bfloat16* out, int64_t out_rs,
+    __nv_bfloat16* res_out, int64_t ro_rs, int H) {   // outputs may alias inputs: one owner each
+  __shared__ float red[NORM_THREADS / 32];
+  const int64_t r = blockIdx.x;
+  float sv[ADD_NORM_PER];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < ADD_NORM_PER; ++k) {
+    const int i = threadIdx.x + k * NORM_THREADS;
+    sv[k] = 0.f;
+    if (i < H) {
+      sv[k] = bfr(__bfloat162float(x[r * x_rs + i]) + __bfloat162float(res[r * res_rs + i]));
+      ss = fmaf(sv[k], sv[k], ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) red[wid] = ss;
+  __syncthreads();
+  if (wid == 0) {
+    ss = lane < NORM_THREADS / 32 ? red[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[0] = ss;
+  }
+  __syncthreads();
+  const float rs = rsqrtf(__fdiv_rn(red[0], (float)H) + eps);
+#pragma unroll
+  for (int k = 0; k < ADD_NORM_PER; ++k) {
+    const int i = threadIdx.x + k * NORM_THREADS;
+    if (i < H) {
+      res_out[r * ro_rs + i] = __float2bfloat16_rn(sv[k]);
+      out[r * out_rs + i] = __float2bfloat16_rn(__bfloat162float(w[i]) * bfr(sv[k] * rs));
+    }
+  }
+}
+
 // out[r, i] = silu(gu[r, i]) * gu[r, I + i], one thread per output element
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t gu_rs,
                                 __nv_bfloat16* __restrict__ out, int64_t out_rs, int I,
@@ -81,6 +127,20 @@ int sd_rmsnorm(const void* x, int64_t x_rs, const void* w, float eps, void* out,
                        reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), x_rs, static_cast<const __nv_bfloat16*>(w), eps,
       static_cast<__nv_bfloat16*>(out), out_rs, H);
+  return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+}
+
+int sd_add_rmsnorm(const void* x, int64_t x_rs, const void* res, int64_t res_rs, const void* w,
+                   float eps, void* out, int64_t out_rs, void* res_out, int64_t ro_rs, int rows,
+                   int H, void* stream) {
+  if (!x || !res || !w || !out || !res_out || rows < 0 || H <= 0) return SD_EINVAL;
+  if (H > sd::ADD_NORM_PER * sd::NORM_THREADS) return SD_ENOTSUP;
+  if (rows == 0) return SD_OK;
+  sd::add_rmsnorm_kernel<<<(unsigned)rows, sd::NORM_THREADS, 0,
+                           reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), x_rs, static_cast<const __nv_bfloat16*>(res), res_rs,
+      static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(out), out_rs,
+      static_cast<__nv_bfloat16*>(res_out), ro_rs, H);
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
 }
 

@@ -41,6 +41,8 @@ _SIGNATURES = {
                                  _i64, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _i32, _i32, _i32,
                                  _i32, _i32, _vp, _vp, _vp], _i32),
     "sd_rmsnorm": ([_vp, _i64, _vp, _f32, _vp, _i64, _i32, _i32, _vp], _i32),
+    "sd_add_rmsnorm": ([_vp, _i64, _vp, _i64, _vp, _f32, _vp, _i64, _vp, _i64, _i32, _i32, _vp],
+                       _i32),
     "sd_silu_mul": ([_vp, _i64, _vp, _i64, _i32, _i32, _vp], _i32),
     "sd_kv_append_paged": ([_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i32,
                             _i32, _i32, _i32, _i32, _vp, _vp], _i32),

@@ -8,10 +8,12 @@ GEMM).  At the engine's batch sizes these forwards are launch-bound, so
 ``install(model)`` gives
 
 * every RMSNorm module one launch of sd_rmsnorm (bf16 inputs; anything else
-  runs the module's own forward), and
+  runs the module's own forward),
 * every SiLU-gated MLP one GEMM over the concatenated gate / up weights (the
   two modules' weights become views into it: no extra memory), one launch of
-  sd_silu_mul and the down GEMM.
+  sd_silu_mul and the down GEMM, and
+* every pre-norm decoder layer (Qwen3, Qwen2, Llama, Mistral) its residual
+  add and post-attention norm as one launch of sd_add_rmsnorm.
 
 Numerics are transformers' bf16 sequence; the norm's float32 sum of squares is
 reduced in another order, so a value can differ by one bf16 ulp.
@@ -22,7 +24,7 @@ import torch
 
 from specdec import _lib as L
 
-__all__ = ["rmsnorm", "silu_mul", "install", "uninstall", "installed_modules"]
+__all__ = ["rmsnorm", "add_rmsnorm", "silu_mul", "install", "uninstall", "installed_modules"]
 
 
 def _rows(x, H):
@@ -55,6 +57,27 @@ def rmsnorm(x, weight, eps, out=None):
                                    o2.stride(0), x2.shape[0], H, L.stream_ptr(x.device)),
                 "rmsnorm")
     return out
+
+
+def add_rmsnorm(x, res, weight, eps):
+    """(rn(x + res), rmsnorm(rn(x + res))): a decoder layer's residual add and
+    the norm after it in one launch (bf16, H <= 8192)."""
+    L.require_cuda(x, res, weight)
+    if x.dtype != torch.bfloat16 or res.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise L.SpecdecError("add_rmsnorm takes bf16 tensors")
+    H = x.shape[-1]
+    if res.shape != x.shape or weight.numel() != H or not weight.is_contiguous():
+        raise L.SpecdecError("add_rmsnorm: x, res [..., H] and a contiguous weight [H]")
+    x2, r2 = _rows(x, H), _rows(res, H)
+    res_out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    o2, ro2 = out.view(-1, H), res_out.view(-1, H)
+    with torch.cuda.device(x.device):
+        L.check(L.lib().sd_add_rmsnorm(L.ptr(x2), x2.stride(0), L.ptr(r2), r2.stride(0),
+                                       L.ptr(weight), float(eps), L.ptr(o2), o2.stride(0),
+                                       L.ptr(ro2), ro2.stride(0), x2.shape[0], H,
+                                       L.stream_ptr(x.device)), "add_rmsnorm")
+    return res_out, out
 
 
 def silu_mul(gu, out=None):
@@ -119,11 +142,48 @@ def _fuse_gate_up(m):
     return W, bias
 
 
+# decoder layers whose forward is the pre-norm sequence
+#   r = x; h = attn(input_layernorm(x)); r = r + h; h = mlp(post_norm(r)); r + h
+_PRE_NORM_LAYERS = ("Qwen3DecoderLayer", "Qwen2DecoderLayer", "LlamaDecoderLayer",
+                    "MistralDecoderLayer")
+
+
+def _is_pre_norm_layer(m):
+    return (type(m).__name__ in _PRE_NORM_LAYERS and not hasattr(m, "_sd_orig_forward")
+            and all(hasattr(m, a) for a in ("self_attn", "mlp", "input_layernorm",
+                                            "post_attention_layernorm")))
+
+
+def _layer_forward(self, hidden_states, attention_mask=None, position_ids=None,
+                   past_key_values=None, use_cache=False, position_embeddings=None, **kwargs):
+    pn = self.post_attention_layernorm
+    if not (hidden_states.is_cuda and hidden_states.dtype == torch.bfloat16
+            and pn.weight.dtype == torch.bfloat16 and hidden_states.shape[-1] <= 8192):
+        return self._sd_orig_forward(hidden_states, attention_mask=attention_mask,
+                                     position_ids=position_ids, past_key_values=past_key_values,
+                                     use_cache=use_cache, position_embeddings=position_embeddings,
+                                     **kwargs)
+    residual = hidden_states
+    h = self.input_layernorm(hidden_states)
+    h, _ = self.self_attn(hidden_states=h, attention_mask=attention_mask,
+                          position_ids=position_ids, past_key_values=past_key_values,
+                          use_cache=use_cache, position_embeddings=position_embeddings, **kwargs)
+    residual, h = add_rmsnorm(h, residual, pn.weight, pn.variance_epsilon)
+    h = self.mlp(h)
+    return residual + h
+
+
 def install(model):
-    """Put the one-launch forwards on every RMSNorm and SiLU-gated MLP of
+    """Put the one-launch forwards on every RMSNorm, SiLU-gated MLP and
+    pre-norm decoder layer (residual add fused into its second norm) of
     ``model``; returns how many modules changed (again: none)."""
     n = 0
     for m in model.modules():
+        if _is_pre_norm_layer(m):
+            m._sd_orig_forward = m.forward
+            m.forward = types.MethodType(_layer_forward, m)
+            n += 1
+            continue
         if _is_rmsnorm(m):
             m._sd_orig_forward = m.forward
             m.forward = types.MethodType(_norm_forward, m)
@@ -152,7 +212,7 @@ def uninstall(model):
 
 def _is_norm_installed(m):
     f = getattr(m.forward, "__func__", None)
-    return f is _norm_forward
+    return f is _norm_forward or f is _layer_forward
 
 
 def _is_mlp_installed(m):

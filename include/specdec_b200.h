@@ -254,6 +254,16 @@ int sd_rmsnorm(const void* x, int64_t x_rs, const void* w, float eps, void* out,
                int rows, int H, void* stream);
 
 /*
+ * A decoder layer's residual add and the norm after it as one launch (bf16):
+ *   res_out = rn(x + res);  out = sd_rmsnorm(res_out)
+ * (transformers' "residual = residual + hidden_states" then
+ * post_attention_layernorm).  H <= 8192.  Outputs may alias the inputs.
+ */
+int sd_add_rmsnorm(const void* x, int64_t x_rs, const void* res, int64_t res_rs, const void* w,
+                   float eps, void* out, int64_t out_rs, void* res_out, int64_t ro_rs, int rows,
+                   int H, void* stream);
+
+/*
  * The gated MLP's activation as one launch (bf16): gu rows hold [gate | up]
  * (2 I elements, rows gu_rs apart);
  *   out[r, i] = rn(rn(silu(gate[r, i])) * up[r, i])

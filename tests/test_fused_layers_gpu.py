@@ -49,6 +49,21 @@ def test_rmsnorm_matches_transformers(shape):
     assert torch.equal(y, got)
 
 
+@pytest.mark.parametrize("shape", [(32, 5, 4096), (32, 1, 1024), (2, 3, 8192)])
+def test_add_rmsnorm_matches_transformers(shape):
+    """residual = residual + h (bf16), then the post-attention norm."""
+    g = torch.Generator(device=DEV).manual_seed(2)
+    H = shape[-1]
+    h = torch.randn(*shape, generator=g, device=DEV).to(torch.bfloat16)
+    res = (4 * torch.randn(*shape, generator=g, device=DEV)).to(torch.bfloat16)
+    w = (1 + 0.2 * torch.randn(H, generator=g, device=DEV)).to(torch.bfloat16)
+    r_got, y_got = FL.add_rmsnorm(h, res, w, 1e-6)
+    r_want = res + h
+    assert torch.equal(r_got, r_want)
+    ok, exact = _ulp_check(y_got, _ref_norm(r_want, w, 1e-6))
+    assert ok and exact >= EXACT_MIN, (ok, exact)
+
+
 def _ref_norm(x, w, eps):
     xf = x.float()
     v = xf.pow(2).mean(-1, keepdim=True)
