@@ -275,3 +275,28 @@ def test_rollback_invariant_tiny_qwen3():
                     layer.values[b, :, int(cc.lengths[b]):] = 99.0
         outs.append(_fwd(m, cc, nxt).clone())
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("case", [
+    # B, Hq, Hkv, qlen, lengths (None: U[512, 640]), valid, C
+    (32, 16, 8, 1, None, None, 1040),                 # a config-4 draft step (2 rows / kv head)
+    (4, 32, 8, 2, [0, 127, 128, 1000], None, 1200),   # 8 rows per kv head, page bounds
+    (3, 8, 8, 8, [5, 300, 0], [9, 303, 4], 320),      # group 1, 8 queries, a capped prefill
+    (2, 16, 8, 1, [7000, 8100], None, 8200),          # long rows: 64 chunks each
+])
+def test_decode_attention_matches_reference_rule(case):
+    """The decode path (<= 8 query rows per kv head: a draft step) against
+    the fp32 mask rule, rows of every length class."""
+    B, Hq, Hkv, ql, lens, valid, C = case
+    g = torch.Generator(device=DEV).manual_seed(4)
+    D = 128
+    if lens is None:
+        lens = torch.randint(512, 641, (B,), generator=torch.Generator().manual_seed(0)).tolist()
+    q = torch.randn(B, Hq, ql, D, generator=g, device=DEV).to(torch.bfloat16)
+    kc = torch.randn(B, Hkv, C, D, generator=g, device=DEV).to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, C, D, generator=g, device=DEV).to(torch.bfloat16)
+    lens_d = torch.tensor(lens, device=DEV)
+    val = None if valid is None else torch.tensor(valid, device=DEV)
+    out = A.verify_attention(q, kc, vc, lens_d, valid=val)
+    ref = _ref_attention(q, kc, vc, lens_d, val, D ** -0.5)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
