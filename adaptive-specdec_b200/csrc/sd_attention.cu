@@ -223,172 +223,6 @@ __global__ void attn_combine_kernel(AttnParams P) {
 }
 
 // ---------------------------------------------------------------------------
-// Decode path (bf16, head_dim 128, R = qlen * group <= DC_RMAX query rows: a
-// draft step's forward).  One CTA per (row, kv head, page of DC_KEYS keys),
-// split-K over the whole grid, so short rows still spread over every SM and
-// no CTA carries a per-segment pipeline.  With so few query rows the work is
-// ~1 FMA per K/V byte, well inside the CUDA cores' rate: thread t takes key
-// s0 + t for the scores (its 256-byte K row in 16-byte loads, the query rows
-// from shared memory), the chunk's softmax is one block reduction per row in
-// base 2, and P V is read one 4-byte bf16 pair per thread and key (threads
-// 0-63 the chunk's first 64 keys, 64-127 the rest).  Each CTA leaves a
-// partial (max, sum, O) that attn_combine_kernel merges.
-// ---------------------------------------------------------------------------
-constexpr int DC_KEYS = 128;             // keys per CTA (one page of a paged cache)
-constexpr int DC_THREADS = 128;
-constexpr int DC_RMAX = 8;
-constexpr int DC_D = 128;
-
-__device__ __forceinline__ float dc_block_max(float v, float* red, int w, int lane, int nw) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  if (lane == 0) red[w] = v;
-  __syncthreads();
-  float r = red[0];
-  for (int i = 1; i < nw; ++i) r = fmaxf(r, red[i]);
-  __syncthreads();
-  return r;
-}
-
-__global__ void __launch_bounds__(DC_THREADS) attn_decode_kernel(AttnParams P) {
-  __shared__ float qs[DC_RMAX][DC_D];
-  __shared__ float ps[DC_RMAX][DC_KEYS];
-  __shared__ float po[DC_RMAX][DC_D];
-  __shared__ float red[DC_THREADS / 32];
-  const int chunk = blockIdx.x % P.nsplit;
-  const int bh = blockIdx.x / P.nsplit;
-  const int h = bh % P.Hkv, b = bh / P.Hkv;
-  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-  const int R = P.R;
-  const int s0 = chunk * DC_KEYS;
-  const int64_t pbase = ((int64_t)bh * P.nsplit + chunk) * R;
-  int lim[DC_RMAX];
-  int kmax = 0;
-#pragma unroll
-  for (int r = 0; r < DC_RMAX; ++r) {
-    lim[r] = r < R ? row_limit(P, b, r / P.group) : 0;
-    kmax = max(kmax, lim[r]);
-  }
-  if (s0 >= kmax) {                                   // no live key of this row here
-    for (int i = t; i < R * DC_D; i += DC_THREADS) P.part_acc[pbase * DC_D + i] = 0.f;
-    if (t < R) {
-      P.part_ml[(pbase + t) * 2] = -INFINITY;
-      P.part_ml[(pbase + t) * 2 + 1] = 0.f;
-    }
-    return;
-  }
-  const __nv_bfloat16* Q = reinterpret_cast<const __nv_bfloat16*>(P.q);
-  const __nv_bfloat16* K = reinterpret_cast<const __nv_bfloat16*>(P.k);
-  const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(P.v);
-  const float sl2 = P.scale * 1.4426950408889634f;
-  for (int i = t; i < R * DC_D; i += DC_THREADS) {
-    const int r = i / DC_D, d = i % DC_D;
-    const int j = r / P.group, hq = h * P.group + r % P.group;
-    qs[r][d] = __bfloat162float(Q[b * P.qbs + hq * P.qhs + j * P.qqs + d]) * sl2;
-  }
-  __syncthreads();
-  // scores of key s0 + t, base 2
-  const int s = s0 + t;
-  float sc[DC_RMAX];
-#pragma unroll
-  for (int r = 0; r < DC_RMAX; ++r) sc[r] = -INFINITY;
-  if (s < kmax) {
-    const uint4* kr = reinterpret_cast<const uint4*>(K + kv_row(P, b, h, s) * DC_D);
-    float acc[DC_RMAX];
-#pragma unroll
-    for (int r = 0; r < DC_RMAX; ++r) acc[r] = 0.f;
-#pragma unroll 4
-    for (int c = 0; c < DC_D / 8; ++c) {
-      const uint4 u = __ldg(kr + c);
-      const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&u);
-      float kf[8];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(hp[e]);
-        kf[2 * e] = f.x;
-        kf[2 * e + 1] = f.y;
-      }
-#pragma unroll
-      for (int r = 0; r < DC_RMAX; ++r) {
-        if (r < R) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[r] = fmaf(qs[r][8 * c + e], kf[e], acc[r]);
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < DC_RMAX; ++r)
-      if (r < R && s < lim[r]) sc[r] = acc[r];
-  }
-  // per row: the chunk's max, p = 2^(s - m), the sum of p
-  float mrow[DC_RMAX], lrow[DC_RMAX];
-#pragma unroll
-  for (int r = 0; r < DC_RMAX; ++r) {
-    mrow[r] = -INFINITY;
-    lrow[r] = 0.f;
-    if (r < R) {
-      const float m = dc_block_max(sc[r], red, w, lane, DC_THREADS / 32);
-      const float p = sc[r] == -INFINITY ? 0.f : exp2f(sc[r] - m);
-      ps[r][t] = p;
-      float sum = p;
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (lane == 0) red[w] = sum;
-      __syncthreads();
-      lrow[r] = (red[0] + red[1]) + (red[2] + red[3]);
-      mrow[r] = m;
-      __syncthreads();
-    }
-  }
-  // O = P V over the chunk: dims 2 dp, 2 dp + 1; keys of half kh
-  const int dp = t & 63, kh = t >> 6;
-  const int kbeg = kh * (DC_KEYS / 2);
-  const int kend = min(kbeg + DC_KEYS / 2, kmax - s0);
-  float o0[DC_RMAX], o1[DC_RMAX];
-#pragma unroll
-  for (int r = 0; r < DC_RMAX; ++r) o0[r] = o1[r] = 0.f;
-#pragma unroll 4
-  for (int i = kbeg; i < kend; ++i) {
-    const __nv_bfloat162 vv =
-        *reinterpret_cast<const __nv_bfloat162*>(V + kv_row(P, b, h, s0 + i) * DC_D + 2 * dp);
-    const float2 vf = __bfloat1622float2(vv);
-#pragma unroll
-    for (int r = 0; r < DC_RMAX; ++r) {
-      if (r < R) {
-        const float p = ps[r][i];
-        o0[r] = fmaf(p, vf.x, o0[r]);
-        o1[r] = fmaf(p, vf.y, o1[r]);
-      }
-    }
-  }
-  if (kh == 1) {
-#pragma unroll
-    for (int r = 0; r < DC_RMAX; ++r)
-      if (r < R) {
-        po[r][2 * dp] = o0[r];
-        po[r][2 * dp + 1] = o1[r];
-      }
-  }
-  __syncthreads();
-  if (kh == 0) {
-#pragma unroll
-    for (int r = 0; r < DC_RMAX; ++r)
-      if (r < R) {
-        float2 v2 = make_float2(o0[r] + po[r][2 * dp], o1[r] + po[r][2 * dp + 1]);
-        *reinterpret_cast<float2*>(P.part_acc + (pbase + r) * DC_D + 2 * dp) = v2;
-      }
-  }
-  if (t < DC_RMAX && t < R) {
-    float m = -INFINITY, l = 0.f;
-#pragma unroll
-    for (int r = 0; r < DC_RMAX; ++r)
-      if (r == t) { m = mrow[r]; l = lrow[r]; }
-    P.part_ml[(pbase + t) * 2] = m == -INFINITY ? -INFINITY : m * 0.6931471805599453f;
-    P.part_ml[(pbase + t) * 2 + 1] = l;
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Tensor-core path (bf16, head_dim 128, R = qlen * group <= 32 query rows)
 // ---------------------------------------------------------------------------
 // One CTA per (row, kv head, split of SPLIT_KEYS keys), 4 warps.  Per tile of
@@ -1563,20 +1397,16 @@ static int launch_tc(const AttnParams& P, cudaStream_t st) {
   }
 }
 
-// Which kernel takes the tensor-core shapes: by default the decode kernel for
-// <= DC_RMAX query rows per kv head and tcgen05 above; SD_ATTN_KERNEL=tc
-// (tcgen05 for every row count) or =mma (the mma.sync kernel) keep the others
-// for comparison.
-static int attn_kernel_mode() {              // 0 mma.sync, 1 tcgen05, 2 decode + tcgen05
+// Which kernel takes the tensor-core shapes: tcgen05 (default) or the
+// mma.sync kernel (SD_ATTN_KERNEL=mma, kept for comparison).
+static bool use_tcgen05() {
   static int mode = -1;
   if (mode < 0) {
     const char* e = getenv("SD_ATTN_KERNEL");
-    mode = (e && e[0] == 'm') ? 0 : (e && e[0] == 't') ? 1 : 2;
+    mode = (e && e[0] == 'm') ? 0 : 1;
   }
-  return mode;
+  return mode == 1;
 }
-static bool use_tcgen05() { return attn_kernel_mode() != 0; }
-static int decode_chunks(int C, int qlen) { return (C + qlen + DC_KEYS - 1) / DC_KEYS; }
 
 }  // namespace sd
 
@@ -1587,9 +1417,7 @@ extern "C" {
 size_t sd_verify_attn_workspace_bytes(int B, int Hq, int Hkv, int D, int C, int qlen) {
   if (B <= 0 || Hkv <= 0 || Hq % Hkv) return 0;
   const int R = qlen * (Hq / Hkv);
-  size_t np = (size_t)nsplit_for(C, qlen) + 1;         // pieces per (row, kv head), either path
-  if (R <= DC_RMAX && D == DC_D) np = np > (size_t)decode_chunks(C, qlen) ?
-                                           np : (size_t)decode_chunks(C, qlen);
+  const size_t np = (size_t)nsplit_for(C, qlen) + 1;   // pieces per (row, kv head), either path
   return (size_t)B * Hkv * np * R * (D + 2) * sizeof(float) +
          ((size_t)B * Hkv + 2 * (size_t)B + 2) * sizeof(int) + 256;
 }
@@ -1623,9 +1451,6 @@ static int verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, con
   float* ws = reinterpret_cast<float*>(workspace);
   P.part_acc = ws;
   P.npiece = P.nsplit + 1;
-  if (P.R <= DC_RMAX && D == DC_D && decode_chunks(C, qlen) > P.npiece)
-    P.npiece = decode_chunks(C, qlen);                 // the decode path's pieces (same sizing
-                                                       // as sd_verify_attn_workspace_bytes)
   P.part_ml = ws + (size_t)B * Hkv * P.npiece * P.R * D;
   P.split_done = reinterpret_cast<int*>(P.part_ml + (size_t)B * Hkv * P.npiece * P.R * 2);
   P.rowpre = P.split_done + (size_t)B * Hkv;
@@ -1642,15 +1467,6 @@ static int verify_attn(const void* q, int64_t qbs, int64_t qhs, int64_t qqs, con
                       qhs % 8 == 0 && qqs % 8 == 0 &&
                       (reinterpret_cast<uintptr_t>(kcache) & 15) == 0 &&
                       (reinterpret_cast<uintptr_t>(vcache) & 15) == 0;
-  if (mma_ok && P.R <= DC_RMAX && attn_kernel_mode() == 2) {
-    P.nrc = 1;
-    P.nsplit = decode_chunks(C, qlen);
-    const int64_t grid = (int64_t)B * Hkv * P.nsplit;
-    if (grid > 0x7FFFFFFF) return SD_ENOTSUP;
-    attn_decode_kernel<<<(unsigned)grid, DC_THREADS, 0, st>>>(P);
-    attn_combine_kernel<__nv_bfloat16><<<B * Hkv * P.R, D, 0, st>>>(P);
-    return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
-  }
   if (mma_ok && use_tcgen05()) {
     P.nrc = 1;
     P.tile_keys = TC_KEYS;

@@ -284,9 +284,9 @@ def test_rollback_invariant_tiny_qwen3():
     (3, 8, 8, 8, [5, 300, 0], [9, 303, 4], 320),      # group 1, 8 queries, a capped prefill
     (2, 16, 8, 1, [7000, 8100], None, 8200),          # long rows: 64 chunks each
 ])
-def test_decode_attention_matches_reference_rule(case):
-    """The decode path (<= 8 query rows per kv head: a draft step) against
-    the fp32 mask rule, rows of every length class."""
+def test_attention_few_query_rows_matches_reference_rule(case):
+    """<= 8 query rows per kv head (a draft step, group-1 layers, short
+    prefills) against the fp32 mask rule, rows of every length class."""
     B, Hq, Hkv, ql, lens, valid, C = case
     g = torch.Generator(device=DEV).manual_seed(4)
     D = 128
