@@ -101,6 +101,103 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(
   }
 }
 
+// Vector forms for the usual widths (H = 256 VPL, rows 16-byte aligned): one
+// warp per row, the row in registers (VPL 16-byte units per lane, unit u of
+// lane l at element 8 (l + 32 u)), one read, one warp reduction.  `res`
+// non-null: the residual add first (res_out = rn(x + res)).
+constexpr int NORM_ROWS_PER_CTA = 4;
+
+__device__ __forceinline__ void bf8_to_f(const uint4& u, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 v = __bfloat1622float2(h[e]);
+    f[2 * e] = v.x;
+    f[2 * e + 1] = v.y;
+  }
+}
+__device__ __forceinline__ uint4 f_to_bf8(const float* f) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+  return u;
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(32 * NORM_ROWS_PER_CTA) rmsnorm_vec_kernel(
+    const __nv_bfloat16* x, int64_t x_rs, const __nv_bfloat16* res, int64_t res_rs,
+    const __nv_bfloat16* __restrict__ w, float eps, __nv_bfloat16* out, int64_t out_rs,
+    __nv_bfloat16* res_out, int64_t ro_rs, int rows) {
+  constexpr int H = 256 * VPL;
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * NORM_ROWS_PER_CTA + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + r * x_rs);
+  uint4 u[VPL];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) u[k] = xr[lane + 32 * k];
+  if (res != nullptr) {
+    const uint4* rr = reinterpret_cast<const uint4*>(res + r * res_rs);
+    uint4* ro = reinterpret_cast<uint4*>(res_out + r * ro_rs);
+    uint4 v[VPL];
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) v[k] = rr[lane + 32 * k];
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      float a[8], c[8];
+      bf8_to_f(u[k], a);
+      bf8_to_f(v[k], c);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a[e] += c[e];
+      u[k] = f_to_bf8(a);                             // s = rn(x + res)
+      ro[lane + 32 * k] = u[k];
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    float a[8];
+    bf8_to_f(u[k], a);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(a[e], a[e], ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rs = rsqrtf(__fdiv_rn(ss, (float)H) + eps);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(out + r * out_rs);
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    float a[8], g[8];
+    bf8_to_f(u[k], a);
+    bf8_to_f(__ldg(wr + lane + 32 * k), g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a[e] = g[e] * bfr(a[e] * rs);
+    yr[lane + 32 * k] = f_to_bf8(a);
+  }
+}
+
+// The vector kernel for this width and alignment, else nullptr.
+typedef void (*NormVecFn)(const __nv_bfloat16*, int64_t, const __nv_bfloat16*, int64_t,
+                          const __nv_bfloat16*, float, __nv_bfloat16*, int64_t, __nv_bfloat16*,
+                          int64_t, int);
+static NormVecFn norm_vec_for(int H, const void* const* ptrs, int nptr, const int64_t* rs,
+                              int nrs) {
+  for (int i = 0; i < nptr; ++i)
+    if (ptrs[i] && (reinterpret_cast<uintptr_t>(ptrs[i]) & 15)) return nullptr;
+  for (int i = 0; i < nrs; ++i)
+    if (rs[i] % 8) return nullptr;
+  switch (H) {
+    case 512: return rmsnorm_vec_kernel<2>;
+    case 1024: return rmsnorm_vec_kernel<4>;
+    case 2048: return rmsnorm_vec_kernel<8>;
+    case 3072: return rmsnorm_vec_kernel<12>;
+    case 4096: return rmsnorm_vec_kernel<16>;
+    default: return nullptr;
+  }
+}
+
 // out[r, i] = silu(gu[r, i]) * gu[r, I + i], one thread per output element
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t gu_rs,
                                 __nv_bfloat16* __restrict__ out, int64_t out_rs, int I,
@@ -123,6 +220,19 @@ int sd_rmsnorm(const void* x, int64_t x_rs, const void* w, float eps, void* out,
                int rows, int H, void* stream) {
   if (!x || !w || !out || rows < 0 || H <= 0) return SD_EINVAL;
   if (rows == 0) return SD_OK;
+  {
+    const void* ptrs[3] = {x, w, out};
+    const int64_t rs[2] = {x_rs, out_rs};
+    sd::NormVecFn f = sd::norm_vec_for(H, ptrs, 3, rs, 2);
+    if (f) {
+      const unsigned grid = (unsigned)((rows + sd::NORM_ROWS_PER_CTA - 1) / sd::NORM_ROWS_PER_CTA);
+      f<<<grid, 32 * sd::NORM_ROWS_PER_CTA, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+          static_cast<const __nv_bfloat16*>(x), x_rs, nullptr, 0,
+          static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(out), out_rs,
+          nullptr, 0, rows);
+      return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+    }
+  }
   sd::rmsnorm_kernel<<<(unsigned)rows, sd::NORM_THREADS, 0,
                        reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), x_rs, static_cast<const __nv_bfloat16*>(w), eps,
@@ -136,6 +246,19 @@ int sd_add_rmsnorm(const void* x, int64_t x_rs, const void* res, int64_t res_rs,
   if (!x || !res || !w || !out || !res_out || rows < 0 || H <= 0) return SD_EINVAL;
   if (H > sd::ADD_NORM_PER * sd::NORM_THREADS) return SD_ENOTSUP;
   if (rows == 0) return SD_OK;
+  {
+    const void* ptrs[5] = {x, res, w, out, res_out};
+    const int64_t rs[4] = {x_rs, res_rs, out_rs, ro_rs};
+    sd::NormVecFn f = sd::norm_vec_for(H, ptrs, 5, rs, 4);
+    if (f) {
+      const unsigned grid = (unsigned)((rows + sd::NORM_ROWS_PER_CTA - 1) / sd::NORM_ROWS_PER_CTA);
+      f<<<grid, 32 * sd::NORM_ROWS_PER_CTA, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+          static_cast<const __nv_bfloat16*>(x), x_rs, static_cast<const __nv_bfloat16*>(res),
+          res_rs, static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(out),
+          out_rs, static_cast<__nv_bfloat16*>(res_out), ro_rs, rows);
+      return cudaGetLastError() == cudaSuccess ? SD_OK : SD_ELAUNCH;
+    }
+  }
   sd::add_rmsnorm_kernel<<<(unsigned)rows, sd::NORM_THREADS, 0,
                            reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), x_rs, static_cast<const __nv_bfloat16*>(res), res_rs,
