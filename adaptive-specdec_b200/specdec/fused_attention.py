@@ -148,6 +148,7 @@ def _fused_forward(self, hidden_states, position_embeddings=None, attention_mask
     if (not isinstance(cache, RaggedCache) or cache.attn_impl != A.IMPL
             or self.config._attn_implementation != A.IMPL or position_embeddings is None
             or hidden_states.dtype != torch.bfloat16 or D % 2 or D > D_MAX
+            or position_embeddings[0].dtype != torch.bfloat16
             or getattr(self, "sliding_window", None) is not None):
         return self._sd_orig_forward(hidden_states, position_embeddings, attention_mask,
                                      past_key_values=past_key_values, **kwargs)

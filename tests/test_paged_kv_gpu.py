@@ -175,6 +175,44 @@ def test_tiny_model_through_paged_cache(dtype):
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@torch.inference_mode()
+def test_long_prefill_through_paged_cache(dtype):
+    """A right-padded prefill longer than 64 tokens on a fresh cache runs
+    torch's SDPA over the first P slots; the paged cache gathers them from
+    its pages (the padding from the sink page).  The last real token's
+    logits and the next forward match the contiguous cache."""
+    from transformers import Qwen3ForCausalLM
+    A.register()
+    torch.manual_seed(0)
+    m = Qwen3ForCausalLM(tiny_config(32, 2)).eval().to(DEV, dtype)
+    m.set_attn_implementation(A.IMPL)
+    if dtype == torch.bfloat16:
+        FA.install(m)
+    B, P = 3, 150
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, VOCAB, (B, P), generator=g).to(DEV)
+    plen = torch.tensor([150, 90, 131])
+    nxt = torch.randint(0, VOCAB, (B, 2), generator=g).to(DEV)
+    outs = []
+    for paged in (False, True):
+        c = PagedRaggedCache(2, B, 3 * PAGE, DEV, n_pages=10) if paged else \
+            RaggedCache(2, B, 3 * PAGE, DEV, attn_impl=A.IMPL)
+        if paged:
+            c.reserve_prefill(P, plen)
+        lg = _fwd(m, c, ids, valid=plen.to(DEV))
+        last = lg[torch.arange(B, device=DEV), (plen - 1).to(DEV)].clone()
+        c.set_lengths(plen)
+        if paged:
+            c.reserve(2)
+        lg2 = _fwd(m, c, nxt).clone()
+        c.check_errors()
+        outs.append((last, lg2))
+    tol = 1e-4 if dtype == torch.float32 else 3e-2
+    for a, b in zip(*outs):
+        torch.testing.assert_close(b.float(), a.float(), atol=tol, rtol=tol)
+
+
 @torch.inference_mode()
 def test_engine_paged_matches_contiguous():
     """The engine with paged caches emits the same tokens as with contiguous
