@@ -398,8 +398,10 @@ def attn_bench(a):
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = peaks.get("hbm_gbs") or 6650.0
     print(json.dumps({
-        "metric": "verify attention GB/s (config 3, one layer: B=64, 32q/8kv x 128, 5 queries, "
-                  "len U[512,8192])", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": steps,
+        "metric": ("verify attention GB/s (config 3, one layer: B=64, 32q/8kv x 128, 5 queries, "
+                   "len U[512,8192])" if cfg3 and B == 64 else
+                   f"verify attention GB/s (one layer: B={B}, {Hq}q/{Hkv}kv x {D}, {ql} queries, "
+                   f"len U[{lo},{hi}])"), "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": steps,
         "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q / k / v)",
         "config": {"workload": ("config 3 verify attention, one layer" if cfg3 else
