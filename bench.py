@@ -229,13 +229,13 @@ def reference_arm(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    rate, steps, kind, cores = ref_rate(a.mode, B, budget_s=60.0, max_steps=a.steps,
-                                        warmup=min(a.warmup, 1))
+    wu = min(max(a.warmup, 3), 5)           # >= 3 warm-up rounds, bounded (~2 s each on CPU)
+    rate, steps, kind, cores = ref_rate(a.mode, B, budget_s=60.0, max_steps=a.steps, warmup=wu)
     src = ("specdec/sampling.py of the reference (baseline/_ref), torch CPU"
            if kind == "reference" else "oracle/sampling_oracle.py (reference not installed)")
     print(json.dumps({
         "impl": "reference", "metric": metric_name(a.mode), "value": rate, "unit": "rows/s",
-        "n_gpus": a.gpus, "steps": steps, "warmup": min(a.warmup, 1),
+        "n_gpus": a.gpus, "steps": steps, "warmup": wu,
         "ms_per_step": 1e3 * B / rate, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded config-2 logits, bf16 inputs)",
